@@ -1,0 +1,44 @@
+// Shared helpers: error type carrying a C-ABI status code, CUDA checks.
+#pragma once
+
+#include <cstdint>
+#include <cstdio>
+#include <stdexcept>
+#include <string>
+
+#include <cuda_runtime.h>
+
+#include "../../include/pyflame_cuda.h"
+
+namespace pfb {
+
+// Exception used inside the library; the C-ABI layer turns it into a status
+// code (no exception crosses extern "C", like rocm_kernels.hip:740-806).
+struct Error : std::runtime_error {
+  int code;
+  Error(int c, const std::string& msg) : std::runtime_error(msg), code(c) {}
+};
+
+[[noreturn]] inline void fail(int code, const std::string& msg) { throw Error(code, msg); }
+
+#define PFB_CHECK_ARG(cond, msg)                                               \
+  do {                                                                         \
+    if (!(cond)) ::pfb::fail(PFC_ERR_INVALID_ARGUMENT, std::string(msg));      \
+  } while (0)
+
+#define PFB_CUDA(expr)                                                         \
+  do {                                                                         \
+    cudaError_t _e = (expr);                                                   \
+    if (_e != cudaSuccess) {                                                   \
+      ::pfb::fail(_e == cudaErrorMemoryAllocation ? PFC_ERR_OUT_OF_MEMORY      \
+                                                  : PFC_ERR_CUDA,              \
+                  std::string(#expr) + ": " + cudaGetErrorString(_e));         \
+    }                                                                          \
+  } while (0)
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline int64_t round_up(int64_t a, int64_t b) { return ceil_div(a, b) * b; }
+
+void set_last_error(const std::string& msg);
+
+}  // namespace pfb

@@ -1,0 +1,2452 @@
+// Graph -> Plan compiler.  See compiler.hpp.
+//
+// Node semantics follow PyFlame's producers and CPU evaluators; each op's
+// reference is cited where it is lowered.  Passes, in order:
+//   1. classify nodes (leaf / view / elementwise / row / gemm / conv / pool / concat)
+//   2. absorb GEMM and conv epilogues: MATMUL -> *splat -> +bias -> act -> +residual,
+//      CONV2D -> +bias[1,C,1,1] -> BATCH_NORM(eval) -> RELU
+//   3. grow convex elementwise regions of equal shape
+//   4. attach row operations (reductions, softmax, LayerNorm) to the region
+//      that produces their input, so the prologue is computed in registers
+//   5. decide which values are materialised, build strided views for shape
+//      ops, emit steps, plan buffer liveness and the arena.
+#include "compiler.hpp"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <functional>
+#include <map>
+#include <set>
+#include <sstream>
+
+#include "jit.hpp"
+
+namespace pfb {
+
+bool View::is_contiguous() const {
+  int64_t expect = 1;
+  for (int d = (int)shape.size() - 1; d >= 0; --d) {
+    if (shape[d] != 1 && strides[d] != expect) return false;
+    expect *= shape[d];
+  }
+  return true;
+}
+
+std::vector<int64_t> View::dense_strides(const std::vector<int64_t>& shape) {
+  std::vector<int64_t> s(shape.size());
+  int64_t acc = 1;
+  for (int d = (int)shape.size() - 1; d >= 0; --d) {
+    s[d] = acc;
+    acc *= shape[d];
+  }
+  return s;
+}
+
+namespace {
+
+enum class Cls : uint8_t { LEAF, VIEW, EW, ROW, GEMM, CONV, POOL, CONCAT };
+
+bool is_view_op(Op op) {
+  switch (op) {
+    case Op::RESHAPE: case Op::VIEW: case Op::SQUEEZE: case Op::UNSQUEEZE: case Op::TRANSPOSE:
+    case Op::SLICE: case Op::BROADCAST: case Op::CONTIGUOUS: case Op::COPY:
+    case Op::LAYOUT_TRANSFORM: case Op::DROPOUT:
+      return true;
+    default:
+      return false;
+  }
+}
+
+bool is_row_op(Op op) {
+  switch (op) {
+    case Op::SUM: case Op::MEAN: case Op::MAX: case Op::MIN: case Op::PROD:
+    case Op::SOFTMAX: case Op::LOG_SOFTMAX: case Op::LAYER_NORM:
+      return true;
+    default:
+      return false;
+  }
+}
+
+bool is_act(Op op) {
+  return op == Op::RELU || op == Op::GELU || op == Op::SIGMOID || op == Op::TANH || op == Op::SILU;
+}
+int act_code(Op op) {
+  switch (op) {
+    case Op::RELU: return 1; case Op::GELU: return 2; case Op::SIGMOID: return 3;
+    case Op::TANH: return 4; case Op::SILU: return 5; default: return 0;
+  }
+}
+
+int64_t prod(const std::vector<int64_t>& v, size_t b = 0, size_t e = SIZE_MAX) {
+  int64_t p = 1;
+  for (size_t i = b; i < std::min(e, v.size()); ++i) p *= v[i];
+  return p;
+}
+
+std::string shape_str(const std::vector<int64_t>& s) {
+  std::string r = "[";
+  for (size_t i = 0; i < s.size(); ++i) r += (i ? "," : "") + std::to_string(s[i]);
+  return r + "]";
+}
+
+// Right-aligned broadcast of a view to `shape` (shape_inference.hpp:16-42).
+View broadcast_to(const View& v, const std::vector<int64_t>& shape) {
+  View r = v;
+  size_t nd = shape.size();
+  if (v.shape.size() > nd) fail(PFC_ERR_GRAPH, "cannot broadcast " + shape_str(v.shape) + " to " + shape_str(shape));
+  r.shape = shape;
+  r.strides.assign(nd, 0);
+  size_t off = nd - v.shape.size();
+  for (size_t d = 0; d < v.shape.size(); ++d) {
+    int64_t sz = v.shape[d], tgt = shape[off + d];
+    if (sz == tgt) r.strides[off + d] = v.strides.empty() ? 0 : v.strides[d];
+    else if (sz == 1) r.strides[off + d] = 0;
+    else fail(PFC_ERR_GRAPH, "Shapes are not broadcastable: " + shape_str(v.shape) + " vs " + shape_str(shape));
+  }
+  return r;
+}
+
+// Stride-preserving reshape; false when the new shape cannot view the data.
+bool reshape_view(const View& v, const std::vector<int64_t>& ns, View* out) {
+  *out = v;
+  out->shape = ns;
+  int64_t n = v.numel();
+  if (n == 0 || n == 1 || v.is_contiguous()) {
+    out->strides = View::dense_strides(ns);
+    return true;
+  }
+  const auto& os = v.shape;
+  const auto& ost = v.strides;
+  std::vector<int64_t> st(ns.size(), 0);
+  int vd = (int)ns.size() - 1;
+  int64_t base = ost.back(), tn = 1, vn = 1;
+  for (int td = (int)os.size() - 1; td >= 0; --td) {
+    tn *= os[td];
+    if (td == 0 || (os[td - 1] != 1 && ost[td - 1] != tn * base)) {
+      while (vd >= 0 && (vn < tn || ns[vd] == 1)) {
+        st[vd] = vn * base;
+        vn *= ns[vd];
+        --vd;
+      }
+      if (vn != tn) return false;
+      if (td > 0) {
+        base = ost[td - 1];
+        tn = 1;
+        vn = 1;
+      }
+    }
+  }
+  if (vd != -1) return false;
+  out->strides = st;
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// Kernel specifications
+// ---------------------------------------------------------------------------
+
+// One elementwise instruction.  LOAD reads load `load`; the others combine
+// earlier instructions (indices in `a`).
+enum class EwKind : uint8_t { LOAD, OP, COPY, BN };
+struct EwInstr {
+  EwKind kind = EwKind::OP;
+  Op op = Op::NONE;
+  std::vector<int> a;
+  int load = -1;
+  float p0 = 0.f;  // BN eps
+};
+
+struct EwSpec {
+  std::vector<int64_t> space;
+  std::vector<View> loads;                     // broadcast to `space`
+  std::vector<EwInstr> instrs;
+  std::vector<std::pair<int, View>> stores;    // instr -> view shaped like `space`
+};
+
+struct RowOp {
+  Op op;
+  int src = -1, gamma = -1, beta = -1;
+  float eps = 1e-5f;
+  View out;   // reductions: dense [outer*inner]; softmax/LN: view shaped like space
+};
+
+struct RowSpec {
+  EwSpec ew;
+  int red_begin = 0, red_end = 0;   // dims [red_begin, red_end) of space are reduced
+  std::vector<RowOp> ops;
+};
+
+// ---------------------------------------------------------------------------
+// Code generation helpers
+// ---------------------------------------------------------------------------
+
+const char* kPrelude = R"(
+#define PF_INF __int_as_float(0x7f800000)
+#define PF_NAN __int_as_float(0x7fffffff)
+struct PfArgs { void* p[48]; };
+// DIV as the CPU reference evaluates it (executor.cpp:322-340): a zero
+// divisor gives NaN for 0/0 and an infinity signed by the dividend.
+__device__ __forceinline__ float pf_div(float a, float b) {
+  if (b == 0.f) return a == 0.f ? PF_NAN : (a > 0.f ? PF_INF : -PF_INF);
+  return a / b;
+}
+__device__ __forceinline__ float pf_relu(float x) { return (0.f < x) ? x : 0.f; }
+__device__ __forceinline__ float pf_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+__device__ __forceinline__ float pf_gelu(float x) {
+  return 0.5f * x * (1.0f + tanhf(0.7978845608f * (x + 0.044715f * x * x * x)));
+}
+__device__ __forceinline__ float pf_silu(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float pf_max(float a, float b) { return fmaxf(a, b); }
+__device__ __forceinline__ float pf_min(float a, float b) { return fminf(a, b); }
+)";
+
+std::string flit(float f) {
+  if (std::isnan(f)) return "PF_NAN";
+  if (std::isinf(f)) return f > 0 ? "PF_INF" : "(-PF_INF)";
+  uint32_t b;
+  std::memcpy(&b, &f, 4);
+  char buf[48];
+  std::snprintf(buf, sizeof buf, "__int_as_float(0x%08x)", b);
+  return buf;
+}
+
+std::string op_expr(const EwInstr& in, const std::vector<std::string>& a) {
+  auto A = [&](int i) { return a.at(i); };
+  switch (in.op) {
+    case Op::ADD: return "(" + A(0) + " + " + A(1) + ")";
+    case Op::SUB: return "(" + A(0) + " - " + A(1) + ")";
+    case Op::MUL: return "(" + A(0) + " * " + A(1) + ")";
+    case Op::DIV: return "pf_div(" + A(0) + ", " + A(1) + ")";
+    case Op::POW: return "powf(" + A(0) + ", " + A(1) + ")";
+    case Op::MAX_BINARY: case Op::MAXIMUM: return "pf_max(" + A(0) + ", " + A(1) + ")";
+    case Op::MIN_BINARY: case Op::MINIMUM: return "pf_min(" + A(0) + ", " + A(1) + ")";
+    case Op::NEG: return "(-" + A(0) + ")";
+    case Op::ABS: return "fabsf(" + A(0) + ")";
+    case Op::SQRT: return "sqrtf(" + A(0) + ")";
+    case Op::EXP: return "expf(" + A(0) + ")";
+    case Op::LOG: return "logf(" + A(0) + ")";
+    case Op::SIN: return "sinf(" + A(0) + ")";
+    case Op::COS: return "cosf(" + A(0) + ")";
+    case Op::TANH: return "tanhf(" + A(0) + ")";
+    case Op::RELU: return "pf_relu(" + A(0) + ")";
+    case Op::SIGMOID: return "pf_sigmoid(" + A(0) + ")";
+    case Op::GELU: return "pf_gelu(" + A(0) + ")";
+    case Op::SILU: return "pf_silu(" + A(0) + ")";
+    case Op::EQ: return "((" + A(0) + " == " + A(1) + ") ? 1.0f : 0.0f)";
+    case Op::NE: return "((" + A(0) + " != " + A(1) + ") ? 1.0f : 0.0f)";
+    case Op::LT: case Op::LESS: return "((" + A(0) + " < " + A(1) + ") ? 1.0f : 0.0f)";
+    case Op::LE: return "((" + A(0) + " <= " + A(1) + ") ? 1.0f : 0.0f)";
+    case Op::GT: return "((" + A(0) + " > " + A(1) + ") ? 1.0f : 0.0f)";
+    case Op::GE: return "((" + A(0) + " >= " + A(1) + ") ? 1.0f : 0.0f)";
+    case Op::WHERE: return "((" + A(0) + " != 0.0f) ? " + A(1) + " : " + A(2) + ")";
+    case Op::CLAMP: return "fminf(fmaxf(" + A(0) + ", " + A(1) + "), " + A(2) + ")";
+    default:
+      fail(PFC_ERR_UNSUPPORTED, std::string("no elementwise lowering for op ") + op_name(in.op));
+  }
+}
+
+// Merged iteration dims shared by a set of views: sizes and, per view, strides.
+struct Dims {
+  std::vector<int64_t> size;
+  std::vector<std::vector<int64_t>> stride;  // [view][dim]
+};
+
+// Reorder dims by `perm` and merge neighbours that every view walks contiguously.
+Dims merge_dims(const std::vector<int64_t>& space, const std::vector<int>& perm,
+                const std::vector<const View*>& views) {
+  Dims d;
+  size_t nv = views.size();
+  d.stride.assign(nv, {});
+  for (int p : perm) {
+    if (space[p] == 1) continue;
+    d.size.push_back(space[p]);
+    for (size_t v = 0; v < nv; ++v) d.stride[v].push_back(views[v]->strides[p]);
+  }
+  if (d.size.empty()) {
+    d.size.push_back(1);
+    for (size_t v = 0; v < nv; ++v) d.stride[v].push_back(0);
+  }
+  // merge k-1 into k when stride[k-1] == stride[k]*size[k] for all views
+  std::vector<int64_t> ms{d.size[0]};
+  std::vector<std::vector<int64_t>> mst(nv);
+  for (size_t v = 0; v < nv; ++v) mst[v].push_back(d.stride[v][0]);
+  for (size_t k = 1; k < d.size.size(); ++k) {
+    bool ok = true;
+    for (size_t v = 0; v < nv && ok; ++v) ok = mst[v].back() == d.stride[v][k] * d.size[k];
+    if (ok) {
+      ms.back() *= d.size[k];
+      for (size_t v = 0; v < nv; ++v) mst[v].back() = d.stride[v][k];
+    } else {
+      ms.push_back(d.size[k]);
+      for (size_t v = 0; v < nv; ++v) mst[v].push_back(d.stride[v][k]);
+    }
+  }
+  d.size = ms;
+  d.stride = mst;
+  return d;
+}
+
+// Physical order for iterating `space`: follow the first store (or load)
+// whose strides are all nonzero, outermost = largest stride.
+std::vector<int> pick_perm(const EwSpec& s) {
+  std::vector<int> perm(s.space.size());
+  for (size_t i = 0; i < perm.size(); ++i) perm[i] = (int)i;
+  const View* ref = nullptr;
+  if (!s.stores.empty()) ref = &s.stores[0].second;
+  if (!ref) {
+    for (const View& v : s.loads) {
+      bool full = !v.is_splat;
+      for (size_t d = 0; d < v.shape.size() && full; ++d) full = v.shape[d] == 1 || v.strides[d] != 0;
+      if (full) { ref = &v; break; }
+    }
+  }
+  if (ref) {
+    std::stable_sort(perm.begin(), perm.end(), [&](int a, int b) {
+      return std::llabs(ref->strides[a]) > std::llabs(ref->strides[b]);
+    });
+  }
+  return perm;
+}
+
+std::string ctype_for(DType d) {
+  switch (d) {
+    case DType::F32: return "float";
+    case DType::F64: return "double";
+    case DType::I64: return "long long";
+    case DType::I32: return "int";
+    case DType::I16: case DType::F16: case DType::BF16: return "unsigned short";
+    case DType::I8: case DType::BOOL: return "unsigned char";
+  }
+  return "float";
+}
+
+// Emits index arithmetic: coords of linear index `lin` over `sizes`, into c0..cn-1.
+std::string emit_coords(const std::string& lin, const std::vector<int64_t>& sizes, const std::string& pfx,
+                        const char* ity) {
+  std::ostringstream o;
+  size_t n = sizes.size();
+  if (n == 1) {
+    o << ity << " " << pfx << "0 = " << lin << ";\n";
+    return o.str();
+  }
+  o << ity << " " << pfx << "r = " << lin << ";\n";
+  for (size_t k = n; k-- > 0;) {
+    if (k == 0) {
+      o << ity << " " << pfx << "0 = " << pfx << "r;\n";
+    } else {
+      o << ity << " " << pfx << k << " = " << pfx << "r % (" << ity << ")" << sizes[k] << "; " << pfx
+        << "r /= (" << ity << ")" << sizes[k] << ";\n";
+    }
+  }
+  return o.str();
+}
+
+std::string emit_offset(const std::vector<int64_t>& strides, const std::string& pfx, size_t ndims,
+                        int skip_last, const char* ity) {
+  std::ostringstream o;
+  o << "(" << ity << ")0";
+  for (size_t k = 0; k + skip_last < ndims; ++k)
+    if (strides[k] != 0) o << " + " << pfx << k << " * (" << ity << ")" << strides[k];
+  return o.str();
+}
+
+bool fits_i32(const Dims& d, int64_t extra) {
+  int64_t total = prod(d.size) + extra;
+  if (total > (int64_t)INT32_MAX / 2) return false;
+  for (const auto& st : d.stride) {
+    int64_t m = 0;
+    for (size_t k = 0; k < st.size(); ++k) m += std::llabs(st[k]) * (d.size[k] - 1);
+    if (m > (int64_t)INT32_MAX / 2) return false;
+  }
+  return true;
+}
+
+// --- fused elementwise kernel ---------------------------------------------
+std::string gen_ew(const EwSpec& s, const std::string& name, int num_sms, int* grid, int* block) {
+  std::vector<int> perm = pick_perm(s);
+  std::vector<const View*> views;
+  for (const View& v : s.loads) views.push_back(&v);
+  for (const auto& st : s.stores) views.push_back(&st.second);
+  Dims d = merge_dims(s.space, perm, views);
+  size_t nd = d.size.size();
+  int64_t total = prod(d.size);
+  // Vector width: 4 when the innermost dim is a multiple of 4 and every view
+  // walks it with stride 0 or 1 from a 16-byte aligned base.
+  int vec = 4;
+  if (d.size.back() % 4 != 0) vec = 1;
+  for (size_t v = 0; v < views.size() && vec == 4; ++v) {
+    if (views[v]->is_splat) continue;
+    if (views[v]->dtype != DType::F32) { vec = 1; break; }
+    int64_t inner = d.stride[v].back();
+    if (inner == 1) {
+      if (views[v]->offset % 4 != 0) vec = 1;
+      for (size_t k = 0; k + 1 < nd; ++k)
+        if (d.stride[v][k] % 4 != 0) vec = 1;
+    }
+  }
+  bool i32 = fits_i32(d, 0);
+  const char* ity = i32 ? "int" : "long long";
+  // a pure copy of a non-float tensor keeps its element type end to end
+  std::string vt = "float";
+  {
+    bool pure = !s.loads.empty();
+    for (const EwInstr& in : s.instrs) pure = pure && (in.kind == EwKind::LOAD || in.kind == EwKind::COPY);
+    for (const View& v : s.loads) pure = pure && !v.is_splat && v.dtype == s.loads[0].dtype;
+    for (const auto& st : s.stores) pure = pure && st.second.dtype == s.loads[0].dtype;
+    if (pure && s.loads[0].dtype != DType::F32) vt = ctype_for(s.loads[0].dtype);
+  }
+  std::ostringstream o;
+  o << kPrelude;
+  o << "extern \"C\" __global__ void __launch_bounds__(256) " << name << "(const PfArgs A) {\n";
+  size_t nl = s.loads.size(), ns = s.stores.size();
+  for (size_t i = 0; i < nl; ++i) {
+    if (s.loads[i].is_splat) continue;
+    o << "  const " << ctype_for(s.loads[i].dtype) << "* __restrict__ in" << i << " = (const "
+      << ctype_for(s.loads[i].dtype) << "*)A.p[" << i << "];\n";
+  }
+  for (size_t j = 0; j < ns; ++j)
+    o << "  " << ctype_for(s.stores[j].second.dtype) << "* __restrict__ out" << j << " = ("
+      << ctype_for(s.stores[j].second.dtype) << "*)A.p[" << nl + j << "];\n";
+  o << "  const float* __restrict__ scal = (const float*)A.p[" << nl + ns << "];\n";
+  for (size_t i = 0; i < nl; ++i)
+    if (s.loads[i].is_splat) o << "  const float sp" << i << " = scal[" << s.loads[i].splat_slot << "];\n";
+  o << "  const " << ity << " NV = (" << ity << ")" << total / vec << ";\n";
+  o << "  for (" << ity << " v = (" << ity << ")blockIdx.x * blockDim.x + threadIdx.x; v < NV; v += (" << ity
+    << ")gridDim.x * blockDim.x) {\n";
+  o << "    const " << ity << " L = v * " << vec << ";\n";
+  o << "    " << emit_coords("L", d.size, "c", ity);
+  // loads
+  for (size_t i = 0; i < nl; ++i) {
+    const View& lv = s.loads[i];
+    std::string ct = ctype_for(lv.dtype);
+    if (lv.is_splat) {
+      o << "    float l" << i << "[" << vec << "]; for (int q = 0; q < " << vec << "; ++q) l" << i << "[q] = sp" << i
+        << ";\n";
+      continue;
+    }
+    const auto& st = d.stride[i];
+    o << "    " << ct << " l" << i << "[" << vec << "];\n    { const " << ct << "* ptr = in" << i << " + ("
+      << emit_offset(st, "c", nd, 0, ity) << ");\n";
+    int64_t inner = st.back();
+    if (vec == 4 && inner == 1) {
+      o << "      float4 t = *(const float4*)ptr; l" << i << "[0]=t.x; l" << i << "[1]=t.y; l" << i << "[2]=t.z; l"
+        << i << "[3]=t.w; }\n";
+    } else if (inner == 0) {
+      o << "      " << ct << " t = ptr[0]; for (int q = 0; q < " << vec << "; ++q) l" << i << "[q] = t; }\n";
+    } else {
+      o << "      for (int q = 0; q < " << vec << "; ++q) l" << i << "[q] = ptr[q * (" << ity << ")" << inner
+        << "]; }\n";
+    }
+  }
+  // compute
+  o << "    " << vt << " res[" << std::max<size_t>(ns, 1) << "][" << vec << "];\n";
+  o << "#pragma unroll\n    for (int q = 0; q < " << vec << "; ++q) {\n";
+  std::vector<std::string> names(s.instrs.size());
+  for (size_t k = 0; k < s.instrs.size(); ++k) {
+    const EwInstr& in = s.instrs[k];
+    names[k] = "t" + std::to_string(k);
+    std::string e;
+    if (in.kind == EwKind::LOAD) {
+      e = "(" + vt + ")l" + std::to_string(in.load) + "[q]";
+    } else if (in.kind == EwKind::COPY) {
+      e = names[in.a[0]];
+    } else if (in.kind == EwKind::BN) {
+      // (x - mean) / sqrt(var + eps) * gamma + beta, args: x, mean, var, gamma, beta
+      std::string x = names[in.a[0]], m = names[in.a[1]], v = names[in.a[2]];
+      e = "((" + x + " - " + m + ") / sqrtf(" + v + " + " + flit(in.p0) + "))";
+      if (in.a[3] >= 0) e = "(" + e + " * " + names[in.a[3]] + ")";
+      if (in.a[4] >= 0) e = "(" + e + " + " + names[in.a[4]] + ")";
+    } else {
+      std::vector<std::string> args;
+      for (int x : in.a) args.push_back(names[x]);
+      e = op_expr(in, args);
+    }
+    o << "      const " << vt << " " << names[k] << " = " << e << ";\n";
+  }
+  for (size_t j = 0; j < ns; ++j) o << "      res[" << j << "][q] = " << names[s.stores[j].first] << ";\n";
+  o << "    }\n";
+  // stores
+  for (size_t j = 0; j < ns; ++j) {
+    const View& sv = s.stores[j].second;
+    std::string ct = ctype_for(sv.dtype);
+    const auto& st = d.stride[nl + j];
+    o << "    { " << ct << "* ptr = out" << j << " + (" << emit_offset(st, "c", nd, 0, ity) << ");\n";
+    if (vec == 4 && st.back() == 1) {
+      o << "      *(float4*)ptr = make_float4(res[" << j << "][0], res[" << j << "][1], res[" << j << "][2], res["
+        << j << "][3]); }\n";
+    } else {
+      o << "      for (int q = 0; q < " << vec << "; ++q) ptr[q * (" << ity << ")" << st.back() << "] = (" << ct
+        << ")res[" << j << "][q]; }\n";
+    }
+  }
+  o << "  }\n}\n";
+  *block = 256;
+  int64_t blocks = ceil_div(std::max<int64_t>(total / vec, 1), 256);
+  *grid = (int)std::max<int64_t>(1, std::min<int64_t>(blocks, (int64_t)num_sms * 16));
+  return o.str();
+}
+
+// --- row kernel: one row (or a few rows) per CTA, values kept in registers ---
+struct RowLayout {
+  int64_t R = 1, C = 1;
+  int tpr = 32, block = 256, rpb = 8, vec = 1, nch = 1;
+  bool reg_mode = true;
+};
+
+std::string gen_row(const RowSpec& rs, const std::string& name, int num_sms, int* grid, int* block) {
+  const EwSpec& s = rs.ew;
+  std::vector<int64_t> outer_sz(s.space.begin(), s.space.begin() + rs.red_begin);
+  std::vector<int64_t> red_sz(s.space.begin() + rs.red_begin, s.space.begin() + rs.red_end);
+  RowLayout L;
+  L.R = prod(outer_sz);
+  L.C = prod(red_sz);
+  // Per-view strides split into row dims and column dims.
+  std::vector<const View*> views;
+  for (const View& v : s.loads) views.push_back(&v);
+  for (const auto& st : s.stores) views.push_back(&st.second);
+  for (const RowOp& op : rs.ops)
+    if (op.op == Op::SOFTMAX || op.op == Op::LOG_SOFTMAX || op.op == Op::LAYER_NORM) views.push_back(&op.out);
+  std::vector<int> rperm, cperm;
+  for (int k = 0; k < rs.red_begin; ++k) rperm.push_back(k);
+  for (int k = rs.red_begin; k < rs.red_end; ++k) cperm.push_back(k);
+  Dims rd = merge_dims(s.space, rperm, views);
+  Dims cd = merge_dims(s.space, cperm, views);
+  size_t nrd = rd.size.size(), ncd = cd.size.size();
+  // vector width along the column
+  L.vec = (cd.size.back() % 4 == 0) ? 4 : 1;
+  for (size_t v = 0; v < views.size() && L.vec == 4; ++v) {
+    if (views[v]->is_splat) continue;
+    int64_t inner = cd.stride[v].back();
+    if (inner == 1) {
+      if (views[v]->offset % 4) L.vec = 1;
+      for (size_t k = 0; k + 1 < ncd; ++k)
+        if (cd.stride[v][k] % 4) L.vec = 1;
+      for (size_t k = 0; k < nrd; ++k)
+        if (rd.stride[v][k] % 4) L.vec = 1;
+    }
+  }
+  int64_t nvec = ceil_div(L.C, L.vec);
+  int tpr = 32;
+  while (tpr < 1024 && (int64_t)tpr * 4 < nvec) tpr *= 2;
+  L.tpr = tpr;
+  L.block = std::max(256, tpr);
+  L.rpb = L.block / tpr;
+  L.nch = (int)ceil_div(nvec, tpr);
+  int nsrc = 0;
+  {
+    std::set<int> srcs;
+    for (const RowOp& op : rs.ops) srcs.insert(op.src);
+    nsrc = (int)srcs.size();
+  }
+  L.reg_mode = (int64_t)L.nch * L.vec * std::max(1, nsrc) <= 64;
+  bool i32 = fits_i32(rd, 0) && fits_i32(cd, 0) && L.R * L.C < (int64_t)INT32_MAX / 2;
+  const char* ity = i32 ? "int" : "long long";
+
+  // which instructions feed the row ops / stores; all are computed per element
+  std::ostringstream o;
+  o << kPrelude;
+  o << "extern \"C\" __global__ void __launch_bounds__(" << L.block << ") " << name << "(const PfArgs A) {\n";
+  size_t nl = s.loads.size(), ns = s.stores.size();
+  for (size_t i = 0; i < nl; ++i) {
+    if (s.loads[i].is_splat) continue;
+    o << "  const float* __restrict__ in" << i << " = (const float*)A.p[" << i << "];\n";
+  }
+  for (size_t j = 0; j < ns; ++j) o << "  float* __restrict__ out" << j << " = (float*)A.p[" << nl + j << "];\n";
+  size_t nops = rs.ops.size();
+  for (size_t r = 0; r < nops; ++r) o << "  float* __restrict__ ro" << r << " = (float*)A.p[" << nl + ns + r << "];\n";
+  o << "  const float* __restrict__ scal = (const float*)A.p[" << nl + ns + nops << "];\n";
+  for (size_t i = 0; i < nl; ++i)
+    if (s.loads[i].is_splat) o << "  const float sp" << i << " = scal[" << s.loads[i].splat_slot << "];\n";
+  const int TPR = L.tpr, RPB = L.rpb, VEC = L.vec, NCH = L.nch;
+  o << "  const int tid = threadIdx.x;\n  const int lr = tid % " << TPR << ";\n  const int rib = tid / " << TPR
+    << ";\n";
+  if (TPR > 32) o << "  __shared__ float red[" << L.block / 32 << "][8];\n";
+  // reduction helpers over the TPR threads of a row
+  auto reduce = [&](const std::string& var, const std::string& combine, int slot) {
+    std::ostringstream r;
+    r << "    for (int off = 16; off > 0; off >>= 1) { float ot = __shfl_xor_sync(0xffffffffu, " << var
+      << ", off); " << var << " = " << combine << "; }\n";
+    if (TPR > 32) {
+      int wpr = TPR / 32;
+      r << "    __syncthreads();\n    if ((tid & 31) == 0) red[tid >> 5][" << slot << "] = " << var << ";\n"
+        << "    __syncthreads();\n    { const int w0 = rib * " << wpr << "; " << var << " = red[w0][" << slot
+        << "];\n      for (int w = 1; w < " << wpr << "; ++w) { float ot = red[w0 + w][" << slot << "]; " << var
+        << " = " << combine << "; } }\n";
+    }
+    return r.str();
+  };
+  o << "  for (" << ity << " rbase = (" << ity << ")blockIdx.x * " << RPB << "; rbase < (" << ity << ")" << L.R
+    << "; rbase += (" << ity << ")gridDim.x * " << RPB << ") {\n";
+  o << "    const " << ity << " row = rbase + rib;\n    const bool rv = row < (" << ity << ")" << L.R << ";\n";
+  o << "    " << emit_coords("(rv ? row : (" + std::string(ity) + ")0)", rd.size, "r", ity);
+  // per-view row offsets
+  for (size_t v = 0; v < views.size(); ++v)
+    o << "    const " << ity << " ro_" << v << " = " << emit_offset(rd.stride[v], "r", nrd, 0, ity) << ";\n";
+  // element evaluation macro: computes instr values for column vector chunk `cv` into arrays
+  std::vector<int> srcs;
+  for (const RowOp& op : rs.ops)
+    if (std::find(srcs.begin(), srcs.end(), op.src) == srcs.end()) srcs.push_back(op.src);
+  auto src_idx = [&](int instr) { return (int)(std::find(srcs.begin(), srcs.end(), instr) - srcs.begin()); };
+  // Instructions needed to produce `roots` (the DAG is in index order).
+  auto closure = [&](const std::vector<int>& roots) {
+    std::vector<bool> need(s.instrs.size(), false);
+    for (int r : roots)
+      if (r >= 0) need[r] = true;
+    for (int k = (int)s.instrs.size() - 1; k >= 0; --k)
+      if (need[k])
+        for (int a : s.instrs[k].a)
+          if (a >= 0) need[a] = true;
+    return need;
+  };
+  std::vector<bool> all_needed(s.instrs.size(), true);
+  // Evaluates the prologue for column chunk `cv`, restricted to `need`.
+  auto emit_eval = [&](bool with_stores, const std::vector<bool>& need) {
+    std::vector<bool> load_needed(nl, false);
+    for (size_t k = 0; k < s.instrs.size(); ++k)
+      if (need[k] && s.instrs[k].kind == EwKind::LOAD) load_needed[s.instrs[k].load] = true;
+    std::ostringstream e;
+    e << "      const " << ity << " cl = cv * " << VEC << ";\n";
+    e << "      const bool cok = rv && cl < (" << ity << ")" << L.C << ";\n";
+    e << "      " << emit_coords("(cok ? cl : (" + std::string(ity) + ")0)", cd.size, "k", ity);
+    for (size_t i = 0; i < nl; ++i) {
+      if (!load_needed[i]) continue;
+      if (s.loads[i].is_splat) {
+        e << "      float l" << i << "[" << VEC << "]; for (int q = 0; q < " << VEC << "; ++q) l" << i << "[q] = sp"
+          << i << ";\n";
+        continue;
+      }
+      const auto& st = cd.stride[i];
+      e << "      float l" << i << "[" << VEC << "];\n      if (cok) { const float* ptr = in" << i << " + ro_" << i
+        << " + (" << emit_offset(st, "k", ncd, 0, ity) << ");\n";
+      if (VEC == 4 && st.back() == 1)
+        e << "        float4 t = *(const float4*)ptr; l" << i << "[0]=t.x; l" << i << "[1]=t.y; l" << i
+          << "[2]=t.z; l" << i << "[3]=t.w; }\n";
+      else if (st.back() == 0)
+        e << "        float t = ptr[0]; for (int q = 0; q < " << VEC << "; ++q) l" << i << "[q] = t; }\n";
+      else
+        e << "        for (int q = 0; q < " << VEC << "; ++q) l" << i << "[q] = ptr[q * (" << ity << ")"
+          << st.back() << "]; }\n";
+      e << "      else { for (int q = 0; q < " << VEC << "; ++q) l" << i << "[q] = 0.f; }\n";
+    }
+    e << "      float ev[" << std::max<size_t>(s.instrs.size(), 1) << "][" << VEC << "];\n";
+    e << "#pragma unroll\n      for (int q = 0; q < " << VEC << "; ++q) {\n";
+    for (size_t k = 0; k < s.instrs.size(); ++k) {
+      if (!need[k]) continue;
+      const EwInstr& in = s.instrs[k];
+      std::string ex;
+      auto nm = [&](int x) { return "ev[" + std::to_string(x) + "][q]"; };
+      if (in.kind == EwKind::LOAD) ex = "l" + std::to_string(in.load) + "[q]";
+      else if (in.kind == EwKind::COPY) ex = nm(in.a[0]);
+      else if (in.kind == EwKind::BN) {
+        ex = "((" + nm(in.a[0]) + " - " + nm(in.a[1]) + ") / sqrtf(" + nm(in.a[2]) + " + " + flit(in.p0) + "))";
+        if (in.a[3] >= 0) ex = "(" + ex + " * " + nm(in.a[3]) + ")";
+        if (in.a[4] >= 0) ex = "(" + ex + " + " + nm(in.a[4]) + ")";
+      } else {
+        std::vector<std::string> args;
+        for (int x : in.a) args.push_back(nm(x));
+        ex = op_expr(in, args);
+      }
+      e << "        ev[" << k << "][q] = " << ex << ";\n";
+    }
+    e << "      }\n";
+    if (with_stores) {
+      for (size_t j = 0; j < ns; ++j) {
+        const auto& st = cd.stride[nl + j];
+        e << "      if (cok) { float* ptr = out" << j << " + ro_" << nl + j << " + ("
+          << emit_offset(st, "k", ncd, 0, ity) << ");\n";
+        int ins = s.stores[j].first;
+        if (VEC == 4 && st.back() == 1)
+          e << "        *(float4*)ptr = make_float4(ev[" << ins << "][0], ev[" << ins << "][1], ev[" << ins
+            << "][2], ev[" << ins << "][3]); }\n";
+        else
+          e << "        for (int q = 0; q < " << VEC << "; ++q) ptr[q * (" << ity << ")" << st.back() << "] = ev["
+            << ins << "][q]; }\n";
+      }
+    }
+    return e.str();
+  };
+  // Which stats are needed per source
+  std::set<int> need_sum, need_max, need_min, need_prod, need_var, need_sexp;
+  for (const RowOp& op : rs.ops) {
+    int si = src_idx(op.src);
+    switch (op.op) {
+      case Op::SUM: case Op::MEAN: need_sum.insert(si); break;
+      case Op::MAX: need_max.insert(si); break;
+      case Op::MIN: need_min.insert(si); break;
+      case Op::PROD: need_prod.insert(si); break;
+      case Op::LAYER_NORM: need_sum.insert(si); need_var.insert(si); break;
+      case Op::SOFTMAX: case Op::LOG_SOFTMAX: need_max.insert(si); need_sexp.insert(si); break;
+      default: break;
+    }
+  }
+  // pass 1: evaluate, keep source values (register mode), accumulate sum/max/min/prod
+  for (size_t si = 0; si < srcs.size(); ++si) {
+    o << "    float s_sum" << si << " = 0.f, s_max" << si << " = -PF_INF, s_min" << si << " = PF_INF, s_prod" << si
+      << " = 1.f, s_var" << si << " = 0.f, s_sexp" << si << " = 0.f;\n";
+    if (L.reg_mode) o << "    float vals" << si << "[" << NCH << "][" << VEC << "];\n";
+  }
+  o << (L.reg_mode ? "#pragma unroll\n" : "#pragma unroll 1\n") << "    for (int ch = 0; ch < " << NCH << "; ++ch) {\n      const " << ity
+    << " cv = (" << ity << ")ch * " << TPR << " + lr;\n";
+  o << emit_eval(true, all_needed);
+  for (size_t si = 0; si < srcs.size(); ++si) {
+    o << "      for (int q = 0; q < " << VEC << "; ++q) {\n        const bool ok = cok && (cl + q) < (" << ity << ")"
+      << L.C << ";\n        const float x = ev[" << srcs[si] << "][q];\n";
+    if (L.reg_mode) o << "        vals" << si << "[ch][q] = x;\n";
+    if (need_sum.count(si)) o << "        if (ok) s_sum" << si << " += x;\n";
+    if (need_max.count(si)) o << "        if (ok) s_max" << si << " = fmaxf(s_max" << si << ", x);\n";
+    if (need_min.count(si)) o << "        if (ok) s_min" << si << " = fminf(s_min" << si << ", x);\n";
+    if (need_prod.count(si)) o << "        if (ok) s_prod" << si << " *= x;\n";
+    o << "      }\n";
+  }
+  o << "    }\n";
+  int slot = 0;
+  for (size_t si = 0; si < srcs.size(); ++si) {
+    if (need_sum.count(si)) o << reduce("s_sum" + std::to_string(si), "s_sum" + std::to_string(si) + " + ot", slot++ % 8);
+    if (need_max.count(si)) o << reduce("s_max" + std::to_string(si), "fmaxf(s_max" + std::to_string(si) + ", ot)", slot++ % 8);
+    if (need_min.count(si)) o << reduce("s_min" + std::to_string(si), "fminf(s_min" + std::to_string(si) + ", ot)", slot++ % 8);
+    if (need_prod.count(si)) o << reduce("s_prod" + std::to_string(si), "s_prod" + std::to_string(si) + " * ot", slot++ % 8);
+  }
+  // pass 2: variance / sum of exp (need pass-1 stats)
+  bool need_pass2 = !need_var.empty() || !need_sexp.empty();
+  if (need_pass2) {
+    for (size_t si = 0; si < srcs.size(); ++si)
+      if (need_var.count(si)) o << "    const float mean" << si << " = s_sum" << si << " / " << flit((float)L.C) << ";\n";
+    o << (L.reg_mode ? "#pragma unroll\n" : "#pragma unroll 1\n") << "    for (int ch = 0; ch < " << NCH << "; ++ch) {\n      const " << ity << " cv = ("
+      << ity << ")ch * " << TPR << " + lr;\n";
+    if (!L.reg_mode) o << emit_eval(false, closure(srcs));
+    else o << "      const " << ity << " cl = cv * " << VEC << ";\n      const bool cok = rv && cl < (" << ity << ")" << L.C << ";\n";
+    for (size_t si = 0; si < srcs.size(); ++si) {
+      if (!need_var.count(si) && !need_sexp.count(si)) continue;
+      o << "      for (int q = 0; q < " << VEC << "; ++q) {\n        const bool ok = cok && (cl + q) < (" << ity
+        << ")" << L.C << ";\n";
+      o << "        const float x = " << (L.reg_mode ? "vals" + std::to_string(si) + "[ch][q]" : "ev[" + std::to_string(srcs[si]) + "][q]") << ";\n";
+      if (need_var.count(si)) o << "        if (ok) { const float dv = x - mean" << si << "; s_var" << si << " += dv * dv; }\n";
+      if (need_sexp.count(si)) o << "        if (ok) s_sexp" << si << " += expf(x - s_max" << si << ");\n";
+      o << "      }\n";
+    }
+    o << "    }\n";
+    for (size_t si = 0; si < srcs.size(); ++si) {
+      if (need_var.count(si)) o << reduce("s_var" + std::to_string(si), "s_var" + std::to_string(si) + " + ot", slot++ % 8);
+      if (need_sexp.count(si)) o << reduce("s_sexp" + std::to_string(si), "s_sexp" + std::to_string(si) + " + ot", slot++ % 8);
+    }
+  }
+  // per-row outputs
+  bool any_row_out = false;
+  for (size_t r = 0; r < nops; ++r) {
+    const RowOp& op = rs.ops[r];
+    int si = src_idx(op.src);
+    std::string v;
+    switch (op.op) {
+      case Op::SUM: v = "s_sum" + std::to_string(si); break;
+      case Op::MEAN: v = "s_sum" + std::to_string(si) + " / " + flit((float)L.C); break;
+      case Op::MAX: v = "s_max" + std::to_string(si); break;
+      case Op::MIN: v = "s_min" + std::to_string(si); break;
+      case Op::PROD: v = "s_prod" + std::to_string(si); break;
+      default: continue;
+    }
+    if (!any_row_out) { o << "    if (rv && lr == 0) {\n"; any_row_out = true; }
+    o << "      ro" << r << "[row] = " << v << ";\n";
+  }
+  if (any_row_out) o << "    }\n";
+  // per-element outputs: softmax / log_softmax / layer_norm
+  bool any_elem = false;
+  for (const RowOp& op : rs.ops)
+    if (op.op == Op::SOFTMAX || op.op == Op::LOG_SOFTMAX || op.op == Op::LAYER_NORM) any_elem = true;
+  if (any_elem) {
+    for (size_t si = 0; si < srcs.size(); ++si) {
+      if (need_var.count(si))
+        o << "    const float inv" << si << " = 1.0f / sqrtf(s_var" << si << " / " << flit((float)L.C) << " + EPS" << si << ");\n";
+      if (need_sexp.count(si)) o << "    const float lse" << si << " = s_max" << si << " + logf(s_sexp" << si << ");\n";
+    }
+    o << (L.reg_mode ? "#pragma unroll\n" : "#pragma unroll 1\n") << "    for (int ch = 0; ch < " << NCH << "; ++ch) {\n      const " << ity << " cv = ("
+      << ity << ")ch * " << TPR << " + lr;\n";
+    bool needs_eval = !L.reg_mode;
+    std::vector<int> roots = L.reg_mode ? std::vector<int>{} : srcs;
+    for (const RowOp& op : rs.ops)
+      if (op.op == Op::LAYER_NORM && (op.gamma >= 0 || op.beta >= 0)) {
+        needs_eval = true;
+        roots.push_back(op.gamma);
+        roots.push_back(op.beta);
+      }
+    if (needs_eval) o << emit_eval(false, closure(roots));
+    else o << "      const " << ity << " cl = cv * " << VEC << ";\n      const bool cok = rv && cl < (" << ity << ")" << L.C << ";\n";
+    o << "      " << emit_coords("(cok ? cl : (" + std::string(ity) + ")0)", cd.size, "w", ity);
+    size_t vbase = nl + ns;
+    for (size_t r = 0; r < nops; ++r) {
+      const RowOp& op = rs.ops[r];
+      if (!(op.op == Op::SOFTMAX || op.op == Op::LOG_SOFTMAX || op.op == Op::LAYER_NORM)) continue;
+      int si = src_idx(op.src);
+      // view index of this op's output in `views`
+      size_t vi = vbase;
+      for (size_t r2 = 0; r2 < r; ++r2)
+        if (rs.ops[r2].op == Op::SOFTMAX || rs.ops[r2].op == Op::LOG_SOFTMAX || rs.ops[r2].op == Op::LAYER_NORM) ++vi;
+      const auto& st = cd.stride[vi];
+      o << "      { float y[" << VEC << "];\n        for (int q = 0; q < " << VEC << "; ++q) {\n          const float x = "
+        << (L.reg_mode ? "vals" + std::to_string(si) + "[ch][q]" : "ev[" + std::to_string(op.src) + "][q]") << ";\n";
+      if (op.op == Op::SOFTMAX)
+        o << "          y[q] = expf(x - s_max" << si << ") / s_sexp" << si << ";\n";
+      else if (op.op == Op::LOG_SOFTMAX)
+        o << "          y[q] = x - lse" << si << ";\n";
+      else {
+        o << "          float t = (x - mean" << si << ") * inv" << si << ";\n";
+        if (op.gamma >= 0) o << "          t = t * ev[" << op.gamma << "][q];\n";
+        if (op.beta >= 0) o << "          t = t + ev[" << op.beta << "][q];\n";
+        o << "          y[q] = t;\n";
+      }
+      o << "        }\n        if (cok) { float* ptr = ro" << r << " + ro_" << vi << " + ("
+        << emit_offset(st, "w", ncd, 0, ity) << ");\n";
+      if (VEC == 4 && st.back() == 1)
+        o << "          *(float4*)ptr = make_float4(y[0], y[1], y[2], y[3]); } }\n";
+      else
+        o << "          for (int q = 0; q < " << VEC << "; ++q) if (cl + q < (" << ity << ")" << L.C
+          << ") ptr[q * (" << ity << ")" << st.back() << "] = y[q]; } }\n";
+    }
+    o << "    }\n";
+  }
+  o << "  }\n}\n";
+  // substitute eps constants
+  std::string src = o.str();
+  for (size_t si = 0; si < srcs.size(); ++si) {
+    float eps = 1e-5f;
+    for (const RowOp& op : rs.ops)
+      if (op.op == Op::LAYER_NORM && src_idx(op.src) == (int)si) eps = op.eps;
+    std::string key = "EPS" + std::to_string(si);
+    size_t p;
+    while ((p = src.find(key)) != std::string::npos) src.replace(p, key.size(), flit(eps));
+  }
+  *block = L.block;
+  int64_t blocks = ceil_div(L.R, L.rpb);
+  int per_sm = std::max(1, 2048 / L.block);
+  *grid = (int)std::max<int64_t>(1, std::min<int64_t>(blocks, (int64_t)num_sms * per_sm));
+  return src;
+}
+
+// --- column kernel: reduction over a dim that is not innermost --------------
+// Each thread owns one (outer, inner) position and walks the reduced extent.
+std::string gen_col(const RowSpec& rs, const std::string& name, int num_sms, int* grid, int* block) {
+  const EwSpec& s = rs.ew;
+  std::vector<int64_t> outer_sz(s.space.begin(), s.space.begin() + rs.red_begin);
+  std::vector<int64_t> inner_sz(s.space.begin() + rs.red_end, s.space.end());
+  std::vector<int64_t> red_sz(s.space.begin() + rs.red_begin, s.space.begin() + rs.red_end);
+  int64_t O = prod(outer_sz), I = prod(inner_sz), C = prod(red_sz);
+  std::vector<const View*> views;
+  for (const View& v : s.loads) views.push_back(&v);
+  for (const auto& st : s.stores) views.push_back(&st.second);
+  for (const RowOp& op : rs.ops)
+    if (op.op == Op::SOFTMAX || op.op == Op::LOG_SOFTMAX || op.op == Op::LAYER_NORM) views.push_back(&op.out);
+  std::vector<int> operm, iperm, cperm;
+  for (int k = 0; k < rs.red_begin; ++k) operm.push_back(k);
+  for (int k = rs.red_end; k < (int)s.space.size(); ++k) iperm.push_back(k);
+  for (int k = rs.red_begin; k < rs.red_end; ++k) cperm.push_back(k);
+  // merge outer and inner as one "position" space (outer-major)
+  std::vector<int> pperm = operm;
+  pperm.insert(pperm.end(), iperm.begin(), iperm.end());
+  Dims pd = merge_dims(s.space, pperm, views);
+  Dims cd = merge_dims(s.space, cperm, views);
+  size_t npd = pd.size.size(), ncd = cd.size.size();
+  const char* ity = "long long";
+  std::ostringstream o;
+  o << kPrelude;
+  o << "extern \"C\" __global__ void __launch_bounds__(256) " << name << "(const PfArgs A) {\n";
+  size_t nl = s.loads.size(), ns = s.stores.size(), nops = rs.ops.size();
+  for (size_t i = 0; i < nl; ++i)
+    if (!s.loads[i].is_splat) o << "  const float* __restrict__ in" << i << " = (const float*)A.p[" << i << "];\n";
+  for (size_t j = 0; j < ns; ++j) o << "  float* __restrict__ out" << j << " = (float*)A.p[" << nl + j << "];\n";
+  for (size_t r = 0; r < nops; ++r) o << "  float* __restrict__ ro" << r << " = (float*)A.p[" << nl + ns + r << "];\n";
+  o << "  const float* __restrict__ scal = (const float*)A.p[" << nl + ns + nops << "];\n";
+  for (size_t i = 0; i < nl; ++i)
+    if (s.loads[i].is_splat) o << "  const float sp" << i << " = scal[" << s.loads[i].splat_slot << "];\n";
+  o << "  for (long long pos = (long long)blockIdx.x * blockDim.x + threadIdx.x; pos < " << O * I
+    << "LL; pos += (long long)gridDim.x * blockDim.x) {\n";
+  o << "    " << emit_coords("pos", pd.size, "p", ity);
+  for (size_t v = 0; v < views.size(); ++v)
+    o << "    const long long po_" << v << " = " << emit_offset(pd.stride[v], "p", npd, 0, ity) << ";\n";
+  std::vector<int> srcs;
+  for (const RowOp& op : rs.ops)
+    if (std::find(srcs.begin(), srcs.end(), op.src) == srcs.end()) srcs.push_back(op.src);
+  auto src_idx = [&](int instr) { return (int)(std::find(srcs.begin(), srcs.end(), instr) - srcs.begin()); };
+  auto emit_eval = [&](bool with_stores) {
+    std::ostringstream e;
+    e << "      " << emit_coords("cc", cd.size, "k", ity);
+    for (size_t i = 0; i < nl; ++i) {
+      if (s.loads[i].is_splat) { e << "      const float l" << i << " = sp" << i << ";\n"; continue; }
+      e << "      const float l" << i << " = in" << i << "[po_" << i << " + " << emit_offset(cd.stride[i], "k", ncd, 0, ity)
+        << "];\n";
+    }
+    for (size_t k = 0; k < s.instrs.size(); ++k) {
+      const EwInstr& in = s.instrs[k];
+      std::string ex;
+      auto nm = [&](int x) { return "e" + std::to_string(x); };
+      if (in.kind == EwKind::LOAD) ex = "l" + std::to_string(in.load);
+      else if (in.kind == EwKind::COPY) ex = nm(in.a[0]);
+      else if (in.kind == EwKind::BN) {
+        ex = "((" + nm(in.a[0]) + " - " + nm(in.a[1]) + ") / sqrtf(" + nm(in.a[2]) + " + " + flit(in.p0) + "))";
+        if (in.a[3] >= 0) ex = "(" + ex + " * " + nm(in.a[3]) + ")";
+        if (in.a[4] >= 0) ex = "(" + ex + " + " + nm(in.a[4]) + ")";
+      } else {
+        std::vector<std::string> args;
+        for (int x : in.a) args.push_back(nm(x));
+        ex = op_expr(in, args);
+      }
+      e << "      const float e" << k << " = " << ex << ";\n";
+    }
+    if (with_stores)
+      for (size_t j = 0; j < ns; ++j)
+        e << "      out" << j << "[po_" << nl + j << " + " << emit_offset(cd.stride[nl + j], "k", ncd, 0, ity)
+          << "] = e" << s.stores[j].first << ";\n";
+    return e.str();
+  };
+  for (size_t si = 0; si < srcs.size(); ++si)
+    o << "    float s_sum" << si << " = 0.f, s_max" << si << " = -PF_INF, s_min" << si << " = PF_INF, s_prod" << si
+      << " = 1.f, s_var" << si << " = 0.f, s_sexp" << si << " = 0.f;\n";
+  o << "    for (long long cc = 0; cc < " << C << "LL; ++cc) {\n" << emit_eval(true);
+  for (size_t si = 0; si < srcs.size(); ++si)
+    o << "      s_sum" << si << " += e" << srcs[si] << "; s_max" << si << " = fmaxf(s_max" << si << ", e" << srcs[si]
+      << "); s_min" << si << " = fminf(s_min" << si << ", e" << srcs[si] << "); s_prod" << si << " *= e" << srcs[si]
+      << ";\n";
+  o << "    }\n";
+  bool pass2 = false, elem = false;
+  for (const RowOp& op : rs.ops) {
+    if (op.op == Op::LAYER_NORM || op.op == Op::SOFTMAX || op.op == Op::LOG_SOFTMAX) pass2 = elem = true;
+  }
+  if (pass2) {
+    for (size_t si = 0; si < srcs.size(); ++si) o << "    const float mean" << si << " = s_sum" << si << " / " << flit((float)C) << ";\n";
+    o << "    for (long long cc = 0; cc < " << C << "LL; ++cc) {\n" << emit_eval(false);
+    for (size_t si = 0; si < srcs.size(); ++si)
+      o << "      { const float dv = e" << srcs[si] << " - mean" << si << "; s_var" << si << " += dv * dv; s_sexp" << si
+        << " += expf(e" << srcs[si] << " - s_max" << si << "); }\n";
+    o << "    }\n";
+  }
+  for (size_t r = 0; r < nops; ++r) {
+    const RowOp& op = rs.ops[r];
+    int si = src_idx(op.src);
+    std::string v;
+    switch (op.op) {
+      case Op::SUM: v = "s_sum" + std::to_string(si); break;
+      case Op::MEAN: v = "s_sum" + std::to_string(si) + " / " + flit((float)C); break;
+      case Op::MAX: v = "s_max" + std::to_string(si); break;
+      case Op::MIN: v = "s_min" + std::to_string(si); break;
+      case Op::PROD: v = "s_prod" + std::to_string(si); break;
+      default: continue;
+    }
+    o << "    ro" << r << "[pos] = " << v << ";\n";
+  }
+  if (elem) {
+    o << "    for (long long cc = 0; cc < " << C << "LL; ++cc) {\n" << emit_eval(false);
+    size_t vi = nl + ns;
+    for (size_t r = 0; r < nops; ++r) {
+      const RowOp& op = rs.ops[r];
+      if (!(op.op == Op::SOFTMAX || op.op == Op::LOG_SOFTMAX || op.op == Op::LAYER_NORM)) continue;
+      int si = src_idx(op.src);
+      std::string x = "e" + std::to_string(op.src), y;
+      if (op.op == Op::SOFTMAX) y = "expf(" + x + " - s_max" + std::to_string(si) + ") / s_sexp" + std::to_string(si);
+      else if (op.op == Op::LOG_SOFTMAX)
+        y = x + " - (s_max" + std::to_string(si) + " + logf(s_sexp" + std::to_string(si) + "))";
+      else {
+        y = "(" + x + " - mean" + std::to_string(si) + ") * (1.0f / sqrtf(s_var" + std::to_string(si) + " / " +
+            flit((float)C) + " + " + flit(op.eps) + "))";
+        if (op.gamma >= 0) y = "(" + y + ") * e" + std::to_string(op.gamma);
+        if (op.beta >= 0) y = "(" + y + ") + e" + std::to_string(op.beta);
+      }
+      o << "      ro" << r << "[po_" << vi << " + " << emit_offset(cd.stride[vi], "k", ncd, 0, ity) << "] = " << y << ";\n";
+      ++vi;
+    }
+    o << "    }\n";
+  }
+  o << "  }\n}\n";
+  *block = 256;
+  *grid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(O * I, 256), (int64_t)num_sms * 8));
+  return o.str();
+}
+
+// --- full reduction: two kernels (per-CTA partials, then one CTA) ----------
+std::string gen_full(const RowSpec& rs, const std::string& name, int num_sms, int* grid, int nstats_out[1]) {
+  const EwSpec& s = rs.ew;
+  int64_t N = prod(s.space);
+  std::vector<const View*> views;
+  for (const View& v : s.loads) views.push_back(&v);
+  for (const auto& st : s.stores) views.push_back(&st.second);
+  std::vector<int> perm = pick_perm(s);
+  Dims d = merge_dims(s.space, perm, views);
+  size_t nd = d.size.size();
+  const char* ity = "long long";
+  size_t nl = s.loads.size(), ns = s.stores.size(), nops = rs.ops.size();
+  // stat slots: one per row op
+  int G = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(N, 256 * 8), (int64_t)num_sms * 4));
+  *grid = G;
+  nstats_out[0] = (int)nops;
+  std::ostringstream o;
+  o << kPrelude;
+  auto head = [&](const std::string& kn) {
+    o << "extern \"C\" __global__ void __launch_bounds__(256) " << kn << "(const PfArgs A) {\n";
+    for (size_t i = 0; i < nl; ++i)
+      if (!s.loads[i].is_splat) o << "  const float* __restrict__ in" << i << " = (const float*)A.p[" << i << "];\n";
+    for (size_t j = 0; j < ns; ++j) o << "  float* __restrict__ out" << j << " = (float*)A.p[" << nl + j << "];\n";
+    for (size_t r = 0; r < nops; ++r) o << "  float* __restrict__ ro" << r << " = (float*)A.p[" << nl + ns + r << "];\n";
+    o << "  const float* __restrict__ scal = (const float*)A.p[" << nl + ns + nops << "];\n";
+    o << "  float* __restrict__ part = (float*)A.p[" << nl + ns + nops + 1 << "];\n";
+    for (size_t i = 0; i < nl; ++i)
+      if (s.loads[i].is_splat) o << "  const float sp" << i << " = scal[" << s.loads[i].splat_slot << "];\n";
+    o << "  __shared__ float red[8][" << std::max<size_t>(nops, 1) << "];\n";
+  };
+  auto comb = [&](Op op, const std::string& a, const std::string& b) -> std::string {
+    switch (op) {
+      case Op::SUM: case Op::MEAN: return a + " + " + b;
+      case Op::MAX: return "fmaxf(" + a + ", " + b + ")";
+      case Op::MIN: return "fminf(" + a + ", " + b + ")";
+      case Op::PROD: return a + " * " + b;
+      default: fail(PFC_ERR_UNSUPPORTED, "full reduction supports sum/mean/max/min/prod only");
+    }
+  };
+  auto neutral = [&](Op op) -> std::string {
+    switch (op) {
+      case Op::MAX: return "-PF_INF";
+      case Op::MIN: return "PF_INF";
+      case Op::PROD: return "1.f";
+      default: return "0.f";
+    }
+  };
+  auto block_reduce = [&]() {
+    for (size_t r = 0; r < nops; ++r) {
+      o << "  for (int off = 16; off > 0; off >>= 1) { float ot = __shfl_xor_sync(0xffffffffu, acc" << r
+        << ", off); acc" << r << " = " << comb(rs.ops[r].op, "acc" + std::to_string(r), "ot") << "; }\n";
+      o << "  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5][" << r << "] = acc" << r << ";\n";
+    }
+    o << "  __syncthreads();\n";
+    for (size_t r = 0; r < nops; ++r) {
+      o << "  acc" << r << " = red[0][" << r << "]; for (int w = 1; w < 8; ++w) acc" << r << " = "
+        << comb(rs.ops[r].op, "acc" + std::to_string(r), "red[w][" + std::to_string(r) + "]") << ";\n";
+    }
+  };
+  head(name);
+  for (size_t r = 0; r < nops; ++r) o << "  float acc" << r << " = " << neutral(rs.ops[r].op) << ";\n";
+  o << "  for (long long L = (long long)blockIdx.x * blockDim.x + threadIdx.x; L < " << N
+    << "LL; L += (long long)gridDim.x * blockDim.x) {\n";
+  o << "    " << emit_coords("L", d.size, "c", ity);
+  for (size_t i = 0; i < nl; ++i) {
+    if (s.loads[i].is_splat) { o << "    const float l" << i << " = sp" << i << ";\n"; continue; }
+    o << "    const float l" << i << " = in" << i << "[" << emit_offset(d.stride[i], "c", nd, 0, ity) << "];\n";
+  }
+  for (size_t k = 0; k < s.instrs.size(); ++k) {
+    const EwInstr& in = s.instrs[k];
+    std::string ex;
+    auto nm = [&](int x) { return "e" + std::to_string(x); };
+    if (in.kind == EwKind::LOAD) ex = "l" + std::to_string(in.load);
+    else if (in.kind == EwKind::COPY) ex = nm(in.a[0]);
+    else if (in.kind == EwKind::BN) {
+      ex = "((" + nm(in.a[0]) + " - " + nm(in.a[1]) + ") / sqrtf(" + nm(in.a[2]) + " + " + flit(in.p0) + "))";
+      if (in.a[3] >= 0) ex = "(" + ex + " * " + nm(in.a[3]) + ")";
+      if (in.a[4] >= 0) ex = "(" + ex + " + " + nm(in.a[4]) + ")";
+    } else {
+      std::vector<std::string> args;
+      for (int x : in.a) args.push_back(nm(x));
+      ex = op_expr(in, args);
+    }
+    o << "    const float e" << k << " = " << ex << ";\n";
+  }
+  for (size_t j = 0; j < ns; ++j)
+    o << "    out" << j << "[" << emit_offset(d.stride[nl + j], "c", nd, 0, ity) << "] = e" << s.stores[j].first << ";\n";
+  for (size_t r = 0; r < nops; ++r)
+    o << "    acc" << r << " = " << comb(rs.ops[r].op, "acc" + std::to_string(r), "e" + std::to_string(rs.ops[r].src))
+      << ";\n";
+  o << "  }\n";
+  block_reduce();
+  o << "  if (threadIdx.x == 0) {\n";
+  for (size_t r = 0; r < nops; ++r) o << "    part[blockIdx.x * " << nops << " + " << r << "] = acc" << r << ";\n";
+  o << "  }\n}\n";
+  // finalize
+  head(name + "_fin");
+  for (size_t r = 0; r < nops; ++r) o << "  float acc" << r << " = " << neutral(rs.ops[r].op) << ";\n";
+  o << "  for (int b = threadIdx.x; b < " << G << "; b += blockDim.x) {\n";
+  for (size_t r = 0; r < nops; ++r)
+    o << "    acc" << r << " = " << comb(rs.ops[r].op, "acc" + std::to_string(r), "part[b * " + std::to_string(nops) + " + " + std::to_string(r) + "]") << ";\n";
+  o << "  }\n";
+  block_reduce();
+  o << "  if (threadIdx.x == 0) {\n";
+  for (size_t r = 0; r < nops; ++r) {
+    if (rs.ops[r].op == Op::MEAN) o << "    ro" << r << "[0] = acc" << r << " / " << flit((float)N) << ";\n";
+    else o << "    ro" << r << "[0] = acc" << r << ";\n";
+  }
+  o << "  }\n}\n";
+  return o.str();
+}
+
+// ---------------------------------------------------------------------------
+// The compiler
+// ---------------------------------------------------------------------------
+
+struct Region {
+  std::vector<uint64_t> nodes;        // topo order
+  std::vector<uint64_t> row_ops;      // attached row operations
+  std::vector<int64_t> shape;
+  int red_begin = -1, red_end = -1;   // shared reduction structure of attached row ops
+  bool full = false;
+};
+
+struct GemmChain {
+  uint64_t mm = 0;                 // MATMUL or CONV2D node
+  std::vector<uint64_t> absorbed;  // epilogue nodes in order
+  uint64_t result = 0;             // node whose value the step produces
+  int alpha_slot = -1;
+  float alpha = 1.f;
+  uint64_t bias = 0;  bool has_bias = false;
+  uint64_t bn = 0;    bool has_bn = false;
+  int act = 0;
+  uint64_t residual = 0; bool has_residual = false;
+};
+
+class Compiler {
+ public:
+  Compiler(const CompileInput& in, SourceMap* src) : in_(in), g_(*in.g), src_(src) {}
+
+  std::unique_ptr<Plan> run();
+
+ private:
+  const CompileInput& in_;
+  const Graph& g_;
+  SourceMap* src_;
+  std::unique_ptr<Plan> P_;
+  std::vector<uint64_t> order_;
+  std::unordered_map<uint64_t, int> pos_;
+  std::unordered_map<uint64_t, std::vector<uint64_t>> users_;
+  std::set<uint64_t> is_out_;
+  std::unordered_map<uint64_t, Cls> cls_;
+  std::unordered_map<uint64_t, View> val_;           // materialised values and views
+  std::unordered_map<uint64_t, int> region_of_;
+  std::vector<Region> regions_;
+  std::unordered_map<uint64_t, int> chain_of_;       // node -> chain index (mm and absorbed)
+  std::vector<GemmChain> chains_;
+  std::unordered_map<uint64_t, int> row_region_;     // row op -> region
+  std::vector<std::pair<int, Step>> steps_;
+  std::unordered_map<uint64_t, int> splat_slot_;
+  int kernel_counter_ = 0;
+  int cur_pos_ = 0;
+  bool depends_on(uint64_t a, uint64_t b);
+  bool convex(const std::set<uint64_t>& S);
+
+  const Node& N(uint64_t id) const { return g_.at(id); }
+
+  int new_buffer(size_t bytes, BufKind kind = BufKind::ARENA, uint64_t node = 0) {
+    Buffer b;
+    b.kind = kind;
+    b.bytes = std::max<size_t>(bytes, 4);
+    b.node = node;
+    P_->buffers.push_back(b);
+    return (int)P_->buffers.size() - 1;
+  }
+  View dense(const std::vector<int64_t>& shape, DType dt) {
+    View v;
+    v.shape = shape;
+    v.strides = View::dense_strides(shape);
+    v.dtype = dt;
+    int64_t n = prod(shape);
+    v.buf = new_buffer((size_t)n * dtype_size(dt));
+    return v;
+  }
+  // Dense view whose dims are laid out in the stride order of `like`.
+  View dense_like(const std::vector<int64_t>& shape, const View* like) {
+    if (!like || like->is_splat || like->shape.size() != shape.size()) return dense(shape, DType::F32);
+    std::vector<int> perm(shape.size());
+    for (size_t i = 0; i < perm.size(); ++i) perm[i] = (int)i;
+    std::stable_sort(perm.begin(), perm.end(),
+                     [&](int a, int b) { return std::llabs(like->strides[a]) > std::llabs(like->strides[b]); });
+    View v;
+    v.shape = shape;
+    v.strides.assign(shape.size(), 0);
+    int64_t acc = 1;
+    for (int k = (int)perm.size() - 1; k >= 0; --k) {
+      v.strides[perm[k]] = acc;
+      acc *= shape[perm[k]];
+    }
+    v.dtype = DType::F32;
+    v.buf = new_buffer((size_t)prod(shape) * 4);
+    return v;
+  }
+
+  const View& value(uint64_t id) {
+    auto it = val_.find(id);
+    if (it == val_.end()) fail(PFC_ERR_INTERNAL, "value of node " + std::to_string(id) + " not materialised");
+    return it->second;
+  }
+
+  void add_step(int /*pos*/, Step s) { steps_.push_back({cur_pos_, std::move(s)}); }
+
+  std::string kname(const char* kind) {
+    return std::string("pf_") + kind + "_" + std::to_string(kernel_counter_++);
+  }
+
+  void classify();
+  void absorb_epilogues();
+  void build_regions();
+  void attach_row_ops();
+  void lower();
+  void lower_leaf(uint64_t id);
+  void lower_view(uint64_t id);
+  void lower_region(int r);
+  void lower_row_alone(uint64_t id);
+  void lower_chain(int c);
+  void lower_matmul(const GemmChain& ch, int at);
+  void lower_conv(const GemmChain& ch, int at);
+  void lower_pool(uint64_t id);
+  void lower_concat(uint64_t id);
+  View materialize_copy(const View& src, int at, const std::string& label);
+  void emit_jit(int at, const std::string& label, const std::string& kernel, const std::string& source, int grid,
+                int block, const std::vector<std::pair<int, int64_t>>& ptrs);
+  void finish();
+
+  bool must_materialize(uint64_t id);
+  bool row_structure(uint64_t row, const std::vector<int64_t>& in_shape, int* rb, int* re, bool* full);
+  View splat_view(uint64_t id, const std::vector<int64_t>& shape);
+};
+
+View Compiler::splat_view(uint64_t id, const std::vector<int64_t>& shape) {
+  View v;
+  v.is_splat = true;
+  v.shape = shape;
+  v.strides.assign(shape.size(), 0);
+  v.dtype = DType::F32;
+  auto it = splat_slot_.find(id);
+  if (it == splat_slot_.end()) {
+    P_->scalars.push_back({id, in_.splats.at(id)});
+    it = splat_slot_.emplace(id, (int)P_->scalars.size() - 1).first;
+    P_->splat_nodes.push_back(id);
+  }
+  v.splat_slot = it->second;
+  v.splat_value = in_.splats.at(id);
+  return v;
+}
+
+bool Compiler::depends_on(uint64_t a, uint64_t b) {
+  // true when node a (transitively) reads node b
+  if (a == b) return true;
+  int pb = pos_[b];
+  std::vector<uint64_t> stack{a};
+  std::set<uint64_t> seen;
+  while (!stack.empty()) {
+    uint64_t x = stack.back();
+    stack.pop_back();
+    if (x == b) return true;
+    if (!seen.insert(x).second || pos_[x] < pb) continue;
+    for (uint64_t in : N(x).inputs) stack.push_back(in);
+  }
+  return false;
+}
+
+void Compiler::classify() {
+  for (uint64_t id : order_) {
+    const Node& n = N(id);
+    Cls c;
+    if (n.type != NodeType::OPERATION) c = Cls::LEAF;
+    else if (is_view_op(n.op)) c = Cls::VIEW;
+    else if (op_is_elementwise(n.op) || n.op == Op::BATCH_NORM) c = Cls::EW;
+    else if (is_row_op(n.op)) c = Cls::ROW;
+    else if (n.op == Op::MATMUL || n.op == Op::BATCH_MATMUL) c = Cls::GEMM;
+    else if (n.op == Op::CONV2D) c = Cls::CONV;
+    else if (n.op == Op::MAX_POOL2D || n.op == Op::AVG_POOL2D || n.op == Op::ADAPTIVE_AVG_POOL2D) c = Cls::POOL;
+    else if (n.op == Op::CONCAT || n.op == Op::STACK) c = Cls::CONCAT;
+    else fail(PFC_ERR_UNSUPPORTED, std::string("Unsupported operation for CUDA execution: ") + op_name(n.op));
+    if (c != Cls::LEAF && c != Cls::VIEW && n.dtype != DType::F32)
+      fail(PFC_ERR_UNSUPPORTED, std::string("CUDA executor computes float32 only; node ") + std::to_string(id) +
+                                    " (" + op_name(n.op) + ") is " + dtype_name(n.dtype));
+    if (n.op == Op::BATCH_NORM && (n.attr_bool("training", false) || !n.attr_bool("track_running_stats", true)))
+      fail(PFC_ERR_UNSUPPORTED, "BATCH_NORM with batch statistics (training mode) is not supported");
+    cls_[id] = c;
+  }
+}
+
+// Shape-compatible bias: broadcasts along every dim but `ndim_n`.
+static bool bias_along(const Node& b, const std::vector<int64_t>& out_shape, int n_dim) {
+  if (b.shape.size() > out_shape.size()) return false;
+  size_t off = out_shape.size() - b.shape.size();
+  bool seen = false;
+  for (size_t d = 0; d < b.shape.size(); ++d) {
+    int od = (int)(off + d);
+    if (od == n_dim) {
+      if (b.shape[d] != out_shape[od]) return false;
+      seen = true;
+    } else if (b.shape[d] != 1) {
+      return false;
+    }
+  }
+  return seen || out_shape[n_dim] == 1;
+}
+
+void Compiler::absorb_epilogues() {
+  for (uint64_t id : order_) {
+    Cls c = cls_[id];
+    if (c != Cls::GEMM && c != Cls::CONV) continue;
+    if (chain_of_.count(id)) continue;  // already absorbed into an earlier chain
+    GemmChain ch;
+    ch.mm = id;
+    uint64_t cur = id;
+    const std::vector<int64_t> shape = N(id).shape;
+    int n_dim = c == Cls::CONV ? 1 : (int)shape.size() - 1;
+    bool stage_alpha = false, stage_bias = false, stage_act = false, stage_res = false;
+    while (!is_out_.count(cur) && users_[cur].size() == 1) {
+      uint64_t u = users_[cur][0];
+      const Node& un = N(u);
+      if (cls_[u] != Cls::EW || un.shape != shape) break;
+      // the other operand of a binary consumer
+      auto other = [&]() -> uint64_t { return un.inputs[0] == cur ? un.inputs[1] : un.inputs[0]; };
+      if (un.op == Op::MUL && un.inputs.size() == 2 && un.inputs[0] != un.inputs[1] && !stage_alpha && !stage_bias &&
+          !stage_act && !stage_res && c == Cls::GEMM) {
+        uint64_t o = other();
+        if (!in_.splats.count(o)) {
+          // a view chain ending at a splat constant counts too
+          const Node* on = &N(o);
+          while (on->type == NodeType::OPERATION && is_view_op(on->op) && on->inputs.size() == 1) on = &N(on->inputs[0]);
+          if (!in_.splats.count(on->id)) break;
+          o = on->id;
+        }
+        stage_alpha = true;
+        splat_view(o, {});
+        ch.alpha_slot = splat_slot_.at(o);
+        ch.alpha = in_.splats.at(o);
+      } else if (un.op == Op::ADD && un.inputs.size() == 2 && un.inputs[0] != un.inputs[1] && !stage_bias &&
+                 !stage_act && !stage_res && !ch.has_bn && bias_along(N(other()), shape, n_dim) &&
+                 prod(N(other()).shape) == shape[n_dim] && !depends_on(other(), id)) {
+        stage_bias = true;
+        ch.has_bias = true;
+        ch.bias = other();
+      } else if (un.op == Op::BATCH_NORM && c == Cls::CONV && un.inputs[0] == cur && !ch.has_bn && !stage_act &&
+                 !stage_res) {
+        bool ok = true;
+        for (size_t i = 1; i < un.inputs.size(); ++i)
+          ok = ok && N(un.inputs[i]).shape.size() == 1 && !depends_on(un.inputs[i], id);
+        if (!ok) break;
+        ch.has_bn = true;
+        ch.bn = u;
+        stage_bias = true;
+      } else if (is_act(un.op) && !stage_act && !stage_res) {
+        stage_act = true;
+        ch.act = act_code(un.op);
+      } else if (un.op == Op::ADD && un.inputs.size() == 2 && un.inputs[0] != un.inputs[1] && !stage_res &&
+                 c == Cls::GEMM && N(other()).shape == shape && !depends_on(other(), id) &&
+                 !in_.splats.count(other())) {
+        stage_res = true;
+        ch.has_residual = true;
+        ch.residual = other();
+      } else {
+        break;
+      }
+      ch.absorbed.push_back(u);
+      cur = u;
+    }
+    ch.result = cur;
+    int ci = (int)chains_.size();
+    chains_.push_back(ch);
+    chain_of_[id] = ci;
+    for (uint64_t a : ch.absorbed) {
+      chain_of_[a] = ci;
+      cls_[a] = cls_[id];  // absorbed nodes no longer form elementwise regions
+    }
+  }
+}
+
+// A set of nodes is convex when no path leaves it and re-enters it; only
+// convex sets can run as one kernel.
+bool Compiler::convex(const std::set<uint64_t>& S) {
+  std::vector<uint64_t> stack;
+  std::set<uint64_t> seen;
+  for (uint64_t s : S)
+    for (uint64_t u : users_[s])
+      if (!S.count(u)) stack.push_back(u);
+  while (!stack.empty()) {
+    uint64_t u = stack.back();
+    stack.pop_back();
+    if (!seen.insert(u).second) continue;
+    if (S.count(u)) return false;
+    for (uint64_t v : users_[u]) stack.push_back(v);
+  }
+  return true;
+}
+
+void Compiler::build_regions() {
+  // Union-find over elementwise nodes: merge every producer/consumer pair of
+  // equal shape while the merged set stays convex.
+  std::unordered_map<uint64_t, uint64_t> parent;
+  std::unordered_map<uint64_t, std::set<uint64_t>> members;
+  std::function<uint64_t(uint64_t)> find = [&](uint64_t x) {
+    while (parent[x] != x) {
+      parent[x] = parent[parent[x]];
+      x = parent[x];
+    }
+    return x;
+  };
+  for (uint64_t id : order_)
+    if (cls_[id] == Cls::EW && !chain_of_.count(id)) {
+      parent[id] = id;
+      members[id] = {id};
+    }
+  for (uint64_t id : order_) {
+    if (!parent.count(id)) continue;
+    for (uint64_t in : N(id).inputs) {
+      if (!parent.count(in) || N(in).shape != N(id).shape) continue;
+      uint64_t ra = find(in), rb = find(id);
+      if (ra == rb) continue;
+      std::set<uint64_t> S = members[ra];
+      S.insert(members[rb].begin(), members[rb].end());
+      if (!convex(S)) continue;
+      parent[ra] = rb;
+      members[rb] = std::move(S);
+      members.erase(ra);
+    }
+  }
+  std::unordered_map<uint64_t, int> index;
+  for (uint64_t id : order_) {
+    if (!parent.count(id)) continue;
+    uint64_t r = find(id);
+    auto it = index.find(r);
+    if (it == index.end()) {
+      Region rg;
+      rg.shape = N(id).shape;
+      regions_.push_back(rg);
+      it = index.emplace(r, (int)regions_.size() - 1).first;
+    }
+    regions_[it->second].nodes.push_back(id);
+    region_of_[id] = it->second;
+  }
+}
+
+// Reduction structure of a row op over an input of shape `s`: dims [rb, re) reduced.
+bool Compiler::row_structure(uint64_t row, const std::vector<int64_t>& s, int* rb, int* re, bool* full) {
+  const Node& n = N(row);
+  int nd = (int)s.size();
+  *full = false;
+  if (n.op == Op::LAYER_NORM) {
+    // normalization.cpp:224-255: normalized over the trailing len(normalized_shape) dims
+    auto ns = n.attr_ints("normalized_shape");
+    int k = (int)ns.size();
+    if (k > nd) fail(PFC_ERR_GRAPH, "LAYER_NORM normalized_shape longer than input");
+    for (int i = 0; i < k; ++i)
+      if (s[nd - k + i] != ns[i]) fail(PFC_ERR_GRAPH, "Input shape doesn't match normalized_shape");
+    *rb = nd - k;
+    *re = nd;
+    return true;
+  }
+  if (n.op == Op::SOFTMAX || n.op == Op::LOG_SOFTMAX) {
+    // tensor_impl.cpp:272-273: attribute `dim` (int), default -1
+    int d = (int)n.attr_int("dim", -1);
+    if (d < 0) d += nd;
+    if (d < 0 || d >= nd) fail(PFC_ERR_GRAPH, "softmax dim out of range");
+    *rb = d;
+    *re = d + 1;
+    return true;
+  }
+  // reductions: optional int `dim`, bool `keepdim` (tensor_impl.cpp:530-533)
+  if (!n.has_attr("dim")) {
+    *rb = 0;
+    *re = nd;
+    *full = true;
+    return true;
+  }
+  int d = (int)n.attr_int("dim");
+  if (d < 0) d += nd;
+  if (d < 0 || d >= nd) fail(PFC_ERR_GRAPH, "Reduction dimension out of range");
+  *rb = d;
+  *re = d + 1;
+  return true;
+}
+
+void Compiler::attach_row_ops() {
+  for (uint64_t id : order_) {
+    if (cls_[id] != Cls::ROW) continue;
+    const Node& n = N(id);
+    uint64_t x = n.inputs.at(0);
+    int rb, re;
+    bool full;
+    row_structure(id, N(x).shape, &rb, &re, &full);
+    auto r = region_of_.find(x);
+    if (r == region_of_.end()) continue;
+    Region& rg = regions_[r->second];
+    if (rg.shape != N(x).shape) continue;
+    if (!rg.row_ops.empty() && (rg.red_begin != rb || rg.red_end != re || rg.full != full)) continue;
+    // LN parameters must not depend on the region
+    bool ok = true;
+    for (size_t i = 1; i < n.inputs.size(); ++i) {
+      auto ri = region_of_.find(n.inputs[i]);
+      if (ri != region_of_.end() && ri->second == r->second) ok = false;
+    }
+    if (ok) {
+      std::set<uint64_t> S(rg.nodes.begin(), rg.nodes.end());
+      S.insert(rg.row_ops.begin(), rg.row_ops.end());
+      S.insert(id);
+      ok = convex(S);
+    }
+    if (!ok) continue;
+    rg.row_ops.push_back(id);
+    rg.red_begin = rb;
+    rg.red_end = re;
+    rg.full = full;
+    row_region_[id] = r->second;
+  }
+}
+
+bool Compiler::must_materialize(uint64_t id) {
+  if (is_out_.count(id)) return true;
+  auto r = region_of_.find(id);
+  for (uint64_t u : users_[id]) {
+    if (r != region_of_.end()) {
+      auto ru = region_of_.find(u);
+      if (ru != region_of_.end() && ru->second == r->second) continue;
+      auto rr = row_region_.find(u);
+      if (rr != row_region_.end() && rr->second == r->second && N(u).inputs[0] == id) {
+        // feeding an attached row op as its main input; LN params still need a value
+        bool also_param = false;
+        for (size_t i = 1; i < N(u).inputs.size(); ++i) also_param |= N(u).inputs[i] == id;
+        if (!also_param) continue;
+      }
+    }
+    auto c = chain_of_.find(u);
+    if (c != chain_of_.end()) {
+      const GemmChain& ch = chains_[c->second];
+      // the running value of the chain is not materialised
+      if (u != ch.mm && (N(u).inputs[0] == id || (N(u).inputs.size() > 1 && N(u).inputs[1] == id))) {
+        bool is_chain_value = (id == ch.mm) || std::find(ch.absorbed.begin(), ch.absorbed.end(), id) != ch.absorbed.end();
+        if (is_chain_value) continue;
+      }
+    }
+    return true;
+  }
+  return false;
+}
+
+void Compiler::emit_jit(int at, const std::string& label, const std::string& kernel, const std::string& source,
+                        int grid, int block, const std::vector<std::pair<int, int64_t>>& ptrs) {
+  Step s;
+  s.kind = StepKind::JIT;
+  s.label = label;
+  s.jit.kernel = kernel;
+  // kernel names are positional; the key covers the source with a fixed name
+  std::string canon = source;
+  size_t p;
+  while ((p = canon.find(kernel)) != std::string::npos) canon.replace(p, kernel.size(), "pf_kernel");
+  s.jit.module_key = hash_hex(canon);
+  s.jit.kernel = "pf_kernel";
+  s.jit.grid = grid;
+  s.jit.block = block;
+  s.jit.ptrs = ptrs;
+  (*src_)[s.jit.module_key] = {canon, "pf_kernel"};
+  add_step(at, std::move(s));
+}
+
+View Compiler::materialize_copy(const View& srcv, int at, const std::string& label) {
+  EwSpec s;
+  s.space = srcv.shape;
+  View out = srcv.is_splat ? dense(srcv.shape, DType::F32) : dense(srcv.shape, srcv.dtype);
+  s.loads.push_back(srcv);
+  EwInstr ld;
+  ld.kind = EwKind::LOAD;
+  ld.load = 0;
+  s.instrs.push_back(ld);
+  s.stores.push_back({0, out});
+  std::string name = kname("copy");
+  int grid, block;
+  std::string code = gen_ew(s, name, in_.num_sms, &grid, &block);
+  std::vector<std::pair<int, int64_t>> ptrs;
+  ptrs.push_back({srcv.is_splat ? -1 : srcv.buf, srcv.offset * (int64_t)dtype_size(srcv.dtype)});
+  ptrs.push_back({out.buf, 0});
+  ptrs.push_back({P_->scalar_buf, 0});
+  emit_jit(at, label, name, code, grid, block, ptrs);
+  return out;
+}
+
+void Compiler::lower_leaf(uint64_t id) {
+  const Node& n = N(id);
+  if (in_.bindings.count(id)) {
+    View v;
+    v.shape = n.shape;
+    v.strides = View::dense_strides(n.shape);
+    v.dtype = n.dtype;
+    v.buf = new_buffer(n.size_bytes(), BufKind::BINDING, id);
+    val_[id] = v;
+    return;
+  }
+  if (in_.splats.count(id)) {
+    val_[id] = splat_view(id, n.shape);
+    return;
+  }
+  if (!n.has_data()) {
+    // Data-less INPUT/PARAMETER/CONSTANT: zero (the ROCm executor zero-fills, rocm_executor.cpp:99-102).
+    if (n.dtype != DType::F32) fail(PFC_ERR_UNSUPPORTED, "data-less non-float32 leaf");
+    fail(PFC_ERR_INTERNAL, "data-less leaf should have been classified as a zero splat");
+  }
+  View v;
+  v.shape = n.shape;
+  v.strides = View::dense_strides(n.shape);
+  v.dtype = n.dtype;
+  v.buf = new_buffer(n.size_bytes(), BufKind::CONST, id);
+  P_->const_nodes.push_back(id);
+  val_[id] = v;
+}
+
+void Compiler::lower_view(uint64_t id) {
+  const Node& n = N(id);
+  const View& x = value(n.inputs.at(0));
+  View out;
+  switch (n.op) {
+    case Op::RESHAPE: case Op::VIEW: case Op::SQUEEZE: case Op::UNSQUEEZE: {
+      if (prod(n.shape) != x.numel()) fail(PFC_ERR_GRAPH, "reshape: total elements must match");
+      if (x.is_splat) { out = x; out.shape = n.shape; out.strides.assign(n.shape.size(), 0); break; }
+      if (!reshape_view(x, n.shape, &out)) {
+        View c = materialize_copy(x, pos_[id], std::string("contiguous copy for reshape of %") + std::to_string(id));
+        reshape_view(c, n.shape, &out);
+      }
+      break;
+    }
+    case Op::TRANSPOSE: {
+      // attributes dim0/dim1 (int), tensor_impl.cpp:577-578; spec shape_inference.hpp:220-239
+      int nd = (int)x.shape.size();
+      int d0 = (int)n.attr_int("dim0"), d1 = (int)n.attr_int("dim1");
+      if (d0 < 0) d0 += nd;
+      if (d1 < 0) d1 += nd;
+      if (d0 < 0 || d0 >= nd || d1 < 0 || d1 >= nd) fail(PFC_ERR_GRAPH, "transpose: dimension out of range");
+      out = x;
+      std::swap(out.shape[d0], out.shape[d1]);
+      std::swap(out.strides[d0], out.strides[d1]);
+      break;
+    }
+    case Op::SLICE: {
+      // attributes dim (int), start/end (int64), tensor.cpp:262-283
+      int nd = (int)x.shape.size();
+      int d = (int)n.attr_int("dim", 0);
+      if (d < 0) d += nd;
+      if (d < 0 || d >= nd) fail(PFC_ERR_GRAPH, "slice: dimension out of range");
+      int64_t size = x.shape[d];
+      int64_t st = n.attr_int("start", 0), en = n.attr_int("end", size);
+      if (st < 0) st += size;
+      if (en < 0) en += size;
+      st = std::max<int64_t>(0, std::min(st, size));
+      en = std::max<int64_t>(0, std::min(en, size));
+      if (en <= st) fail(PFC_ERR_GRAPH, "slice: end must be greater than start");
+      out = x;
+      out.shape[d] = en - st;
+      if (!x.is_splat) out.offset += st * x.strides[d];
+      break;
+    }
+    case Op::BROADCAST:
+      out = broadcast_to(x, n.shape);
+      break;
+    default:  // CONTIGUOUS, COPY, LAYOUT_TRANSFORM, DROPOUT (inference: identity, dropout.cpp:26-30)
+      out = x;
+      if (n.op == Op::DROPOUT && n.attr_bool("training", false))
+        fail(PFC_ERR_UNSUPPORTED, "DROPOUT in training mode is not supported");
+      break;
+  }
+  if (out.shape != n.shape) {
+    if (out.numel() != prod(n.shape)) fail(PFC_ERR_GRAPH, "shape op output shape mismatch at node " + std::to_string(id));
+    View o2;
+    if (out.is_splat) { o2 = out; o2.shape = n.shape; o2.strides.assign(n.shape.size(), 0); }
+    else if (!reshape_view(out, n.shape, &o2)) {
+      View c = materialize_copy(out, pos_[id], "contiguous copy");
+      reshape_view(c, n.shape, &o2);
+    }
+    out = o2;
+  }
+  val_[id] = out;
+}
+
+// Lower an elementwise region (and its attached row ops).
+void Compiler::lower_region(int r) {
+  Region& rg = regions_[r];
+  RowSpec rs;
+  EwSpec& s = rs.ew;
+  s.space = rg.shape;
+  std::unordered_map<uint64_t, int> instr_of;
+  std::unordered_map<uint64_t, int> load_of;  // external node -> load index
+  int at = 0;
+  const View* layout_ref = nullptr;
+  auto operand = [&](uint64_t in) -> int {
+    auto it = instr_of.find(in);
+    if (it != instr_of.end()) return it->second;
+    auto lt = load_of.find(in);
+    int li;
+    if (lt == load_of.end()) {
+      const View& v = value(in);
+      View b = broadcast_to(v, s.space);
+      s.loads.push_back(b);
+      li = (int)s.loads.size() - 1;
+      load_of[in] = li;
+      if (!layout_ref && !v.is_splat && v.shape == s.space) layout_ref = &value(in);
+    } else {
+      li = lt->second;
+    }
+    EwInstr ld;
+    ld.kind = EwKind::LOAD;
+    ld.load = li;
+    s.instrs.push_back(ld);
+    int k = (int)s.instrs.size() - 1;
+    instr_of[in] = k;
+    return k;
+  };
+  for (uint64_t id : rg.nodes) {
+    const Node& n = N(id);
+    at = std::max(at, pos_[id]);
+    EwInstr e;
+    if (n.op == Op::BATCH_NORM) {
+      // inputs {x, [weight, bias], [running_mean, running_var]} (normalization.cpp:71-80)
+      bool affine = n.attr_bool("affine", n.inputs.size() == 5);
+      e.kind = EwKind::BN;
+      e.p0 = (float)n.attr_float("eps", 1e-5);
+      int x = operand(n.inputs[0]);
+      size_t k = 1;
+      int gamma = -1, beta = -1;
+      // per-channel params broadcast along dim 1 of [N,C,H,W]
+      auto chan = [&](uint64_t p) -> int {
+        const View& pv = value(p);
+        View b;
+        b = pv;
+        b.shape = s.space;
+        b.strides.assign(s.space.size(), 0);
+        if (!pv.is_splat) b.strides[1] = pv.strides.empty() ? 1 : pv.strides[0];
+        s.loads.push_back(b);
+        EwInstr ld;
+        ld.kind = EwKind::LOAD;
+        ld.load = (int)s.loads.size() - 1;
+        s.instrs.push_back(ld);
+        return (int)s.instrs.size() - 1;
+      };
+      if (affine) {
+        gamma = chan(n.inputs[k++]);
+        beta = chan(n.inputs[k++]);
+      }
+      if (k + 2 > n.inputs.size()) fail(PFC_ERR_UNSUPPORTED, "BATCH_NORM without running statistics");
+      int mean = chan(n.inputs[k++]);
+      int var = chan(n.inputs[k++]);
+      e.a = {x, mean, var, gamma, beta};
+    } else if (n.op == Op::CLAMP) {
+      e.op = Op::CLAMP;
+      int x = operand(n.inputs[0]);
+      if (n.inputs.size() >= 3) {
+        e.a = {x, operand(n.inputs[1]), operand(n.inputs[2])};
+      } else {
+        fail(PFC_ERR_UNSUPPORTED, "CLAMP node needs min and max inputs");
+      }
+    } else {
+      e.op = n.op;
+      for (uint64_t in : n.inputs) e.a.push_back(operand(in));
+      uint16_t ov = (uint16_t)n.op;
+      size_t need = (n.op == Op::WHERE) ? 3 : (ov >= 200 && ov < 400) ? 1 : 2;
+      if (e.a.size() != need)
+        fail(PFC_ERR_GRAPH, std::string("wrong input count for ") + op_name(n.op) + " at node " + std::to_string(id));
+    }
+    s.instrs.push_back(e);
+    instr_of[id] = (int)s.instrs.size() - 1;
+  }
+  // stores
+  for (uint64_t id : rg.nodes) {
+    if (!must_materialize(id)) continue;
+    View out = dense_like(s.space, layout_ref);
+    s.stores.push_back({instr_of[id], out});
+    val_[id] = out;
+  }
+  std::vector<std::pair<int, int64_t>> ptrs;
+  auto push_ptrs = [&]() {
+    for (const View& l : s.loads) ptrs.push_back({l.is_splat ? -1 : l.buf, l.offset * (int64_t)dtype_size(l.dtype)});
+    for (auto& st : s.stores) ptrs.push_back({st.second.buf, 0});
+  };
+  if (rg.row_ops.empty()) {
+    std::string name = kname("ew");
+    int grid, block;
+    std::string code = gen_ew(s, name, in_.num_sms, &grid, &block);
+    push_ptrs();
+    ptrs.push_back({P_->scalar_buf, 0});
+    emit_jit(at, "fused elementwise " + shape_str(s.space), name, code, grid, block, ptrs);
+    return;
+  }
+  // row group
+  rs.red_begin = rg.red_begin;
+  rs.red_end = rg.red_end;
+  for (uint64_t rid : rg.row_ops) {
+    const Node& rn = N(rid);
+    at = std::max(at, pos_[rid]);
+    RowOp op;
+    op.op = rn.op;
+    op.src = instr_of.at(rn.inputs[0]);
+    if (rn.op == Op::LAYER_NORM) {
+      op.eps = (float)rn.attr_float("eps", 1e-5);
+      bool affine = rn.attr_bool("elementwise_affine", rn.inputs.size() >= 3);
+      if (affine && rn.inputs.size() >= 3) {
+        // gamma/beta have shape normalized_shape: broadcast to the row space
+        op.gamma = operand(rn.inputs[1]);
+        op.beta = operand(rn.inputs[2]);
+      }
+    }
+    if (rn.op == Op::SOFTMAX || rn.op == Op::LOG_SOFTMAX || rn.op == Op::LAYER_NORM) {
+      op.out = dense_like(s.space, layout_ref);
+    } else {
+      op.out = dense(rn.shape, DType::F32);
+    }
+    val_[rid] = op.out;
+    rs.ops.push_back(op);
+  }
+  push_ptrs();
+  for (const RowOp& op : rs.ops) ptrs.push_back({op.out.buf, 0});
+  ptrs.push_back({P_->scalar_buf, 0});
+  int64_t outer = prod(s.space, 0, rs.red_begin), inner = prod(s.space, rs.red_end);
+  std::string label;
+  for (const RowOp& op : rs.ops) label += std::string(op_name(op.op)) + " ";
+  if (rg.full) {
+    std::string name = kname("full");
+    int grid, nst[1];
+    std::string code = gen_full(rs, name, in_.num_sms, &grid, nst);
+    int part = new_buffer((size_t)grid * std::max(1, nst[0]) * 4);
+    ptrs.push_back({part, 0});
+    // two kernels share one module: emit as two steps with the same source
+    Step s1;
+    emit_jit(at, "full reduction (" + label + ") " + shape_str(s.space), name, code, grid, 256, ptrs);
+    // second kernel
+    Step s2 = steps_.back().second;
+    s2.jit.kernel = "pf_kernel_fin";
+    s2.jit.grid = 1;
+    s2.label = "full reduction finalize";
+    add_step(at, s2);
+    return;
+  }
+  std::string name = kname(inner == 1 ? "row" : "col");
+  int grid, block;
+  std::string code = inner == 1 ? gen_row(rs, name, in_.num_sms, &grid, &block)
+                                 : gen_col(rs, name, in_.num_sms, &grid, &block);
+  (void)outer;
+  emit_jit(at, std::string(inner == 1 ? "row kernel (" : "column kernel (") + label + ") " + shape_str(s.space), name,
+           code, grid, block, ptrs);
+}
+
+void Compiler::lower_row_alone(uint64_t id) {
+  // A row op whose input is a materialised value: a region with one load.
+  Region rg;
+  const Node& n = N(id);
+  rg.shape = N(n.inputs[0]).shape;
+  int rb, re;
+  bool full;
+  row_structure(id, rg.shape, &rb, &re, &full);
+  rg.red_begin = rb;
+  rg.red_end = re;
+  rg.full = full;
+  rg.row_ops.push_back(id);
+  regions_.push_back(rg);
+  int r = (int)regions_.size() - 1;
+  // the region's prologue is just the load of the input: emulate via a COPY-less region
+  // by lowering with zero nodes: operand() creates the load lazily.
+  Region& R = regions_[r];
+  (void)R;
+  // Inline lowering (mirrors lower_region with no elementwise nodes)
+  RowSpec rs;
+  EwSpec& s = rs.ew;
+  s.space = rg.shape;
+  auto load_instr = [&](uint64_t in, const std::vector<int64_t>& space) -> int {
+    View b = broadcast_to(value(in), space);
+    s.loads.push_back(b);
+    EwInstr ld;
+    ld.kind = EwKind::LOAD;
+    ld.load = (int)s.loads.size() - 1;
+    s.instrs.push_back(ld);
+    return (int)s.instrs.size() - 1;
+  };
+  RowOp op;
+  op.op = n.op;
+  op.src = load_instr(n.inputs[0], s.space);
+  if (n.op == Op::LAYER_NORM) {
+    op.eps = (float)n.attr_float("eps", 1e-5);
+    bool affine = n.attr_bool("elementwise_affine", n.inputs.size() >= 3);
+    if (affine && n.inputs.size() >= 3) {
+      op.gamma = load_instr(n.inputs[1], s.space);
+      op.beta = load_instr(n.inputs[2], s.space);
+    }
+  }
+  const View& xin = value(n.inputs[0]);
+  if (n.op == Op::SOFTMAX || n.op == Op::LOG_SOFTMAX || n.op == Op::LAYER_NORM)
+    op.out = dense_like(s.space, xin.is_splat ? nullptr : &xin);
+  else
+    op.out = dense(n.shape, DType::F32);
+  val_[id] = op.out;
+  rs.ops.push_back(op);
+  rs.red_begin = rb;
+  rs.red_end = re;
+  std::vector<std::pair<int, int64_t>> ptrs;
+  for (const View& l : s.loads) ptrs.push_back({l.is_splat ? -1 : l.buf, l.offset * (int64_t)dtype_size(l.dtype)});
+  ptrs.push_back({op.out.buf, 0});
+  ptrs.push_back({P_->scalar_buf, 0});
+  int64_t inner = prod(s.space, re);
+  if (full) {
+    std::string name = kname("full");
+    int grid, nst[1];
+    std::string code = gen_full(rs, name, in_.num_sms, &grid, nst);
+    int part = new_buffer((size_t)grid * std::max(1, nst[0]) * 4);
+    ptrs.push_back({part, 0});
+    emit_jit(pos_[id], std::string("full reduction (") + op_name(n.op) + ")", name, code, grid, 256, ptrs);
+    Step s2 = steps_.back().second;
+    s2.jit.kernel = "pf_kernel_fin";
+    s2.jit.grid = 1;
+    s2.label = "full reduction finalize";
+    add_step(pos_[id], s2);
+    return;
+  }
+  std::string name = kname(inner == 1 ? "row" : "col");
+  int grid, block;
+  std::string code = inner == 1 ? gen_row(rs, name, in_.num_sms, &grid, &block)
+                                 : gen_col(rs, name, in_.num_sms, &grid, &block);
+  emit_jit(pos_[id], std::string(inner == 1 ? "row kernel (" : "column kernel (") + op_name(n.op) + ") " +
+                         shape_str(s.space),
+           name, code, grid, block, ptrs);
+}
+
+// Collapse the batch dims [0, nb) of a view to one stride; false if impossible.
+static bool collapse_batch(const View& v, int nb, int64_t* stride) {
+  if (nb == 0) { *stride = 0; return true; }
+  int64_t st = v.strides[nb - 1];
+  int64_t span = v.shape[nb - 1];
+  for (int d = nb - 2; d >= 0; --d) {
+    if (v.shape[d] == 1) continue;
+    if (v.strides[d] != st * span) {
+      // allow broadcast (all-zero) batch strides
+      bool all0 = true;
+      for (int e = 0; e < nb; ++e) all0 = all0 && (v.strides[e] == 0 || v.shape[e] == 1);
+      if (all0) { *stride = 0; return true; }
+      return false;
+    }
+    span *= v.shape[d];
+  }
+  *stride = st;
+  return true;
+}
+
+void Compiler::lower_matmul(const GemmChain& ch, int at) {
+  const Node& mm = N(ch.mm);
+  View a = value(mm.inputs.at(0));
+  View b = value(mm.inputs.at(1));
+  if (a.is_splat) a = materialize_copy(a, at, "materialise splat operand");
+  if (b.is_splat) b = materialize_copy(b, at, "materialise splat operand");
+  // infer_matmul_spec (shape_inference.hpp:146-217): promote 1-D operands.
+  bool a1 = a.shape.size() == 1, b1 = b.shape.size() == 1;
+  if (a.shape.empty() || b.shape.empty()) fail(PFC_ERR_GRAPH, "matmul requires non-scalar inputs");
+  if (a1) { a.shape.insert(a.shape.begin(), 1); a.strides.insert(a.strides.begin(), 0); }
+  if (b1) { b.shape.push_back(1); b.strides.push_back(0); }
+  int64_t M = a.shape[a.shape.size() - 2], K = a.shape.back();
+  int64_t Kb = b.shape[b.shape.size() - 2], Nn = b.shape.back();
+  if (K != Kb) fail(PFC_ERR_GRAPH, "matmul: inner dimensions don't match");
+  std::vector<int64_t> ab(a.shape.begin(), a.shape.end() - 2), bb(b.shape.begin(), b.shape.end() - 2);
+  // broadcast batch shape
+  size_t nb = std::max(ab.size(), bb.size());
+  std::vector<int64_t> batch(nb);
+  for (size_t i = 0; i < nb; ++i) {
+    int64_t da = i < nb - ab.size() ? 1 : ab[i - (nb - ab.size())];
+    int64_t db = i < nb - bb.size() ? 1 : bb[i - (nb - bb.size())];
+    if (da != db && da != 1 && db != 1) fail(PFC_ERR_GRAPH, "matmul: batch dims not broadcastable");
+    batch[i] = std::max(da, db);
+  }
+  int64_t nbatch = prod(batch);
+  int prec = in_.precision;
+  int64_t kalign = prec == PFC_PRECISION_BF16 ? 64 : 32;
+  int64_t kpad = round_up(std::max<int64_t>(K, 1), kalign);
+  // A view broadcast to [batch..., M, K]
+  std::vector<int64_t> afull = batch;
+  afull.push_back(M);
+  afull.push_back(K);
+  View av = broadcast_to(a, afull);
+  // B as [batch..., N, K]: swap the last two dims of the [.., K, N] view
+  std::vector<int64_t> bfull = batch;
+  bfull.push_back(K);
+  bfull.push_back(Nn);
+  bool b_batched = !bb.empty() && prod(bb) > 1;
+  View bv = b_batched ? broadcast_to(b, bfull) : b;
+  if (!b_batched) {
+    // drop size-1 batch dims of b
+    View t;
+    t = b;
+    t.shape = {K, Nn};
+    t.strides = {b.strides[b.strides.size() - 2], b.strides.back()};
+    bv = t;
+  }
+  {
+    size_t r = bv.shape.size();
+    std::swap(bv.shape[r - 2], bv.shape[r - 1]);
+    std::swap(bv.strides[r - 2], bv.strides[r - 1]);
+  }
+  int64_t gbatch = b_batched ? nbatch : 1;
+  int64_t gM = b_batched ? M : nbatch * M;
+  // prepared operands
+  size_t esz = prec == PFC_PRECISION_BF16 ? 2 : 4;
+  int64_t arows = nbatch * M, brows = (b_batched ? nbatch : 1) * Nn;
+  Step sa;
+  sa.kind = StepKind::SPLIT;
+  sa.label = "prepare A " + shape_str(afull);
+  sa.split.src = av;
+  sa.split.precision = prec;
+  sa.split.rows = arows;
+  sa.split.cols = K;
+  sa.split.kpad = kpad;
+  sa.split.out_hi = new_buffer((size_t)arows * kpad * esz);
+  sa.split.out_lo = prec == PFC_PRECISION_BF16 ? -1 : new_buffer((size_t)arows * kpad * esz);
+  Step sb;
+  sb.kind = StepKind::SPLIT;
+  sb.label = "prepare B " + shape_str(bv.shape);
+  sb.split.src = bv;
+  sb.split.precision = prec;
+  sb.split.rows = brows;
+  sb.split.cols = K;
+  sb.split.kpad = kpad;
+  sb.split.out_hi = new_buffer((size_t)brows * kpad * esz);
+  sb.split.out_lo = prec == PFC_PRECISION_BF16 ? -1 : new_buffer((size_t)brows * kpad * esz);
+  // output: node shape of the chain result (same as matmul shape)
+  View c = dense(mm.shape, DType::F32);
+  Step sg;
+  sg.kind = StepKind::GEMM;
+  sg.label = "gemm " + std::to_string(gbatch) + "x[" + std::to_string(gM) + "x" + std::to_string(Nn) + "x" +
+             std::to_string(K) + "]";
+  GemmArgs& G = sg.gemm;
+  G.precision = prec;
+  G.a_hi = sa.split.out_hi;
+  G.a_lo = sa.split.out_lo;
+  G.b_hi = sb.split.out_hi;
+  G.b_lo = sb.split.out_lo;
+  G.batch = gbatch;
+  G.M = gM;
+  G.N = Nn;
+  G.K = K;
+  G.kpad = kpad;
+  G.a_sb = gbatch > 1 ? M * kpad : 0;
+  G.b_sb = gbatch > 1 ? Nn * kpad : 0;
+  G.c = c;
+  G.c_sn = 1;
+  G.c_sm = Nn;
+  G.c_sb = gbatch > 1 ? M * Nn : 0;
+  G.alpha = ch.alpha;
+  G.alpha_slot = ch.alpha_slot;
+  G.act = ch.act;
+  if (ch.has_bias) {
+    View bv2 = value(ch.bias);
+    // contiguous along n? (a bias of equal values stays a scalar)
+    int64_t sn = 0;
+    for (size_t d = 0; d < bv2.shape.size(); ++d)
+      if (bv2.shape[d] != 1) sn = bv2.strides[d];
+    if (!bv2.is_splat && sn != 1 && Nn > 1) bv2 = materialize_copy(bv2, at, "contiguous bias");
+    G.bias = bv2;
+    G.has_bias = true;
+  }
+  if (ch.has_residual) {
+    View r = broadcast_to(value(ch.residual), mm.shape);
+    if (r.is_splat) r = materialize_copy(r, at, "materialise residual");
+    size_t rd = r.shape.size();
+    int64_t rsb = 0;
+    bool ok;
+    if (gbatch > 1) {
+      ok = collapse_batch(r, (int)rd - 2, &rsb);
+      G.r_sm = r.strides[rd - 2];
+    } else {
+      // rows (batch..., M) must collapse into one stride
+      View rr = r;
+      int64_t st;
+      ok = collapse_batch(rr, (int)rd - 1, &st);
+      G.r_sm = rd >= 2 ? st : 0;
+      if (rd == 1) G.r_sm = 0;
+    }
+    if (!ok) {
+      r = materialize_copy(r, at, "contiguous residual");
+      rsb = gbatch > 1 ? M * Nn : 0;
+      G.r_sm = Nn;
+    }
+    G.residual = r;
+    G.r_sb = rsb;
+    G.r_sn = r.strides[rd - 1];
+    G.has_residual = true;
+  }
+  add_step(at, sa);
+  add_step(at, sb);
+  add_step(at, sg);
+  // result view with the chain result's shape (== mm shape)
+  val_[ch.result] = c;
+}
+
+void Compiler::lower_conv(const GemmChain& ch, int at) {
+  const Node& cv = N(ch.mm);
+  View x = value(cv.inputs.at(0));
+  View w = value(cv.inputs.at(1));
+  if (x.is_splat) x = materialize_copy(x, at, "materialise conv input");
+  if (w.is_splat) w = materialize_copy(w, at, "materialise conv weight");
+  if (x.shape.size() != 4 || w.shape.size() != 4) fail(PFC_ERR_GRAPH, "Conv2d expects 4D input and weight");
+  // attributes stride/padding/dilation (vector<int64_t>), groups (int64_t): conv.cpp:114-117
+  auto st = cv.attr_ints("stride", {1, 1}), pd = cv.attr_ints("padding", {0, 0}), dl = cv.attr_ints("dilation", {1, 1});
+  int64_t groups = cv.attr_int("groups", 1);
+  if (groups != 1) fail(PFC_ERR_UNSUPPORTED, "grouped CONV2D is not supported");
+  int64_t Nimg = x.shape[0], Cin = x.shape[1], H = x.shape[2], W = x.shape[3];
+  int64_t O = w.shape[0], KH = w.shape[2], KW = w.shape[3];
+  if (w.shape[1] != Cin) fail(PFC_ERR_GRAPH, "Input channels mismatch");
+  int64_t OH = (H + 2 * pd[0] - dl[0] * (KH - 1) - 1) / st[0] + 1;  // conv.cpp:75-78
+  int64_t OW = (W + 2 * pd[1] - dl[1] * (KW - 1) - 1) / st[1] + 1;
+  if (cv.shape != std::vector<int64_t>{Nimg, O, OH, OW}) fail(PFC_ERR_GRAPH, "CONV2D output shape mismatch");
+  int prec = in_.precision;
+  int64_t K = Cin * KH * KW;
+  int64_t kpad = round_up(K, prec == PFC_PRECISION_BF16 ? 64 : 32);
+  size_t esz = prec == PFC_PRECISION_BF16 ? 2 : 4;
+  int64_t M = Nimg * OH * OW;
+  Step si;
+  si.kind = StepKind::IM2COL;
+  si.label = "im2col " + shape_str(x.shape);
+  Im2colArgs& I = si.im2col;
+  I.x = x;
+  I.kh = KH; I.kw = KW; I.sh = st[0]; I.sw = st[1]; I.ph = pd[0]; I.pw = pd[1]; I.dh = dl[0]; I.dw = dl[1];
+  I.oh = OH; I.ow = OW; I.kpad = kpad; I.precision = prec;
+  I.out_hi = new_buffer((size_t)M * kpad * esz);
+  I.out_lo = prec == PFC_PRECISION_BF16 ? -1 : new_buffer((size_t)M * kpad * esz);
+  // weight [O, C, KH, KW] -> [O, K]
+  View wv;
+  if (!reshape_view(w, {O, K}, &wv)) wv = materialize_copy(w, at, "contiguous weight"), reshape_view(wv, {O, K}, &wv);
+  Step sb;
+  sb.kind = StepKind::SPLIT;
+  sb.label = "prepare conv weight";
+  sb.split.src = wv;
+  sb.split.precision = prec;
+  sb.split.rows = O;
+  sb.split.cols = K;
+  sb.split.kpad = kpad;
+  sb.split.out_hi = new_buffer((size_t)O * kpad * esz);
+  sb.split.out_lo = prec == PFC_PRECISION_BF16 ? -1 : new_buffer((size_t)O * kpad * esz);
+  // output NHWC: logical [N,O,OH,OW], strides (OH*OW*O, 1, OW*O, O)
+  View c;
+  c.shape = {Nimg, O, OH, OW};
+  c.strides = {OH * OW * O, 1, OW * O, O};
+  c.dtype = DType::F32;
+  c.buf = new_buffer((size_t)M * O * 4);
+  Step sg;
+  sg.kind = StepKind::GEMM;
+  sg.label = "conv gemm [" + std::to_string(M) + "x" + std::to_string(O) + "x" + std::to_string(K) + "]";
+  GemmArgs& G = sg.gemm;
+  G.precision = prec;
+  G.a_hi = I.out_hi; G.a_lo = I.out_lo; G.b_hi = sb.split.out_hi; G.b_lo = sb.split.out_lo;
+  G.batch = 1; G.M = M; G.N = O; G.K = K; G.kpad = kpad;
+  G.c = c; G.c_sm = O; G.c_sn = 1; G.c_sb = 0;
+  G.act = ch.act;
+  if (ch.has_bias && !ch.has_bn) {
+    View bv = value(ch.bias);
+    int64_t sn = 0;
+    for (size_t d = 0; d < bv.shape.size(); ++d)
+      if (bv.shape[d] != 1) sn = bv.strides[d];
+    if (!bv.is_splat && sn != 1 && O > 1) bv = materialize_copy(bv, at, "contiguous bias");
+    G.bias = bv;
+    G.has_bias = true;
+  }
+  if (ch.has_bn) {
+    const Node& bn = N(ch.bn);
+    Step sf;
+    sf.kind = StepKind::BN_FOLD;
+    sf.label = "fold batch_norm";
+    BnFoldArgs& F = sf.bnfold;
+    F.channels = O;
+    F.eps = (float)bn.attr_float("eps", 1e-5);
+    bool affine = bn.attr_bool("affine", bn.inputs.size() == 5);
+    size_t k = 1;
+    if (affine) {
+      F.gamma = value(bn.inputs[k++]);
+      F.beta = value(bn.inputs[k++]);
+      F.has_gamma = F.has_beta = true;
+    }
+    if (k + 2 > bn.inputs.size()) fail(PFC_ERR_UNSUPPORTED, "BATCH_NORM without running statistics");
+    F.mean = value(bn.inputs[k++]);
+    F.var = value(bn.inputs[k++]);
+    if (ch.has_bias) {
+      F.bias = value(ch.bias);
+      F.has_bias = true;
+    }
+    F.out_scale = new_buffer((size_t)O * 4);
+    F.out_shift = new_buffer((size_t)O * 4);
+    G.scale_buf = F.out_scale;
+    G.shift_buf = F.out_shift;
+    add_step(at, sf);
+  }
+  add_step(at, si);
+  add_step(at, sb);
+  add_step(at, sg);
+  val_[ch.result] = c;
+}
+
+void Compiler::lower_chain(int ci) {
+  const GemmChain& ch = chains_[ci];
+  int at = pos_[ch.result];
+  if (cls_[ch.mm] == Cls::CONV) lower_conv(ch, at);
+  else lower_matmul(ch, at);
+}
+
+void Compiler::lower_pool(uint64_t id) {
+  const Node& n = N(id);
+  View x = value(n.inputs.at(0));
+  if (x.is_splat) x = materialize_copy(x, pos_[id], "materialise pool input");
+  if (x.shape.size() != 4) fail(PFC_ERR_GRAPH, "pooling expects 4D input [N, C, H, W]");
+  Step s;
+  s.kind = StepKind::POOL;
+  PoolArgs& p = s.pool;
+  p.x = x;
+  if (n.op == Op::ADAPTIVE_AVG_POOL2D) {
+    // attribute output_size (vector<int64_t>), pooling.cpp:163-164
+    p.mode = 2;
+    s.label = "adaptive_avg_pool2d";
+  } else {
+    // attributes kernel_size/stride/padding (vector<int64_t>), pooling.cpp:57-59
+    auto ks = n.attr_ints("kernel_size"), st = n.attr_ints("stride", ks), pd = n.attr_ints("padding", {0, 0});
+    p.mode = n.op == Op::MAX_POOL2D ? 0 : 1;
+    p.kh = ks[0]; p.kw = ks[1]; p.sh = st[0]; p.sw = st[1]; p.ph = pd[0]; p.pw = pd[1];
+    int64_t oh = (x.shape[2] + 2 * p.ph - p.kh) / p.sh + 1, ow = (x.shape[3] + 2 * p.pw - p.kw) / p.sw + 1;
+    if (n.shape != std::vector<int64_t>{x.shape[0], x.shape[1], oh, ow}) fail(PFC_ERR_GRAPH, "pool output shape mismatch");
+    s.label = n.op == Op::MAX_POOL2D ? "max_pool2d" : "avg_pool2d";
+  }
+  p.y = dense_like(n.shape, &x);
+  val_[id] = p.y;
+  add_step(pos_[id], s);
+}
+
+void Compiler::lower_concat(uint64_t id) {
+  const Node& n = N(id);
+  View out = dense(n.shape, n.dtype);
+  int nd = (int)n.shape.size();
+  int d = (int)n.attr_int("dim", 0);
+  bool stack = n.op == Op::STACK;
+  if (d < 0) d += nd;
+  if (d < 0 || d >= nd) fail(PFC_ERR_GRAPH, "concat: dimension out of range");
+  int64_t off = 0;
+  for (uint64_t in : n.inputs) {
+    View src = value(in);
+    View dst = out;
+    int64_t len = stack ? 1 : src.shape[d];
+    dst.shape[d] = len;
+    dst.offset = out.offset + off * out.strides[d];
+    if (stack) {
+      View s2;
+      std::vector<int64_t> sh = src.shape;
+      sh.insert(sh.begin() + d, 1);
+      if (src.is_splat) { s2 = src; s2.shape = sh; s2.strides.assign(sh.size(), 0); }
+      else { s2 = src; s2.shape = sh; s2.strides.insert(s2.strides.begin() + d, 0); }
+      src = s2;
+    }
+    EwSpec s;
+    s.space = dst.shape;
+    s.loads.push_back(broadcast_to(src, s.space));
+    EwInstr ld;
+    ld.kind = EwKind::LOAD;
+    ld.load = 0;
+    s.instrs.push_back(ld);
+    View dstv = dst;
+    dstv.offset = 0;  // pointer argument carries the offset
+    s.stores.push_back({0, dstv});
+    std::string name = kname("concat");
+    int grid, block;
+    std::string code = gen_ew(s, name, in_.num_sms, &grid, &block);
+    std::vector<std::pair<int, int64_t>> ptrs;
+    ptrs.push_back({src.is_splat ? -1 : src.buf, src.offset * (int64_t)dtype_size(src.dtype)});
+    ptrs.push_back({out.buf, dst.offset * (int64_t)dtype_size(out.dtype)});
+    ptrs.push_back({P_->scalar_buf, 0});
+    emit_jit(pos_[id], "concat part", name, code, grid, block, ptrs);
+    off += len;
+  }
+  val_[id] = out;
+}
+
+void Compiler::lower() {
+  // Units: an elementwise region (with its attached row ops), an epilogue
+  // chain, or a single node.  Regions are convex and chains only absorb
+  // operands that do not depend on them, so the unit graph is acyclic.
+  std::unordered_map<uint64_t, int> unit_of;
+  std::vector<int> kind;  // 0 node, 1 region, 2 chain
+  std::vector<int64_t> ref;
+  std::unordered_map<int, int> unit_of_region, unit_of_chain;
+  for (uint64_t id : order_) {
+    int u;
+    auto ch = chain_of_.find(id);
+    auto rr = row_region_.find(id);
+    auto rg = region_of_.find(id);
+    if (ch != chain_of_.end()) {
+      auto it = unit_of_chain.find(ch->second);
+      if (it == unit_of_chain.end()) {
+        kind.push_back(2); ref.push_back(ch->second);
+        it = unit_of_chain.emplace(ch->second, (int)kind.size() - 1).first;
+      }
+      u = it->second;
+    } else if (rg != region_of_.end() || rr != row_region_.end()) {
+      int r = rg != region_of_.end() ? rg->second : rr->second;
+      auto it = unit_of_region.find(r);
+      if (it == unit_of_region.end()) {
+        kind.push_back(1); ref.push_back(r);
+        it = unit_of_region.emplace(r, (int)kind.size() - 1).first;
+      }
+      u = it->second;
+    } else {
+      kind.push_back(0); ref.push_back((int64_t)id);
+      u = (int)kind.size() - 1;
+    }
+    unit_of[id] = u;
+  }
+  int nu = (int)kind.size();
+  std::vector<std::set<int>> succ(nu);
+  std::vector<int> indeg(nu, 0), prio(nu, INT32_MAX);
+  for (uint64_t id : order_) {
+    int u = unit_of[id];
+    prio[u] = std::min(prio[u], pos_[id]);
+    for (uint64_t in : N(id).inputs) {
+      int v = unit_of.at(in);
+      if (v != u && succ[v].insert(u).second) indeg[u]++;
+    }
+  }
+  std::set<std::pair<int, int>> ready;
+  for (int u = 0; u < nu; ++u)
+    if (!indeg[u]) ready.insert({prio[u], u});
+  if (std::getenv("PFB_DEBUG_UNITS"))
+    for (uint64_t id : order_) std::fprintf(stderr, "node %llu -> unit %d (indeg %d)\n", (unsigned long long)id, unit_of[id], indeg[unit_of[id]]);
+  int step_pos = 0;
+  int lowered = 0;
+  while (!ready.empty()) {
+    int u = ready.begin()->second;
+    ready.erase(ready.begin());
+    ++lowered;
+    cur_pos_ = step_pos++;
+    if (std::getenv("PFB_DEBUG_UNITS"))
+      std::fprintf(stderr, "unit %d kind %d ref %lld prio %d\n", u, kind[u], (long long)ref[u], prio[u]);
+    if (kind[u] == 1) {
+      lower_region((int)ref[u]);
+    } else if (kind[u] == 2) {
+      lower_chain((int)ref[u]);
+    } else {
+      uint64_t id = (uint64_t)ref[u];
+      switch (cls_[id]) {
+        case Cls::LEAF: lower_leaf(id); break;
+        case Cls::VIEW: lower_view(id); break;
+        case Cls::ROW: lower_row_alone(id); break;
+        case Cls::POOL: lower_pool(id); break;
+        case Cls::CONCAT: lower_concat(id); break;
+        default: fail(PFC_ERR_INTERNAL, "unlowered node class");
+      }
+    }
+    for (int v : succ[u])
+      if (--indeg[v] == 0) ready.insert({prio[v], v});
+  }
+  if (lowered != nu) fail(PFC_ERR_INTERNAL, "fusion produced a cyclic unit graph");
+  cur_pos_ = step_pos;
+}
+
+void Compiler::finish() {
+  // outputs: dense contiguous views (copies run after everything else)
+  for (uint64_t o : in_.outputs) {
+    View v = value(o);
+    const Node& n = N(o);
+    bool dense_ok = !v.is_splat && v.is_contiguous() && v.shape == n.shape && v.offset == 0;
+    if (!dense_ok) {
+      View c = materialize_copy(v, cur_pos_, "materialise output %" + std::to_string(o));
+      c.shape = n.shape;
+      c.strides = View::dense_strides(n.shape);
+      v = c;
+    }
+    P_->output_views.push_back(v);
+  }
+  P_->buffers[P_->scalar_buf].bytes = std::max<size_t>(4, P_->scalars.size() * 4);
+  // order steps by position (stable keeps emission order within a position)
+  std::stable_sort(steps_.begin(), steps_.end(), [](const auto& a, const auto& b) { return a.first < b.first; });
+  for (auto& [pos, s] : steps_) P_->steps.push_back(std::move(s));
+  // liveness
+  auto use = [&](int buf, int step) {
+    if (buf < 0) return;
+    Buffer& b = P_->buffers[buf];
+    if (b.first_use < 0 || step < b.first_use) b.first_use = step;
+    b.last_use = std::max(b.last_use, step);
+  };
+  for (int i = 0; i < (int)P_->steps.size(); ++i) {
+    const Step& s = P_->steps[i];
+    switch (s.kind) {
+      case StepKind::JIT: for (auto& p : s.jit.ptrs) use(p.first, i); break;
+      case StepKind::SPLIT: use(s.split.src.buf, i); use(s.split.out_hi, i); use(s.split.out_lo, i); break;
+      case StepKind::IM2COL: use(s.im2col.x.buf, i); use(s.im2col.out_hi, i); use(s.im2col.out_lo, i); break;
+      case StepKind::GEMM: {
+        const GemmArgs& G = s.gemm;
+        use(G.a_hi, i); use(G.a_lo, i); use(G.b_hi, i); use(G.b_lo, i); use(G.c.buf, i);
+        if (G.has_bias) use(G.bias.buf, i);
+        if (G.has_residual) use(G.residual.buf, i);
+        use(G.scale_buf, i); use(G.shift_buf, i);
+        break;
+      }
+      case StepKind::POOL: use(s.pool.x.buf, i); use(s.pool.y.buf, i); break;
+      case StepKind::BN_FOLD: {
+        const BnFoldArgs& F = s.bnfold;
+        if (F.has_gamma) use(F.gamma.buf, i);
+        if (F.has_beta) use(F.beta.buf, i);
+        use(F.mean.buf, i); use(F.var.buf, i);
+        if (F.has_bias) use(F.bias.buf, i);
+        use(F.out_scale, i); use(F.out_shift, i);
+        break;
+      }
+      case StepKind::MEMSET: use(s.memset_buf, i); break;
+    }
+  }
+  int nsteps = (int)P_->steps.size();
+  for (const View& v : P_->output_views) {
+    Buffer& b = P_->buffers[v.buf];
+    b.pinned_live = true;
+    if (b.first_use < 0) b.first_use = 0;
+    b.last_use = nsteps;
+  }
+  P_->buffers[P_->scalar_buf].pinned_live = true;
+  P_->buffers[P_->scalar_buf].first_use = 0;
+  P_->buffers[P_->scalar_buf].last_use = nsteps;
+  // arena: greedy first-fit by size over liveness intervals, 256-byte aligned
+  struct Iv { int b; int s, e; size_t sz; };
+  std::vector<Iv> ivs;
+  for (int i = 0; i < (int)P_->buffers.size(); ++i) {
+    Buffer& b = P_->buffers[i];
+    if (b.kind != BufKind::ARENA && b.kind != BufKind::CONST) continue;
+    if (b.kind == BufKind::CONST) { b.first_use = 0; b.last_use = nsteps; }
+    if (b.first_use < 0) continue;  // unused
+    ivs.push_back({i, b.first_use, b.last_use, (size_t)round_up((int64_t)b.bytes, 256)});
+  }
+  std::sort(ivs.begin(), ivs.end(), [](const Iv& a, const Iv& b) { return a.sz > b.sz; });
+  std::vector<std::pair<size_t, Iv>> placed;
+  size_t arena = 0;
+  for (const Iv& iv : ivs) {
+    // collect conflicting placed ranges
+    std::vector<std::pair<size_t, size_t>> busy;
+    for (auto& [off, p] : placed)
+      if (!(p.e < iv.s || iv.e < p.s)) busy.push_back({off, off + p.sz});
+    std::sort(busy.begin(), busy.end());
+    size_t off = 0;
+    for (auto& [b0, b1] : busy) {
+      if (off + iv.sz <= b0) break;
+      off = std::max(off, b1);
+    }
+    P_->buffers[iv.b].arena_offset = (int64_t)off;
+    placed.push_back({off, iv});
+    arena = std::max(arena, off + iv.sz);
+  }
+  P_->arena_bytes = arena;
+  // description
+  std::ostringstream d;
+  d << "plan: " << P_->steps.size() << " steps, arena " << arena << " bytes, " << P_->scalars.size()
+    << " splat constants\n";
+  for (size_t i = 0; i < P_->steps.size(); ++i) d << "  [" << i << "] " << P_->steps[i].label << "\n";
+  P_->description = d.str();
+}
+
+std::unique_ptr<Plan> Compiler::run() {
+  P_ = std::make_unique<Plan>();
+  P_->precision = in_.precision;
+  P_->outputs = in_.outputs;
+  order_ = topo_order(g_, in_.outputs);
+  for (size_t i = 0; i < order_.size(); ++i) pos_[order_[i]] = (int)i;
+  for (uint64_t id : order_)
+    for (uint64_t in : N(id).inputs) users_[in].push_back(id);
+  for (uint64_t o : in_.outputs) is_out_.insert(o);
+  P_->scalar_buf = new_buffer(4 * 64);
+  classify();
+  absorb_epilogues();
+  build_regions();
+  attach_row_ops();
+  lower();
+  finish();
+  return std::move(P_);
+}
+
+}  // namespace
+
+std::unique_ptr<Plan> compile_plan(const CompileInput& in, SourceMap* sources) {
+  Compiler c(in, sources);
+  return c.run();
+}
+
+}  // namespace pfb

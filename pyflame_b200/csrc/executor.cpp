@@ -1,0 +1,608 @@
+#include "executor.hpp"
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cstring>
+#include <thread>
+
+#include "jit.hpp"
+#include "kernels/kernels.hpp"
+
+namespace pfb {
+
+namespace {
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) PFB_CUDA(cudaSetDevice(dev));
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+double ms_since(std::chrono::steady_clock::time_point t0) {
+  return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+}
+
+// True when every element equals the first (bitwise).  Large buffers are
+// scanned by several threads; a mismatch stops all of them.
+bool all_equal_f32(const float* p, int64_t n, float* value) {
+  uint32_t first;
+  std::memcpy(&first, p, 4);
+  *value = p[0];
+  const uint32_t* u = (const uint32_t*)p;
+  auto scan = [&](int64_t b, int64_t e, std::atomic<bool>* stop) {
+    for (int64_t i = b; i < e; i += 4096) {
+      if (stop->load(std::memory_order_relaxed)) return;
+      int64_t end = std::min(e, i + 4096);
+      for (int64_t j = i; j < end; ++j)
+        if (u[j] != first) {
+          stop->store(true);
+          return;
+        }
+    }
+  };
+  std::atomic<bool> stop{false};
+  if (n < (1 << 22)) {
+    scan(0, n, &stop);
+  } else {
+    int nt = (int)std::min<unsigned>(8, std::max(1u, std::thread::hardware_concurrency()));
+    std::vector<std::thread> th;
+    int64_t chunk = (n + nt - 1) / nt;
+    for (int t = 0; t < nt; ++t) {
+      int64_t b = t * chunk, e = std::min(n, b + chunk);
+      if (b < e) th.emplace_back(scan, b, e, &stop);
+    }
+    for (auto& t : th) t.join();
+  }
+  return !stop.load();
+}
+
+inline uint64_t mix(uint64_t h, uint64_t v) {
+  h ^= v + 0x9e3779b97f4a7c15ULL + (h << 6) + (h >> 2);
+  return h * 0xff51afd7ed558ccdULL;
+}
+
+}  // namespace
+
+CudaExecutor::CudaExecutor(const pfc_executor_config& cfg) : cfg_(cfg) {
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    fail(PFC_ERR_NO_DEVICE, "CUDA backend requested but no CUDA device is available");
+  }
+  if (cfg.device_id < 0 || cfg.device_id >= n)
+    fail(PFC_ERR_INVALID_ARGUMENT, "device_id " + std::to_string(cfg.device_id) + " out of range (" +
+                                       std::to_string(n) + " devices)");
+  DeviceGuard dg(cfg.device_id);
+  cudaDeviceProp prop;
+  PFB_CUDA(cudaGetDeviceProperties(&prop, cfg.device_id));
+  if (prop.major < 10)
+    fail(PFC_ERR_NO_DEVICE, std::string("device ") + prop.name + " is not sm_100 class (compute capability " +
+                                std::to_string(prop.major) + "." + std::to_string(prop.minor) + ")");
+  num_sms_ = prop.multiProcessorCount;
+  PFB_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+  CudaMemoryPool::Config pc;
+  pc.device = cfg.device_id;
+  pc.release_threshold = (cfg.workspace_size_mb ? cfg.workspace_size_mb : 256) << 20;
+  pc.fail_after_n = cfg.fail_after_n_allocations;
+  pool_ = std::make_unique<CudaMemoryPool>(pc);
+  PFB_CUDA(cudaMalloc((void**)&err_dev_, 256));
+  PFB_CUDA(cudaMemset(err_dev_, 0, 256));
+}
+
+CudaExecutor::~CudaExecutor() {
+  DeviceGuard dg(cfg_.device_id);
+  if (stream_) cudaStreamSynchronize(stream_);
+  release_constants();
+  if (err_dev_) cudaFree(err_dev_);
+  pool_.reset();
+  if (stream_) cudaStreamDestroy(stream_);
+}
+
+void CudaExecutor::release_constants() {
+  if (stream_) cudaStreamSynchronize(stream_);
+  for (auto& [k, pe] : plans_) {
+    if (pe.gexec) cudaGraphExecDestroy(pe.gexec);
+    if (pe.arena) pool_->deallocate(pe.arena, stream_);
+  }
+  plans_.clear();
+  for (auto& [k, r] : resident_) {
+    pool_->deallocate(r.dev, stream_);
+    pool_->add_resident(-(long long)r.bytes);
+  }
+  resident_.clear();
+  resident_splat_.clear();
+  if (stream_) cudaStreamSynchronize(stream_);
+}
+
+pfc_device_info CudaExecutor::device_info() const {
+  pfc_device_info info;
+  std::memset(&info, 0, sizeof info);
+  pfc_cuda_get_device_info(cfg_.device_id, &info);
+  return info;
+}
+
+std::unordered_map<uint64_t, float> detect_splats(const Graph& g, const std::vector<uint64_t>& order,
+                                                  const std::unordered_set<uint64_t>& bindings) {
+  std::unordered_map<uint64_t, float> out;
+  for (uint64_t id : order) {
+    const Node& n = g.at(id);
+    if (n.type == NodeType::OPERATION || bindings.count(id)) continue;
+    if (!n.has_data()) {
+      if (n.dtype != DType::F32)
+        fail(PFC_ERR_UNSUPPORTED, "node " + std::to_string(id) + " has no data and is not float32");
+      out[id] = 0.f;
+      continue;
+    }
+    if (n.dtype != DType::F32 || n.numel() == 0) continue;
+    float v = 0.f;
+    if (all_equal_f32((const float*)n.data, n.numel(), &v)) out[id] = v;
+  }
+  return out;
+}
+
+std::unordered_map<uint64_t, float> CudaExecutor::detect_splats(const Graph& g, const std::vector<uint64_t>& order,
+                                                                const std::unordered_set<uint64_t>& bindings) {
+  std::unordered_map<uint64_t, float> out;
+  for (uint64_t id : order) {
+    const Node& n = g.at(id);
+    if (n.type == NodeType::OPERATION || bindings.count(id)) continue;
+    if (!n.has_data()) {
+      // data-less leaf: zero-filled like the ROCm executor (rocm_executor.cpp:99-102)
+      if (n.dtype != DType::F32)
+        fail(PFC_ERR_UNSUPPORTED, "node " + std::to_string(id) + " has no data and is not float32");
+      out[id] = 0.f;
+      continue;
+    }
+    if (n.data_bytes != n.size_bytes())
+      fail(PFC_ERR_INVALID_ARGUMENT, "constant payload of node " + std::to_string(id) + " has " +
+                                         std::to_string(n.data_bytes) + " bytes, expected " +
+                                         std::to_string(n.size_bytes()));
+    if (n.dtype != DType::F32 || n.numel() == 0) continue;
+    float v = 0.f;
+    bool splat;
+    if (n.data_flags & PFC_CONST_RESIDENT) {
+      auto key = std::make_pair(n.data_key, n.data_bytes);
+      auto it = resident_splat_.find(key);
+      if (it == resident_splat_.end()) {
+        SplatInfo si;
+        si.splat = all_equal_f32((const float*)n.data, n.numel(), &si.value);
+        it = resident_splat_.emplace(key, si).first;
+      }
+      splat = it->second.splat;
+      v = it->second.value;
+    } else {
+      splat = all_equal_f32((const float*)n.data, n.numel(), &v);
+    }
+    if (splat) out[id] = v;
+  }
+  return out;
+}
+
+CudaExecutor::PlanEntry& CudaExecutor::prepare(Graph& g, const std::vector<uint64_t>& outs,
+                                               const std::unordered_set<uint64_t>& bindings, double* compile_ms) {
+  auto t0 = std::chrono::steady_clock::now();
+  validate_graph(g);
+  std::vector<uint64_t> order = topo_order(g, outs);
+  auto splats = detect_splats(g, order, bindings);
+  uint64_t key = structural_hash(g, outs);
+  key = mix(key, (uint64_t)cfg_.precision);
+  std::vector<uint64_t> b(bindings.begin(), bindings.end());
+  std::sort(b.begin(), b.end());
+  for (uint64_t x : b) key = mix(key, x ^ 0xb1b1);
+  std::vector<uint64_t> sp;
+  for (auto& [id, v] : splats) sp.push_back(id);
+  std::sort(sp.begin(), sp.end());
+  for (uint64_t x : sp) key = mix(key, x ^ 0x5a5a);
+  auto it = plans_.find(key);
+  if (it == plans_.end()) {
+    CompileInput ci;
+    ci.g = &g;
+    ci.outputs = outs;
+    ci.splats = splats;
+    ci.bindings = bindings;
+    ci.precision = cfg_.precision;
+    ci.num_sms = num_sms_;
+    SourceMap sources;
+    PlanEntry pe;
+    pe.plan = compile_plan(ci, &sources);
+    pe.plan->key = key;
+    pe.kernels.resize(pe.plan->steps.size(), nullptr);
+    for (size_t i = 0; i < pe.plan->steps.size(); ++i) {
+      const Step& s = pe.plan->steps[i];
+      if (s.kind != StepKind::JIT) continue;
+      const auto& src = sources.at(s.jit.module_key);
+      pe.kernels[i] = global_jit().get(s.jit.module_key, src.first, s.jit.kernel);
+    }
+    if (pe.plan->arena_bytes) pe.arena = pool_->allocate(pe.plan->arena_bytes, stream_);
+    it = plans_.emplace(key, std::move(pe)).first;
+  } else {
+    // refresh the splat values seen by this call (the structure is unchanged)
+    for (auto& sc : it->second.plan->scalars) sc.value = splats.at(sc.node);
+  }
+  if (compile_ms) *compile_ms = ms_since(t0);
+  return it->second;
+}
+
+std::vector<void*> CudaExecutor::resolve(PlanEntry& pe, const Graph& g,
+                                         const std::unordered_map<uint64_t, const void*>& bind, cudaStream_t s,
+                                         std::vector<std::pair<void*, const Node*>>* uploads) {
+  const Plan& P = *pe.plan;
+  std::vector<void*> ptrs(P.buffers.size(), nullptr);
+  for (size_t i = 0; i < P.buffers.size(); ++i) {
+    const Buffer& b = P.buffers[i];
+    switch (b.kind) {
+      case BufKind::ARENA:
+        if (b.arena_offset >= 0) ptrs[i] = (char*)pe.arena + b.arena_offset;
+        break;
+      case BufKind::BINDING:
+        ptrs[i] = const_cast<void*>(bind.at(b.node));
+        break;
+      case BufKind::CONST: {
+        const Node& n = g.at(b.node);
+        if (n.data_flags & PFC_CONST_RESIDENT) {
+          auto key = std::make_pair(n.data_key, n.data_bytes);
+          auto it = resident_.find(key);
+          if (it == resident_.end()) {
+            Resident r;
+            r.bytes = n.data_bytes;
+            r.dev = pool_->allocate(n.data_bytes, s);
+            PFB_CUDA(cudaMemcpyAsync(r.dev, n.data, n.data_bytes, cudaMemcpyHostToDevice, s));
+            pool_->add_resident((long long)r.bytes);
+            it = resident_.emplace(key, r).first;
+          }
+          ptrs[i] = it->second.dev;
+        } else {
+          ptrs[i] = (char*)pe.arena + b.arena_offset;
+          uploads->push_back({ptrs[i], &n});
+        }
+        break;
+      }
+    }
+  }
+  return ptrs;
+}
+
+void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>& ptrs, cudaStream_t s) {
+  const Plan& P = *pe.plan;
+  const Step& st = P.steps[i];
+  auto bufp = [&](int buf, int64_t byte_off) -> void* {
+    if (buf < 0) return nullptr;
+    return (char*)ptrs[buf] + byte_off;
+  };
+  auto viewp = [&](const View& v) -> const float* {
+    if (v.is_splat) return (const float*)bufp(P.scalar_buf, (int64_t)v.splat_slot * 4);
+    return (const float*)bufp(v.buf, v.offset * (int64_t)dtype_size(v.dtype));
+  };
+  switch (st.kind) {
+    case StepKind::JIT: {
+      struct { void* p[48]; } args;
+      std::memset(&args, 0, sizeof args);
+      if (st.jit.ptrs.size() > 48) fail(PFC_ERR_UNSUPPORTED, "fused kernel with more than 48 operands");
+      for (size_t k = 0; k < st.jit.ptrs.size(); ++k) args.p[k] = bufp(st.jit.ptrs[k].first, st.jit.ptrs[k].second);
+      void* kargs[] = {&args};
+      PFB_CUDA(cudaLaunchKernel((const void*)pe.kernels[i], dim3(st.jit.grid), dim3(st.jit.block), kargs,
+                                st.jit.smem, s));
+      break;
+    }
+    case StepKind::SPLIT: {
+      const SplitArgs& a = st.split;
+      PrepLaunch L;
+      L.src = viewp(a.src);
+      L.rank = (int)a.src.shape.size();
+      if (L.rank > 6) fail(PFC_ERR_UNSUPPORTED, "matmul operand of rank > 6");
+      for (int d = 0; d < L.rank; ++d) {
+        L.shape[d] = a.src.shape[d];
+        L.stride[d] = a.src.is_splat ? 0 : a.src.strides[d];
+      }
+      L.precision = a.precision;
+      L.hi = bufp(a.out_hi, 0);
+      L.lo = (float*)bufp(a.out_lo, 0);
+      L.kpad = a.kpad;
+      launch_prepare(L, s);
+      break;
+    }
+    case StepKind::IM2COL: {
+      const Im2colArgs& a = st.im2col;
+      Im2colLaunch L;
+      L.x = viewp(a.x);
+      L.n = a.x.shape[0]; L.c = a.x.shape[1]; L.h = a.x.shape[2]; L.w = a.x.shape[3];
+      L.sn = a.x.strides[0]; L.sc = a.x.strides[1]; L.sh = a.x.strides[2]; L.sw = a.x.strides[3];
+      L.kh = a.kh; L.kw = a.kw; L.stride_h = a.sh; L.stride_w = a.sw; L.pad_h = a.ph; L.pad_w = a.pw;
+      L.dil_h = a.dh; L.dil_w = a.dw; L.oh = a.oh; L.ow = a.ow; L.kpad = a.kpad; L.precision = a.precision;
+      L.hi = bufp(a.out_hi, 0);
+      L.lo = (float*)bufp(a.out_lo, 0);
+      launch_im2col(L, s);
+      break;
+    }
+    case StepKind::GEMM: {
+      const GemmArgs& a = st.gemm;
+      GemmLaunch L;
+      L.precision = a.precision;
+      L.a_hi = bufp(a.a_hi, 0);
+      L.a_lo = bufp(a.a_lo, 0);
+      L.b_hi = bufp(a.b_hi, 0);
+      L.b_lo = bufp(a.b_lo, 0);
+      L.a_sb = a.a_sb; L.b_sb = a.b_sb; L.batch = a.batch; L.M = a.M; L.N = a.N; L.K = a.K; L.kpad = a.kpad;
+      L.c = (float*)viewp(a.c);
+      L.c_sb = a.c_sb; L.c_sm = a.c_sm; L.c_sn = a.c_sn;
+      L.alpha = a.alpha;
+      L.alpha_ptr = a.alpha_slot >= 0 ? (const float*)bufp(P.scalar_buf, (int64_t)a.alpha_slot * 4) : nullptr;
+      if (a.has_bias) {
+        if (a.bias.is_splat) L.bias_scalar = viewp(a.bias);
+        else L.bias = viewp(a.bias);
+      }
+      L.scale = (const float*)bufp(a.scale_buf, 0);
+      L.shift = (const float*)bufp(a.shift_buf, 0);
+      L.act = a.act;
+      if (a.has_residual) {
+        L.residual = viewp(a.residual);
+        L.r_sb = a.r_sb; L.r_sm = a.r_sm; L.r_sn = a.r_sn;
+      }
+      L.err = err_dev_;
+      launch_gemm(L, s);
+      break;
+    }
+    case StepKind::POOL: {
+      const PoolArgs& a = st.pool;
+      PoolLaunch L;
+      L.x = viewp(a.x);
+      L.y = (float*)viewp(a.y);
+      L.mode = a.mode;
+      L.n = a.x.shape[0]; L.c = a.x.shape[1]; L.h = a.x.shape[2]; L.w = a.x.shape[3];
+      L.sn = a.x.strides[0]; L.sc = a.x.strides[1]; L.sh = a.x.strides[2]; L.sw = a.x.strides[3];
+      L.kh = a.kh; L.kw = a.kw; L.stride_h = a.sh; L.stride_w = a.sw; L.pad_h = a.ph; L.pad_w = a.pw;
+      L.oh = a.y.shape[2]; L.ow = a.y.shape[3];
+      L.osn = a.y.strides[0]; L.osc = a.y.strides[1]; L.osh = a.y.strides[2]; L.osw = a.y.strides[3];
+      launch_pool(L, s);
+      break;
+    }
+    case StepKind::BN_FOLD: {
+      const BnFoldArgs& a = st.bnfold;
+      BnFoldLaunch L;
+      auto param = [&](const View& v, bool has, const float** p, int64_t* stride) {
+        if (!has) return;
+        *p = viewp(v);
+        *stride = v.is_splat ? 0 : (v.strides.empty() ? 0 : v.strides.back());
+        if (!v.is_splat) {
+          for (size_t d = 0; d < v.shape.size(); ++d)
+            if (v.shape[d] != 1) *stride = v.strides[d];
+        }
+      };
+      param(a.gamma, a.has_gamma, &L.gamma, &L.gs);
+      param(a.beta, a.has_beta, &L.beta, &L.bs);
+      param(a.mean, true, &L.mean, &L.ms);
+      param(a.var, true, &L.var, &L.vs);
+      param(a.bias, a.has_bias, &L.bias, &L.cs);
+      L.eps = a.eps;
+      L.channels = a.channels;
+      L.scale = (float*)bufp(a.out_scale, 0);
+      L.shift = (float*)bufp(a.out_shift, 0);
+      launch_bn_fold(L, s);
+      break;
+    }
+    case StepKind::MEMSET:
+      PFB_CUDA(cudaMemsetAsync(bufp(st.memset_buf, 0), 0, P.buffers[st.memset_buf].bytes, s));
+      break;
+  }
+  if (cfg_.sync_after_launch) {
+    PFB_CUDA(cudaStreamSynchronize(s));
+    PFB_CUDA(cudaGetLastError());
+  }
+}
+
+static int launches_of(const Step& s) { return s.kind == StepKind::MEMSET ? 0 : 1; }
+
+int64_t CudaExecutor::run_steps(PlanEntry& pe, const std::vector<void*>& ptrs, cudaStream_t s) {
+  const Plan& P = *pe.plan;
+  int64_t launches = 0;
+  for (const Step& st : P.steps) launches += launches_of(st);
+  profile_.clear();
+  if (cfg_.enable_profiling) {
+    std::vector<cudaEvent_t> ev(P.steps.size() + 1);
+    for (auto& e : ev) PFB_CUDA(cudaEventCreate(&e));
+    PFB_CUDA(cudaEventRecord(ev[0], s));
+    for (size_t i = 0; i < P.steps.size(); ++i) {
+      launch_step(pe, i, ptrs, s);
+      PFB_CUDA(cudaEventRecord(ev[i + 1], s));
+    }
+    PFB_CUDA(cudaEventSynchronize(ev.back()));
+    for (size_t i = 0; i < P.steps.size(); ++i) {
+      float ms = 0;
+      cudaEventElapsedTime(&ms, ev[i], ev[i + 1]);
+      profile_.push_back({P.steps[i].label, (double)ms});
+    }
+    for (auto& e : ev) cudaEventDestroy(e);
+    return launches;
+  }
+  bool graph_ok = cfg_.use_cuda_graph && !cfg_.sync_after_launch;
+  if (graph_ok && pe.gexec && pe.gexec_ptrs == ptrs) {
+    PFB_CUDA(cudaGraphLaunch(pe.gexec, s));
+    ++pe.runs;
+    return launches;
+  }
+  if (graph_ok && pe.runs >= 1) {
+    // capture once the plan has run eagerly (kernel attributes are set)
+    if (pe.gexec) {
+      cudaGraphExecDestroy(pe.gexec);
+      pe.gexec = nullptr;
+    }
+    cudaGraph_t graph;
+    PFB_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    try {
+      for (size_t i = 0; i < P.steps.size(); ++i) launch_step(pe, i, ptrs, s);
+    } catch (...) {
+      cudaStreamEndCapture(s, &graph);
+      throw;
+    }
+    PFB_CUDA(cudaStreamEndCapture(s, &graph));
+    cudaError_t e = cudaGraphInstantiate(&pe.gexec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      pe.gexec = nullptr;
+      for (size_t i = 0; i < P.steps.size(); ++i) launch_step(pe, i, ptrs, s);
+    } else {
+      pe.gexec_ptrs = ptrs;
+      PFB_CUDA(cudaGraphLaunch(pe.gexec, s));
+    }
+    ++pe.runs;
+    return launches;
+  }
+  for (size_t i = 0; i < P.steps.size(); ++i) launch_step(pe, i, ptrs, s);
+  ++pe.runs;
+  return launches;
+}
+
+void CudaExecutor::check_device_error(cudaStream_t s) {
+  int h = 0;
+  PFB_CUDA(cudaMemcpyAsync(&h, err_dev_, 4, cudaMemcpyDeviceToHost, s));
+  PFB_CUDA(cudaStreamSynchronize(s));
+  if (h != 0) {
+    PFB_CUDA(cudaMemsetAsync(err_dev_, 0, 4, s));
+    PFB_CUDA(cudaStreamSynchronize(s));
+    fail(h, "a device-side bounded wait expired (tensor-core pipeline did not make progress)");
+  }
+}
+
+void CudaExecutor::execute(Graph& g, const std::vector<uint64_t>& outs, void* const* host_out,
+                           const size_t* out_bytes, pfc_execution_result* res) {
+  std::lock_guard<std::mutex> lock(mu_);
+  auto t0 = std::chrono::steady_clock::now();
+  DeviceGuard dg(cfg_.device_id);
+  for (size_t i = 0; i < outs.size(); ++i) {
+    const Node* n = g.find(outs[i]);
+    if (!n) fail(PFC_ERR_INVALID_ARGUMENT, "output id " + std::to_string(outs[i]) + " is not in the graph");
+    if (!host_out[i]) fail(PFC_ERR_INVALID_ARGUMENT, "null output buffer");
+    if (out_bytes[i] != n->size_bytes())
+      fail(PFC_ERR_INVALID_ARGUMENT, "output buffer for node " + std::to_string(outs[i]) + " has " +
+                                         std::to_string(out_bytes[i]) + " bytes, expected " +
+                                         std::to_string(n->size_bytes()));
+  }
+  double compile_ms = 0;
+  PlanEntry& pe = prepare(g, outs, {}, &compile_ms);
+  const Plan& P = *pe.plan;
+  cudaStream_t s = stream_;
+  cudaEvent_t e0, e1, e2, e3;
+  PFB_CUDA(cudaEventCreate(&e0));
+  PFB_CUDA(cudaEventCreate(&e1));
+  PFB_CUDA(cudaEventCreate(&e2));
+  PFB_CUDA(cudaEventCreate(&e3));
+  PFB_CUDA(cudaEventRecord(e0, s));
+  std::vector<std::pair<void*, const Node*>> uploads;
+  std::vector<void*> ptrs = resolve(pe, g, {}, s, &uploads);
+  for (auto& [dst, n] : uploads) PFB_CUDA(cudaMemcpyAsync(dst, n->data, n->data_bytes, cudaMemcpyHostToDevice, s));
+  {
+    // splat values live in a small device table; upload only when they change
+    std::vector<float> table(P.scalars.size());
+    for (size_t i = 0; i < P.scalars.size(); ++i) table[i] = P.scalars[i].value;
+    if (!table.empty() && (table != pe.table || pe.table_ptr != ptrs[P.scalar_buf])) {
+      PFB_CUDA(cudaMemcpyAsync(ptrs[P.scalar_buf], table.data(), table.size() * 4, cudaMemcpyHostToDevice, s));
+      pe.table = table;
+      pe.table_ptr = ptrs[P.scalar_buf];
+    }
+  }
+  PFB_CUDA(cudaEventRecord(e1, s));
+  int64_t launches = run_steps(pe, ptrs, s);
+  PFB_CUDA(cudaEventRecord(e2, s));
+  for (size_t i = 0; i < outs.size(); ++i) {
+    const View& v = P.output_views[i];
+    const void* src = (const char*)ptrs[v.buf] + v.offset * (int64_t)dtype_size(v.dtype);
+    if (out_bytes[i]) PFB_CUDA(cudaMemcpyAsync(host_out[i], src, out_bytes[i], cudaMemcpyDeviceToHost, s));
+  }
+  PFB_CUDA(cudaEventRecord(e3, s));
+  cudaError_t se = cudaStreamSynchronize(s);
+  if (se != cudaSuccess) fail(PFC_ERR_CUDA, std::string("execution failed: ") + cudaGetErrorString(se));
+  check_device_error(s);
+  float up = 0, comp = 0, down = 0;
+  cudaEventElapsedTime(&up, e0, e1);
+  cudaEventElapsedTime(&comp, e1, e2);
+  cudaEventElapsedTime(&down, e2, e3);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaEventDestroy(e2);
+  cudaEventDestroy(e3);
+  res->success = 1;
+  res->compile_time_ms = compile_ms;
+  res->transfer_time_ms = up + down;
+  res->compute_time_ms = comp;
+  res->total_time_ms = ms_since(t0);
+  res->kernel_launches = launches;
+}
+
+void CudaExecutor::execute_device(Graph& g, const std::vector<uint64_t>& in_ids, const void* const* in_dev,
+                                  const std::vector<uint64_t>& outs, void* const* out_dev, cudaStream_t stream,
+                                  pfc_execution_result* res) {
+  std::lock_guard<std::mutex> lock(mu_);
+  auto t0 = std::chrono::steady_clock::now();
+  DeviceGuard dg(cfg_.device_id);
+  std::unordered_set<uint64_t> bindings;
+  std::unordered_map<uint64_t, const void*> bind;
+  for (size_t i = 0; i < in_ids.size(); ++i) {
+    const Node* n = g.find(in_ids[i]);
+    if (!n) fail(PFC_ERR_INVALID_ARGUMENT, "input id " + std::to_string(in_ids[i]) + " is not in the graph");
+    if (n->type == NodeType::OPERATION) fail(PFC_ERR_INVALID_ARGUMENT, "only leaf nodes can be bound to device data");
+    if (((uintptr_t)in_dev[i] & 15) != 0) fail(PFC_ERR_INVALID_ARGUMENT, "device input pointers must be 16-byte aligned");
+    bindings.insert(in_ids[i]);
+    bind[in_ids[i]] = in_dev[i];
+  }
+  for (size_t i = 0; i < outs.size(); ++i)
+    if (!g.find(outs[i])) fail(PFC_ERR_INVALID_ARGUMENT, "output id " + std::to_string(outs[i]) + " is not in the graph");
+  double compile_ms = 0;
+  PlanEntry& pe = prepare(g, outs, bindings, &compile_ms);
+  const Plan& P = *pe.plan;
+  cudaStream_t s = stream ? stream : stream_;
+  std::vector<std::pair<void*, const Node*>> uploads;
+  std::vector<void*> ptrs = resolve(pe, g, bind, s, &uploads);
+  // Outputs whose buffer is exclusively theirs are written in place.
+  std::vector<bool> direct(outs.size(), false);
+  std::unordered_map<int, int> owner;
+  for (size_t i = 0; i < outs.size(); ++i) owner[P.output_views[i].buf]++;
+  for (size_t i = 0; i < outs.size(); ++i) {
+    const View& v = P.output_views[i];
+    const Buffer& b = P.buffers[v.buf];
+    if (b.kind == BufKind::ARENA && v.offset == 0 && owner[v.buf] == 1 && ((uintptr_t)out_dev[i] & 255) == 0) {
+      ptrs[v.buf] = out_dev[i];
+      direct[i] = true;
+    }
+  }
+  for (auto& [dst, n] : uploads) PFB_CUDA(cudaMemcpyAsync(dst, n->data, n->data_bytes, cudaMemcpyHostToDevice, s));
+  {
+    // splat values live in a small device table; upload only when they change
+    std::vector<float> table(P.scalars.size());
+    for (size_t i = 0; i < P.scalars.size(); ++i) table[i] = P.scalars[i].value;
+    if (!table.empty() && (table != pe.table || pe.table_ptr != ptrs[P.scalar_buf])) {
+      PFB_CUDA(cudaMemcpyAsync(ptrs[P.scalar_buf], table.data(), table.size() * 4, cudaMemcpyHostToDevice, s));
+      pe.table = table;
+      pe.table_ptr = ptrs[P.scalar_buf];
+    }
+  }
+  int64_t launches = run_steps(pe, ptrs, s);
+  for (size_t i = 0; i < outs.size(); ++i) {
+    if (direct[i]) continue;
+    const View& v = P.output_views[i];
+    const void* src = (const char*)ptrs[v.buf] + v.offset * (int64_t)dtype_size(v.dtype);
+    PFB_CUDA(cudaMemcpyAsync(out_dev[i], src, g.at(outs[i]).size_bytes(), cudaMemcpyDeviceToDevice, s));
+  }
+  res->success = 1;
+  res->compile_time_ms = compile_ms;
+  res->total_time_ms = ms_since(t0);
+  res->kernel_launches = launches;
+}
+
+std::string CudaExecutor::describe(Graph& g, const std::vector<uint64_t>& outs) {
+  std::lock_guard<std::mutex> lock(mu_);
+  DeviceGuard dg(cfg_.device_id);
+  PlanEntry& pe = prepare(g, outs, {}, nullptr);
+  return pe.plan->description;
+}
+
+}  // namespace pfb

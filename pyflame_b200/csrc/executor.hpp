@@ -1,0 +1,90 @@
+// CudaExecutor: the B200 counterpart of rocm::ROCmExecutor
+// (include/pyflame/backend/rocm/rocm_executor.hpp:37-194).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/pyflame_cuda.h"
+#include "compiler.hpp"
+#include "graph.hpp"
+#include "memory_pool.hpp"
+#include "plan.hpp"
+
+namespace pfb {
+
+// Constants whose elements are all equal (and data-less leaves, which read as
+// zero) become scalars: node id -> value.
+std::unordered_map<uint64_t, float> detect_splats(const Graph& g, const std::vector<uint64_t>& order,
+                                                  const std::unordered_set<uint64_t>& bindings);
+
+class CudaExecutor {
+ public:
+  explicit CudaExecutor(const pfc_executor_config& cfg);
+  ~CudaExecutor();
+  CudaExecutor(const CudaExecutor&) = delete;
+  CudaExecutor& operator=(const CudaExecutor&) = delete;
+
+  // Host-buffer path (ROCmExecutor::execute, rocm_executor.cpp:66-161).
+  void execute(Graph& g, const std::vector<uint64_t>& outs, void* const* host_out, const size_t* out_bytes,
+               pfc_execution_result* res);
+  // Device-resident path: caller device pointers for inputs and outputs.
+  void execute_device(Graph& g, const std::vector<uint64_t>& in_ids, const void* const* in_dev,
+                      const std::vector<uint64_t>& outs, void* const* out_dev, cudaStream_t stream,
+                      pfc_execution_result* res);
+
+  pfc_device_info device_info() const;
+  pfc_memory_stats memory_stats() const { return pool_->stats(); }
+  void release_constants();
+  std::string describe(Graph& g, const std::vector<uint64_t>& outs);
+  const std::vector<std::pair<std::string, double>>& last_profile() const { return profile_; }
+
+ private:
+  struct PlanEntry {
+    std::unique_ptr<Plan> plan;
+    void* arena = nullptr;
+    std::vector<cudaKernel_t> kernels;  // per step (JIT steps)
+    cudaGraphExec_t gexec = nullptr;
+    std::vector<void*> gexec_ptrs;      // buffer pointers the graph was captured with
+    int runs = 0;
+    std::vector<float> table;           // splat values last uploaded to the scalar table
+    void* table_ptr = nullptr;
+  };
+  struct Resident {
+    void* dev = nullptr;
+    size_t bytes = 0;
+  };
+  struct SplatInfo {
+    bool splat = false;
+    float value = 0.f;
+  };
+
+  pfc_executor_config cfg_;
+  cudaStream_t stream_ = nullptr;
+  std::unique_ptr<CudaMemoryPool> pool_;
+  int* err_dev_ = nullptr;
+  int num_sms_ = 148;
+  std::mutex mu_;
+  std::unordered_map<uint64_t, PlanEntry> plans_;
+  std::map<std::pair<uint64_t, size_t>, Resident> resident_;
+  std::map<std::pair<uint64_t, size_t>, SplatInfo> resident_splat_;
+  std::vector<std::pair<std::string, double>> profile_;
+
+  PlanEntry& prepare(Graph& g, const std::vector<uint64_t>& outs, const std::unordered_set<uint64_t>& bindings,
+                     double* compile_ms);
+  std::unordered_map<uint64_t, float> detect_splats(const Graph& g, const std::vector<uint64_t>& order,
+                                                    const std::unordered_set<uint64_t>& bindings);
+  std::vector<void*> resolve(PlanEntry& pe, const Graph& g, const std::unordered_map<uint64_t, const void*>& bind,
+                             cudaStream_t s, std::vector<std::pair<void*, const Node*>>* uploads);
+  int64_t run_steps(PlanEntry& pe, const std::vector<void*>& ptrs, cudaStream_t s);
+  void launch_step(PlanEntry& pe, size_t i, const std::vector<void*>& ptrs, cudaStream_t s);
+  void check_device_error(cudaStream_t s);
+};
+
+}  // namespace pfb

@@ -1,0 +1,82 @@
+// Host-side launchers of the precompiled device kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace pfb {
+
+struct GemmLaunch {
+  int precision = 0;
+  const void* a_hi = nullptr;
+  const void* a_lo = nullptr;
+  const void* b_hi = nullptr;
+  const void* b_lo = nullptr;
+  int64_t a_sb = 0, b_sb = 0;  // nonzero: operand has `batch` slices
+  int64_t batch = 1, M = 0, N = 0, K = 0, kpad = 0;
+  float* c = nullptr;
+  int64_t c_sb = 0, c_sm = 0, c_sn = 1;
+  float alpha = 1.f;
+  const float* alpha_ptr = nullptr;
+  const float* bias = nullptr;
+  const float* bias_scalar = nullptr;  // device scalar added to every element (bias of equal values)
+  const float* scale = nullptr;  // folded BatchNorm: v = acc*scale[n] + shift[n]
+  const float* shift = nullptr;
+  int act = 0;
+  const float* residual = nullptr;
+  int64_t r_sb = 0, r_sm = 0, r_sn = 0;
+  int* err = nullptr;
+};
+void launch_gemm(const GemmLaunch& L, cudaStream_t stream);
+
+// Operand preparation from a strided view of rank <= 6: the last dim is K,
+// all leading dims flatten (row-major) into rows.  Output [rows][kpad].
+struct PrepLaunch {
+  const float* src = nullptr;
+  int rank = 2;
+  int64_t shape[6] = {0};
+  int64_t stride[6] = {0};
+  int precision = 0;
+  void* hi = nullptr;  // fp32 hi (tf32x3) or bf16 values
+  float* lo = nullptr;
+  int64_t kpad = 0;
+};
+void launch_prepare(const PrepLaunch& L, cudaStream_t stream);
+
+struct Im2colLaunch {
+  const float* x = nullptr;
+  int64_t n = 0, c = 0, h = 0, w = 0, sn = 0, sc = 0, sh = 0, sw = 0;
+  int64_t kh = 1, kw = 1, stride_h = 1, stride_w = 1, pad_h = 0, pad_w = 0, dil_h = 1, dil_w = 1;
+  int64_t oh = 0, ow = 0, kpad = 0;
+  int precision = 0;
+  void* hi = nullptr;
+  float* lo = nullptr;
+};
+void launch_im2col(const Im2colLaunch& L, cudaStream_t stream);
+
+struct PoolLaunch {
+  const float* x = nullptr;
+  float* y = nullptr;
+  int mode = 0;
+  int64_t n = 0, c = 0, h = 0, w = 0, sn = 0, sc = 0, sh = 0, sw = 0;
+  int64_t kh = 1, kw = 1, stride_h = 1, stride_w = 1, pad_h = 0, pad_w = 0;
+  int64_t oh = 0, ow = 0, osn = 0, osc = 0, osh = 0, osw = 0;
+};
+void launch_pool(const PoolLaunch& L, cudaStream_t stream);
+
+struct BnFoldLaunch {
+  const float* gamma = nullptr; int64_t gs = 0;  // strides in elements (0 = splat)
+  const float* beta = nullptr;  int64_t bs = 0;
+  const float* mean = nullptr;  int64_t ms = 0;
+  const float* var = nullptr;   int64_t vs = 0;
+  const float* bias = nullptr;  int64_t cs = 0;
+  float gamma_c = 1.f, beta_c = 0.f, mean_c = 0.f, var_c = 1.f, bias_c = 0.f;  // used when the pointer is null
+  float eps = 1e-5f;
+  int64_t channels = 0;
+  float* scale = nullptr;
+  float* shift = nullptr;
+};
+void launch_bn_fold(const BnFoldLaunch& L, cudaStream_t stream);
+
+}  // namespace pfb

@@ -1,0 +1,319 @@
+// Memory-bound kernels around the tensor-core GEMM: operand preparation
+// (fp32 -> tf32 hi/lo split or bf16, K-major, zero-padded K), im2col for
+// Conv2d as implicit GEMM, pooling, and BatchNorm(eval) folding.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+
+#include "../common.hpp"
+#include "kernels.hpp"
+
+namespace pfb {
+
+namespace {
+
+int num_sms() {
+  static int sms[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!sms[dev & 63]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    sms[dev & 63] = v > 0 ? v : 148;
+  }
+  return sms[dev & 63];
+}
+
+unsigned grid_for(int64_t work, int block) {
+  int64_t g = ceil_div(std::max<int64_t>(work, 1), block);
+  return (unsigned)std::max<int64_t>(1, std::min<int64_t>(g, (int64_t)num_sms() * 32));
+}
+
+struct View6 {
+  int rank;
+  long long shape[6];
+  long long stride[6];
+};
+
+// tf32x3 split: hi keeps the sign, exponent and top 10 mantissa bits; lo is
+// the exact remainder.  Non-finite values go entirely into hi.
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+  if (!isfinite(x)) {
+    hi = isnan(x) ? __int_as_float(0x7fc00000) : x;
+    lo = 0.f;
+    return;
+  }
+  hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+  lo = x - hi;
+}
+
+__device__ __forceinline__ long long row_offset(const View6& v, long long row) {
+  // rows enumerate dims [0, rank-1) row-major
+  long long off = 0;
+  for (int d = v.rank - 2; d >= 0; --d) {
+    long long sz = v.shape[d];
+    off += (row % sz) * v.stride[d];
+    row /= sz;
+  }
+  return off;
+}
+
+// Generic path: one output element per thread (k fastest, coalesced writes).
+template <int PREC>
+__global__ void prepare_generic(const float* __restrict__ src, View6 v, long long rows, long long kpad,
+                                void* __restrict__ hi, float* __restrict__ lo) {
+  const long long K = v.shape[v.rank - 1];
+  const long long sk = v.stride[v.rank - 1];
+  const long long total = rows * kpad;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / kpad, k = i % kpad;
+    float x = 0.f;
+    if (k < K) x = src[row_offset(v, r) + k * sk];
+    if constexpr (PREC == PFC_PRECISION_BF16) {
+      ((__nv_bfloat16*)hi)[i] = __float2bfloat16_rn(x);
+    } else {
+      float h, l;
+      split_tf32(x, h, l);
+      ((float*)hi)[i] = h;
+      lo[i] = l;
+    }
+  }
+}
+
+// Vector path: K contiguous (stride 1), K % 4 == 0, 16-byte aligned rows.
+template <int PREC>
+__global__ void prepare_vec4(const float* __restrict__ src, View6 v, long long rows, long long kpad,
+                             void* __restrict__ hi, float* __restrict__ lo) {
+  const long long K = v.shape[v.rank - 1];
+  const long long kq = kpad / 4;
+  const long long total = rows * kq;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / kq, k = (i % kq) * 4;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (k < K) x = *(const float4*)(src + row_offset(v, r) + k);
+    const long long o = r * kpad + k;
+    if constexpr (PREC == PFC_PRECISION_BF16) {
+      __nv_bfloat162 a = __floats2bfloat162_rn(x.x, x.y), b = __floats2bfloat162_rn(x.z, x.w);
+      uint2 pk;
+      pk.x = *(uint32_t*)&a;
+      pk.y = *(uint32_t*)&b;
+      *(uint2*)((__nv_bfloat16*)hi + o) = pk;
+    } else {
+      float4 h, l;
+      split_tf32(x.x, h.x, l.x);
+      split_tf32(x.y, h.y, l.y);
+      split_tf32(x.z, h.z, l.z);
+      split_tf32(x.w, h.w, l.w);
+      *(float4*)((float*)hi + o) = h;
+      *(float4*)(lo + o) = l;
+    }
+  }
+}
+
+// Transposed source: the last row dim is contiguous (stride 1) and K is
+// strided.  32x32 tiles through shared memory keep both sides coalesced.
+template <int PREC>
+__global__ void prepare_transpose(const float* __restrict__ src, View6 v, long long rows, long long kpad,
+                                  void* __restrict__ hi, float* __restrict__ lo) {
+  __shared__ float tile[32][33];
+  const long long K = v.shape[v.rank - 1];
+  const long long sk = v.stride[v.rank - 1];
+  const long long R = v.shape[v.rank - 2];  // innermost row dim (contiguous)
+  const long long outer = rows / R;
+  const long long tiles_r = (R + 31) / 32, tiles_k = (kpad + 31) / 32;
+  const long long ntiles = outer * tiles_r * tiles_k;
+  for (long long t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    const long long tk = t % tiles_k, tr = (t / tiles_k) % tiles_r, ob = t / (tiles_k * tiles_r);
+    const long long base = row_offset(v, ob * R);  // offset of (ob, r=0)
+    // load: threadIdx.x walks r (contiguous in memory)
+    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+      const long long k = tk * 32 + j, r = tr * 32 + threadIdx.x;
+      float x = 0.f;
+      if (k < K && r < R) x = src[base + r * v.stride[v.rank - 2] + k * sk];
+      tile[j][threadIdx.x] = x;
+    }
+    __syncthreads();
+    // store: threadIdx.x walks k (contiguous in the output)
+    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+      const long long r = tr * 32 + j, k = tk * 32 + threadIdx.x;
+      if (r < R && k < kpad) {
+        const float x = tile[threadIdx.x][j];
+        const long long o = (ob * R + r) * kpad + k;
+        if constexpr (PREC == PFC_PRECISION_BF16) {
+          ((__nv_bfloat16*)hi)[o] = __float2bfloat16_rn(x);
+        } else {
+          float h, l;
+          split_tf32(x, h, l);
+          ((float*)hi)[o] = h;
+          lo[o] = l;
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+template <int PREC>
+__global__ void im2col_kernel(const float* __restrict__ x, Im2colLaunch L, void* __restrict__ hi, float* __restrict__ lo) {
+  const long long K = L.c * L.kh * L.kw;
+  const long long M = L.n * L.oh * L.ow;
+  const long long total = M * L.kpad;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long m = i / L.kpad, k = i % L.kpad;
+    float v = 0.f;
+    if (k < K) {
+      const long long ow = m % L.ow, oh = (m / L.ow) % L.oh, n = m / (L.ow * L.oh);
+      const long long kw = k % L.kw, kh = (k / L.kw) % L.kh, c = k / (L.kw * L.kh);
+      const long long ih = oh * L.stride_h - L.pad_h + kh * L.dil_h;
+      const long long iw = ow * L.stride_w - L.pad_w + kw * L.dil_w;
+      if (ih >= 0 && ih < L.h && iw >= 0 && iw < L.w) v = x[n * L.sn + c * L.sc + ih * L.sh + iw * L.sw];
+    }
+    if constexpr (PREC == PFC_PRECISION_BF16) {
+      ((__nv_bfloat16*)hi)[i] = __float2bfloat16_rn(v);
+    } else {
+      float h, l;
+      split_tf32(v, h, l);
+      ((float*)hi)[i] = h;
+      lo[i] = l;
+    }
+  }
+}
+
+// Pooling (pooling.cpp:38-63,97-122,150-168): one output element per thread,
+// enumerated channel-fastest when the output is channels-last.
+__global__ void pool_kernel(PoolLaunch L) {
+  const long long total = L.n * L.c * L.oh * L.ow;
+  const bool cl = L.osc == 1;  // channels-last output
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    long long n, c, oh, ow;
+    if (cl) {
+      c = i % L.c; ow = (i / L.c) % L.ow; oh = (i / (L.c * L.ow)) % L.oh; n = i / (L.c * L.ow * L.oh);
+    } else {
+      ow = i % L.ow; oh = (i / L.ow) % L.oh; c = (i / (L.ow * L.oh)) % L.c; n = i / (L.ow * L.oh * L.c);
+    }
+    const float* xb = L.x + n * L.sn + c * L.sc;
+    float out;
+    if (L.mode == 2) {
+      // adaptive average: window [floor(i*H/OH), ceil((i+1)*H/OH))
+      const long long h0 = (oh * L.h) / L.oh, h1 = ((oh + 1) * L.h + L.oh - 1) / L.oh;
+      const long long w0 = (ow * L.w) / L.ow, w1 = ((ow + 1) * L.w + L.ow - 1) / L.ow;
+      float s = 0.f;
+      for (long long h = h0; h < h1; ++h)
+        for (long long w = w0; w < w1; ++w) s += xb[h * L.sh + w * L.sw];
+      out = s / (float)((h1 - h0) * (w1 - w0));
+    } else {
+      const long long hs = oh * L.stride_h - L.pad_h, ws = ow * L.stride_w - L.pad_w;
+      if (L.mode == 0) {
+        float m = -__int_as_float(0x7f800000);
+        for (long long kh = 0; kh < L.kh; ++kh) {
+          const long long h = hs + kh;
+          if (h < 0 || h >= L.h) continue;
+          for (long long kw = 0; kw < L.kw; ++kw) {
+            const long long w = ws + kw;
+            if (w < 0 || w >= L.w) continue;
+            const float v = xb[h * L.sh + w * L.sw];
+            if (v > m || isnan(v)) m = v;
+          }
+        }
+        out = m;
+      } else {
+        float s = 0.f;
+        for (long long kh = 0; kh < L.kh; ++kh) {
+          const long long h = hs + kh;
+          if (h < 0 || h >= L.h) continue;
+          for (long long kw = 0; kw < L.kw; ++kw) {
+            const long long w = ws + kw;
+            if (w < 0 || w >= L.w) continue;
+            s += xb[h * L.sh + w * L.sw];
+          }
+        }
+        out = s / (float)(L.kh * L.kw);  // count includes padding
+      }
+    }
+    L.y[n * L.osn + c * L.osc + oh * L.osh + ow * L.osw] = out;
+  }
+}
+
+__global__ void bn_fold_kernel(BnFoldLaunch L) {
+  for (long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x; c < L.channels; c += (long long)gridDim.x * blockDim.x) {
+    const float g = L.gamma ? L.gamma[c * L.gs] : L.gamma_c;
+    const float b = L.beta ? L.beta[c * L.bs] : L.beta_c;
+    const float m = L.mean ? L.mean[c * L.ms] : L.mean_c;
+    const float v = L.var ? L.var[c * L.vs] : L.var_c;
+    const float cb = L.bias ? L.bias[c * L.cs] : L.bias_c;
+    const float s = g / sqrtf(v + L.eps);
+    L.scale[c] = s;
+    L.shift[c] = (cb - m) * s + b;
+  }
+}
+
+}  // namespace
+
+void launch_prepare(const PrepLaunch& L, cudaStream_t stream) {
+  PFB_CHECK_ARG(L.rank >= 1 && L.rank <= 6, "prepare: rank must be 1..6");
+  View6 v;
+  v.rank = L.rank;
+  long long rows = 1;
+  for (int d = 0; d < L.rank; ++d) {
+    v.shape[d] = L.shape[d];
+    v.stride[d] = L.stride[d];
+    if (d + 1 < L.rank) rows *= L.shape[d];
+  }
+  if (L.rank == 1) {  // a single row
+    v.rank = 2;
+    v.shape[1] = v.shape[0];
+    v.stride[1] = v.stride[0];
+    v.shape[0] = 1;
+    v.stride[0] = 0;
+  }
+  const long long K = v.shape[v.rank - 1];
+  const long long sk = v.stride[v.rank - 1];
+  if (rows * L.kpad == 0) return;
+  const bool bf = L.precision == PFC_PRECISION_BF16;
+  bool vec = sk == 1 && K % 4 == 0 && ((uintptr_t)L.src & 15) == 0;
+  for (int d = 0; d + 1 < v.rank && vec; ++d) vec = (v.stride[d] % 4) == 0 || v.shape[d] == 1;
+  const bool trans = !vec && sk != 1 && v.stride[v.rank - 2] == 1 && v.shape[v.rank - 2] > 1;
+  if (vec) {
+    unsigned g = grid_for(rows * (L.kpad / 4), 256);
+    if (bf) prepare_vec4<PFC_PRECISION_BF16><<<g, 256, 0, stream>>>(L.src, v, rows, L.kpad, L.hi, L.lo);
+    else prepare_vec4<PFC_PRECISION_TF32X3><<<g, 256, 0, stream>>>(L.src, v, rows, L.kpad, L.hi, L.lo);
+  } else if (trans) {
+    const long long R = v.shape[v.rank - 2];
+    long long ntiles = (rows / R) * ceil_div(R, 32) * ceil_div(L.kpad, 32);
+    unsigned g = (unsigned)std::max<long long>(1, std::min<long long>(ntiles, (long long)num_sms() * 16));
+    dim3 blk(32, 8);
+    if (bf) prepare_transpose<PFC_PRECISION_BF16><<<g, blk, 0, stream>>>(L.src, v, rows, L.kpad, L.hi, L.lo);
+    else prepare_transpose<PFC_PRECISION_TF32X3><<<g, blk, 0, stream>>>(L.src, v, rows, L.kpad, L.hi, L.lo);
+  } else {
+    unsigned g = grid_for(rows * L.kpad, 256);
+    if (bf) prepare_generic<PFC_PRECISION_BF16><<<g, 256, 0, stream>>>(L.src, v, rows, L.kpad, L.hi, L.lo);
+    else prepare_generic<PFC_PRECISION_TF32X3><<<g, 256, 0, stream>>>(L.src, v, rows, L.kpad, L.hi, L.lo);
+  }
+  PFB_CUDA(cudaGetLastError());
+}
+
+void launch_im2col(const Im2colLaunch& L, cudaStream_t stream) {
+  const long long total = L.n * L.oh * L.ow * L.kpad;
+  if (total == 0) return;
+  unsigned g = grid_for(total, 256);
+  if (L.precision == PFC_PRECISION_BF16) im2col_kernel<PFC_PRECISION_BF16><<<g, 256, 0, stream>>>(L.x, L, L.hi, L.lo);
+  else im2col_kernel<PFC_PRECISION_TF32X3><<<g, 256, 0, stream>>>(L.x, L, L.hi, L.lo);
+  PFB_CUDA(cudaGetLastError());
+}
+
+void launch_pool(const PoolLaunch& L, cudaStream_t stream) {
+  const long long total = L.n * L.c * L.oh * L.ow;
+  if (total == 0) return;
+  pool_kernel<<<grid_for(total, 256), 256, 0, stream>>>(L);
+  PFB_CUDA(cudaGetLastError());
+}
+
+void launch_bn_fold(const BnFoldLaunch& L, cudaStream_t stream) {
+  if (L.channels == 0) return;
+  bn_fold_kernel<<<grid_for(L.channels, 256), 256, 0, stream>>>(L);
+  PFB_CUDA(cudaGetLastError());
+}
+
+}  // namespace pfb

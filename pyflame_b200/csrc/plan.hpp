@@ -1,0 +1,150 @@
+// Compiled execution plan for one graph structure: buffers, strided views
+// over them, and the ordered list of device steps (kernel launches).
+#pragma once
+
+#include <cstdint>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "graph.hpp"
+
+namespace pfb {
+
+// A buffer is a byte range the plan reads or writes.
+enum class BufKind : uint8_t {
+  ARENA,     // intermediate or output: offset into the plan's arena
+  CONST,     // constant payload uploaded from the host (resident or per call)
+  BINDING,   // device pointer supplied by the caller (execute_device)
+};
+
+struct Buffer {
+  BufKind kind = BufKind::ARENA;
+  size_t bytes = 0;
+  int64_t arena_offset = -1;   // ARENA
+  uint64_t node = 0;           // CONST / BINDING: source node id
+  int first_use = -1, last_use = -1;  // step indices (liveness)
+  bool pinned_live = false;    // keep to the end (graph outputs)
+};
+
+// Strided view of a buffer: element (i0..ir) is at
+// base + (offset + sum_d i_d*strides[d]) * elem_size.  A buffer index of -1
+// with is_splat means every element equals scalar table entry `splat_slot`.
+struct View {
+  int buf = -1;
+  int64_t offset = 0;
+  std::vector<int64_t> shape;
+  std::vector<int64_t> strides;
+  DType dtype = DType::F32;
+  bool is_splat = false;
+  int splat_slot = -1;
+  float splat_value = 0.f;  // value at compile time (the table is refreshed per call)
+
+  int64_t numel() const {
+    int64_t n = 1;
+    for (int64_t d : shape) n *= d;
+    return n;
+  }
+  bool is_contiguous() const;
+  static std::vector<int64_t> dense_strides(const std::vector<int64_t>& shape);
+};
+
+enum class StepKind : uint8_t {
+  JIT,        // NVRTC-generated kernel (fused elementwise / row / column / full reduction)
+  SPLIT,      // pfk_split_tf32 / pfk_convert_bf16 operand preparation
+  IM2COL,     // pfk_im2col
+  GEMM,       // pfk_gemm (tcgen05)
+  POOL,       // pfk_pool2d
+  BN_FOLD,    // fold BatchNorm(eval) into per-channel scale/shift
+  MEMSET,     // zero a buffer range
+};
+
+struct JitLaunch {
+  std::string module_key;  // hash of the generated source
+  std::string kernel;      // kernel symbol
+  int grid = 1, block = 256;
+  size_t smem = 0;
+  std::vector<std::pair<int, int64_t>> ptrs;  // (buffer, byte offset) for each pointer argument
+};
+
+struct SplitArgs {
+  View src;             // [batch..., rows, cols] logical
+  int out_hi = -1, out_lo = -1;  // buffers; lo == -1 for bf16
+  int64_t batch = 1, rows = 0, cols = 0, kpad = 0;
+  // flattened batch strides (requires the batch dims of src to collapse)
+  int64_t sb = 0, sr = 0, sk = 0;
+  int precision = 0;
+};
+
+struct Im2colArgs {
+  View x;  // [N,C,H,W]
+  int out_hi = -1, out_lo = -1;
+  int64_t kh = 1, kw = 1, sh = 1, sw = 1, ph = 0, pw = 0, dh = 1, dw = 1, oh = 0, ow = 0, kpad = 0;
+  int precision = 0;
+};
+
+struct GemmArgs {
+  int a_hi = -1, a_lo = -1, b_hi = -1, b_lo = -1;
+  int64_t a_sb = 0, b_sb = 0, batch = 1, M = 0, N = 0, K = 0, kpad = 0;
+  View c;  // output view; strides used for (batch, m, n)
+  int64_t c_sb = 0, c_sm = 0, c_sn = 0;
+  int precision = 0;
+  float alpha = 1.f;
+  int alpha_slot = -1;            // splat scale from the scalar table (overrides alpha)
+  View bias;  bool has_bias = false;   // [N] view
+  int scale_buf = -1, shift_buf = -1;  // folded BatchNorm: per-n scale and shift (replace alpha/bias)
+  int act = 0;
+  View residual; bool has_residual = false;
+  int64_t r_sb = 0, r_sm = 0, r_sn = 0;
+};
+
+struct PoolArgs {
+  View x;
+  View y;
+  int mode = 0;
+  int64_t kh = 1, kw = 1, sh = 1, sw = 1, ph = 0, pw = 0;
+};
+
+struct BnFoldArgs {
+  // scale[c] = gamma[c] / sqrt(var[c] + eps); shift[c] = (bias[c] - mean[c]) * scale[c] + beta[c]
+  View gamma, beta, mean, var, bias;
+  bool has_gamma = false, has_beta = false, has_bias = false;
+  float eps = 1e-5f;
+  int64_t channels = 0;
+  int out_scale = -1, out_shift = -1;
+};
+
+struct Step {
+  StepKind kind = StepKind::JIT;
+  std::string label;           // for describe/profile
+  JitLaunch jit;
+  SplitArgs split;
+  Im2colArgs im2col;
+  GemmArgs gemm;
+  PoolArgs pool;
+  BnFoldArgs bnfold;
+  int memset_buf = -1;
+};
+
+struct ScalarSlot {
+  uint64_t node;   // splat constant node
+  float value;     // value seen when the plan was built
+};
+
+struct Plan {
+  uint64_t key = 0;
+  std::vector<Buffer> buffers;
+  std::vector<Step> steps;
+  std::vector<ScalarSlot> scalars;   // splat constants; table lives in the arena
+  int scalar_buf = -1;
+  int error_buf = -1;                // device int for bounded-wait errors
+  size_t arena_bytes = 0;
+  std::vector<uint64_t> outputs;
+  std::vector<View> output_views;    // dense views of requested outputs
+  std::vector<uint64_t> const_nodes; // constants with device payload (buffer kind CONST)
+  std::vector<uint64_t> splat_nodes; // constants replaced by scalar slots
+  std::string description;
+  int precision = 0;
+};
+
+}  // namespace pfb

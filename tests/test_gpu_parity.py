@@ -1,0 +1,404 @@
+"""CUDA executor vs the oracle on the same seeded graphs.
+
+Every case builds a graph with the PyFlame-mirroring front end, evaluates it
+through libpyflame_cuda.so (CudaExecutor.execute -> pfc_executor_execute)
+and compares with the CPU restatement (oracle/oracle.cpp), which itself is
+pinned to PyFlame's own executor and kernels by tests/test_oracle_pinned.py.
+"""
+import numpy as np
+import pytest
+
+import pyflame_b200 as pf
+from pyflame_b200 import nn
+from tests.helpers import (RTOL_GEMM_BF16, RTOL_GEMM_TF32X3, bitexact, close, close_rows, close_sum)
+
+pytestmark = pytest.mark.gpu
+
+
+def run(ex, outs, oracle_mod, precision="f32"):
+    g = outs[0].graph()
+    ids = [t.node().id() for t in outs]
+    res = ex.execute(g, ids)
+    assert res.success, res.error_message
+    assert res.kernel_launches >= 0
+    ref = oracle_mod.run(g, ids, precision)
+    return [res.outputs[i] for i in ids], [ref[i] for i in ids]
+
+
+# ---- known-answer tests from PyFlame's tests/cpp/test_operations.cpp ---------------
+
+def test_kat_operations(cuda_executor, oracle_mod):
+    x = pf.tensor([-2.0, -1.0, 0.0, 1.0, 2.0])
+    s = pf.tensor([1.0, 2.0, 3.0, 4.0])
+    outs = [pf.relu(x), pf.sigmoid(pf.tensor([0.0])), pf.exp(pf.tensor([0.0, 1.0])),
+            pf.log(pf.tensor([1.0, float(np.exp(np.float32(1.0)))])), pf.sqrt(pf.tensor([1.0, 4.0, 9.0])),
+            pf.abs(pf.tensor([-3.0, -1.0, 0.0, 1.0, 3.0])), s.sum(), s.mean(), pf.tensor([1.0, 5.0, 3.0, 2.0]).max(),
+            pf.tensor([5.0, 1.0, 3.0, 2.0]).min(), (pf.ones([10]) + pf.full([10], 2.0)) * 3.0 - 1.0,
+            pf.matmul(pf.tensor([[1.0, 2.0], [3.0, 4.0]]), pf.tensor([[5.0, 6.0], [7.0, 8.0]])),
+            pf.matmul(pf.tensor([[1.0, 2.0, 3.0]]), pf.tensor([[1.0], [2.0], [3.0]])),
+            pf.arange(1, 11).sum(), pf.arange(1, 11).mean()]
+    gpu, _ = run(cuda_executor, outs, oracle_mod)
+    expect = [[0, 0, 0, 1, 2], [0.5], [1, np.e], [0, 1], [1, 2, 3], [3, 1, 0, 1, 3], 10.0, 2.5, 5.0, 1.0, [8.0] * 10,
+              [[19, 22], [43, 50]], [[14]], 55.0, 5.5]
+    for g_, e in zip(gpu, expect):
+        np.testing.assert_allclose(g_, np.asarray(e, np.float32), rtol=1e-5, atol=1e-5)
+
+
+# ---- elementwise --------------------------------------------------------------------
+
+SPECIAL = np.array([0.0, -0.0, 1.0, -1.0, 1e-30, -1e-30, 1e30, -1e30, np.inf, -np.inf, np.nan, 88.0, -88.0,
+                    20.0, -20.0], np.float32)
+
+
+@pytest.mark.parametrize("fn", ["neg", "abs", "sqrt", "exp", "log", "sin", "cos", "tanh", "relu", "sigmoid",
+                                "gelu", "silu"])
+def test_unary(cuda_executor, oracle_mod, rng, fn):
+    data = np.concatenate([rng.standard_normal(1021).astype(np.float32) * 4, SPECIAL])
+    x = pf.tensor(data)
+    f = {"neg": lambda t: -t}.get(fn, getattr(pf, fn, None))
+    (g,), (r,) = run(cuda_executor, [f(x)], oracle_mod)
+    close(g, r, rtol=2e-6 if fn in ("relu", "neg", "abs") else 1e-5, atol=1e-6, what=fn)
+    if fn in ("neg", "abs", "relu"):
+        bitexact(g, r)
+
+
+@pytest.mark.parametrize("shapes", [((37, 129), (37, 129)), ((64, 256), (256,)), ((64, 256), (64, 1)),
+                                    ((2, 5, 7, 3), (1, 5, 1, 1)), ((3, 1, 8), (4, 1)), ((1000,), ())])
+@pytest.mark.parametrize("op", ["add", "sub", "mul", "div"])
+def test_binary_broadcast(cuda_executor, oracle_mod, rng, shapes, op):
+    a = pf.tensor(rng.standard_normal(shapes[0]).astype(np.float32))
+    b = pf.tensor(rng.standard_normal(shapes[1]).astype(np.float32))
+    out = {"add": a + b, "sub": a - b, "mul": a * b, "div": a / b}[op]
+    (g,), (r,) = run(cuda_executor, [out], oracle_mod)
+    bitexact(g, r)  # IEEE +,-,*,/ are correctly rounded on both sides
+
+
+def test_div_by_zero_semantics(cuda_executor, oracle_mod):
+    # executor.cpp:322-340: 0/0 -> NaN, x/0 -> +-inf by the dividend's sign (also for -0 divisors)
+    a = pf.tensor([0.0, 1.0, -1.0, 2.0, -2.0, 0.0, 3.0])
+    b = pf.tensor([0.0, 0.0, 0.0, -0.0, -0.0, 5.0, 2.0])
+    (g,), (r,) = run(cuda_executor, [a / b], oracle_mod)
+    bitexact(g, r)
+    assert np.isnan(g[0]) and g[1] == np.inf and g[2] == -np.inf and g[3] == np.inf and g[4] == -np.inf
+
+
+def test_comparisons_bitexact(cuda_executor, oracle_mod, rng):
+    a = pf.tensor(np.round(rng.standard_normal((33, 65)) * 2).astype(np.float32))
+    b = pf.tensor(np.round(rng.standard_normal((33, 65)) * 2).astype(np.float32))
+    outs = [a == b, a != b, a < b, a <= b, a > b, a >= b, pf.maximum(a, b), pf.minimum(a, b),
+            pf.clamp(a, -1.0, 1.5)]
+    gpu, ref = run(cuda_executor, outs, oracle_mod)
+    for g, r in zip(gpu, ref):
+        bitexact(g, r)
+
+
+def test_pow(cuda_executor, oracle_mod, rng):
+    a = pf.tensor(np.abs(rng.standard_normal(500)).astype(np.float32) + 0.1)
+    (g,), (r,) = run(cuda_executor, [pf.pow(a, 2.5)], oracle_mod)
+    close(g, r, rtol=1e-5)
+
+
+# ---- reductions, softmax, LayerNorm -----------------------------------------------
+
+@pytest.mark.parametrize("shape,dim", [((8, 4096), 1), ((37, 1000), -1), ((5, 3), 1), ((7, 4097), 1),
+                                       ((130, 77), 0), ((6, 33, 10), 1), ((4, 5, 6), 2), ((1, 1), 1),
+                                       ((3000,), 0), ((64, 10), -1)])
+@pytest.mark.parametrize("kind", ["sum", "mean", "max", "min"])
+def test_reductions(cuda_executor, oracle_mod, rng, shape, dim, kind):
+    data = rng.standard_normal(shape).astype(np.float32)
+    x = pf.tensor(data)
+    out = getattr(x, kind)(dim)
+    (g,), (r,) = run(cuda_executor, [out], oracle_mod)
+    if kind in ("max", "min"):
+        bitexact(g, r)
+    else:
+        terms = np.abs(data).sum(axis=dim)
+        if kind == "mean":
+            terms = terms / data.shape[dim]
+        close_sum(g, r, terms, what=f"{kind}{shape}")
+
+
+@pytest.mark.parametrize("kind", ["sum", "mean", "max", "min", "prod"])
+def test_full_reduction(cuda_executor, oracle_mod, rng, kind):
+    data = rng.standard_normal((1000, 777)).astype(np.float32)
+    if kind == "prod":
+        data = (1.0 + data[:3, :7] * 1e-2).astype(np.float32)
+    x = pf.tensor(data)
+    (g,), (r,) = run(cuda_executor, [getattr(x, kind)()], oracle_mod)
+    assert g.shape == ()
+    if kind in ("max", "min"):
+        bitexact(g, r)
+    else:
+        close_sum(g, r, np.abs(data).sum() / (data.size if kind == "mean" else 1) if kind != "prod"
+                  else np.abs(r) * 10, what=kind)
+
+
+def test_keepdim(cuda_executor, oracle_mod, rng):
+    data = rng.standard_normal((6, 40)).astype(np.float32)
+    x = pf.tensor(data)
+    outs = [x.sum(1, keepdim=True), x.max(0, keepdim=True), x.mean(keepdim=True)]
+    gpu, ref = run(cuda_executor, outs, oracle_mod)
+    assert gpu[0].shape == (6, 1) and gpu[1].shape == (1, 40) and gpu[2].shape == (1, 1)
+    close_sum(gpu[0], ref[0], np.abs(data).sum(1, keepdims=True))
+    bitexact(gpu[1], ref[1])
+
+
+@pytest.mark.parametrize("shape,dim", [((64, 10), -1), ((8, 512), -1), ((3, 7, 5), 1), ((4, 2, 33), 2),
+                                       ((2, 4097), 1)])
+@pytest.mark.parametrize("log", [False, True])
+def test_softmax(cuda_executor, oracle_mod, rng, shape, dim, log):
+    x = pf.tensor((rng.standard_normal(shape) * 3).astype(np.float32))
+    out = (pf.log_softmax if log else pf.softmax)(x, dim)
+    (g,), (r,) = run(cuda_executor, [out], oracle_mod)
+    close(g, r, rtol=1e-5, atol=1e-6 * (10 if log else 1), what="softmax")
+
+
+@pytest.mark.parametrize("shape,ns,affine", [((16, 768), [768], True), ((37, 100), [100], False),
+                                             ((4, 6, 10), [6, 10], True), ((3, 4096), [4096], True)])
+def test_layer_norm(cuda_executor, oracle_mod, rng, shape, ns, affine):
+    x = pf.tensor(rng.standard_normal(shape).astype(np.float32) * 2 + 0.5)
+    ln = nn.LayerNorm(ns, eps=1e-5, elementwise_affine=affine)
+    if affine:
+        ln.set_parameter("weight", rng.standard_normal(ns).astype(np.float32))
+        ln.set_parameter("bias", rng.standard_normal(ns).astype(np.float32))
+    (g,), (r,) = run(cuda_executor, [ln(x)], oracle_mod)
+    close_rows(g, r, 1e-5, what="layernorm")
+
+
+@pytest.mark.parametrize("rows,cols", [(256, 4096), (37, 1000), (5, 3)])
+def test_fused_graph(cuda_executor, oracle_mod, rows, cols):
+    from pyflame_b200 import workloads
+    w = workloads.fused(rows, cols)
+    gpu, ref = run(cuda_executor, w.outputs, oracle_mod)
+    plan = cuda_executor.describe_plan(w.outputs[0].graph(), [t.node().id() for t in w.outputs])
+    assert plan.count("row kernel") == 1 and "fused elementwise" not in plan, plan
+    x = w.inputs["x"].node().constant_data()
+    y = w.inputs["y"].node().constant_data()
+    z = ref[3]  # unused except for shape
+    zz = oracle_mod.run(w.outputs[0].graph(), [w.outputs[0].node().inputs()[0].id()])
+    zabs = np.abs(list(zz.values())[0]).sum(1)
+    close_sum(gpu[0], ref[0], zabs, what="sum")
+    close_sum(gpu[1], ref[1], zabs / cols, what="mean")
+    bitexact(gpu[2], ref[2])
+    close_rows(gpu[3], ref[3], 1e-5, what="layernorm")
+    assert z.shape == (rows, cols) and x.shape == y.shape
+
+
+# ---- shape ops -------------------------------------------------------------------------
+
+def test_views_bitexact(cuda_executor, oracle_mod, rng):
+    a = pf.tensor(rng.standard_normal((4, 6, 8)).astype(np.float32))
+    b = pf.tensor(rng.standard_normal((4, 6, 8)).astype(np.float32))
+    outs = [a.transpose(0, 2), a.reshape([24, 8]).t(), a.slice(1, 2, 5), a.transpose(1, 2).reshape([4, 48]),
+            a.unsqueeze(1).squeeze(1), a[2], pf.cat([a, b], 1), pf.stack([a, b], 0), (a + b).transpose(-1, -2),
+            a.slice(2, -3, 100)]
+    gpu, ref = run(cuda_executor, outs, oracle_mod)
+    for g, r in zip(gpu, ref):
+        bitexact(g, r)
+
+
+# ---- contractions ------------------------------------------------------------------------
+
+@pytest.mark.parametrize("m,k,n", [(64, 784, 256), (5, 7, 3), (130, 200, 70), (256, 512, 384), (1, 1, 1),
+                                   (128, 4096, 128), (300, 33, 257)])
+def test_matmul_2d(cuda_executor, oracle_mod, rng, m, k, n):
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32)
+    (g,), (r,) = run(cuda_executor, [pf.matmul(pf.tensor(a), pf.tensor(b))], oracle_mod)
+    r64 = a.astype(np.float64) @ b.astype(np.float64)
+    close_rows(g, r64, RTOL_GEMM_TF32X3, what="matmul vs fp64")
+    close_rows(r, r64, RTOL_GEMM_TF32X3, what="oracle vs fp64")
+
+
+@pytest.mark.parametrize("a_shape,b_shape", [((2, 3, 17, 40), (2, 3, 40, 9)), ((4, 33, 64), (64, 48)),
+                                             ((3, 16, 8), (1, 8, 5)), ((40,), (40, 7)), ((7, 40), (40,)),
+                                             ((40,), (40,)), ((2, 1, 8, 16), (3, 16, 4))])
+def test_matmul_batched_and_1d(cuda_executor, oracle_mod, rng, a_shape, b_shape):
+    a = rng.standard_normal(a_shape).astype(np.float32)
+    b = rng.standard_normal(b_shape).astype(np.float32)
+    (g,), (r,) = run(cuda_executor, [pf.matmul(pf.tensor(a), pf.tensor(b))], oracle_mod)
+    r64 = np.matmul(a.astype(np.float64), b.astype(np.float64))
+    assert g.shape == r64.shape
+    close_rows(g, r64.reshape(g.shape) if g.ndim else r64, RTOL_GEMM_TF32X3) if g.ndim else \
+        close(g, r64, rtol=RTOL_GEMM_TF32X3, atol=1e-4 * np.abs(a).sum())
+
+
+def test_linear_relu_softmax_mlp(cuda_executor, oracle_mod):
+    from pyflame_b200 import workloads
+    w = workloads.mlp(64)
+    (g,), (r,) = run(cuda_executor, w.outputs, oracle_mod)
+    close(g, r, rtol=1e-4, atol=1e-6, what="mlp softmax")
+    plan = cuda_executor.describe_plan(w.outputs[0].graph(), [w.outputs[0].node().id()])
+    assert plan.count("gemm") == 2, plan  # bias + relu fused into the GEMM epilogues
+
+
+def test_gemm_epilogues(cuda_executor, oracle_mod, rng):
+    x = pf.tensor(rng.standard_normal((96, 160)).astype(np.float32))
+    res = pf.tensor(rng.standard_normal((96, 72)).astype(np.float32))
+    lin = nn.Linear(160, 72)
+    lin.set_parameter("bias", rng.standard_normal(72).astype(np.float32))
+    outs = [pf.gelu(lin(x)) + res, pf.matmul(x, lin.p("weight").transpose(0, 1)) * 0.125, pf.sigmoid(lin(x)),
+            pf.tanh(lin(x)), pf.silu(lin(x))]
+    gpu, ref = run(cuda_executor, outs, oracle_mod)
+    for g, r in zip(gpu, ref):
+        close_rows(g, r, RTOL_GEMM_TF32X3)
+
+
+def test_gemm_bf16_mode(oracle_mod, rng, native):
+    ex = pf.CudaExecutor(pf.CudaExecutor.Config(precision="bf16"))
+    a = rng.standard_normal((200, 300)).astype(np.float32)
+    b = rng.standard_normal((300, 150)).astype(np.float32)
+    out = pf.matmul(pf.tensor(a), pf.tensor(b))
+    (g,), _ = run(ex, [out], oracle_mod)
+    r64 = a.astype(np.float64) @ b.astype(np.float64)
+    close_rows(g, r64, RTOL_GEMM_BF16, what="bf16 matmul")
+    ex.close()
+
+
+# ---- convolution and pooling ---------------------------------------------------------------
+
+@pytest.mark.parametrize("cfg", [dict(n=2, c=3, h=17, w=15, o=8, k=3, s=1, p=1),
+                                 dict(n=2, c=3, h=32, w=32, o=16, k=7, s=2, p=3),
+                                 dict(n=1, c=5, h=9, w=11, o=4, k=2, s=3, p=0)])
+def test_conv2d(cuda_executor, oracle_mod, rng, cfg):
+    x = rng.random((cfg["n"], cfg["c"], cfg["h"], cfg["w"])).astype(np.float32)
+    conv = nn.Conv2d(cfg["c"], cfg["o"], cfg["k"], cfg["s"], cfg["p"])
+    conv.set_parameter("weight", rng.standard_normal((cfg["o"], cfg["c"], cfg["k"], cfg["k"])).astype(np.float32))
+    conv.set_parameter("bias", rng.standard_normal(cfg["o"]).astype(np.float32))
+    (g,), (r,) = run(cuda_executor, [conv(pf.tensor(x))], oracle_mod)
+    close_rows(g.reshape(g.shape[0] * g.shape[1], -1), r.reshape(r.shape[0] * r.shape[1], -1), RTOL_GEMM_TF32X3)
+
+
+def test_conv_bn_relu_pool_stack(cuda_executor, oracle_mod, rng):
+    x = pf.tensor(rng.random((2, 3, 40, 40)).astype(np.float32))
+    conv = nn.Conv2d(3, 16, 7, 2, 3)
+    bn = nn.BatchNorm2d(16)
+    bn.eval()
+    for name, lo, hi in [("weight", 0.5, 1.5), ("bias", -0.5, 0.5), ("running_mean", -0.5, 0.5),
+                         ("running_var", 0.5, 2.0)]:
+        bn.set_parameter(name, rng.uniform(lo, hi, 16).astype(np.float32))
+    pool = nn.MaxPool2d(3, 2)
+    out = pool(pf.relu(bn(conv(x))))
+    gap = nn.AdaptiveAvgPool2d(1)(out)
+    avg = nn.AvgPool2d(2)(out)
+    gpu, ref = run(cuda_executor, [out, gap, avg], oracle_mod)
+    for g, r in zip(gpu, ref):
+        close_rows(g.reshape(-1, g.shape[-1] * g.shape[-2]), r.reshape(-1, r.shape[-1] * r.shape[-2]),
+                   RTOL_GEMM_TF32X3)
+
+
+def test_batchnorm_alone_and_pools(cuda_executor, oracle_mod, rng):
+    x = pf.tensor(rng.standard_normal((3, 4, 9, 7)).astype(np.float32))
+    bn = nn.BatchNorm2d(4)
+    bn.set_parameter("running_var", rng.uniform(0.5, 2, 4).astype(np.float32))
+    outs = [bn(x), nn.MaxPool2d(2, 2, 1)(x), nn.AvgPool2d(3, 2, 1)(x), nn.AdaptiveAvgPool2d((2, 3))(x)]
+    gpu, ref = run(cuda_executor, outs, oracle_mod)
+    close(gpu[0], ref[0], rtol=1e-5, atol=1e-6)
+    bitexact(gpu[1], ref[1])
+    close(gpu[2], ref[2], rtol=1e-6, atol=1e-7)
+    close(gpu[3], ref[3], rtol=1e-6, atol=1e-7)
+
+
+# ---- attention / encoder block ---------------------------------------------------------
+
+def test_multihead_attention(cuda_executor, oracle_mod, rng):
+    x = pf.tensor(rng.standard_normal((2, 9, 16)).astype(np.float32))
+    mha = nn.MultiheadAttention(16, 2, batch_first=True)
+    for name, p in list(mha.named_parameters()):
+        mha.set_parameter(name, (rng.standard_normal(p.shape) * 0.3).astype(np.float32))
+    (g,), (r,) = run(cuda_executor, [mha(x)], oracle_mod)
+    close_rows(g, r, RTOL_GEMM_TF32X3, what="mha")
+
+
+def test_encoder_block_small(cuda_executor, oracle_mod):
+    from pyflame_b200 import workloads
+    w = workloads.encoder(batch=2, seq=16, d=64, heads=4, ff=256)
+    (g,), (r,) = run(cuda_executor, w.outputs, oracle_mod)
+    close_rows(g, r, RTOL_GEMM_TF32X3, what="encoder")
+
+
+def test_gemm_chain_small(cuda_executor, oracle_mod):
+    from pyflame_b200 import workloads
+    w = workloads.gemm_chain(rows=64, d=512, h=1024)
+    (g,), (r,) = run(cuda_executor, w.outputs, oracle_mod)
+    close_rows(g, r, RTOL_GEMM_TF32X3, what="gemm chain")
+
+
+def test_convstack_small(cuda_executor, oracle_mod):
+    from pyflame_b200 import workloads
+    w = workloads.convstack(batch=2, hw=64)
+    (g,), (r,) = run(cuda_executor, w.outputs, oracle_mod)
+    close_rows(g, r, RTOL_GEMM_TF32X3, what="convstack")
+
+
+# ---- executor behaviour --------------------------------------------------------------------
+
+def test_repeat_execution_uses_cached_plan(cuda_executor, oracle_mod, rng):
+    x = pf.tensor(rng.standard_normal((64, 128)).astype(np.float32))
+    out = pf.softmax(pf.relu(x) * 2.0, -1)
+    g = out.graph()
+    r1 = cuda_executor.execute(g, [out.node().id()])
+    r2 = cuda_executor.execute(g, [out.node().id()])
+    r3 = cuda_executor.execute(g, [out.node().id()])
+    assert r1.success and r2.success and r3.success
+    bitexact(r1.outputs[out.node().id()], r2.outputs[out.node().id()])
+    bitexact(r1.outputs[out.node().id()], r3.outputs[out.node().id()])
+    assert r3.compile_time_ms < 1000.0
+
+
+def test_errors_do_not_raise(cuda_executor):
+    a = pf.tensor(np.ones((4, 4), np.float32))
+    g = a.graph()
+    bad = g.create_op(pf.OpType.CONV3D, [a.node()], pf.TensorSpec([4, 4]))
+    res = cuda_executor.execute(g, [bad.id()])
+    assert not res.success and "Unsupported" in res.error_message
+    res = cuda_executor.execute(g, [123456])
+    assert not res.success
+    # the executor stays usable
+    ok = cuda_executor.execute(g, [pf.relu(a).node().id()])
+    assert ok.success
+
+
+def test_executor_boundary_dispatch():
+    ex = pf.Executor(pf.ExecutorConfig(backend=pf.Backend.CUDA))
+    a = pf.tensor([1.0, -2.0, 3.0])
+    r = ex.execute(a.graph(), [pf.relu(a).node().id()])
+    assert r.success
+    np.testing.assert_array_equal(list(r.outputs.values())[0], [1, 0, 3])
+    assert not pf.Executor(pf.ExecutorConfig(backend=pf.Backend.SIMULATOR)).execute(a.graph(), []).success
+
+
+def test_tensor_api_eval_numpy():
+    pf.set_device("cuda")
+    a = pf.tensor([[1.0, 2.0], [3.0, 4.0]])
+    b = pf.tensor([[5.0, 6.0], [7.0, 8.0]])
+    np.testing.assert_allclose(pf.matmul(a, b).numpy(), [[19, 22], [43, 50]], rtol=1e-6)
+    np.testing.assert_allclose((a * 2.0 + 1.0).numpy(), [[3, 5], [7, 9]])
+    info = pf.device_info()
+    assert info["type"] == "cuda" and info["compute_units"] > 0
+
+
+def test_device_resident_execution(cuda_executor, oracle_mod):
+    import torch
+    from pyflame_b200 import workloads
+    w = workloads.fused(64, 512)
+    g = w.outputs[0].graph()
+    ids = [t.node().id() for t in w.outputs]
+    xd = torch.from_numpy(w.inputs["x"].node().constant_data().copy()).cuda()
+    yd = torch.from_numpy(w.inputs["y"].node().constant_data().copy()).cuda()
+    outs = [torch.empty(t.shape, device="cuda") for t in w.outputs]
+    for _ in range(3):
+        cuda_executor.execute_device(g, {w.inputs["x"].node().id(): xd.data_ptr(),
+                                         w.inputs["y"].node().id(): yd.data_ptr()}, ids,
+                                     [o.data_ptr() for o in outs])
+    torch.cuda.synchronize()
+    ref = oracle_mod.run(g, ids)
+    bitexact(outs[2].cpu().numpy(), ref[ids[2]])
+    close_rows(outs[3].cpu().numpy(), ref[ids[3]], 1e-5)
+
+
+def test_memory_stats_and_release(cuda_executor):
+    s = cuda_executor.get_memory_stats()
+    assert s.total_allocations >= 1
+    info = cuda_executor.get_device_info()
+    assert info.architecture.startswith("sm_10")
