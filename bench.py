@@ -44,7 +44,7 @@ FULL = {
 }
 # CPU-baseline samples (bounded, seconds of CPU work)
 CPU_SAMPLE = {
-    "fused": dict(rows=512, cols=4096),
+    "fused": dict(rows=8192, cols=4096),
     "mlp": dict(batch=64),
     "gemm_chain": dict(rows=16),
     "encoder": dict(batch=1, seq=512),
@@ -82,7 +82,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -93,6 +93,13 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+
+    def wait_first_sample(self, timeout: float = 5.0):
+        """nvidia-smi needs a moment to start; begin timing once it samples."""
+        t0 = time.time()
+        while self.proc and not self.lines and time.time() - t0 < timeout:
+            time.sleep(0.02)
+        self.n0 = len(self.lines)
 
     def __exit__(self, *exc):
         if self.proc:
@@ -106,7 +113,7 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[getattr(self, "n0", 0):]:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -179,12 +186,15 @@ def run_ours(args):
         keep.append(d)
         bind[nid] = d.data_ptr()
     outs = [torch.empty(t.shape, dtype=torch.float32, device="cuda") for t in w.outputs]
-    stream = torch.cuda.current_stream()
+    # a dedicated stream: the executor runs its work on it and the events are recorded on it
+    stream = torch.cuda.Stream()
     sp = stream.cuda_stream
+    assert sp != 0
 
     def step():
         return ex.execute_device(g, bind, out_ids, [o.data_ptr() for o in outs], stream=sp)
 
+    torch.cuda.synchronize()  # inputs and weights were uploaded on the default stream
     for _ in range(max(args.warmup, 3)):
         r = step()
     torch.cuda.synchronize()
@@ -194,6 +204,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     with ClockSampler(local) as clk:
+        clk.wait_first_sample()
         ev[0].record(stream)
         for i in range(args.steps):
             step()
@@ -246,17 +257,23 @@ def run_ours(args):
         pk, pk_kind = peaks()
         total_kernel_ms = sum(ms for _, ms in kernels) or 1e-9
         top = max(kernels, key=lambda k: k[1]) if kernels else ("", 0.0)
-        # algorithmic work of the dominant kernel per launch
+        # Algorithmic work of the dominant kernel(s) per step divided by their
+        # average duration in the timed region: the per-step time measured with
+        # CUDA events on the launching stream, apportioned by each kernel's
+        # share of device time in a profiled step of the same plan.
         if w.flops:
             bound, unit = "tensor", "TFLOP/s"
             gemm_ms = sum(ms for name, ms in kernels if name.startswith("gemm") or name.startswith("conv gemm"))
-            achieved = w.flops / (gemm_ms / 1e3) / 1e12 if gemm_ms else 0.0
-            peak = pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+            dom_ms = ms_per_step * gemm_ms / total_kernel_ms
+            achieved = w.flops / (dom_ms / 1e3) / 1e12 if gemm_ms else 0.0
+            # kernels run inside a long loop: the sustained GEMM figure
+            peak = pk.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
             if args.precision == "tf32x3":
                 peak = peak / 2.0 / 3.0  # tf32 is half the bf16 rate; three products per output term
         else:
             bound, unit = "hbm", "GB/s"
-            achieved = w.bytes / (top[1] / 1e3) / 1e9 if top[1] else 0.0
+            dom_ms = ms_per_step * top[1] / total_kernel_ms
+            achieved = w.bytes / (dom_ms / 1e3) / 1e9 if top[1] else 0.0
             peak = pk.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
         traffic = None
         tf = ROOT / "profiles" / f"{args.workload}_traffic.json"
@@ -275,7 +292,8 @@ def run_ours(args):
             "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                          "frac": achieved / peak if peak else None, "traffic": traffic,
                          "peak_source": f"{pk_kind}" + (" (bf16/2/3 for 3xTF32)" if bound == "tensor" else ""),
-                         "kernel": top[0], "kernel_ms": top[1], "kernel_share": top[1] / total_kernel_ms},
+                         "kernel": top[0], "kernel_avg_ms_timed": dom_ms, "kernel_ms_profiled_once": top[1],
+                         "kernel_share": top[1] / total_kernel_ms},
             "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
             "gpu_launches": launches_per_step * args.steps,
             "kernels": [{"name": n, "ms": round(ms, 4)} for n, ms in kernels],
@@ -394,7 +412,8 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default: about 2 s of device time for the workload)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="fused", choices=sorted(FULL))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -402,6 +421,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer measurement")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = {"fused": 20000, "mlp": 20000, "gemm_chain": 200, "encoder": 100, "convstack": 100}[
+            args.workload] if args.impl == "ours" else 5
     if args.impl == "reference":
         run_reference(args)
     else:

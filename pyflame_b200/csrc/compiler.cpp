@@ -203,6 +203,47 @@ __device__ __forceinline__ float pf_max(float a, float b) { return fmaxf(a, b); 
 __device__ __forceinline__ float pf_min(float a, float b) { return fminf(a, b); }
 )";
 
+// Helpers for kernels that stream rows into shared memory with 1-D TMA bulk
+// copies completing on mbarriers.  Waits are bounded by the global timer: on
+// expiry the kernel records PFC_ERR_TIMEOUT (-8) in *err and carries on
+// without blocking.
+const char* kTmaPrelude = R"(
+__device__ __forceinline__ unsigned pf_smem(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void pf_mbar_init(unsigned a, unsigned n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(a), "r"(n) : "memory");
+}
+__device__ __forceinline__ void pf_expect_tx(unsigned a, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(a), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void pf_bulk_load(unsigned dst, const void* src, unsigned bytes, unsigned bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               :: "r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+__device__ __forceinline__ bool pf_mbar_try(unsigned a, unsigned parity) {
+  unsigned ok;
+  asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+               : "=r"(ok) : "r"(a), "r"(parity) : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ unsigned long long pf_gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ bool pf_mbar_wait(unsigned a, unsigned parity, int* err) {
+  if (pf_mbar_try(a, parity)) return true;
+  const unsigned long long t0 = pf_gtimer();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (pf_mbar_try(a, parity)) return true;
+    if (*(volatile int*)err != 0 || pf_gtimer() - t0 > 2000000000ull) {
+      atomicCAS(err, 0, -8);
+      return false;
+    }
+  }
+}
+)";
+
 std::string flit(float f) {
   if (std::isnan(f)) return "PF_NAN";
   if (std::isinf(f)) return f > 0 ? "PF_INF" : "(-PF_INF)";
@@ -496,7 +537,8 @@ struct RowLayout {
   bool reg_mode = true;
 };
 
-std::string gen_row(const RowSpec& rs, const std::string& name, int num_sms, int* grid, int* block) {
+std::string gen_row(const RowSpec& rs, const std::string& name, int num_sms, int* grid, int* block,
+                    size_t* smem_bytes) {
   const EwSpec& s = rs.ew;
   std::vector<int64_t> outer_sz(s.space.begin(), s.space.begin() + rs.red_begin);
   std::vector<int64_t> red_sz(s.space.begin() + rs.red_begin, s.space.begin() + rs.red_end);
@@ -529,8 +571,10 @@ std::string gen_row(const RowSpec& rs, const std::string& name, int num_sms, int
     }
   }
   int64_t nvec = ceil_div(L.C, L.vec);
+  // threads per row: about two vector chunks per thread (more warps per SM to
+  // hide the latency of the transcendental and reduction chains)
   int tpr = 32;
-  while (tpr < 1024 && (int64_t)tpr * 4 < nvec) tpr *= 2;
+  while (tpr < 1024 && (int64_t)tpr * 2 < nvec) tpr *= 2;
   L.tpr = tpr;
   L.block = std::max(256, tpr);
   L.rpb = L.block / tpr;
@@ -544,12 +588,40 @@ std::string gen_row(const RowSpec& rs, const std::string& name, int num_sms, int
   L.reg_mode = (int64_t)L.nch * L.vec * std::max(1, nsrc) <= 64;
   bool i32 = fits_i32(rd, 0) && fits_i32(cd, 0) && L.R * L.C < (int64_t)INT32_MAX / 2;
   const char* ity = i32 ? "int" : "long long";
+  size_t nl = s.loads.size(), ns = s.stores.size();
+
+  // TMA row streaming: when every per-row input is a contiguous, 16-byte
+  // aligned row, a ring of shared-memory stages is filled with 1-D bulk copies
+  // for the rows ahead while the CTA computes the current one.  Inputs that
+  // do not vary by row (LayerNorm gamma/beta) stay ordinary loads.
+  std::vector<int> tma_slot(nl, -1);
+  int n_tma = 0;
+  bool tma = L.reg_mode && L.rpb == 1 && L.vec == 4 && ncd == 1 && (L.C * 4) % 16 == 0;
+  for (size_t i = 0; i < nl && tma; ++i) {
+    const View& lv = s.loads[i];
+    if (lv.is_splat) continue;
+    bool row_const = true;
+    for (size_t k = 0; k < nrd; ++k) row_const = row_const && rd.stride[i][k] == 0;
+    if (row_const) continue;
+    bool contiguous = cd.stride[i][0] == 1 && lv.offset % 4 == 0 && lv.dtype == DType::F32;
+    for (size_t k = 0; k < nrd; ++k) contiguous = contiguous && rd.stride[i][k] % 4 == 0;
+    if (!contiguous) tma = false;
+    else tma_slot[i] = n_tma++;
+  }
+  const int64_t stage_bytes = (int64_t)n_tma * L.C * 4;
+  int stages = 0;
+  if (tma && n_tma > 0 && stage_bytes * 2 <= 110 * 1024) {
+    stages = (int)std::min<int64_t>(4, (110 * 1024) / stage_bytes);
+  } else {
+    tma = false;
+  }
+  *smem_bytes = tma ? (size_t)(stages * stage_bytes + 64) : 0;
 
   // which instructions feed the row ops / stores; all are computed per element
   std::ostringstream o;
   o << kPrelude;
+  if (tma) o << kTmaPrelude;
   o << "extern \"C\" __global__ void __launch_bounds__(" << L.block << ") " << name << "(const PfArgs A) {\n";
-  size_t nl = s.loads.size(), ns = s.stores.size();
   for (size_t i = 0; i < nl; ++i) {
     if (s.loads[i].is_splat) continue;
     o << "  const float* __restrict__ in" << i << " = (const float*)A.p[" << i << "];\n";
@@ -564,6 +636,28 @@ std::string gen_row(const RowSpec& rs, const std::string& name, int num_sms, int
   o << "  const int tid = threadIdx.x;\n  const int lr = tid % " << TPR << ";\n  const int rib = tid / " << TPR
     << ";\n";
   if (TPR > 32) o << "  __shared__ float red[" << L.block / 32 << "][8];\n";
+  if (tma) {
+    o << "  int* err = (int*)A.p[" << nl + ns + rs.ops.size() + 1 << "];\n";
+    o << "  extern __shared__ __align__(128) unsigned char pf_dyn[];\n";
+    o << "  float* stg = (float*)pf_dyn;\n";
+    o << "  unsigned long long* bars = (unsigned long long*)(pf_dyn + " << stages * stage_bytes << ");\n";
+    // rows of this CTA: blockIdx.x, blockIdx.x + gridDim.x, ...
+    o << "  const " << ity << " nmine = (" << ity << ")blockIdx.x < (" << ity << ")" << L.R << " ? ((" << ity << ")"
+      << L.R << " - 1 - blockIdx.x) / gridDim.x + 1 : 0;\n";
+    o << "  auto issue = [&](" << ity << " it) {\n    const " << ity << " row = (" << ity
+      << ")blockIdx.x + it * gridDim.x;\n    const int st = (int)(it % " << stages << ");\n";
+    o << "    " << emit_coords("row", rd.size, "q", ity);
+    o << "    const unsigned bar = pf_smem(&bars[st]);\n    pf_expect_tx(bar, " << stage_bytes << "u);\n";
+    for (size_t i = 0; i < nl; ++i) {
+      if (tma_slot[i] < 0) continue;
+      o << "    pf_bulk_load(pf_smem(stg + (size_t)st * " << stage_bytes / 4 << " + " << tma_slot[i] * L.C
+        << "), in" << i << " + (" << emit_offset(rd.stride[i], "q", nrd, 0, ity) << "), " << L.C * 4 << "u, bar);\n";
+    }
+    o << "  };\n";
+    o << "  if (tid == 0) {\n    for (int s2 = 0; s2 < " << stages << "; ++s2) pf_mbar_init(pf_smem(&bars[s2]), 1);\n"
+      << "    asm volatile(\"fence.mbarrier_init.release.cluster;\" ::: \"memory\");\n  }\n  __syncthreads();\n";
+    o << "  if (tid == 0)\n    for (" << ity << " it = 0; it < nmine && it < " << stages << "; ++it) issue(it);\n";
+  }
   // reduction helpers over the TPR threads of a row
   auto reduce = [&](const std::string& var, const std::string& combine, int slot) {
     std::ostringstream r;
@@ -578,9 +672,16 @@ std::string gen_row(const RowSpec& rs, const std::string& name, int num_sms, int
     }
     return r.str();
   };
-  o << "  for (" << ity << " rbase = (" << ity << ")blockIdx.x * " << RPB << "; rbase < (" << ity << ")" << L.R
-    << "; rbase += (" << ity << ")gridDim.x * " << RPB << ") {\n";
-  o << "    const " << ity << " row = rbase + rib;\n    const bool rv = row < (" << ity << ")" << L.R << ";\n";
+  if (tma) {
+    o << "  for (" << ity << " it = 0; it < nmine; ++it) {\n    const " << ity << " row = (" << ity
+      << ")blockIdx.x + it * gridDim.x;\n    const bool rv = true;\n    const int st = (int)(it % " << stages
+      << ");\n    pf_mbar_wait(pf_smem(&bars[st]), (unsigned)((it / " << stages << ") & 1), err);\n"
+      << "    const float* stgp = stg + (size_t)st * " << stage_bytes / 4 << ";\n";
+  } else {
+    o << "  for (" << ity << " rbase = (" << ity << ")blockIdx.x * " << RPB << "; rbase < (" << ity << ")" << L.R
+      << "; rbase += (" << ity << ")gridDim.x * " << RPB << ") {\n";
+    o << "    const " << ity << " row = rbase + rib;\n    const bool rv = row < (" << ity << ")" << L.R << ";\n";
+  }
   o << "    " << emit_coords("(rv ? row : (" + std::string(ity) + ")0)", rd.size, "r", ity);
   // per-view row offsets
   for (size_t v = 0; v < views.size(); ++v)
@@ -619,8 +720,12 @@ std::string gen_row(const RowSpec& rs, const std::string& name, int num_sms, int
         continue;
       }
       const auto& st = cd.stride[i];
-      e << "      float l" << i << "[" << VEC << "];\n      if (cok) { const float* ptr = in" << i << " + ro_" << i
-        << " + (" << emit_offset(st, "k", ncd, 0, ity) << ");\n";
+      if (tma_slot[i] >= 0)  // staged in shared memory by the bulk copy of this row
+        e << "      float l" << i << "[" << VEC << "];\n      if (cok) { const float* ptr = stgp + "
+          << tma_slot[i] * L.C << " + (" << emit_offset(st, "k", ncd, 0, ity) << ");\n";
+      else
+        e << "      float l" << i << "[" << VEC << "];\n      if (cok) { const float* ptr = in" << i << " + ro_" << i
+          << " + (" << emit_offset(st, "k", ncd, 0, ity) << ");\n";
       if (VEC == 4 && st.back() == 1)
         e << "        float4 t = *(const float4*)ptr; l" << i << "[0]=t.x; l" << i << "[1]=t.y; l" << i
           << "[2]=t.z; l" << i << "[3]=t.w; }\n";
@@ -702,12 +807,46 @@ std::string gen_row(const RowSpec& rs, const std::string& name, int num_sms, int
     o << "      }\n";
   }
   o << "    }\n";
-  int slot = 0;
-  for (size_t si = 0; si < srcs.size(); ++si) {
-    if (need_sum.count(si)) o << reduce("s_sum" + std::to_string(si), "s_sum" + std::to_string(si) + " + ot", slot++ % 8);
-    if (need_max.count(si)) o << reduce("s_max" + std::to_string(si), "fmaxf(s_max" + std::to_string(si) + ", ot)", slot++ % 8);
-    if (need_min.count(si)) o << reduce("s_min" + std::to_string(si), "fminf(s_min" + std::to_string(si) + ", ot)", slot++ % 8);
-    if (need_prod.count(si)) o << reduce("s_prod" + std::to_string(si), "s_prod" + std::to_string(si) + " * ot", slot++ % 8);
+  // One reduction round for several statistics: warp shuffles, then (rows
+  // wider than a warp) one shared-memory exchange between two barriers.
+  // `between` is emitted after the first barrier, when every thread of the
+  // CTA has finished the pass that precedes the round.
+  auto reduce_round = [&](const std::vector<std::pair<std::string, std::string>>& vals, const std::string& between) {
+    std::ostringstream r;
+    for (auto& [v, comb] : vals)
+      r << "    for (int off = 16; off > 0; off >>= 1) { float ot = __shfl_xor_sync(0xffffffffu, " << v
+        << ", off); " << v << " = " << comb << "; }\n";
+    if (TPR > 32) {
+      const int wpr = TPR / 32;
+      r << "    __syncthreads();\n" << between;
+      r << "    if ((tid & 31) == 0) {\n";
+      for (size_t k = 0; k < vals.size(); ++k) r << "      red[tid >> 5][" << k << "] = " << vals[k].first << ";\n";
+      r << "    }\n    __syncthreads();\n    { const int w0 = rib * " << wpr << ";\n";
+      for (size_t k = 0; k < vals.size(); ++k)
+        r << "      " << vals[k].first << " = red[w0][" << k << "];\n      for (int w = 1; w < " << wpr
+          << "; ++w) { float ot = red[w0 + w][" << k << "]; " << vals[k].first << " = " << vals[k].second
+          << "; }\n";
+      r << "    }\n";
+    } else {
+      r << between;
+    }
+    return r.str();
+  };
+  (void)reduce;
+  {
+    std::vector<std::pair<std::string, std::string>> round1;
+    for (size_t si = 0; si < srcs.size(); ++si) {
+      std::string i = std::to_string(si);
+      if (need_sum.count(si)) round1.push_back({"s_sum" + i, "s_sum" + i + " + ot"});
+      if (need_max.count(si)) round1.push_back({"s_max" + i, "fmaxf(s_max" + i + ", ot)"});
+      if (need_min.count(si)) round1.push_back({"s_min" + i, "fminf(s_min" + i + ", ot)"});
+      if (need_prod.count(si)) round1.push_back({"s_prod" + i, "s_prod" + i + " * ot"});
+    }
+    if (round1.size() > 8) fail(PFC_ERR_UNSUPPORTED, "row group with more than 8 statistics");
+    std::string refill = tma ? "    if (tid == 0 && it + " + std::to_string(stages) + " < nmine) issue(it + " +
+                                   std::to_string(stages) + ");\n"
+                             : "";
+    o << reduce_round(round1, refill);
   }
   // pass 2: variance / sum of exp (need pass-1 stats)
   bool need_pass2 = !need_var.empty() || !need_sexp.empty();
@@ -728,10 +867,14 @@ std::string gen_row(const RowSpec& rs, const std::string& name, int num_sms, int
       o << "      }\n";
     }
     o << "    }\n";
+    std::vector<std::pair<std::string, std::string>> round2;
     for (size_t si = 0; si < srcs.size(); ++si) {
-      if (need_var.count(si)) o << reduce("s_var" + std::to_string(si), "s_var" + std::to_string(si) + " + ot", slot++ % 8);
-      if (need_sexp.count(si)) o << reduce("s_sexp" + std::to_string(si), "s_sexp" + std::to_string(si) + " + ot", slot++ % 8);
+      std::string i = std::to_string(si);
+      if (need_var.count(si)) round2.push_back({"s_var" + i, "s_var" + i + " + ot"});
+      if (need_sexp.count(si)) round2.push_back({"s_sexp" + i, "s_sexp" + i + " + ot"});
     }
+    if (round2.size() > 8) fail(PFC_ERR_UNSUPPORTED, "row group with more than 8 statistics");
+    o << reduce_round(round2, "");
   }
   // per-row outputs
   bool any_row_out = false;
@@ -1194,7 +1337,7 @@ class Compiler {
   void lower_concat(uint64_t id);
   View materialize_copy(const View& src, int at, const std::string& label);
   void emit_jit(int at, const std::string& label, const std::string& kernel, const std::string& source, int grid,
-                int block, const std::vector<std::pair<int, int64_t>>& ptrs);
+                int block, const std::vector<std::pair<int, int64_t>>& ptrs, size_t smem = 0);
   void finish();
 
   bool must_materialize(uint64_t id);
@@ -1515,7 +1658,7 @@ bool Compiler::must_materialize(uint64_t id) {
 }
 
 void Compiler::emit_jit(int at, const std::string& label, const std::string& kernel, const std::string& source,
-                        int grid, int block, const std::vector<std::pair<int, int64_t>>& ptrs) {
+                        int grid, int block, const std::vector<std::pair<int, int64_t>>& ptrs, size_t smem) {
   Step s;
   s.kind = StepKind::JIT;
   s.label = label;
@@ -1528,6 +1671,7 @@ void Compiler::emit_jit(int at, const std::string& label, const std::string& ker
   s.jit.kernel = "pf_kernel";
   s.jit.grid = grid;
   s.jit.block = block;
+  s.jit.smem = smem;
   s.jit.ptrs = ptrs;
   (*src_)[s.jit.module_key] = {canon, "pf_kernel"};
   add_step(at, std::move(s));
@@ -1808,11 +1952,13 @@ void Compiler::lower_region(int r) {
   }
   std::string name = kname(inner == 1 ? "row" : "col");
   int grid, block;
-  std::string code = inner == 1 ? gen_row(rs, name, in_.num_sms, &grid, &block)
+  size_t smem = 0;
+  std::string code = inner == 1 ? gen_row(rs, name, in_.num_sms, &grid, &block, &smem)
                                  : gen_col(rs, name, in_.num_sms, &grid, &block);
   (void)outer;
+  ptrs.push_back({kErrorFlagBuffer, 0});
   emit_jit(at, std::string(inner == 1 ? "row kernel (" : "column kernel (") + label + ") " + shape_str(s.space), name,
-           code, grid, block, ptrs);
+           code, grid, block, ptrs, smem);
 }
 
 void Compiler::lower_row_alone(uint64_t id) {
@@ -1887,11 +2033,13 @@ void Compiler::lower_row_alone(uint64_t id) {
   }
   std::string name = kname(inner == 1 ? "row" : "col");
   int grid, block;
-  std::string code = inner == 1 ? gen_row(rs, name, in_.num_sms, &grid, &block)
+  size_t smem = 0;
+  std::string code = inner == 1 ? gen_row(rs, name, in_.num_sms, &grid, &block, &smem)
                                  : gen_col(rs, name, in_.num_sms, &grid, &block);
+  ptrs.push_back({kErrorFlagBuffer, 0});
   emit_jit(pos_[id], std::string(inner == 1 ? "row kernel (" : "column kernel (") + op_name(n.op) + ") " +
                          shape_str(s.space),
-           name, code, grid, block, ptrs);
+           name, code, grid, block, ptrs, smem);
 }
 
 // Collapse the batch dims [0, nb) of a view to one stride; false if impossible.

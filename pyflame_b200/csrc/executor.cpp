@@ -217,10 +217,24 @@ CudaExecutor::PlanEntry& CudaExecutor::prepare(Graph& g, const std::vector<uint6
     pe.plan->key = key;
     pe.kernels.resize(pe.plan->steps.size(), nullptr);
     for (size_t i = 0; i < pe.plan->steps.size(); ++i) {
-      const Step& s = pe.plan->steps[i];
+      Step& s = pe.plan->steps[i];
       if (s.kind != StepKind::JIT) continue;
       const auto& src = sources.at(s.jit.module_key);
-      pe.kernels[i] = global_jit().get(s.jit.module_key, src.first, s.jit.kernel);
+      cudaKernel_t k = global_jit().get(s.jit.module_key, src.first, s.jit.kernel);
+      pe.kernels[i] = k;
+      if (s.jit.smem > 48 * 1024)
+        PFB_CUDA(cudaKernelSetAttributeForDevice(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s.jit.smem,
+                                                 cfg_.device_id));
+      // every generated kernel strides over its work: launch exactly the CTAs
+      // that fit on the device at once (no partial second wave)
+      int per_sm = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, (const void*)k, s.jit.block, s.jit.smem) ==
+              cudaSuccess &&
+          per_sm > 0) {
+        s.jit.grid = std::max(1, std::min(s.jit.grid, per_sm * num_sms_));
+      } else {
+        cudaGetLastError();
+      }
     }
     if (pe.plan->arena_bytes) pe.arena = pool_->allocate(pe.plan->arena_bytes, stream_);
     it = plans_.emplace(key, std::move(pe)).first;
@@ -275,6 +289,7 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
   const Plan& P = *pe.plan;
   const Step& st = P.steps[i];
   auto bufp = [&](int buf, int64_t byte_off) -> void* {
+    if (buf == kErrorFlagBuffer) return err_dev_;
     if (buf < 0) return nullptr;
     return (char*)ptrs[buf] + byte_off;
   };

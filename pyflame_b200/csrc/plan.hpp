@@ -59,6 +59,10 @@ enum class StepKind : uint8_t {
   MEMSET,     // zero a buffer range
 };
 
+// Pointer-argument buffer index that resolves to the executor's device error
+// flag (bounded waits record PFC_ERR_TIMEOUT there).
+constexpr int kErrorFlagBuffer = -2;
+
 struct JitLaunch {
   std::string module_key;  // hash of the generated source
   std::string kernel;      // kernel symbol

@@ -179,7 +179,7 @@ def test_fused_graph(cuda_executor, oracle_mod, rows, cols):
     zabs = np.abs(list(zz.values())[0]).sum(1)
     close_sum(gpu[0], ref[0], zabs, what="sum")
     close_sum(gpu[1], ref[1], zabs / cols, what="mean")
-    bitexact(gpu[2], ref[2])
+    close(gpu[2], ref[2], rtol=1e-5, atol=1e-6, what="max")  # selection of z, which carries ulp-level exp differences
     close_rows(gpu[3], ref[3], 1e-5, what="layernorm")
     assert z.shape == (rows, cols) and x.shape == y.shape
 
