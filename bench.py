@@ -60,6 +60,19 @@ def peaks():
     return FALLBACK_PEAKS, "fallback"
 
 
+def profiled_traffic(workload):
+    """DRAM bytes (read + write) per launch of the workload's dominant kernel,
+    from the ncu summaries kept under profiles/ (a line
+    `traffic_per_launch_bytes[<workload>] = <bytes>`), or None."""
+    import re
+    pat = re.compile(r"traffic_per_launch_bytes\[(\w+)\]\s*=\s*(\d+)")
+    for f in sorted((ROOT / "profiles").glob("*.md")):
+        for m in pat.finditer(f.read_text()):
+            if m.group(1) == workload:
+                return int(m.group(2))
+    return None
+
+
 def ensure_built():
     from pyflame_b200 import _native
     if not _native.LIB_PATH.exists():
@@ -275,10 +288,7 @@ def run_ours(args):
             dom_ms = ms_per_step * top[1] / total_kernel_ms
             achieved = w.bytes / (dom_ms / 1e3) / 1e9 if top[1] else 0.0
             peak = pk.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
-        traffic = None
-        tf = ROOT / "profiles" / f"{args.workload}_traffic.json"
-        if tf.exists():
-            traffic = json.loads(tf.read_text()).get("bytes_per_launch")
+        traffic = profiled_traffic(args.workload)
         cpu = cpu_baseline(args.workload) if (world == 1 and not args.no_cpu) else None
         line = {
             "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
@@ -420,7 +430,15 @@ def main():
     ap.add_argument("--precision", default="tf32x3", choices=["tf32x3", "bf16"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer measurement")
+    ap.add_argument("--size", action="append", default=[], metavar="KEY=INT",
+                    help="override a workload size (e.g. rows=1024) for small profiling runs; "
+                         "the default sizes are the benchmark configuration")
     args = ap.parse_args()
+    for kv in args.size:
+        k, v = kv.split("=")
+        if k not in FULL[args.workload]:
+            ap.error(f"{args.workload} has no size '{k}' (sizes: {', '.join(FULL[args.workload])})")
+        FULL[args.workload][k] = int(v)
     if args.steps is None:
         args.steps = {"fused": 20000, "mlp": 20000, "gemm_chain": 200, "encoder": 100, "convstack": 100}[
             args.workload] if args.impl == "ours" else 5
