@@ -300,6 +300,21 @@ typedef struct pfk_pool_params {
 } pfk_pool_params;
 PFC_API int pfk_pool2d(const float* x, float* y, const pfk_pool_params* p, void* stream);
 
+/* C[M,N] = A[M,K] @ B[K,N] (fp32, row-major; MATMUL as matmul.cpp:12-31) on
+ * the 3xTF32 tcgen05 GEMM, allocating nothing: the split operands and the
+ * wait-timeout flag live in a fixed 64 MiB device array inside the library
+ * (one per device), for hosts that cannot grant the library device memory or
+ * must not call cudaMalloc/cudaFree on this path.  No counterpart in the
+ * reference (its kernels take caller-allocated buffers, rocm_kernels.hip:740-806).
+ * Needs 256 + 2*ru(4*M*Kp) + 2*ru(4*N*Kp) bytes, Kp = K rounded up to 32,
+ * ru = round up to 256; larger problems return PFC_ERR_INVALID_ARGUMENT.
+ * All calls share the array, so overlapping calls race: serialise them (one
+ * stream).  The first call on a device sets up the array's address; make it
+ * before any stream capture begins.  `err`: optional device int receiving the
+ * kernel's wait-timeout code (0 = none) in stream order. */
+PFC_API int pfk_matmul_tf32x3_static(const float* a, const float* b, float* c, int64_t M, int64_t N,
+                                     int64_t K, int* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
