@@ -224,6 +224,18 @@ PFC_API int pfc_executor_get_device_info(pfc_executor* ex, pfc_device_info* info
 PFC_API int pfc_executor_get_memory_stats(pfc_executor* ex, pfc_memory_stats* stats);
 /* Drop every resident constant and compiled plan. */
 PFC_API int pfc_executor_release_constants(pfc_executor* ex);
+/* Use caller-owned device memory as the resident copy of every constant
+ * whose payload key is `cache_key` and whose size is `bytes` (the pair given
+ * to pfc_graph_set_constant with PFC_CONST_RESIDENT), instead of uploading
+ * the host payload.  For weights that arrive on the device by other means,
+ * e.g. broadcast from rank 0 over NCCL.  The executor reads the memory and
+ * never writes or frees it; it must stay valid and unchanged until
+ * pfc_executor_release_constants or pfc_executor_destroy.  Tensor-core
+ * operands derived from earlier contents are rebuilt on next use.  No
+ * counterpart in the reference (ROCmExecutor re-uploads constants on every
+ * call, rocm_executor.cpp:93-103). */
+PFC_API int pfc_executor_set_resident(pfc_executor* ex, uint64_t cache_key, const void* dev_ptr,
+                                      size_t bytes);
 /* Human-readable description of the compiled plan for (g, output_ids):
  * kernels, fusion groups and buffers.  Writes a NUL-terminated string. */
 PFC_API int pfc_executor_describe_plan(pfc_executor* ex, pfc_graph* g, const uint64_t* output_ids,

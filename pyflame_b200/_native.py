@@ -91,6 +91,7 @@ SIGNATURES = {
     "pfc_executor_get_device_info": (C.c_int, [_P, C.POINTER(DeviceInfo)]),
     "pfc_executor_get_memory_stats": (C.c_int, [_P, C.POINTER(MemoryStatsC)]),
     "pfc_executor_release_constants": (C.c_int, [_P]),
+    "pfc_executor_set_resident": (C.c_int, [_P, C.c_uint64, _P, C.c_size_t]),
     "pfc_executor_describe_plan": (C.c_int, [_P, _P, C.POINTER(C.c_uint64), C.c_int, C.c_char_p, C.c_size_t]),
     "pfc_compile_check": (C.c_int, [_P, C.POINTER(C.c_uint64), C.c_int, C.c_int, C.c_char_p, C.c_size_t]),
     "pfc_executor_last_profile": (C.c_int, [_P, _P, C.POINTER(C.c_double), C.c_int, C.POINTER(C.c_int)]),

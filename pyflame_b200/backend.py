@@ -312,6 +312,16 @@ class CudaExecutor:
     def release_constants(self):
         N.check(N.lib().pfc_executor_release_constants(self.handle))
 
+    def set_resident(self, node: Node, device_ptr: int):
+        """Use device memory at `device_ptr` (caller-owned, same bytes as the
+        node's payload) as the resident copy of `node`'s constant payload, e.g.
+        a weight broadcast over NCCL.  It must stay valid and unchanged while
+        this executor may run graphs holding the node."""
+        if not node.has_constant_data():
+            raise ValueError(f"node {node.id()} has no constant payload")
+        N.check(N.lib().pfc_executor_set_resident(self.handle, node._data_key, device_ptr,
+                                                  node.constant_data().nbytes))
+
     def describe_plan(self, graph: Graph, output_ids: Sequence[int]) -> str:
         output_ids = [int(i) for i in output_ids]
         ng = native_graph(graph, output_ids)

@@ -329,6 +329,13 @@ int pfc_executor_release_constants(pfc_executor* ex) {
   });
 }
 
+int pfc_executor_set_resident(pfc_executor* ex, uint64_t cache_key, const void* dev_ptr, size_t bytes) {
+  return guarded([&] {
+    PFB_CHECK_ARG(ex, "null executor");
+    ex->ex->set_resident(cache_key, dev_ptr, bytes);
+  });
+}
+
 int pfc_executor_describe_plan(pfc_executor* ex, pfc_graph* g, const uint64_t* output_ids, int n_outputs,
                                char* buf, size_t buf_len) {
   return guarded([&] {

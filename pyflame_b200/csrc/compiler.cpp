@@ -1319,6 +1319,71 @@ class Compiler {
 
   void add_step(int /*pos*/, Step s) { steps_.push_back({cur_pos_, std::move(s)}); }
 
+  // Tensor-core operand of a view: [rows][kpad] hi/lo fp32 (3xTF32) or bf16.
+  struct Operand {
+    int hi = -1, lo = -1;
+  };
+  std::unordered_map<std::string, Operand> operands_;  // view signature -> operand already in the plan
+
+  // Emit (or reuse) the preparation of `src` ([rows, cols] logical, any
+  // strides) as a GEMM operand.  Values are written once in a plan, so an
+  // identical preparation earlier in the plan is reused.  When the source is
+  // a resident constant (a weight), the operand is a PREPARED buffer that the
+  // executor keeps with the constant, and its step runs only while unfilled.
+  // conv_cp > 0: `src` is a Conv2d weight [O,C,KH,KW] laid out for the
+  // implicit GEMM (k = (kh*KW + kw)*conv_cp + c).
+  Operand prepare_operand(const View& src, int64_t rows, int64_t cols, int64_t kpad, int prec,
+                          const std::string& label, int at, int64_t conv_cp = 0) {
+    std::ostringstream sig;
+    sig << src.buf << ':' << src.offset << ':' << (int)src.dtype << ':' << src.is_splat << ':' << src.splat_slot;
+    for (size_t d = 0; d < src.shape.size(); ++d) sig << ',' << src.shape[d] << '/' << src.strides[d];
+    sig << '|' << rows << ',' << cols << ',' << kpad << ',' << prec << ',' << conv_cp;
+    auto it = operands_.find(sig.str());
+    if (it != operands_.end()) return it->second;
+    const size_t esz = prec == PFC_PRECISION_BF16 ? 2 : 4;
+    const size_t bytes = (size_t)rows * (size_t)kpad * esz;
+    bool resident = false;
+    uint64_t pkey = 0;
+    if (!src.is_splat && src.buf >= 0 && P_->buffers[src.buf].kind == BufKind::CONST) {
+      const Node& cn = N(P_->buffers[src.buf].node);
+      if (cn.data_flags & PFC_CONST_RESIDENT) {
+        resident = true;
+        // FNV-1a over (payload key, payload size, layout signature)
+        pkey = 1469598103934665603ull;
+        auto mix = [&](uint64_t v) {
+          for (int b = 0; b < 8; ++b) pkey = (pkey ^ ((v >> (8 * b)) & 0xFF)) * 1099511628211ull;
+        };
+        mix(cn.data_key);
+        mix(cn.data_bytes);
+        for (char ch : sig.str()) mix((uint64_t)(unsigned char)ch);
+      }
+    }
+    Operand op;
+    auto make = [&](int part) {
+      int b = new_buffer(bytes, resident ? BufKind::PREPARED : BufKind::ARENA,
+                         resident ? P_->buffers[src.buf].node : 0);
+      if (resident) P_->buffers[b].prep_key = pkey * 2 + (uint64_t)part;
+      return b;
+    };
+    op.hi = make(0);
+    op.lo = prec == PFC_PRECISION_BF16 ? -1 : make(1);
+    Step s;
+    s.kind = StepKind::SPLIT;
+    s.once = resident;
+    s.label = label + (resident ? " (once per weight)" : "");
+    s.split.src = src;
+    s.split.precision = prec;
+    s.split.rows = rows;
+    s.split.cols = cols;
+    s.split.kpad = kpad;
+    s.split.out_hi = op.hi;
+    s.split.out_lo = op.lo;
+    s.split.conv_cp = conv_cp;
+    add_step(at, std::move(s));
+    operands_.emplace(sig.str(), op);
+    return op;
+  }
+
   std::string kname(const char* kind) {
     return std::string("pf_") + kind + "_" + std::to_string(kernel_counter_++);
   }
@@ -2119,28 +2184,9 @@ void Compiler::lower_matmul(const GemmChain& ch, int at) {
   int64_t gbatch = b_batched ? nbatch : 1;
   int64_t gM = b_batched ? M : nbatch * M;
   // prepared operands
-  size_t esz = prec == PFC_PRECISION_BF16 ? 2 : 4;
   int64_t arows = nbatch * M, brows = (b_batched ? nbatch : 1) * Nn;
-  Step sa;
-  sa.kind = StepKind::SPLIT;
-  sa.label = "prepare A " + shape_str(afull);
-  sa.split.src = av;
-  sa.split.precision = prec;
-  sa.split.rows = arows;
-  sa.split.cols = K;
-  sa.split.kpad = kpad;
-  sa.split.out_hi = new_buffer((size_t)arows * kpad * esz);
-  sa.split.out_lo = prec == PFC_PRECISION_BF16 ? -1 : new_buffer((size_t)arows * kpad * esz);
-  Step sb;
-  sb.kind = StepKind::SPLIT;
-  sb.label = "prepare B " + shape_str(bv.shape);
-  sb.split.src = bv;
-  sb.split.precision = prec;
-  sb.split.rows = brows;
-  sb.split.cols = K;
-  sb.split.kpad = kpad;
-  sb.split.out_hi = new_buffer((size_t)brows * kpad * esz);
-  sb.split.out_lo = prec == PFC_PRECISION_BF16 ? -1 : new_buffer((size_t)brows * kpad * esz);
+  const Operand opa = prepare_operand(av, arows, K, kpad, prec, "prepare A " + shape_str(afull), at);
+  const Operand opb = prepare_operand(bv, brows, K, kpad, prec, "prepare B " + shape_str(bv.shape), at);
   // output: node shape of the chain result (same as matmul shape)
   View c = dense(mm.shape, DType::F32);
   Step sg;
@@ -2149,10 +2195,10 @@ void Compiler::lower_matmul(const GemmChain& ch, int at) {
              std::to_string(K) + "]";
   GemmArgs& G = sg.gemm;
   G.precision = prec;
-  G.a_hi = sa.split.out_hi;
-  G.a_lo = sa.split.out_lo;
-  G.b_hi = sb.split.out_hi;
-  G.b_lo = sb.split.out_lo;
+  G.a_hi = opa.hi;
+  G.a_lo = opa.lo;
+  G.b_hi = opb.hi;
+  G.b_lo = opb.lo;
   G.batch = gbatch;
   G.M = gM;
   G.N = Nn;
@@ -2204,8 +2250,6 @@ void Compiler::lower_matmul(const GemmChain& ch, int at) {
     G.r_sn = r.strides[rd - 1];
     G.has_residual = true;
   }
-  add_step(at, sa);
-  add_step(at, sb);
   add_step(at, sg);
   // result view with the chain result's shape (== mm shape)
   val_[ch.result] = c;
@@ -2229,32 +2273,26 @@ void Compiler::lower_conv(const GemmChain& ch, int at) {
   int64_t OW = (W + 2 * pd[1] - dl[1] * (KW - 1) - 1) / st[1] + 1;
   if (cv.shape != std::vector<int64_t>{Nimg, O, OH, OW}) fail(PFC_ERR_GRAPH, "CONV2D output shape mismatch");
   int prec = in_.precision;
-  int64_t K = Cin * KH * KW;
+  // Implicit GEMM: rows m = (n*OH + oh)*OW + ow, columns k = (kh*KW + kw)*Cp + c
+  // over a channels-last copy of the input with Cp channels (C rounded up to
+  // a 16-byte chunk), gathered tile by tile inside the GEMM.
+  const int64_t chunk = prec == PFC_PRECISION_BF16 ? 8 : 4;
+  const int64_t Cp = round_up(Cin, chunk);
+  int64_t K = KH * KW * Cp;
   int64_t kpad = round_up(K, prec == PFC_PRECISION_BF16 ? 64 : 32);
   size_t esz = prec == PFC_PRECISION_BF16 ? 2 : 4;
   int64_t M = Nimg * OH * OW;
   Step si;
-  si.kind = StepKind::IM2COL;
-  si.label = "im2col " + shape_str(x.shape);
-  Im2colArgs& I = si.im2col;
+  si.kind = StepKind::CONV_INPUT;
+  si.label = "conv input (channels-last) " + shape_str(x.shape);
+  ConvInputArgs& I = si.convin;
   I.x = x;
-  I.kh = KH; I.kw = KW; I.sh = st[0]; I.sw = st[1]; I.ph = pd[0]; I.pw = pd[1]; I.dh = dl[0]; I.dw = dl[1];
-  I.oh = OH; I.ow = OW; I.kpad = kpad; I.precision = prec;
-  I.out_hi = new_buffer((size_t)M * kpad * esz);
-  I.out_lo = prec == PFC_PRECISION_BF16 ? -1 : new_buffer((size_t)M * kpad * esz);
-  // weight [O, C, KH, KW] -> [O, K]
-  View wv;
-  if (!reshape_view(w, {O, K}, &wv)) wv = materialize_copy(w, at, "contiguous weight"), reshape_view(wv, {O, K}, &wv);
-  Step sb;
-  sb.kind = StepKind::SPLIT;
-  sb.label = "prepare conv weight";
-  sb.split.src = wv;
-  sb.split.precision = prec;
-  sb.split.rows = O;
-  sb.split.cols = K;
-  sb.split.kpad = kpad;
-  sb.split.out_hi = new_buffer((size_t)O * kpad * esz);
-  sb.split.out_lo = prec == PFC_PRECISION_BF16 ? -1 : new_buffer((size_t)O * kpad * esz);
+  I.cp = Cp;
+  I.precision = prec;
+  const size_t xbytes = (size_t)(Nimg * H * W * Cp) * esz;
+  I.out_hi = new_buffer(xbytes);
+  I.out_lo = prec == PFC_PRECISION_BF16 ? -1 : new_buffer(xbytes);
+  const Operand opw = prepare_operand(w, O, K, kpad, prec, "prepare conv weight", at, Cp);
   // output NHWC: logical [N,O,OH,OW], strides (OH*OW*O, 1, OW*O, O)
   View c;
   c.shape = {Nimg, O, OH, OW};
@@ -2266,7 +2304,11 @@ void Compiler::lower_conv(const GemmChain& ch, int at) {
   sg.label = "conv gemm [" + std::to_string(M) + "x" + std::to_string(O) + "x" + std::to_string(K) + "]";
   GemmArgs& G = sg.gemm;
   G.precision = prec;
-  G.a_hi = I.out_hi; G.a_lo = I.out_lo; G.b_hi = sb.split.out_hi; G.b_lo = sb.split.out_lo;
+  G.b_hi = opw.hi; G.b_lo = opw.lo;
+  G.conv = true;
+  G.x_hi = I.out_hi; G.x_lo = I.out_lo;
+  G.H = H; G.W = W; G.Cp = Cp; G.KH = KH; G.KW = KW; G.sh = st[0]; G.sw = st[1];
+  G.ph = pd[0]; G.pw = pd[1]; G.dh = dl[0]; G.dw = dl[1]; G.OH = OH; G.OW = OW;
   G.batch = 1; G.M = M; G.N = O; G.K = K; G.kpad = kpad;
   G.c = c; G.c_sm = O; G.c_sn = 1; G.c_sb = 0;
   G.act = ch.act;
@@ -2308,7 +2350,6 @@ void Compiler::lower_conv(const GemmChain& ch, int at) {
     add_step(at, sf);
   }
   add_step(at, si);
-  add_step(at, sb);
   add_step(at, sg);
   val_[ch.result] = c;
 }
@@ -2505,9 +2546,11 @@ void Compiler::finish() {
       case StepKind::JIT: for (auto& p : s.jit.ptrs) use(p.first, i); break;
       case StepKind::SPLIT: use(s.split.src.buf, i); use(s.split.out_hi, i); use(s.split.out_lo, i); break;
       case StepKind::IM2COL: use(s.im2col.x.buf, i); use(s.im2col.out_hi, i); use(s.im2col.out_lo, i); break;
+      case StepKind::CONV_INPUT: use(s.convin.x.buf, i); use(s.convin.out_hi, i); use(s.convin.out_lo, i); break;
       case StepKind::GEMM: {
         const GemmArgs& G = s.gemm;
         use(G.a_hi, i); use(G.a_lo, i); use(G.b_hi, i); use(G.b_lo, i); use(G.c.buf, i);
+        if (G.conv) { use(G.x_hi, i); use(G.x_lo, i); }
         if (G.has_bias) use(G.bias.buf, i);
         if (G.has_residual) use(G.residual.buf, i);
         use(G.scale_buf, i); use(G.shift_buf, i);

@@ -115,12 +115,39 @@ void CudaExecutor::release_constants() {
   }
   plans_.clear();
   for (auto& [k, r] : resident_) {
+    if (!r.owned) continue;
     pool_->deallocate(r.dev, stream_);
     pool_->add_resident(-(long long)r.bytes);
   }
   resident_.clear();
   resident_splat_.clear();
+  for (auto& [k, pr] : prepared_) {
+    pool_->deallocate(pr.dev, stream_);
+    pool_->add_resident(-(long long)pr.bytes);
+  }
+  prepared_.clear();
   if (stream_) cudaStreamSynchronize(stream_);
+}
+
+void CudaExecutor::set_resident(uint64_t cache_key, const void* dev, size_t bytes) {
+  std::lock_guard<std::mutex> lock(mu_);
+  DeviceGuard dg(cfg_.device_id);
+  if (!dev || bytes == 0) fail(PFC_ERR_INVALID_ARGUMENT, "set_resident: null pointer or empty payload");
+  if (((uintptr_t)dev & 15) != 0) fail(PFC_ERR_INVALID_ARGUMENT, "set_resident: device pointer must be 16-byte aligned");
+  auto key = std::make_pair(cache_key, bytes);
+  auto it = resident_.find(key);
+  if (it != resident_.end() && it->second.owned) {
+    if (stream_) PFB_CUDA(cudaStreamSynchronize(stream_));
+    pool_->deallocate(it->second.dev, stream_);
+    pool_->add_resident(-(long long)it->second.bytes);
+  }
+  Resident r;
+  r.dev = const_cast<void*>(dev);
+  r.bytes = bytes;
+  r.owned = false;
+  resident_[key] = r;
+  // operands derived from earlier contents of this key are refilled on next use
+  for (auto& [k, pr] : prepared_) pr.filled = false;
 }
 
 pfc_device_info CudaExecutor::device_info() const {
@@ -280,6 +307,18 @@ std::vector<void*> CudaExecutor::resolve(PlanEntry& pe, const Graph& g,
         }
         break;
       }
+      case BufKind::PREPARED: {
+        auto it = prepared_.find(b.prep_key);
+        if (it == prepared_.end()) {
+          Prepared pr;
+          pr.bytes = b.bytes;
+          pr.dev = pool_->allocate(b.bytes, s);
+          pool_->add_resident((long long)b.bytes);
+          it = prepared_.emplace(b.prep_key, pr).first;
+        }
+        ptrs[i] = it->second.dev;
+        break;
+      }
     }
   }
   return ptrs;
@@ -322,7 +361,29 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
       L.hi = bufp(a.out_hi, 0);
       L.lo = (float*)bufp(a.out_lo, 0);
       L.kpad = a.kpad;
-      launch_prepare(L, s);
+      if (a.conv_cp > 0) {
+        ConvWeightLaunch W;
+        W.w = L.src;
+        W.o = a.src.shape[0]; W.c = a.src.shape[1]; W.kh = a.src.shape[2]; W.kw = a.src.shape[3];
+        W.so = L.stride[0]; W.sc = L.stride[1]; W.skh = L.stride[2]; W.skw = L.stride[3];
+        W.cp = a.conv_cp; W.kpad = a.kpad; W.precision = a.precision;
+        W.hi = L.hi; W.lo = L.lo;
+        launch_conv_weight(W, s);
+      } else {
+        launch_prepare(L, s);
+      }
+      break;
+    }
+    case StepKind::CONV_INPUT: {
+      const ConvInputArgs& a = st.convin;
+      ConvInputLaunch L;
+      L.x = viewp(a.x);
+      L.n = a.x.shape[0]; L.c = a.x.shape[1]; L.h = a.x.shape[2]; L.w = a.x.shape[3];
+      L.sn = a.x.strides[0]; L.sc = a.x.strides[1]; L.sh = a.x.strides[2]; L.sw = a.x.strides[3];
+      L.cp = a.cp; L.precision = a.precision;
+      L.hi = bufp(a.out_hi, 0);
+      L.lo = (float*)bufp(a.out_lo, 0);
+      launch_conv_input(L, s);
       break;
     }
     case StepKind::IM2COL: {
@@ -363,6 +424,13 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
         L.r_sb = a.r_sb; L.r_sm = a.r_sm; L.r_sn = a.r_sn;
       }
       L.err = err_dev_;
+      if (a.conv) {
+        L.conv = true;
+        L.x_hi = bufp(a.x_hi, 0);
+        L.x_lo = bufp(a.x_lo, 0);
+        L.H = a.H; L.W = a.W; L.Cp = a.Cp; L.KH = a.KH; L.KW = a.KW; L.sh = a.sh; L.sw = a.sw;
+        L.ph = a.ph; L.pw = a.pw; L.dh = a.dh; L.dw = a.dw; L.OH = a.OH; L.OW = a.OW;
+      }
       launch_gemm(L, s);
       break;
     }
@@ -419,18 +487,34 @@ static int launches_of(const Step& s) { return s.kind == StepKind::MEMSET ? 0 : 
 int64_t CudaExecutor::run_steps(PlanEntry& pe, const std::vector<void*>& ptrs, cudaStream_t s) {
   const Plan& P = *pe.plan;
   int64_t launches = 0;
-  for (const Step& st : P.steps) launches += launches_of(st);
+  // Operands derived from resident constants: prepared once, before (and
+  // outside) the per-call sequence and its CUDA graph.
+  for (size_t i = 0; i < P.steps.size(); ++i) {
+    const Step& st = P.steps[i];
+    if (!st.once) {
+      launches += launches_of(st);
+      continue;
+    }
+    Prepared& hi = prepared_.at(P.buffers[st.split.out_hi].prep_key);
+    Prepared* lo = st.split.out_lo >= 0 ? &prepared_.at(P.buffers[st.split.out_lo].prep_key) : nullptr;
+    if (hi.filled && (!lo || lo->filled)) continue;
+    launch_step(pe, i, ptrs, s);
+    launches += launches_of(st);
+    hi.filled = true;
+    if (lo) lo->filled = true;
+  }
   profile_.clear();
   if (cfg_.enable_profiling) {
     std::vector<cudaEvent_t> ev(P.steps.size() + 1);
     for (auto& e : ev) PFB_CUDA(cudaEventCreate(&e));
     PFB_CUDA(cudaEventRecord(ev[0], s));
     for (size_t i = 0; i < P.steps.size(); ++i) {
-      launch_step(pe, i, ptrs, s);
+      if (!P.steps[i].once) launch_step(pe, i, ptrs, s);
       PFB_CUDA(cudaEventRecord(ev[i + 1], s));
     }
     PFB_CUDA(cudaEventSynchronize(ev.back()));
     for (size_t i = 0; i < P.steps.size(); ++i) {
+      if (P.steps[i].once) continue;
       float ms = 0;
       cudaEventElapsedTime(&ms, ev[i], ev[i + 1]);
       profile_.push_back({P.steps[i].label, (double)ms});
@@ -453,7 +537,8 @@ int64_t CudaExecutor::run_steps(PlanEntry& pe, const std::vector<void*>& ptrs, c
     cudaGraph_t graph;
     PFB_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
     try {
-      for (size_t i = 0; i < P.steps.size(); ++i) launch_step(pe, i, ptrs, s);
+      for (size_t i = 0; i < P.steps.size(); ++i)
+        if (!P.steps[i].once) launch_step(pe, i, ptrs, s);
     } catch (...) {
       cudaStreamEndCapture(s, &graph);
       throw;
@@ -464,7 +549,8 @@ int64_t CudaExecutor::run_steps(PlanEntry& pe, const std::vector<void*>& ptrs, c
     if (e != cudaSuccess) {
       cudaGetLastError();
       pe.gexec = nullptr;
-      for (size_t i = 0; i < P.steps.size(); ++i) launch_step(pe, i, ptrs, s);
+      for (size_t i = 0; i < P.steps.size(); ++i)
+        if (!P.steps[i].once) launch_step(pe, i, ptrs, s);
     } else {
       pe.gexec_ptrs = ptrs;
       PFB_CUDA(cudaGraphLaunch(pe.gexec, s));
@@ -472,7 +558,8 @@ int64_t CudaExecutor::run_steps(PlanEntry& pe, const std::vector<void*>& ptrs, c
     ++pe.runs;
     return launches;
   }
-  for (size_t i = 0; i < P.steps.size(); ++i) launch_step(pe, i, ptrs, s);
+  for (size_t i = 0; i < P.steps.size(); ++i)
+    if (!P.steps[i].once) launch_step(pe, i, ptrs, s);
   ++pe.runs;
   return launches;
 }

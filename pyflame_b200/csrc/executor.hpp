@@ -42,6 +42,9 @@ class CudaExecutor {
   pfc_device_info device_info() const;
   pfc_memory_stats memory_stats() const { return pool_->stats(); }
   void release_constants();
+  // Caller-owned device memory holding the payload of constants keyed
+  // (cache_key, bytes): used in place of an upload, never written or freed.
+  void set_resident(uint64_t cache_key, const void* dev, size_t bytes);
   std::string describe(Graph& g, const std::vector<uint64_t>& outs);
   const std::vector<std::pair<std::string, double>>& last_profile() const { return profile_; }
 
@@ -59,6 +62,12 @@ class CudaExecutor {
   struct Resident {
     void* dev = nullptr;
     size_t bytes = 0;
+    bool owned = true;   // false: registered by the caller (set_resident)
+  };
+  struct Prepared {      // operand derived from a resident constant (BufKind::PREPARED)
+    void* dev = nullptr;
+    size_t bytes = 0;
+    bool filled = false;
   };
   struct SplatInfo {
     bool splat = false;
@@ -74,6 +83,7 @@ class CudaExecutor {
   std::unordered_map<uint64_t, PlanEntry> plans_;
   std::map<std::pair<uint64_t, size_t>, Resident> resident_;
   std::map<std::pair<uint64_t, size_t>, SplatInfo> resident_splat_;
+  std::unordered_map<uint64_t, Prepared> prepared_;
   std::vector<std::pair<std::string, double>> profile_;
 
   PlanEntry& prepare(Graph& g, const std::vector<uint64_t>& outs, const std::unordered_set<uint64_t>& bindings,

@@ -4,18 +4,29 @@
 // executor (rocm_blas.cpp:75-153, called from rocm_executor.cpp:278-335) and
 // the fused bias/activation epilogues of rocm_kernels.hip:649-732.
 //
-// Structure (one 128 x BN output tile per CTA, 192 threads):
+// Structure: a persistent kernel, one CTA of 192 threads per SM, each CTA
+// walking 128 x BN output tiles (tile blockIdx.x, +gridDim.x, ...):
 //   warp 0      TMA producer: K-major 128-byte-swizzled tiles of A and B into a
-//               ring of shared-memory stages, completion on mbarriers.
+//               ring of shared-memory stages, completion on mbarriers; the
+//               ring runs on across tile boundaries.
 //   warp 1      TMEM allocator and MMA issuer: one elected thread issues
 //               tcgen05.mma (kind::tf32 x3 for split-fp32 operands, or
-//               kind::f16 with bf16 operands) into a TMEM fp32 accumulator and
-//               frees each stage with tcgen05.commit.
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM
-//               lanes 32*(w%4)..+31), alpha/bias/folded-BN/activation/residual,
-//               global stores.
+//               kind::f16 with bf16 operands) into one of two TMEM fp32
+//               accumulators and frees each stage with tcgen05.commit.
+//   warps 2..5  epilogue: tcgen05.ld of each finished accumulator (warp w
+//               reads TMEM lanes 32*(w%4)..+31) into fp32 registers, returns
+//               it to the MMA warp, and once a tile's K is complete
+//               transposes 32x32 blocks through shared memory so that a warp
+//               stores 32 consecutive columns of a row, applying
+//               alpha/bias/folded-BN/activation/residual.  With two
+//               accumulators the epilogue of tile i overlaps the MMAs of i+1.
+// K is accumulated in chunks of 512 elements, each into a fresh accumulator,
+// and the chunks are summed in fp32 registers: a long accumulation inside the
+// tensor core drifts (at K = 16384 by about 1e-4 of the row scale, always
+// toward zero), a chunk of 512 stays well inside fp32-reference accuracy.
 // Every mbarrier wait is bounded by the global timer; on expiry the kernel
-// records PFC_ERR_TIMEOUT in *err, drains its own copies, frees TMEM and exits.
+// records PFC_ERR_TIMEOUT in *err, drains its own copies, waits for its own
+// MMAs to retire, frees TMEM and exits.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -30,7 +41,11 @@ namespace pfb {
 namespace {
 
 constexpr int kBM = 128;
-constexpr int kThreads = 192;
+// Warps: producers (1 TMA warp, or 4 gathering warps for CONV), 1 MMA warp, 4 epilogue warps.
+template <bool CONV>
+constexpr int kProdWarps = CONV ? 4 : 1;
+template <bool CONV>
+constexpr int kThreads = (kProdWarps<CONV> + 5) * 32;
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s per wait
 
 struct GemmParams {
@@ -47,7 +62,12 @@ struct GemmParams {
   const float* res;
   long long r_sb, r_sm, r_sn;
   int* err;
-  int num_m, num_n;
+  int num_m, num_n, batch;
+  int kchunk, nchunks;  // k-blocks per accumulation chunk; chunks per tile
+  // implicit-GEMM Conv2d (CONV kernels): channels-last input [N][H][W][Cp]
+  const void* x_hi;
+  const void* x_lo;
+  int H, W, Cp, KH, KW, sh, sw, ph, pw, dh, dw, OH, OW;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -91,6 +111,22 @@ __device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, int* err)
     if (gtimer() - t0 > kWaitNs) {
       atomicCAS(err, 0, PFC_ERR_TIMEOUT);
       return false;
+    }
+  }
+}
+
+// Wait for this CTA's own asynchronous work (copies in flight, issued MMAs)
+// before its shared memory or TMEM goes away: bounded by time only, even when
+// another role already recorded an error.
+__device__ __forceinline__ void mbar_wait_own(uint32_t a, uint32_t parity, int* err) {
+  if (mbar_try(a, parity)) return;
+  unsigned long long t0 = gtimer();
+  while (true) {
+    for (int i = 0; i < 128; ++i)
+      if (mbar_try(a, parity)) return;
+    if (gtimer() - t0 > kWaitNs) {
+      atomicCAS(err, 0, PFC_ERR_TIMEOUT);
+      return;
     }
   }
 }
@@ -141,15 +177,6 @@ __device__ __forceinline__ void umma_commit(uint32_t mbar) {
                : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
 __device__ __forceinline__ float act_apply(float v, int act) {
   switch (act) {
     case 1: return (0.f < v) ? v : 0.f;
@@ -164,32 +191,83 @@ __device__ __forceinline__ float act_apply(float v, int act) {
 template <int PREC, int BN>
 struct Cfg {
   static constexpr int ESZ = PREC == PFC_PRECISION_BF16 ? 2 : 4;
-  static constexpr int BK = 128 / ESZ;
+  static constexpr int BK = 128 / ESZ;  // K elements per 128-byte swizzle row
   static constexpr int UK = PREC == PFC_PRECISION_BF16 ? 16 : 8;
   static constexpr int KSTEPS = BK / UK;
   static constexpr int NOPS = PREC == PFC_PRECISION_BF16 ? 1 : 2;
   static constexpr int A_TILE = kBM * 128;
   static constexpr int B_TILE = BN * 128;
   static constexpr int STAGE = NOPS * (A_TILE + B_TILE);
-  static constexpr int STAGES = (200 * 1024) / STAGE > 8 ? 8 : (200 * 1024) / STAGE;
-  static constexpr int SMEM = STAGES * STAGE + 1024 /*barriers*/ + 1024 /*align*/;
-  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+  // epilogue staging: per epilogue warp a 32 x 33 fp32 tile (padded: no bank conflicts)
+  static constexpr int EPI_WARP_FLOATS = 32 * 33;
+  static constexpr int EPI_BYTES = 4 * EPI_WARP_FLOATS * 4;
+  static constexpr int SMEM_LIMIT = 232448;  // 227 KB opt-in maximum per block
+  static constexpr int STAGES_FIT = (SMEM_LIMIT - EPI_BYTES - 2048) / STAGE;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int SMEM = STAGES * STAGE + EPI_BYTES + 1024 /*barriers*/ + 1024 /*align*/;
+  static constexpr int TMEM_COLS = 2 * BN;  // two accumulators: epilogue of tile i overlaps MMAs of tile i+1
   static constexpr uint32_t IDESC = idesc(kBM, BN, PREC == PFC_PRECISION_BF16 ? 1u : 2u);
+  static_assert(STAGES >= 2, "shared memory too small for two stages");
+  static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation");
 };
 
-template <int PREC, int BN>
-__global__ void __launch_bounds__(kThreads, 1)
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t a) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory");
+}
+
+// 16-byte global->shared copy; src_bytes 0 writes zeros (padding).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+// make this thread's completed generic-proxy shared-memory writes visible to
+// the tensor cores (async proxy)
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Tile t of the persistent schedule -> (batch, m tile, n tile).  Within a
+// batch slice, groups of 16 M-tiles sweep all N-tiles, so the B tiles of a
+// group stay in L2 while the group's A rows stream.
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& bz, int& tm, int& tn) {
+  const int per_batch = p.num_m * p.num_n;
+  bz = t / per_batch;
+  const int r = t - bz * per_batch;
+  const int group = 16;
+  const int per_group = group * p.num_n;
+  const int first_m = (r / per_group) * group;
+  const int gsz = min(p.num_m - first_m, group);
+  tm = first_m + (r % per_group) % gsz;
+  tn = (r % per_group) / gsz;
+}
+
+// Persistent kernel: each CTA walks tiles blockIdx.x, +gridDim.x, ...
+// CONV: the A operand is gathered by four producer warps from a channels-last
+// input (implicit-GEMM Conv2d) instead of loaded by TMA.
+template <int PREC, int BN, bool CONV>
+__global__ void __launch_bounds__(kThreads<CONV>, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
                 const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
                 const GemmParams p) {
   using C = Cfg<PREC, BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* bars = (uint64_t*)(smem + C::STAGES * C::STAGE);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + C::STAGES;
-  uint64_t* accum = bars + 2 * C::STAGES;
-  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * C::STAGES + 1);
+  float* epi = (float*)(smem + C::STAGES * C::STAGE);
+  uint64_t* bars = (uint64_t*)(smem + C::STAGES * C::STAGE + C::EPI_BYTES);
+  uint64_t* full = bars;                       // [STAGES] TMA -> MMA
+  uint64_t* empty = bars + C::STAGES;          // [STAGES] MMA -> TMA
+  uint64_t* acc_full = bars + 2 * C::STAGES;   // [2] MMA -> epilogue
+  uint64_t* acc_empty = acc_full + 2;          // [2] epilogue -> MMA
+  uint64_t* done = acc_empty + 2;              // all MMAs of this CTA retired
+  uint32_t* tmem_slot = (uint32_t*)(done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // an earlier CTA gave up: stop early (block-uniform decision)
@@ -198,26 +276,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (s_stop != 0) return;
 
-  // tile coordinates: grouped rasterization (16 M-tiles per group) for L2 reuse
-  const int t = blockIdx.x;
-  const int group = 16;
-  const int per_group = group * p.num_n;
-  const int first_m = (t / per_group) * group;
-  const int gsz = min(p.num_m - first_m, group);
-  const int tm = first_m + (t % per_group) % gsz;
-  const int tn = (t % per_group) / gsz;
-  const int bz = blockIdx.y;
-  const int m0 = tm * kBM, n0 = tn * BN;
-
+  constexpr int PW = kProdWarps<CONV>;  // warp index of the MMA issuer
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(smem_u32(&full[s]), 1);
+      // CONV: the B copy's expect_tx arrival plus one arrival per gathering thread
+      mbar_init(smem_u32(&full[s]), CONV ? 1 + 32 * PW : 1);
       mbar_init(smem_u32(&empty[s]), 1);
     }
-    mbar_init(smem_u32(accum), 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&acc_full[b]), 1);
+      mbar_init(smem_u32(&acc_empty[b]), 4);  // one arrival per epilogue warp
+    }
+    mbar_init(smem_u32(done), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {
+  if (warp == PW) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"((uint32_t)C::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -228,106 +301,227 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   const int nkb = p.nkb;
-  bool aborted = false;
-  if (warp == 0 && lane == 0) {
-    // ---------------- producer ----------------
-    const int ca = p.a_batched ? bz : 0, cb = p.b_batched ? bz : 0;
-    int issued = 0;
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % C::STAGES;
-      const uint32_t ph = (uint32_t)(kb / C::STAGES) & 1u;
-      if (kb >= C::STAGES && !mbar_wait(smem_u32(&empty[s]), ph ^ 1u, p.err)) { aborted = true; break; }
-      uint8_t* st = smem + s * C::STAGE;
-      const uint32_t fb = smem_u32(&full[s]);
-      mbar_expect_tx(fb, C::STAGE);
-      const int kc = kb * C::BK;
-      tma_load_3d(smem_u32(st), &ta_hi, fb, kc, m0, ca);
-      tma_load_3d(smem_u32(st + C::A_TILE), &tb_hi, fb, kc, n0, cb);
-      if constexpr (C::NOPS == 2) {
-        tma_load_3d(smem_u32(st + C::A_TILE + C::B_TILE), &ta_lo, fb, kc, m0, ca);
-        tma_load_3d(smem_u32(st + 2 * C::A_TILE + C::B_TILE), &tb_lo, fb, kc, n0, cb);
-      }
-      issued = kb + 1;
-    }
-    // drain: every issued copy must have landed before the CTA can exit
-    for (int kb = issued > C::STAGES ? issued - C::STAGES : 0; kb < issued; ++kb)
-      mbar_wait(smem_u32(&full[kb % C::STAGES]), (uint32_t)(kb / C::STAGES) & 1u, p.err);
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer ----------------
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % C::STAGES;
-      const uint32_t ph = (uint32_t)(kb / C::STAGES) & 1u;
-      if (!mbar_wait(smem_u32(&full[s]), ph, p.err)) { aborted = true; break; }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t st = smem_u32(smem + s * C::STAGE);
-      const uint32_t a_hi = st, b_hi = st + C::A_TILE;
-      const uint32_t a_lo = st + C::A_TILE + C::B_TILE, b_lo = st + 2 * C::A_TILE + C::B_TILE;
-#pragma unroll
-      for (int ks = 0; ks < C::KSTEPS; ++ks) {
-        const uint32_t koff = ks * 32;  // 32 bytes of K per instruction
-        const uint32_t acc = (kb > 0 || ks > 0) ? 1u : 0u;
-        if constexpr (C::NOPS == 2) {
-          // small products first, then the leading term
-          umma<PREC>(tmem, sdesc(a_lo + koff), sdesc(b_hi + koff), C::IDESC, acc);
-          umma<PREC>(tmem, sdesc(a_hi + koff), sdesc(b_lo + koff), C::IDESC, 1u);
-          umma<PREC>(tmem, sdesc(a_hi + koff), sdesc(b_hi + koff), C::IDESC, 1u);
-        } else {
-          umma<PREC>(tmem, sdesc(a_hi + koff), sdesc(b_hi + koff), C::IDESC, acc);
-        }
-      }
-      umma_commit(smem_u32(&empty[s]));
-    }
-    // signal the epilogue (also after an abort, so in-flight MMAs are tracked)
-    umma_commit(smem_u32(accum));
-  } else if (warp >= 2) {
-    // ---------------- epilogue ----------------
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+  const int ntiles = p.num_m * p.num_n * p.batch;
+  if (CONV && warp < PW) {
+    // ---------------- implicit-GEMM producer: thread r gathers A row r ----------------
+    const int r = threadIdx.x;
+    constexpr int CH = 16 / C::ESZ;  // K elements per 16-byte chunk
+    constexpr int D = C::STAGES - 1 < 2 ? C::STAGES - 1 : 2;  // k-blocks in flight before signalling
+    const int taps = p.KH * p.KW;
+    const int ohw = p.OH * p.OW;
+    int g = 0, pending = 0;
     bool ok = true;
-    if (nkb > 0) ok = mbar_wait(smem_u32(accum), 0u, p.err);
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const int row = m0 + q * 32 + lane;
-    const float alpha = p.alpha_ptr ? *p.alpha_ptr : p.alpha;
-    const float bsc = p.bias_scalar ? *p.bias_scalar : 0.f;
-    if (ok && *(volatile int*)p.err == 0) {
-      float* crow = p.c + (long long)bz * p.c_sb + (long long)row * p.c_sm;
-      const float* rrow = p.res ? p.res + (long long)bz * p.r_sb + (long long)row * p.r_sm : nullptr;
-#pragma unroll 1
-      for (int cc = 0; cc < BN; cc += 16) {
-        uint32_t r[16];
-        if (nkb > 0) {
-          tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)cc, r);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) r[j] = 0u;
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      int bz, tm, tn;
+      tile_coords(p, t, bz, tm, tn);
+      const int n0 = tn * BN;
+      const int m = tm * kBM + r;
+      const bool mok = m < p.M;
+      int ih0 = 0, iw0 = 0;
+      long long img_base = 0;
+      if (mok) {
+        const int img = m / ohw, rem = m - img * ohw;
+        const int oh = rem / p.OW, ow = rem - oh * p.OW;
+        ih0 = oh * p.sh - p.ph;
+        iw0 = ow * p.sw - p.pw;
+        img_base = (long long)img * p.H * p.W * p.Cp;
+      }
+      int c = 0, kw = 0, kh = 0, tap = 0;  // position of the next chunk along k
+      for (int kb = 0; kb < nkb; ++kb, ++g) {
+        const int s = g % C::STAGES;
+        const uint32_t ph = (uint32_t)(g / C::STAGES) & 1u;
+        if (g >= C::STAGES && !mbar_wait(smem_u32(&empty[s]), ph ^ 1u, p.err)) { ok = false; break; }
+        uint8_t* st = smem + s * C::STAGE;
+        if (r == 0) {
+          const uint32_t fb = smem_u32(&full[s]);
+          mbar_expect_tx(fb, C::NOPS * C::B_TILE);
+          tma_load_3d(smem_u32(st + C::A_TILE), &tb_hi, fb, kb * C::BK, n0, 0);
+          if constexpr (C::NOPS == 2) tma_load_3d(smem_u32(st + 2 * C::A_TILE + C::B_TILE), &tb_lo, fb, kb * C::BK, n0, 0);
         }
-        if (row < p.M) {
+        const uint32_t arow_hi = smem_u32(st) + (uint32_t)r * 128u;
+        const uint32_t arow_lo = smem_u32(st + C::A_TILE + C::B_TILE) + (uint32_t)r * 128u;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int n = n0 + cc + j;
-            if (n < p.N) {
-              float v = __uint_as_float(r[j]);
-              if (p.scale) v = v * p.scale[n] + p.shift[n];
-              else {
-                v = v * alpha;
-                if (p.bias) v = v + p.bias[n];
-                else if (p.bias_scalar) v = v + bsc;
-              }
-              v = act_apply(v, p.act);
-              if (rrow) v = v + rrow[(long long)n * p.r_sn];
-              crow[(long long)n * p.c_sn] = v;
-            }
+        for (int j = 0; j < 8; ++j) {
+          const int ih = ih0 + kh * p.dh, iw = iw0 + kw * p.dw;
+          const bool in = mok && tap < taps && (unsigned)ih < (unsigned)p.H && (unsigned)iw < (unsigned)p.W;
+          const long long off = in ? (img_base + ((long long)ih * p.W + iw) * p.Cp + c) * C::ESZ : 0;
+          const uint32_t sw = (uint32_t)((j ^ (r & 7)) << 4);  // 128-byte swizzle, as TMA writes it
+          cp_async16(arow_hi + sw, (const char*)p.x_hi + off, in ? 16u : 0u);
+          if constexpr (C::NOPS == 2) cp_async16(arow_lo + sw, (const char*)p.x_lo + off, in ? 16u : 0u);
+          c += CH;
+          if (c == p.Cp) {
+            c = 0;
+            ++tap;
+            if (++kw == p.KW) { kw = 0; ++kh; }
           }
         }
+        cp_async_commit();
+        if (++pending > D) {
+          cp_async_wait<D>();
+          fence_proxy_async();
+          mbar_arrive(smem_u32(&full[(g - D) % C::STAGES]));
+          --pending;
+        }
+      }
+    }
+    cp_async_wait<0>();
+    fence_proxy_async();
+    for (int k = g - pending; k < g; ++k) mbar_arrive(smem_u32(&full[k % C::STAGES]));
+    if (!ok && r == 0) {
+      // an error stopped the pipeline: let this thread's B copies land before exit
+      for (int k = g > C::STAGES ? g - C::STAGES : 0; k < g; ++k)
+        mbar_wait_own(smem_u32(&full[k % C::STAGES]), (uint32_t)(k / C::STAGES) & 1u, p.err);
+    }
+  } else if (!CONV && warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    int g = 0;  // k-block counter across all tiles of this CTA
+    bool ok = true;
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      int bz, tm, tn;
+      tile_coords(p, t, bz, tm, tn);
+      const int ca = p.a_batched ? bz : 0, cb = p.b_batched ? bz : 0;
+      const int m0 = tm * kBM, n0 = tn * BN;
+      for (int kb = 0; kb < nkb; ++kb, ++g) {
+        const int s = g % C::STAGES;
+        const uint32_t ph = (uint32_t)(g / C::STAGES) & 1u;
+        if (g >= C::STAGES && !mbar_wait(smem_u32(&empty[s]), ph ^ 1u, p.err)) { ok = false; break; }
+        uint8_t* st = smem + s * C::STAGE;
+        const uint32_t fb = smem_u32(&full[s]);
+        mbar_expect_tx(fb, C::STAGE);
+        const int kc = kb * C::BK;
+        tma_load_3d(smem_u32(st), &ta_hi, fb, kc, m0, ca);
+        tma_load_3d(smem_u32(st + C::A_TILE), &tb_hi, fb, kc, n0, cb);
+        if constexpr (C::NOPS == 2) {
+          tma_load_3d(smem_u32(st + C::A_TILE + C::B_TILE), &ta_lo, fb, kc, m0, ca);
+          tma_load_3d(smem_u32(st + 2 * C::A_TILE + C::B_TILE), &tb_lo, fb, kc, n0, cb);
+        }
+      }
+    }
+    // drain: every issued copy must have landed before the CTA can exit
+    for (int k = g > C::STAGES ? g - C::STAGES : 0; k < g; ++k)
+      mbar_wait_own(smem_u32(&full[k % C::STAGES]), (uint32_t)(k / C::STAGES) & 1u, p.err);
+  } else if (warp == PW && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    // K is accumulated in chunks of kchunk k-blocks, each into a fresh TMEM
+    // accumulator (alternating between the two); the epilogue sums the chunks
+    // in fp32 registers.  Short accumulation runs inside the tensor core keep
+    // long contractions (K = 16384) within fp32-reference accuracy.
+    int g = 0, u = 0;  // k-blocks consumed; accumulator uses
+    bool ok = true;
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      for (int ch = 0; ch < p.nchunks && ok; ++ch, ++u) {
+        const int b = u & 1;
+        const uint32_t use = (uint32_t)(u >> 1);
+        if (u >= 2 && !mbar_wait(smem_u32(&acc_empty[b]), (use & 1u) ^ 1u, p.err)) { ok = false; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t acc_t = tmem + (uint32_t)(b * BN);
+        const int kb0 = ch * p.kchunk, kb1 = min(nkb, kb0 + p.kchunk);
+        for (int kb = kb0; kb < kb1; ++kb, ++g) {
+          const int s = g % C::STAGES;
+          const uint32_t ph = (uint32_t)(g / C::STAGES) & 1u;
+          if (!mbar_wait(smem_u32(&full[s]), ph, p.err)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t st = smem_u32(smem + s * C::STAGE);
+          const uint32_t a_hi = st, b_hi = st + C::A_TILE;
+          const uint32_t a_lo = st + C::A_TILE + C::B_TILE, b_lo = st + 2 * C::A_TILE + C::B_TILE;
+#pragma unroll
+          for (int ks = 0; ks < C::KSTEPS; ++ks) {
+            const uint32_t koff = ks * 32;  // 32 bytes of K per instruction
+            const uint32_t acc = (kb > kb0 || ks > 0) ? 1u : 0u;
+            if constexpr (C::NOPS == 2) {
+              // small products first, then the leading term
+              umma<PREC>(acc_t, sdesc(a_lo + koff), sdesc(b_hi + koff), C::IDESC, acc);
+              umma<PREC>(acc_t, sdesc(a_hi + koff), sdesc(b_lo + koff), C::IDESC, 1u);
+              umma<PREC>(acc_t, sdesc(a_hi + koff), sdesc(b_hi + koff), C::IDESC, 1u);
+            } else {
+              umma<PREC>(acc_t, sdesc(a_hi + koff), sdesc(b_hi + koff), C::IDESC, acc);
+            }
+          }
+          umma_commit(smem_u32(&empty[s]));
+        }
+        if (ok) umma_commit(smem_u32(&acc_full[b]));
+      }
+    }
+    // retire every MMA this thread issued before TMEM is released
+    umma_commit(smem_u32(done));
+  } else if (warp > PW) {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    float* ep = epi + (warp - PW - 1) * C::EPI_WARP_FLOATS;
+    const float alpha = p.alpha_ptr ? *p.alpha_ptr : p.alpha;
+    const float bsc = p.bias_scalar ? *p.bias_scalar : 0.f;
+    const bool has_shift = p.scale || p.bias || p.bias_scalar;
+    int u = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      // this thread's row of the tile: the sum of the chunk accumulators
+      float acc[BN];
+#pragma unroll
+      for (int j = 0; j < BN; ++j) acc[j] = 0.f;
+      for (int ch = 0; ch < p.nchunks; ++ch, ++u) {
+        const int b = u & 1;
+        const uint32_t use = (uint32_t)(u >> 1);
+        if (!mbar_wait(smem_u32(&acc_full[b]), use & 1u, p.err)) { ok = false; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (nkb > 0) {
+#pragma unroll
+          for (int cc = 0; cc < BN; cc += 32) {
+            uint32_t r[32];
+            const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + cc);
+            tmem_ld16_nowait(ta, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+            tmem_ld16_nowait(ta + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[cc + j] += __uint_as_float(r[j]);
+          }
+        }
+        // the chunk is in registers: hand the accumulator back to the MMA warp
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&acc_empty[b]));
+      }
+      if (!ok) break;
+      int bz, tm, tn;
+      tile_coords(p, t, bz, tm, tn);
+      const int m0 = tm * kBM + q * 32, n0 = tn * BN;
+      float* cbase = p.c + (long long)bz * p.c_sb;
+      const float* rbase = p.res ? p.res + (long long)bz * p.r_sb : nullptr;
+#pragma unroll
+      for (int cc = 0; cc < BN; cc += 32) {
+        // transpose through shared memory: lane = row on the way in, lane = column on the way out
+#pragma unroll
+        for (int j = 0; j < 32; ++j) ep[lane * 33 + j] = acc[cc + j];
+        __syncwarp();
+        const int n = n0 + cc + lane;
+        const bool nok = n < p.N;
+        float sc = alpha, sh = bsc;
+        if (nok) {
+          if (p.scale) { sc = p.scale[n]; sh = p.shift[n]; }
+          else if (p.bias) sh = p.bias[n];
+        }
+#pragma unroll 4
+        for (int rr = 0; rr < 32; ++rr) {
+          const int row = m0 + rr;
+          float v = ep[rr * 33 + lane];
+          v = v * sc;
+          if (has_shift) v = v + sh;
+          v = act_apply(v, p.act);
+          if (nok && row < p.M) {
+            if (rbase) v = v + rbase[(long long)row * p.r_sm + (long long)n * p.r_sn];
+            cbase[(long long)row * p.c_sm + (long long)n * p.c_sn] = v;
+          }
+        }
+        __syncwarp();
       }
     }
   }
-  // teardown: all tcgen05 traffic of this CTA is complete once the epilogue
-  // observed `accum` (or gave up); release TMEM.
-  (void)aborted;
+  // teardown: wait until every MMA of this CTA retired, then release TMEM
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  if (warp == 1) {
+  if (warp == PW) {
+    if (lane == 0) mbar_wait_own(smem_u32(done), 0u, p.err);
+    __syncwarp();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)C::TMEM_COLS));
   }
 }
@@ -368,21 +562,23 @@ CUtensorMap make_map(const void* base, int prec, int64_t kpad, int64_t rows, int
   return m;
 }
 
-template <int PREC, int BN>
+template <int PREC, int BN, bool CONV>
 void launch_t(const GemmLaunch& L, cudaStream_t stream) {
   using C = Cfg<PREC, BN>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
-    PFB_CUDA(cudaFuncSetAttribute(gemm_kernel<PREC, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    PFB_CUDA(cudaFuncSetAttribute(gemm_kernel<PREC, BN, CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_set[dev & 63] = true;
   }
   const int64_t a_rows = L.M, b_rows = L.N;
-  CUtensorMap ta_hi = make_map(L.a_hi, PREC, L.kpad, a_rows, L.a_sb ? L.batch : 1, kBM);
   CUtensorMap tb_hi = make_map(L.b_hi, PREC, L.kpad, b_rows, L.b_sb ? L.batch : 1, BN);
-  CUtensorMap ta_lo = PREC == PFC_PRECISION_BF16 ? ta_hi : make_map(L.a_lo, PREC, L.kpad, a_rows, L.a_sb ? L.batch : 1, kBM);
   CUtensorMap tb_lo = PREC == PFC_PRECISION_BF16 ? tb_hi : make_map(L.b_lo, PREC, L.kpad, b_rows, L.b_sb ? L.batch : 1, BN);
+  // CONV gathers A itself: its maps are unused
+  CUtensorMap ta_hi = CONV ? tb_hi : make_map(L.a_hi, PREC, L.kpad, a_rows, L.a_sb ? L.batch : 1, kBM);
+  CUtensorMap ta_lo = CONV || PREC == PFC_PRECISION_BF16 ? ta_hi
+                                                         : make_map(L.a_lo, PREC, L.kpad, a_rows, L.a_sb ? L.batch : 1, kBM);
   GemmParams p;
   p.M = (int)L.M;
   p.N = (int)L.N;
@@ -407,9 +603,27 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream) {
   p.err = L.err;
   p.num_m = (int)ceil_div(L.M, kBM);
   p.num_n = (int)ceil_div(L.N, BN);
+  p.batch = (int)L.batch;
+  p.x_hi = L.x_hi;
+  p.x_lo = L.x_lo;
+  p.H = (int)L.H; p.W = (int)L.W; p.Cp = (int)L.Cp; p.KH = (int)L.KH; p.KW = (int)L.KW;
+  p.sh = (int)L.sh; p.sw = (int)L.sw; p.ph = (int)L.ph; p.pw = (int)L.pw; p.dh = (int)L.dh; p.dw = (int)L.dw;
+  p.OH = (int)L.OH; p.OW = (int)L.OW;
   if (L.K == 0) p.nkb = 0;
-  dim3 grid((unsigned)(p.num_m * p.num_n), (unsigned)L.batch, 1);
-  gemm_kernel<PREC, BN><<<grid, kThreads, C::SMEM, stream>>>(ta_hi, ta_lo, tb_hi, tb_lo, p);
+  // accumulation chunks of 512 elements of K (16 tf32 / 8 bf16 k-blocks)
+  p.kchunk = 512 / C::BK;
+  p.nchunks = p.nkb > 0 ? (p.nkb + p.kchunk - 1) / p.kchunk : 1;
+  const int64_t ntiles = (int64_t)p.num_m * p.num_n * L.batch;
+  PFB_CHECK_ARG(ntiles < (1ll << 31), "gemm: too many tiles");
+  // persistent: one CTA per SM (the shared-memory ring admits one), never more CTAs than tiles
+  static int sms[64] = {};
+  if (!sms[dev & 63]) {
+    int v = 0;
+    PFB_CUDA(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev));
+    sms[dev & 63] = v > 0 ? v : 148;
+  }
+  const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sms[dev & 63]);
+  gemm_kernel<PREC, BN, CONV><<<grid, kThreads<CONV>, C::SMEM, stream>>>(ta_hi, ta_lo, tb_hi, tb_lo, p);
   PFB_CUDA(cudaGetLastError());
 }
 
@@ -421,14 +635,37 @@ void launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
   PFB_CHECK_ARG(L.err != nullptr, "gemm: error flag pointer required");
   const int64_t kal = L.precision == PFC_PRECISION_BF16 ? 64 : 32;
   PFB_CHECK_ARG(L.kpad % kal == 0 && L.kpad >= L.K, "gemm: kpad must be a multiple of the K tile and >= K");
-  PFB_CHECK_ARG(((uintptr_t)L.a_hi & 15) == 0 && ((uintptr_t)L.b_hi & 15) == 0, "gemm: operands must be 16-byte aligned");
-  if (L.precision == PFC_PRECISION_BF16) {
-    if (L.N > 64) launch_t<PFC_PRECISION_BF16, 128>(L, stream);
-    else launch_t<PFC_PRECISION_BF16, 64>(L, stream);
+  if (L.conv) {
+    const int64_t ch = L.precision == PFC_PRECISION_BF16 ? 8 : 4;  // elements per 16-byte chunk
+    PFB_CHECK_ARG(L.batch == 1 && L.a_sb == 0 && L.b_sb == 0, "conv gemm: no batch slices");
+    PFB_CHECK_ARG(L.x_hi && ((uintptr_t)L.x_hi & 15) == 0 && (L.precision == PFC_PRECISION_BF16 ||
+                                                               (L.x_lo && ((uintptr_t)L.x_lo & 15) == 0)),
+                  "conv gemm: channels-last input must be 16-byte aligned");
+    PFB_CHECK_ARG(L.Cp > 0 && L.Cp % ch == 0 && L.K == L.KH * L.KW * L.Cp, "conv gemm: bad channel padding");
+    PFB_CHECK_ARG(L.M == L.M / (L.OH * L.OW) * L.OH * L.OW && L.H * L.W * L.Cp < (1ll << 40) &&
+                      L.OH * L.OW < (1ll << 31) && L.KH * L.KW < (1 << 20),
+                  "conv gemm: bad geometry");
   } else {
-    PFB_CHECK_ARG(L.a_lo && L.b_lo, "gemm: tf32x3 needs lo operands");
-    if (L.N > 64) launch_t<PFC_PRECISION_TF32X3, 128>(L, stream);
-    else launch_t<PFC_PRECISION_TF32X3, 64>(L, stream);
+    PFB_CHECK_ARG(((uintptr_t)L.a_hi & 15) == 0, "gemm: operands must be 16-byte aligned");
+  }
+  PFB_CHECK_ARG(((uintptr_t)L.b_hi & 15) == 0, "gemm: operands must be 16-byte aligned");
+  if (L.precision == PFC_PRECISION_BF16) {
+    if (L.conv) {
+      if (L.N > 64) launch_t<PFC_PRECISION_BF16, 128, true>(L, stream);
+      else launch_t<PFC_PRECISION_BF16, 64, true>(L, stream);
+    } else {
+      if (L.N > 64) launch_t<PFC_PRECISION_BF16, 128, false>(L, stream);
+      else launch_t<PFC_PRECISION_BF16, 64, false>(L, stream);
+    }
+  } else {
+    PFB_CHECK_ARG(L.b_lo && (L.conv || L.a_lo), "gemm: tf32x3 needs lo operands");
+    if (L.conv) {
+      if (L.N > 64) launch_t<PFC_PRECISION_TF32X3, 128, true>(L, stream);
+      else launch_t<PFC_PRECISION_TF32X3, 64, true>(L, stream);
+    } else {
+      if (L.N > 64) launch_t<PFC_PRECISION_TF32X3, 128, false>(L, stream);
+      else launch_t<PFC_PRECISION_TF32X3, 64, false>(L, stream);
+    }
   }
 }
 

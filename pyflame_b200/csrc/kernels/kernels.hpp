@@ -27,8 +27,41 @@ struct GemmLaunch {
   const float* residual = nullptr;
   int64_t r_sb = 0, r_sm = 0, r_sn = 0;
   int* err = nullptr;
+  // Implicit-GEMM Conv2d: when conv is set, A is not a prepared operand; its
+  // rows m = (n*OH + oh)*OW + ow and columns k = (kh*KW + kw)*Cp + c are
+  // gathered from x_hi/x_lo, a channels-last copy [N][H][W][Cp] of the input
+  // (launch_conv_input), with zeros outside the padded image.  K = KH*KW*Cp.
+  bool conv = false;
+  const void* x_hi = nullptr;
+  const void* x_lo = nullptr;
+  int64_t H = 0, W = 0, Cp = 0, KH = 1, KW = 1, sh = 1, sw = 1, ph = 0, pw = 0, dh = 1, dw = 1, OH = 0, OW = 0;
 };
 void launch_gemm(const GemmLaunch& L, cudaStream_t stream);
+
+// Channels-last copy of a Conv2d input for the implicit GEMM: x is a strided
+// [N,C,H,W] view; output [N][H][W][Cp] (Cp >= C, zero channels above C) as
+// tf32x3 hi/lo fp32 pairs, or bf16 in hi when precision is bf16.
+struct ConvInputLaunch {
+  const float* x = nullptr;
+  int64_t n = 0, c = 0, h = 0, w = 0, sn = 0, sc = 0, sh = 0, sw = 0;
+  int64_t cp = 0;
+  int precision = 0;
+  void* hi = nullptr;
+  float* lo = nullptr;
+};
+void launch_conv_input(const ConvInputLaunch& L, cudaStream_t stream);
+
+// Conv2d weight [O,C,KH,KW] (strided view) as the implicit GEMM's B operand:
+// [O][kpad] with k = (kh*KW + kw)*Cp + c, zero for c >= C and k >= KH*KW*Cp.
+struct ConvWeightLaunch {
+  const float* w = nullptr;
+  int64_t o = 0, c = 0, kh = 0, kw = 0, so = 0, sc = 0, skh = 0, skw = 0;
+  int64_t cp = 0, kpad = 0;
+  int precision = 0;
+  void* hi = nullptr;
+  float* lo = nullptr;
+};
+void launch_conv_weight(const ConvWeightLaunch& L, cudaStream_t stream);
 
 // Operand preparation from a strided view of rank <= 6: the last dim is K,
 // all leading dims flatten (row-major) into rows.  Output [rows][kpad].

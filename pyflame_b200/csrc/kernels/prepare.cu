@@ -183,15 +183,21 @@ __global__ void im2col_kernel(const float* __restrict__ x, Im2colLaunch L, void*
 
 // Pooling (pooling.cpp:38-63,97-122,150-168): one output element per thread,
 // enumerated channel-fastest when the output is channels-last.
+// grid.y walks output rows (n, oh); threads walk (ow, c) of a row with 32-bit
+// index math, channel fastest for a channels-last output (coalesced reads of
+// a channels-last input and coalesced writes), column fastest otherwise.
 __global__ void pool_kernel(PoolLaunch L) {
-  const long long total = L.n * L.c * L.oh * L.ow;
   const bool cl = L.osc == 1;  // channels-last output
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    long long n, c, oh, ow;
+  const int C = (int)L.c, OW = (int)L.ow;
+  const int inner = C * OW;
+  for (long long row = blockIdx.y; row < L.n * L.oh; row += gridDim.y) {
+   const long long n = row / L.oh, oh = row - n * L.oh;
+   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < inner; i += gridDim.x * blockDim.x) {
+    long long c, ow;
     if (cl) {
-      c = i % L.c; ow = (i / L.c) % L.ow; oh = (i / (L.c * L.ow)) % L.oh; n = i / (L.c * L.ow * L.oh);
+      c = i % C; ow = i / C;
     } else {
-      ow = i % L.ow; oh = (i / L.ow) % L.oh; c = (i / (L.ow * L.oh)) % L.c; n = i / (L.ow * L.oh * L.c);
+      ow = i % OW; c = i / OW;
     }
     const float* xb = L.x + n * L.sn + c * L.sc;
     float out;
@@ -233,6 +239,58 @@ __global__ void pool_kernel(PoolLaunch L) {
       }
     }
     L.y[n * L.osn + c * L.osc + oh * L.osh + ow * L.osw] = out;
+   }
+  }
+}
+
+// Channels-last copy of a Conv2d input: one thread per output element,
+// channel fastest (coalesced writes; coalesced reads when the input is
+// already channels-last).  IDX is int when every index fits in 32 bits.
+template <int PREC, typename IDX>
+__global__ void conv_input_kernel(ConvInputLaunch L) {
+  const IDX C = (IDX)L.c, Cp = (IDX)L.cp, H = (IDX)L.h, W = (IDX)L.w;
+  const IDX total = (IDX)L.n * H * W * Cp;
+  for (IDX i = (IDX)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (IDX)gridDim.x * blockDim.x) {
+    const IDX c = i % Cp;
+    const IDX pix = i / Cp;
+    const IDX w = pix % W;
+    const IDX hn = pix / W;
+    const IDX h = hn % H;
+    const IDX n = hn / H;
+    float x = 0.f;
+    if (c < C) x = L.x[(long long)n * L.sn + (long long)c * L.sc + (long long)h * L.sh + (long long)w * L.sw];
+    if constexpr (PREC == PFC_PRECISION_BF16) {
+      ((__nv_bfloat16*)L.hi)[i] = __float2bfloat16_rn(x);
+    } else {
+      float hv, lv;
+      split_tf32(x, hv, lv);
+      ((float*)L.hi)[i] = hv;
+      L.lo[i] = lv;
+    }
+  }
+}
+
+// Conv2d weight [O,C,KH,KW] -> [O][kpad], k = (kh*KW + kw)*Cp + c.
+template <int PREC>
+__global__ void conv_weight_kernel(ConvWeightLaunch L) {
+  const long long total = L.o * L.kpad;
+  const long long taps = L.kh * L.kw;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long o = i / L.kpad, k = i % L.kpad;
+    const long long tap = k / L.cp, c = k % L.cp;
+    float x = 0.f;
+    if (tap < taps && c < L.c) {
+      const long long kh = tap / L.kw, kw = tap % L.kw;
+      x = L.w[o * L.so + c * L.sc + kh * L.skh + kw * L.skw];
+    }
+    if constexpr (PREC == PFC_PRECISION_BF16) {
+      ((__nv_bfloat16*)L.hi)[i] = __float2bfloat16_rn(x);
+    } else {
+      float hv, lv;
+      split_tf32(x, hv, lv);
+      ((float*)L.hi)[i] = hv;
+      L.lo[i] = lv;
+    }
   }
 }
 
@@ -306,7 +364,37 @@ void launch_im2col(const Im2colLaunch& L, cudaStream_t stream) {
 void launch_pool(const PoolLaunch& L, cudaStream_t stream) {
   const long long total = L.n * L.c * L.oh * L.ow;
   if (total == 0) return;
-  pool_kernel<<<grid_for(total, 256), 256, 0, stream>>>(L);
+  PFB_CHECK_ARG(L.c * L.ow < (1ll << 31), "pool: channels x output width too large");
+  const long long inner = L.c * L.ow, rows = L.n * L.oh;
+  dim3 grid((unsigned)ceil_div(inner, 256), (unsigned)std::min<long long>(rows, 65535), 1);
+  pool_kernel<<<grid, 256, 0, stream>>>(L);
+  PFB_CUDA(cudaGetLastError());
+}
+
+void launch_conv_input(const ConvInputLaunch& L, cudaStream_t stream) {
+  PFB_CHECK_ARG(L.x && L.hi && (L.precision == PFC_PRECISION_BF16 || L.lo), "conv input: null pointer");
+  PFB_CHECK_ARG(L.cp >= L.c && L.c > 0, "conv input: padded channels must cover the channels");
+  const long long total = L.n * L.h * L.w * L.cp;
+  if (total == 0) return;
+  const unsigned g = grid_for(total, 256);
+  const bool small = total < (1ll << 30);  // i + grid stride stays below 2^31
+  if (L.precision == PFC_PRECISION_BF16) {
+    if (small) conv_input_kernel<PFC_PRECISION_BF16, int><<<g, 256, 0, stream>>>(L);
+    else conv_input_kernel<PFC_PRECISION_BF16, long long><<<g, 256, 0, stream>>>(L);
+  } else {
+    if (small) conv_input_kernel<PFC_PRECISION_TF32X3, int><<<g, 256, 0, stream>>>(L);
+    else conv_input_kernel<PFC_PRECISION_TF32X3, long long><<<g, 256, 0, stream>>>(L);
+  }
+  PFB_CUDA(cudaGetLastError());
+}
+
+void launch_conv_weight(const ConvWeightLaunch& L, cudaStream_t stream) {
+  PFB_CHECK_ARG(L.w && L.hi && (L.precision == PFC_PRECISION_BF16 || L.lo), "conv weight: null pointer");
+  PFB_CHECK_ARG(L.cp >= L.c && L.kpad >= L.kh * L.kw * L.cp, "conv weight: bad layout");
+  const long long total = L.o * L.kpad;
+  if (total == 0) return;
+  if (L.precision == PFC_PRECISION_BF16) conv_weight_kernel<PFC_PRECISION_BF16><<<grid_for(total, 256), 256, 0, stream>>>(L);
+  else conv_weight_kernel<PFC_PRECISION_TF32X3><<<grid_for(total, 256), 256, 0, stream>>>(L);
   PFB_CUDA(cudaGetLastError());
 }
 

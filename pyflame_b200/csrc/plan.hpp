@@ -16,13 +16,16 @@ enum class BufKind : uint8_t {
   ARENA,     // intermediate or output: offset into the plan's arena
   CONST,     // constant payload uploaded from the host (resident or per call)
   BINDING,   // device pointer supplied by the caller (execute_device)
+  PREPARED,  // tensor-core operand derived from a resident constant: kept by the
+             // executor across calls (keyed by prep_key), filled once
 };
 
 struct Buffer {
   BufKind kind = BufKind::ARENA;
   size_t bytes = 0;
   int64_t arena_offset = -1;   // ARENA
-  uint64_t node = 0;           // CONST / BINDING: source node id
+  uint64_t node = 0;           // CONST / BINDING / PREPARED: source node id
+  uint64_t prep_key = 0;       // PREPARED: constant payload key x operand layout
   int first_use = -1, last_use = -1;  // step indices (liveness)
   bool pinned_live = false;    // keep to the end (graph outputs)
 };
@@ -53,6 +56,7 @@ enum class StepKind : uint8_t {
   JIT,        // NVRTC-generated kernel (fused elementwise / row / column / full reduction)
   SPLIT,      // pfk_split_tf32 / pfk_convert_bf16 operand preparation
   IM2COL,     // pfk_im2col
+  CONV_INPUT, // channels-last hi/lo copy of a Conv2d input (implicit GEMM)
   GEMM,       // pfk_gemm (tcgen05)
   POOL,       // pfk_pool2d
   BN_FOLD,    // fold BatchNorm(eval) into per-channel scale/shift
@@ -78,6 +82,16 @@ struct SplitArgs {
   // flattened batch strides (requires the batch dims of src to collapse)
   int64_t sb = 0, sr = 0, sk = 0;
   int precision = 0;
+  // conv_cp > 0: src is a Conv2d weight [O,C,KH,KW] laid out for the implicit
+  // GEMM, k = (kh*KW + kw)*conv_cp + c
+  int64_t conv_cp = 0;
+};
+
+struct ConvInputArgs {
+  View x;  // [N,C,H,W]
+  int out_hi = -1, out_lo = -1;  // [N][H][W][cp]
+  int64_t cp = 0;
+  int precision = 0;
 };
 
 struct Im2colArgs {
@@ -100,6 +114,10 @@ struct GemmArgs {
   int act = 0;
   View residual; bool has_residual = false;
   int64_t r_sb = 0, r_sm = 0, r_sn = 0;
+  // implicit-GEMM Conv2d: A gathered from the channels-last input x_hi/x_lo
+  bool conv = false;
+  int x_hi = -1, x_lo = -1;
+  int64_t H = 0, W = 0, Cp = 0, KH = 1, KW = 1, sh = 1, sw = 1, ph = 0, pw = 0, dh = 1, dw = 1, OH = 0, OW = 0;
 };
 
 struct PoolArgs {
@@ -120,10 +138,12 @@ struct BnFoldArgs {
 
 struct Step {
   StepKind kind = StepKind::JIT;
+  bool once = false;           // fills PREPARED buffers: runs only while they are unfilled
   std::string label;           // for describe/profile
   JitLaunch jit;
   SplitArgs split;
   Im2colArgs im2col;
+  ConvInputArgs convin;
   GemmArgs gemm;
   PoolArgs pool;
   BnFoldArgs bnfold;

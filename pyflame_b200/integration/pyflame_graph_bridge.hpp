@@ -36,13 +36,64 @@ inline void check(int rc) {
   if (rc != PFC_OK) throw std::runtime_error(pfc_last_error());
 }
 
+// Cache keys for constant payloads kept on the device across calls.  PyFlame
+// node ids restart at 0 in every graph and a freed payload's address is
+// reused by later allocations, so neither names a payload on its own.  A key
+// here is issued per live node object (tracked through a weak_ptr) and
+// payload (address, size, and a fingerprint of 64 sampled words): when the
+// node dies or its payload is replaced (Node::set_constant_data,
+// node.hpp:175-177), the next lookup issues a fresh key.
+class PayloadKeys {
+ public:
+  uint64_t key(const std::shared_ptr<ir::Node>& n) {
+    const auto& d = n->constant_data();
+    const uint64_t fp = fingerprint(d.data(), d.size());
+    auto it = keys_.find(n.get());
+    if (it != keys_.end()) {
+      const Entry& e = it->second;
+      if (!e.node.expired() && e.node.lock() == n && e.data == d.data() && e.bytes == d.size() && e.fp == fp)
+        return e.key;
+    }
+    if (keys_.size() > 4096) prune();
+    Entry e{n, d.data(), d.size(), fp, next_++};
+    keys_[n.get()] = e;
+    return e.key;
+  }
+
+ private:
+  struct Entry {
+    std::weak_ptr<ir::Node> node;
+    const void* data;
+    size_t bytes;
+    uint64_t fp;
+    uint64_t key;
+  };
+  std::unordered_map<const ir::Node*, Entry> keys_;
+  uint64_t next_ = 1;
+
+  static uint64_t fingerprint(const uint8_t* p, size_t n) {
+    uint64_t h = 1469598103934665603ull ^ n;
+    const size_t words = n / 8;
+    for (size_t i = 0; i < 64 && words; ++i) {
+      uint64_t w;
+      std::memcpy(&w, p + 8 * ((i * words) / 64), 8);
+      h = (h ^ w) * 1099511628211ull;
+    }
+    return h;
+  }
+  void prune() {
+    for (auto it = keys_.begin(); it != keys_.end();)
+      it = it->second.node.expired() ? keys_.erase(it) : std::next(it);
+  }
+};
+
 // Owns a pfc_graph holding every node of `graph` (ids, types, ops, specs,
 // edges, typed attributes, constant payloads borrowed from the nodes).
 class GraphBridge {
  public:
-  explicit GraphBridge(const ir::Graph& graph) {
+  GraphBridge(const ir::Graph& graph, PayloadKeys& keys) {
     check(pfc_graph_create(&g_));
-    for (const auto& n : graph.topological_order()) add(*n);
+    for (const auto& n : graph.topological_order()) add(n, keys);
   }
   ~GraphBridge() { pfc_graph_destroy(g_); }
   GraphBridge(const GraphBridge&) = delete;
@@ -52,7 +103,8 @@ class GraphBridge {
  private:
   pfc_graph* g_ = nullptr;
 
-  void add(const ir::Node& n) {
+  void add(const std::shared_ptr<ir::Node>& np, PayloadKeys& keys) {
+    const ir::Node& n = *np;
     std::vector<uint64_t> ins;
     for (const auto& i : n.inputs()) ins.push_back(i->id());
     const auto& shape = n.shape();
@@ -85,10 +137,11 @@ class GraphBridge {
     }
     if (n.has_constant_data()) {
       const auto& d = n.constant_data();
-      // PyFlame constants are immutable once created; key the device copy by
-      // the node's payload address (stable for the node's lifetime).
-      uint32_t flags = n.is_input() ? 0u : (uint32_t)PFC_CONST_RESIDENT;
-      check(pfc_graph_set_constant(g_, n.id(), d.data(), d.size(), flags, (uint64_t)(uintptr_t)d.data()));
+      // CONSTANT and PARAMETER payloads stay on the device across calls; an
+      // INPUT node's payload is runtime data (node.hpp:24), uploaded per call
+      const bool resident = !n.is_input();
+      check(pfc_graph_set_constant(g_, n.id(), d.data(), d.size(), resident ? (uint32_t)PFC_CONST_RESIDENT : 0u,
+                                   resident ? keys.key(np) : 0));
     }
   }
 };
@@ -126,7 +179,7 @@ class CudaExecutor {
   Result execute(ir::Graph& graph, const std::vector<ir::NodeId>& output_ids) {
     Result result;
     try {
-      GraphBridge bridge(graph);
+      GraphBridge bridge(graph, keys_);
       std::vector<uint64_t> ids;
       std::vector<void*> ptrs;
       std::vector<size_t> sizes;
@@ -166,6 +219,7 @@ class CudaExecutor {
 
  private:
   pfc_executor* ex_ = nullptr;
+  PayloadKeys keys_;
 };
 
 }  // namespace pyflame::backend::cuda

@@ -55,5 +55,16 @@ def test_full_batch_rows_match_single_sample_oracle(cuda_executor, oracle_mod, n
     ws = build(**small)
     ws.inputs[key].node().set_constant_data(np.ascontiguousarray(x[pick]))
     (ref,) = _oracle(oracle_mod, ws)
-    got = gpu[pick]
-    close_rows(got.reshape(len(pick), -1), ref.reshape(len(pick), -1), RTOL_GEMM_TF32X3, what=f"{name} full batch")
+    g = ws.outputs[0].graph()
+    oid = ws.outputs[0].node().id()
+    ref64 = oracle_mod.run(g, [oid], "f64")[oid]
+    got = gpu[pick].reshape(len(pick), -1)
+    ref = ref.reshape(len(pick), -1)
+    ref64 = ref64.reshape(len(pick), -1)
+    # Long contractions (K = 16384) carry the fp32 reference's own rounding
+    # (sequential fp32 sums): the GPU is held to 1e-4 of the exact (fp64)
+    # result, and to 1e-4 plus the reference's own deviation from it.
+    close_rows(got, ref64, RTOL_GEMM_TF32X3, what=f"{name} full batch vs fp64")
+    own = np.abs(ref.astype(np.float64) - ref64)
+    close(got, ref, rtol=RTOL_GEMM_TF32X3, atol=RTOL_GEMM_TF32X3 * np.sqrt(np.mean(ref64 ** 2, axis=1, keepdims=True)) + own,
+          what=f"{name} full batch vs fp32 reference")
