@@ -177,14 +177,71 @@ __device__ __forceinline__ void umma_commit(uint32_t mbar) {
                : "memory");
 }
 
-__device__ __forceinline__ float act_apply(float v, int act) {
-  switch (act) {
-    case 1: return (0.f < v) ? v : 0.f;
-    case 2: return 0.5f * v * (1.0f + tanhf(0.7978845608f * (v + 0.044715f * v * v * v)));
-    case 3: return 1.0f / (1.0f + expf(-v));
-    case 4: return tanhf(v);
-    case 5: return v / (1.0f + expf(-v));
-    default: return v;
+template <int ACT>
+__device__ __forceinline__ float act_apply(float v) {
+  if constexpr (ACT == 1) return (0.f < v) ? v : 0.f;
+  else if constexpr (ACT == 2) return 0.5f * v * (1.0f + tanhf(0.7978845608f * (v + 0.044715f * v * v * v)));
+  else if constexpr (ACT == 3) return 1.0f / (1.0f + expf(-v));
+  else if constexpr (ACT == 4) return tanhf(v);
+  else if constexpr (ACT == 5) return v / (1.0f + expf(-v));
+  else return v;
+}
+
+// Store one 32-row x 32-column block of a tile.  `ep` holds it row-major
+// with a 36-float row pitch; each pass a warp writes 4 rows x 32 columns,
+// lane l taking row l/8 and columns 4*(l%8)..+3 (a float4 where the output
+// is contiguous and aligned).  v = act(acc*sc[n] + sh[n]) (+ residual).
+template <int ACT>
+__device__ __forceinline__ void store_block(const GemmParams& p, const float* ep, int row0, int n0, float* cbase,
+                                            const float* rbase, bool vec_c, bool vec_r, float alpha, float bsc,
+                                            bool has_shift, int lane) {
+  const int rsub = lane >> 3, c4 = (lane & 7) * 4;
+  const int n = n0 + c4;
+  float sc[4], sh[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    sc[j] = alpha;
+    sh[j] = bsc;
+    if (n + j < p.N) {
+      if (p.scale) { sc[j] = p.scale[n + j]; sh[j] = p.shift[n + j]; }
+      else if (p.bias) sh[j] = p.bias[n + j];
+    }
+  }
+  const bool full_n = n + 3 < p.N;
+#pragma unroll 2
+  for (int rr = 0; rr < 32; rr += 4) {
+    const int row = row0 + rr + rsub;
+    const float4 a = *reinterpret_cast<const float4*>(ep + (rr + rsub) * 36 + c4);
+    float v[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[j] = v[j] * sc[j];
+      if (has_shift) v[j] = v[j] + sh[j];
+      v[j] = act_apply<ACT>(v[j]);
+    }
+    if (row >= p.M) continue;
+    const long long co = (long long)row * p.c_sm + (long long)n * p.c_sn;
+    if (full_n && vec_c) {
+      if (rbase) {
+        const long long ro = (long long)row * p.r_sm + (long long)n * p.r_sn;
+        if (vec_r) {
+          const float4 r4 = *reinterpret_cast<const float4*>(rbase + ro);
+          v[0] += r4.x; v[1] += r4.y; v[2] += r4.z; v[3] += r4.w;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) v[j] += rbase[ro + (long long)j * p.r_sn];
+        }
+      }
+      *reinterpret_cast<float4*>(cbase + co) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (n + j >= p.N) break;
+        float w = v[j];
+        if (rbase) w += rbase[(long long)row * p.r_sm + (long long)(n + j) * p.r_sn];
+        cbase[co + (long long)j * p.c_sn] = w;
+      }
+    }
   }
 }
 
@@ -199,7 +256,7 @@ struct Cfg {
   static constexpr int B_TILE = BN * 128;
   static constexpr int STAGE = NOPS * (A_TILE + B_TILE);
   // epilogue staging: per epilogue warp a 32 x 33 fp32 tile (padded: no bank conflicts)
-  static constexpr int EPI_WARP_FLOATS = 32 * 33;
+  static constexpr int EPI_WARP_FLOATS = 32 * 36;
   static constexpr int EPI_BYTES = 4 * EPI_WARP_FLOATS * 4;
   static constexpr int SMEM_LIMIT = 232448;  // 227 KB opt-in maximum per block
   static constexpr int STAGES_FIT = (SMEM_LIMIT - EPI_BYTES - 2048) / STAGE;
@@ -486,30 +543,23 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
       const int m0 = tm * kBM + q * 32, n0 = tn * BN;
       float* cbase = p.c + (long long)bz * p.c_sb;
       const float* rbase = p.res ? p.res + (long long)bz * p.r_sb : nullptr;
+      // float4 stores need contiguous, 16-byte aligned rows of the output (and residual)
+      const bool vec_c = p.c_sn == 1 && (p.c_sm & 3) == 0 && (((uintptr_t)cbase) & 15) == 0;
+      const bool vec_r = rbase && p.r_sn == 1 && (p.r_sm & 3) == 0 && (((uintptr_t)rbase) & 15) == 0;
 #pragma unroll
       for (int cc = 0; cc < BN; cc += 32) {
-        // transpose through shared memory: lane = row on the way in, lane = column on the way out
+        // transpose through shared memory: this lane's row in, 4 rows x 32 columns out per pass
 #pragma unroll
-        for (int j = 0; j < 32; ++j) ep[lane * 33 + j] = acc[cc + j];
+        for (int j = 0; j < 32; j += 4)
+          *reinterpret_cast<float4*>(ep + lane * 36 + j) = make_float4(acc[cc + j], acc[cc + j + 1], acc[cc + j + 2], acc[cc + j + 3]);
         __syncwarp();
-        const int n = n0 + cc + lane;
-        const bool nok = n < p.N;
-        float sc = alpha, sh = bsc;
-        if (nok) {
-          if (p.scale) { sc = p.scale[n]; sh = p.shift[n]; }
-          else if (p.bias) sh = p.bias[n];
-        }
-#pragma unroll 4
-        for (int rr = 0; rr < 32; ++rr) {
-          const int row = m0 + rr;
-          float v = ep[rr * 33 + lane];
-          v = v * sc;
-          if (has_shift) v = v + sh;
-          v = act_apply(v, p.act);
-          if (nok && row < p.M) {
-            if (rbase) v = v + rbase[(long long)row * p.r_sm + (long long)n * p.r_sn];
-            cbase[(long long)row * p.c_sm + (long long)n * p.c_sn] = v;
-          }
+        switch (p.act) {
+          case 1: store_block<1>(p, ep, m0, n0 + cc, cbase, rbase, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          case 2: store_block<2>(p, ep, m0, n0 + cc, cbase, rbase, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          case 3: store_block<3>(p, ep, m0, n0 + cc, cbase, rbase, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          case 4: store_block<4>(p, ep, m0, n0 + cc, cbase, rbase, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          case 5: store_block<5>(p, ep, m0, n0 + cc, cbase, rbase, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          default: store_block<0>(p, ep, m0, n0 + cc, cbase, rbase, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
         }
         __syncwarp();
       }
