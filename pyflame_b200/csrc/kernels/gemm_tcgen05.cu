@@ -4,21 +4,24 @@
 // executor (rocm_blas.cpp:75-153, called from rocm_executor.cpp:278-335) and
 // the fused bias/activation epilogues of rocm_kernels.hip:649-732.
 //
-// Structure: a persistent kernel, one CTA of 192 threads per SM, each CTA
+// Structure: a persistent kernel, one CTA of 320 threads per SM, each CTA
 // walking 128 x BN output tiles (tile blockIdx.x, +gridDim.x, ...):
 //   warp 0      TMA producer: K-major 128-byte-swizzled tiles of A and B into a
 //               ring of shared-memory stages, completion on mbarriers; the
-//               ring runs on across tile boundaries.
+//               ring runs on across tile boundaries.  (Implicit-GEMM Conv2d:
+//               warps 0..3 gather A rows instead, and the roles below shift
+//               up by three warps.)
 //   warp 1      TMEM allocator and MMA issuer: one elected thread issues
 //               tcgen05.mma (kind::tf32 x3 for split-fp32 operands, or
 //               kind::f16 with bf16 operands) into one of two TMEM fp32
 //               accumulators and frees each stage with tcgen05.commit.
-//   warps 2..5  epilogue: tcgen05.ld of each finished accumulator (warp w
-//               reads TMEM lanes 32*(w%4)..+31) into fp32 registers, returns
-//               it to the MMA warp, and once a tile's K is complete
-//               transposes 32x32 blocks through shared memory so that a warp
-//               stores 32 consecutive columns of a row, applying
-//               alpha/bias/folded-BN/activation/residual.  With two
+//   warps 2..9  epilogue, two warps per TMEM lane quarter (warp w reads
+//               lanes 32*(w%4)..+31), each taking half of the tile's
+//               columns: tcgen05.ld of each finished accumulator into fp32
+//               registers, returned at once to the MMA warp; once a tile's K
+//               is complete, 32x16 blocks go through shared memory so that a
+//               warp stores 8 rows x 16 consecutive columns per float4 pass,
+//               applying alpha/bias/folded-BN/activation/residual.  With two
 //               accumulators the epilogue of tile i overlaps the MMAs of i+1.
 // K is accumulated in chunks of 512 elements, each into a fresh accumulator,
 // and the chunks are summed in fp32 registers: a long accumulation inside the
@@ -41,11 +44,13 @@ namespace pfb {
 namespace {
 
 constexpr int kBM = 128;
-// Warps: producers (1 TMA warp, or 4 gathering warps for CONV), 1 MMA warp, 4 epilogue warps.
+// Warps: producers (1 TMA warp, or 4 gathering warps for CONV), 1 MMA warp,
+// 8 epilogue warps (two per TMEM lane quarter, each taking half the columns).
+constexpr int kEpiWarps = 8;
 template <bool CONV>
 constexpr int kProdWarps = CONV ? 4 : 1;
 template <bool CONV>
-constexpr int kThreads = (kProdWarps<CONV> + 5) * 32;
+constexpr int kThreads = (kProdWarps<CONV> + 1 + kEpiWarps) * 32;
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s per wait
 
 struct GemmParams {
@@ -187,15 +192,15 @@ __device__ __forceinline__ float act_apply(float v) {
   else return v;
 }
 
-// Store one 32-row x 32-column block of a tile.  `ep` holds it row-major
-// with a 36-float row pitch; each pass a warp writes 4 rows x 32 columns,
-// lane l taking row l/8 and columns 4*(l%8)..+3 (a float4 where the output
+// Store one 32-row x 16-column block of a tile.  `ep` holds it row-major
+// with a 20-float row pitch; each pass a warp writes 8 rows x 16 columns,
+// lane l taking row l/4 and columns 4*(l%4)..+3 (a float4 where the output
 // is contiguous and aligned).  v = act(acc*sc[n] + sh[n]) (+ residual).
 template <int ACT>
 __device__ __forceinline__ void store_block(const GemmParams& p, const float* ep, int row0, int n0, float* cbase,
                                             const float* rbase, bool vec_c, bool vec_r, float alpha, float bsc,
                                             bool has_shift, int lane) {
-  const int rsub = lane >> 3, c4 = (lane & 7) * 4;
+  const int rsub = lane >> 2, c4 = (lane & 3) * 4;
   const int n = n0 + c4;
   float sc[4], sh[4];
 #pragma unroll
@@ -208,11 +213,31 @@ __device__ __forceinline__ void store_block(const GemmParams& p, const float* ep
     }
   }
   const bool full_n = n + 3 < p.N;
-#pragma unroll 2
-  for (int rr = 0; rr < 32; rr += 4) {
-    const int row = row0 + rr + rsub;
-    const float4 a = *reinterpret_cast<const float4*>(ep + (rr + rsub) * 36 + c4);
-    float v[4] = {a.x, a.y, a.z, a.w};
+  // all four passes' shared-memory reads in flight at once
+  float4 a[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) a[k] = *reinterpret_cast<const float4*>(ep + (8 * k + rsub) * 20 + c4);
+  if (full_n && vec_c && row0 + 32 <= p.M && !rbase) {
+    // whole block inside the output, no residual: straight float4 stores
+    float* dst = cbase + (long long)(row0 + rsub) * p.c_sm + n;
+    const long long step = 8 * p.c_sm;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float v[4] = {a[k].x, a[k].y, a[k].z, a[k].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[j] = v[j] * sc[j];
+        if (has_shift) v[j] = v[j] + sh[j];
+        v[j] = act_apply<ACT>(v[j]);
+      }
+      *reinterpret_cast<float4*>(dst + k * step) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+    return;
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int row = row0 + 8 * k + rsub;
+    float v[4] = {a[k].x, a[k].y, a[k].z, a[k].w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       v[j] = v[j] * sc[j];
@@ -256,8 +281,8 @@ struct Cfg {
   static constexpr int B_TILE = BN * 128;
   static constexpr int STAGE = NOPS * (A_TILE + B_TILE);
   // epilogue staging: per epilogue warp a 32 x 33 fp32 tile (padded: no bank conflicts)
-  static constexpr int EPI_WARP_FLOATS = 32 * 36;
-  static constexpr int EPI_BYTES = 4 * EPI_WARP_FLOATS * 4;
+  static constexpr int EPI_WARP_FLOATS = 32 * 20;  // a 32 x 16 block, 20-float pitch
+  static constexpr int EPI_BYTES = kEpiWarps * EPI_WARP_FLOATS * 4;
   static constexpr int SMEM_LIMIT = 232448;  // 227 KB opt-in maximum per block
   static constexpr int STAGES_FIT = (SMEM_LIMIT - EPI_BYTES - 2048) / STAGE;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
@@ -290,6 +315,7 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // make this thread's completed generic-proxy shared-memory writes visible to
 // the tensor cores (async proxy)
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 
 // Tile t of the persistent schedule -> (batch, m tile, n tile).  Within a
 // batch slice, groups of 16 M-tiles sweep all N-tiles, so the B tiles of a
@@ -342,7 +368,7 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&acc_full[b]), 1);
-      mbar_init(smem_u32(&acc_empty[b]), 4);  // one arrival per epilogue warp
+      mbar_init(smem_u32(&acc_empty[b]), kEpiWarps);  // one arrival per epilogue warp
     }
     mbar_init(smem_u32(done), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -503,18 +529,21 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
     umma_commit(smem_u32(done));
   } else if (warp > PW) {
     // ---------------- epilogue ----------------
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    float* ep = epi + (warp - PW - 1) * C::EPI_WARP_FLOATS;
+    constexpr int HALF = BN / 2;  // columns per epilogue warp
+    const int e = warp - PW - 1;  // 0..7
+    const int q = warp & 3;       // TMEM lane quarter this warp may access
+    const int col0 = (e >> 2) * HALF;
+    float* ep = epi + e * C::EPI_WARP_FLOATS;
     const float alpha = p.alpha_ptr ? *p.alpha_ptr : p.alpha;
     const float bsc = p.bias_scalar ? *p.bias_scalar : 0.f;
     const bool has_shift = p.scale || p.bias || p.bias_scalar;
     int u = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-      // this thread's row of the tile: the sum of the chunk accumulators
-      float acc[BN];
+      // this thread's row of the tile, columns col0..col0+HALF: the sum of the chunk accumulators
+      float acc[HALF];
 #pragma unroll
-      for (int j = 0; j < BN; ++j) acc[j] = 0.f;
+      for (int j = 0; j < HALF; ++j) acc[j] = 0.f;
       for (int ch = 0; ch < p.nchunks; ++ch, ++u) {
         const int b = u & 1;
         const uint32_t use = (uint32_t)(u >> 1);
@@ -522,9 +551,9 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         if (nkb > 0) {
 #pragma unroll
-          for (int cc = 0; cc < BN; cc += 32) {
+          for (int cc = 0; cc < HALF; cc += 32) {
             uint32_t r[32];
-            const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + cc);
+            const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + col0 + cc);
             tmem_ld16_nowait(ta, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
             tmem_ld16_nowait(ta + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
@@ -540,18 +569,18 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
       if (!ok) break;
       int bz, tm, tn;
       tile_coords(p, t, bz, tm, tn);
-      const int m0 = tm * kBM + q * 32, n0 = tn * BN;
+      const int m0 = tm * kBM + q * 32, n0 = tn * BN + col0;
       float* cbase = p.c + (long long)bz * p.c_sb;
       const float* rbase = p.res ? p.res + (long long)bz * p.r_sb : nullptr;
       // float4 stores need contiguous, 16-byte aligned rows of the output (and residual)
       const bool vec_c = p.c_sn == 1 && (p.c_sm & 3) == 0 && (((uintptr_t)cbase) & 15) == 0;
       const bool vec_r = rbase && p.r_sn == 1 && (p.r_sm & 3) == 0 && (((uintptr_t)rbase) & 15) == 0;
 #pragma unroll
-      for (int cc = 0; cc < BN; cc += 32) {
-        // transpose through shared memory: this lane's row in, 4 rows x 32 columns out per pass
+      for (int cc = 0; cc < HALF; cc += 16) {
+        // transpose through shared memory: this lane's row in, 8 rows x 16 columns out per pass
 #pragma unroll
-        for (int j = 0; j < 32; j += 4)
-          *reinterpret_cast<float4*>(ep + lane * 36 + j) = make_float4(acc[cc + j], acc[cc + j + 1], acc[cc + j + 2], acc[cc + j + 3]);
+        for (int j = 0; j < 16; j += 4)
+          *reinterpret_cast<float4*>(ep + lane * 20 + j) = make_float4(acc[cc + j], acc[cc + j + 1], acc[cc + j + 2], acc[cc + j + 3]);
         __syncwarp();
         switch (p.act) {
           case 1: store_block<1>(p, ep, m0, n0 + cc, cbase, rbase, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
@@ -701,8 +730,7 @@ void launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
   PFB_CHECK_ARG(((uintptr_t)L.b_hi & 15) == 0, "gemm: operands must be 16-byte aligned");
   if (L.precision == PFC_PRECISION_BF16) {
     if (L.conv) {
-      if (L.N > 64) launch_t<PFC_PRECISION_BF16, 128, true>(L, stream);
-      else launch_t<PFC_PRECISION_BF16, 64, true>(L, stream);
+      launch_t<PFC_PRECISION_BF16, 64, true>(L, stream);
     } else {
       if (L.N > 64) launch_t<PFC_PRECISION_BF16, 128, false>(L, stream);
       else launch_t<PFC_PRECISION_BF16, 64, false>(L, stream);
@@ -710,8 +738,9 @@ void launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
   } else {
     PFB_CHECK_ARG(L.b_lo && (L.conv || L.a_lo), "gemm: tf32x3 needs lo operands");
     if (L.conv) {
-      if (L.N > 64) launch_t<PFC_PRECISION_TF32X3, 128, true>(L, stream);
-      else launch_t<PFC_PRECISION_TF32X3, 64, true>(L, stream);
+      // 64-column tiles: the gathering warps leave too few registers for a
+      // 128-column accumulator (wider convolutions take several column tiles)
+      launch_t<PFC_PRECISION_TF32X3, 64, true>(L, stream);
     } else {
       if (L.N > 64) launch_t<PFC_PRECISION_TF32X3, 128, false>(L, stream);
       else launch_t<PFC_PRECISION_TF32X3, 64, false>(L, stream);
