@@ -40,7 +40,7 @@ def _sources():
 
 
 def _headers():
-    hs = list(CSRC.rglob("*.hpp")) + list((ROOT / "include").glob("*.h"))
+    hs = list(CSRC.rglob("*.hpp")) + list(CSRC.rglob("*.cuh")) + list((ROOT / "include").glob("*.h"))
     return max((h.stat().st_mtime for h in hs), default=0.0)
 
 

@@ -171,6 +171,10 @@ struct RowOp {
   int src = -1, gamma = -1, beta = -1;
   float eps = 1e-5f;
   View out;   // reductions: dense [outer*inner]; softmax/LN: view shaped like space
+  // softmax/LN feeding GEMMs: the row kernel also writes the tf32x3 operand
+  // (hi/lo at the dense offsets of `out`); `out` itself only when read elsewhere
+  int op_hi = -1, op_lo = -1;
+  bool write_out = true;
 };
 
 struct RowSpec {
@@ -201,6 +205,14 @@ __device__ __forceinline__ float pf_gelu(float x) {
 __device__ __forceinline__ float pf_silu(float x) { return x / (1.0f + expf(-x)); }
 __device__ __forceinline__ float pf_max(float a, float b) { return fmaxf(a, b); }
 __device__ __forceinline__ float pf_min(float a, float b) { return fminf(a, b); }
+// The 3xTF32 operand split (identical to the precompiled kernels'): hi keeps
+// sign, exponent and the top 10 mantissa bits, lo the exact remainder;
+// non-finite values go entirely into hi (NaN canonicalised).
+__device__ __forceinline__ void pf_split(float x, float& hi, float& lo) {
+  if (!isfinite(x)) { hi = isnan(x) ? __int_as_float(0x7fc00000) : x; lo = 0.f; return; }
+  hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+  lo = x - hi;
+}
 )";
 
 // Helpers for kernels that stream rows into shared memory with 1-D TMA bulk
@@ -632,6 +644,15 @@ std::string gen_row(const RowSpec& rs, const std::string& name, int num_sms, int
   size_t nops = rs.ops.size();
   for (size_t r = 0; r < nops; ++r) o << "  float* __restrict__ ro" << r << " = (float*)A.p[" << nl + ns + r << "];\n";
   o << "  const float* __restrict__ scal = (const float*)A.p[" << nl + ns + nops << "];\n";
+  {
+    // operand outputs follow the error flag: hi, lo per row op that has them
+    size_t k = nl + ns + nops + 2;
+    for (size_t r = 0; r < nops; ++r) {
+      if (rs.ops[r].op_hi < 0) continue;
+      o << "  float* __restrict__ oph" << r << " = (float*)A.p[" << k++ << "];\n";
+      o << "  float* __restrict__ opl" << r << " = (float*)A.p[" << k++ << "];\n";
+    }
+  }
   for (size_t i = 0; i < nl; ++i)
     if (s.loads[i].is_splat) o << "  const float sp" << i << " = scal[" << s.loads[i].splat_slot << "];\n";
   const int TPR = L.tpr, RPB = L.rpb, VEC = L.vec, NCH = L.nch;
@@ -941,13 +962,21 @@ std::string gen_row(const RowSpec& rs, const std::string& name, int num_sms, int
         if (op.beta >= 0) o << "          t = t + ev[" << op.beta << "][q];\n";
         o << "          y[q] = t;\n";
       }
-      o << "        }\n        if (cok) { float* ptr = ro" << r << " + ro_" << vi << " + ("
+      o << "        }\n        if (cok) { const " << ity << " off = ro_" << vi << " + ("
         << emit_offset(st, "w", ncd, 0, ity) << ");\n";
-      if (VEC == 4 && st.back() == 1)
-        o << "          *(float4*)ptr = make_float4(y[0], y[1], y[2], y[3]); } }\n";
-      else
+      if (op.write_out) {
+        if (VEC == 4 && st.back() == 1)
+          o << "          *(float4*)(ro" << r << " + off) = make_float4(y[0], y[1], y[2], y[3]);\n";
+        else
+          o << "          for (int q = 0; q < " << VEC << "; ++q) if (cl + q < (" << ity << ")" << L.C << ") ro" << r
+            << "[off + q * (" << ity << ")" << st.back() << "] = y[q];\n";
+      }
+      if (op.op_hi >= 0) {
+        // dense row-major `out`: the operand element shares its offset
         o << "          for (int q = 0; q < " << VEC << "; ++q) if (cl + q < (" << ity << ")" << L.C
-          << ") ptr[q * (" << ity << ")" << st.back() << "] = y[q]; } }\n";
+          << ") { float h, l; pf_split(y[q], h, l); oph" << r << "[off + q] = h; opl" << r << "[off + q] = l; }\n";
+      }
+      o << "        } }\n";
     }
     o << "    }\n";
   }
@@ -1324,6 +1353,41 @@ class Compiler {
     int hi = -1, lo = -1;
   };
   std::unordered_map<std::string, Operand> operands_;  // view signature -> operand already in the plan
+  // operands written by row kernels, keyed (buffer, rows, cols, kpad, precision)
+  using OpKey = std::tuple<int, int64_t, int64_t, int64_t, int>;
+  std::map<OpKey, Operand> pending_;
+  std::set<OpKey> claimed_;
+  std::set<OpKey> must_claim_;  // the fp32 value is not written: a GEMM must take the operand
+
+  // A softmax/LayerNorm output that MATMULs read as their A operand is
+  // written by its row kernel as a tf32x3 operand too; the fp32 value stays
+  // when anything else reads it.
+  void plan_row_operand(uint64_t id, RowOp& op) {
+    if (in_.precision != PFC_PRECISION_TF32X3) return;
+    if (!(op.op == Op::SOFTMAX || op.op == Op::LOG_SOFTMAX || op.op == Op::LAYER_NORM)) return;
+    const View& o = op.out;
+    if (o.is_splat || o.offset != 0 || o.strides != View::dense_strides(o.shape) || o.shape.size() < 2) return;
+    const int64_t C = o.shape.back();
+    if (C % 32 != 0) return;
+    bool any_mm = false, other = is_out_.count(id) > 0;
+    for (uint64_t u : users_[id]) {
+      const Node& un = N(u);
+      auto ci = cls_.find(u);
+      const bool a_operand = un.op == Op::MATMUL && ci != cls_.end() && ci->second == Cls::GEMM &&
+                             un.inputs.size() == 2 && un.inputs[0] == id && un.inputs[1] != id &&
+                             N(un.inputs[1]).shape.size() <= o.shape.size();
+      if (a_operand) any_mm = true;
+      else other = true;
+    }
+    if (!any_mm) return;
+    const int64_t rows = o.numel() / C;
+    op.op_hi = new_buffer((size_t)rows * C * 4);
+    op.op_lo = new_buffer((size_t)rows * C * 4);
+    op.write_out = other;
+    const OpKey key = std::make_tuple(o.buf, rows, C, C, in_.precision);
+    pending_[key] = Operand{op.op_hi, op.op_lo};
+    if (!other) must_claim_.insert(key);
+  }
 
   // Emit (or reuse) the preparation of `src` ([rows, cols] logical, any
   // strides) as a GEMM operand.  Values are written once in a plan, so an
@@ -1334,6 +1398,13 @@ class Compiler {
   // implicit GEMM (k = (kh*KW + kw)*conv_cp + c).
   Operand prepare_operand(const View& src, int64_t rows, int64_t cols, int64_t kpad, int prec,
                           const std::string& label, int at, int64_t conv_cp = 0) {
+    if (conv_cp == 0 && !src.is_splat && src.buf >= 0 && src.offset == 0 && src.strides == View::dense_strides(src.shape)) {
+      auto pit = pending_.find(std::make_tuple(src.buf, rows, cols, kpad, prec));
+      if (pit != pending_.end()) {
+        claimed_.insert(pit->first);
+        return pit->second;
+      }
+    }
     std::ostringstream sig;
     sig << src.buf << ':' << src.offset << ':' << (int)src.dtype << ':' << src.is_splat << ':' << src.splat_slot;
     for (size_t d = 0; d < src.shape.size(); ++d) sig << ',' << src.shape[d] << '/' << src.strides[d];
@@ -1406,6 +1477,7 @@ class Compiler {
   void emit_jit(int at, const std::string& label, const std::string& kernel, const std::string& source, int grid,
                 int block, const std::vector<std::pair<int, int64_t>>& ptrs, size_t smem = 0);
   void finish();
+  void emit_operands_at_producers();
 
   bool must_materialize(uint64_t id);
   bool row_structure(uint64_t row, const std::vector<int64_t>& in_shape, int* rb, int* re, bool* full);
@@ -1992,10 +2064,11 @@ void Compiler::lower_region(int r) {
       op.out = dense(rn.shape, DType::F32);
     }
     val_[rid] = op.out;
+    if (!rg.full && prod(s.space, rg.red_end) == 1) plan_row_operand(rid, op);
     rs.ops.push_back(op);
   }
   push_ptrs();
-  for (const RowOp& op : rs.ops) ptrs.push_back({op.out.buf, 0});
+  for (const RowOp& op : rs.ops) ptrs.push_back({op.write_out ? op.out.buf : -1, 0});
   ptrs.push_back({P_->scalar_buf, 0});
   int64_t outer = prod(s.space, 0, rs.red_begin), inner = prod(s.space, rs.red_end);
   std::string label;
@@ -2024,6 +2097,8 @@ void Compiler::lower_region(int r) {
                                  : gen_col(rs, name, in_.num_sms, &grid, &block);
   (void)outer;
   ptrs.push_back({kErrorFlagBuffer, 0});
+  for (const RowOp& op : rs.ops)
+    if (op.op_hi >= 0) ptrs.push_back({op.op_hi, 0}), ptrs.push_back({op.op_lo, 0});
   emit_jit(at, std::string(inner == 1 ? "row kernel (" : "column kernel (") + label + ") " + shape_str(s.space), name,
            code, grid, block, ptrs, smem);
 }
@@ -2076,12 +2151,13 @@ void Compiler::lower_row_alone(uint64_t id) {
   else
     op.out = dense(n.shape, DType::F32);
   val_[id] = op.out;
+  if (!full && prod(s.space, re) == 1) plan_row_operand(id, op);
   rs.ops.push_back(op);
   rs.red_begin = rb;
   rs.red_end = re;
   std::vector<std::pair<int, int64_t>> ptrs;
   for (const View& l : s.loads) ptrs.push_back({l.is_splat ? -1 : l.buf, l.offset * (int64_t)dtype_size(l.dtype)});
-  ptrs.push_back({op.out.buf, 0});
+  ptrs.push_back({op.write_out ? op.out.buf : -1, 0});
   ptrs.push_back({P_->scalar_buf, 0});
   int64_t inner = prod(s.space, re);
   if (full) {
@@ -2104,6 +2180,7 @@ void Compiler::lower_row_alone(uint64_t id) {
   std::string code = inner == 1 ? gen_row(rs, name, in_.num_sms, &grid, &block, &smem)
                                  : gen_col(rs, name, in_.num_sms, &grid, &block);
   ptrs.push_back({kErrorFlagBuffer, 0});
+  if (rs.ops[0].op_hi >= 0) ptrs.push_back({rs.ops[0].op_hi, 0}), ptrs.push_back({rs.ops[0].op_lo, 0});
   emit_jit(pos_[id], std::string(inner == 1 ? "row kernel (" : "column kernel (") + op_name(n.op) + ") " +
                          shape_str(s.space),
            name, code, grid, block, ptrs, smem);
@@ -2515,7 +2592,118 @@ void Compiler::lower() {
   cur_pos_ = step_pos;
 }
 
+// Operand preparation moved into the producer.  A SPLIT of a GEMM's output
+// (the A operand of the next GEMM: dense rows, K = the producer's N = kpad)
+// and a CONV_INPUT of a GEMM's or pool's channels-last output (C = Cp) are
+// written by the producer's epilogue directly, and the preparation step is
+// dropped; the fp32 value is still written when anything else reads it.
+void Compiler::emit_operands_at_producers() {
+  std::vector<Step>& S = P_->steps;
+  const int nb = (int)P_->buffers.size();
+  std::vector<std::vector<int>> refs(nb);  // buffer -> steps referring to it
+  auto add = [&](int buf, int i) {
+    if (buf >= 0 && buf < nb) refs[buf].push_back(i);
+  };
+  for (int i = 0; i < (int)S.size(); ++i) {
+    const Step& st = S[i];
+    switch (st.kind) {
+      case StepKind::JIT: for (auto& pr : st.jit.ptrs) add(pr.first, i); break;
+      case StepKind::SPLIT: add(st.split.src.buf, i); add(st.split.out_hi, i); add(st.split.out_lo, i); break;
+      case StepKind::IM2COL: add(st.im2col.x.buf, i); add(st.im2col.out_hi, i); add(st.im2col.out_lo, i); break;
+      case StepKind::CONV_INPUT: add(st.convin.x.buf, i); add(st.convin.out_hi, i); add(st.convin.out_lo, i); break;
+      case StepKind::GEMM: {
+        const GemmArgs& G = st.gemm;
+        add(G.a_hi, i); add(G.a_lo, i); add(G.b_hi, i); add(G.b_lo, i); add(G.c.buf, i);
+        if (G.has_bias) add(G.bias.buf, i);
+        if (G.has_residual) add(G.residual.buf, i);
+        add(G.scale_buf, i); add(G.shift_buf, i); add(G.x_hi, i); add(G.x_lo, i);
+        break;
+      }
+      case StepKind::POOL: add(st.pool.x.buf, i); add(st.pool.y.buf, i); break;
+      case StepKind::BN_FOLD: {
+        const BnFoldArgs& F = st.bnfold;
+        add(F.gamma.buf, i); add(F.beta.buf, i); add(F.mean.buf, i); add(F.var.buf, i); add(F.bias.buf, i);
+        add(F.out_scale, i); add(F.out_shift, i);
+        break;
+      }
+      case StepKind::MEMSET: add(st.memset_buf, i); break;
+    }
+  }
+  std::unordered_set<int> out_bufs;
+  for (const View& v : P_->output_views) out_bufs.insert(v.buf);
+  // the step writing buffer b: the GEMM or pool whose output it is
+  auto producer = [&](int b) -> int {
+    for (int j : refs[b]) {
+      const Step& st = S[j];
+      if (st.kind == StepKind::GEMM && st.gemm.c.buf == b && st.gemm.write_c) return j;
+      if (st.kind == StepKind::POOL && st.pool.y.buf == b && st.pool.write_y) return j;
+    }
+    return -1;
+  };
+  std::vector<bool> drop(S.size(), false);
+  auto others_read = [&](int b, int j, int i) {
+    if (out_bufs.count(b)) return true;
+    for (int u : refs[b])
+      if (u != j && u != i && !drop[u]) return true;
+    return false;
+  };
+  for (int i = 0; i < (int)S.size(); ++i) {
+    Step& st = S[i];
+    if (st.kind == StepKind::SPLIT && !st.once && st.split.conv_cp == 0) {
+      const View& v = st.split.src;
+      if (v.is_splat || v.buf < 0 || v.offset != 0 || v.strides != View::dense_strides(v.shape)) continue;
+      const int j = producer(v.buf);
+      if (j < 0 || j > i || S[j].kind != StepKind::GEMM) continue;
+      GemmArgs& G = S[j].gemm;
+      const bool dense_c = G.c.offset == 0 && G.c_sn == 1 && G.c_sm == G.N && (G.batch == 1 || G.c_sb == G.M * G.N);
+      if (G.op_hi >= 0 || !dense_c || st.split.cols != G.N || st.split.kpad != G.N || G.N % 4 != 0 ||
+          st.split.rows != G.batch * G.M)
+        continue;
+      G.op_hi = st.split.out_hi;
+      G.op_lo = st.split.out_lo;
+      G.op_sm = st.split.kpad;
+      drop[i] = true;
+      G.write_c = others_read(v.buf, j, i);
+      S[j].label += " +operand";
+    } else if (st.kind == StepKind::CONV_INPUT) {
+      const View& x = st.convin.x;  // [N,C,H,W]
+      if (x.is_splat || x.buf < 0 || x.offset != 0 || x.shape.size() != 4 || x.shape[1] != st.convin.cp) continue;
+      const int64_t C = x.shape[1], H = x.shape[2], W = x.shape[3];
+      if (x.strides != std::vector<int64_t>{H * W * C, 1, W * C, C}) continue;  // channels-last
+      const int j = producer(x.buf);
+      if (j < 0 || j > i) continue;
+      if (S[j].kind == StepKind::GEMM) {
+        GemmArgs& G = S[j].gemm;
+        if (G.op_hi >= 0 || G.batch != 1 || G.c.offset != 0 || G.c_sn != 1 || G.c_sm != C || G.N != C || C % 4 != 0)
+          continue;
+        G.op_hi = st.convin.out_hi;
+        G.op_lo = st.convin.out_lo;
+        G.op_sm = C;
+        drop[i] = true;
+        G.write_c = others_read(x.buf, j, i);
+        S[j].label += " +operand";
+      } else if (S[j].kind == StepKind::POOL) {
+        PoolArgs& Pl = S[j].pool;
+        if (Pl.op_hi >= 0 || Pl.y.offset != 0 || Pl.y.strides != x.strides || Pl.y.shape != x.shape) continue;
+        Pl.op_hi = st.convin.out_hi;
+        Pl.op_lo = st.convin.out_lo;
+        drop[i] = true;
+        Pl.write_y = others_read(x.buf, j, i);
+        S[j].label += " +operand";
+      }
+    }
+  }
+  std::vector<Step> kept;
+  for (int i = 0; i < (int)S.size(); ++i)
+    if (!drop[i]) kept.push_back(std::move(S[i]));
+  S = std::move(kept);
+}
+
 void Compiler::finish() {
+  for (const OpKey& k : must_claim_)
+    if (!claimed_.count(k))
+      fail(PFC_ERR_INTERNAL, "a row kernel's operand output was not taken by its GEMM (buffer " +
+                                 std::to_string(std::get<0>(k)) + ")");
   // outputs: dense contiguous views (copies run after everything else)
   for (uint64_t o : in_.outputs) {
     View v = value(o);
@@ -2533,6 +2721,7 @@ void Compiler::finish() {
   // order steps by position (stable keeps emission order within a position)
   std::stable_sort(steps_.begin(), steps_.end(), [](const auto& a, const auto& b) { return a.first < b.first; });
   for (auto& [pos, s] : steps_) P_->steps.push_back(std::move(s));
+  emit_operands_at_producers();
   // liveness
   auto use = [&](int buf, int step) {
     if (buf < 0) return;
@@ -2549,14 +2738,20 @@ void Compiler::finish() {
       case StepKind::CONV_INPUT: use(s.convin.x.buf, i); use(s.convin.out_hi, i); use(s.convin.out_lo, i); break;
       case StepKind::GEMM: {
         const GemmArgs& G = s.gemm;
-        use(G.a_hi, i); use(G.a_lo, i); use(G.b_hi, i); use(G.b_lo, i); use(G.c.buf, i);
+        use(G.a_hi, i); use(G.a_lo, i); use(G.b_hi, i); use(G.b_lo, i);
+        if (G.write_c) use(G.c.buf, i);
+        use(G.op_hi, i); use(G.op_lo, i);
         if (G.conv) { use(G.x_hi, i); use(G.x_lo, i); }
         if (G.has_bias) use(G.bias.buf, i);
         if (G.has_residual) use(G.residual.buf, i);
         use(G.scale_buf, i); use(G.shift_buf, i);
         break;
       }
-      case StepKind::POOL: use(s.pool.x.buf, i); use(s.pool.y.buf, i); break;
+      case StepKind::POOL:
+        use(s.pool.x.buf, i);
+        if (s.pool.write_y) use(s.pool.y.buf, i);
+        use(s.pool.op_hi, i); use(s.pool.op_lo, i);
+        break;
       case StepKind::BN_FOLD: {
         const BnFoldArgs& F = s.bnfold;
         if (F.has_gamma) use(F.gamma.buf, i);

@@ -424,6 +424,10 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
         L.r_sb = a.r_sb; L.r_sm = a.r_sm; L.r_sn = a.r_sn;
       }
       L.err = err_dev_;
+      if (!a.write_c) L.c = nullptr;
+      L.out_hi = bufp(a.op_hi, 0);
+      L.out_lo = (float*)bufp(a.op_lo, 0);
+      L.o_sm = a.op_sm;
       if (a.conv) {
         L.conv = true;
         L.x_hi = bufp(a.x_hi, 0);
@@ -445,6 +449,10 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
       L.kh = a.kh; L.kw = a.kw; L.stride_h = a.sh; L.stride_w = a.sw; L.pad_h = a.ph; L.pad_w = a.pw;
       L.oh = a.y.shape[2]; L.ow = a.y.shape[3];
       L.osn = a.y.strides[0]; L.osc = a.y.strides[1]; L.osh = a.y.strides[2]; L.osw = a.y.strides[3];
+      if (!a.write_y) L.y = nullptr;
+      L.out_hi = bufp(a.op_hi, 0);
+      L.out_lo = (float*)bufp(a.op_lo, 0);
+      L.precision = P.precision;
       launch_pool(L, s);
       break;
     }

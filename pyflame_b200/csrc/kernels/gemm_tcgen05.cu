@@ -36,8 +36,11 @@
 #include <cstdint>
 #include <cstring>
 
+#include <cuda_bf16.h>
+
 #include "../common.hpp"
 #include "kernels.hpp"
+#include "split.cuh"
 
 namespace pfb {
 
@@ -69,6 +72,9 @@ struct GemmParams {
   int* err;
   int num_m, num_n, batch;
   int kchunk, nchunks;  // k-blocks per accumulation chunk; chunks per tile
+  void* o_hi;           // operand outputs for a following GEMM (or null)
+  float* o_lo;
+  long long o_sm;
   // implicit-GEMM Conv2d (CONV kernels): channels-last input [N][H][W][Cp]
   const void* x_hi;
   const void* x_lo;
@@ -196,10 +202,41 @@ __device__ __forceinline__ float act_apply(float v) {
 // with a 20-float row pitch; each pass a warp writes 8 rows x 16 columns,
 // lane l taking row l/4 and columns 4*(l%4)..+3 (a float4 where the output
 // is contiguous and aligned).  v = act(acc*sc[n] + sh[n]) (+ residual).
-template <int ACT>
+// Write 4 consecutive values of a row as operand elements (split or bf16).
+template <int PREC>
+__device__ __forceinline__ void store_operand4(void* ohi, float* olo, long long off, const float (&v)[4]) {
+  if constexpr (PREC == PFC_PRECISION_BF16) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+    uint2 pk;
+    pk.x = *reinterpret_cast<uint32_t*>(&a);
+    pk.y = *reinterpret_cast<uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(ohi) + off) = pk;
+  } else {
+    float4 h, l;
+    split_tf32(v[0], h.x, l.x);
+    split_tf32(v[1], h.y, l.y);
+    split_tf32(v[2], h.z, l.z);
+    split_tf32(v[3], h.w, l.w);
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(ohi) + off) = h;
+    *reinterpret_cast<float4*>(olo + off) = l;
+  }
+}
+template <int PREC>
+__device__ __forceinline__ void store_operand1(void* ohi, float* olo, long long off, float v) {
+  if constexpr (PREC == PFC_PRECISION_BF16) {
+    reinterpret_cast<__nv_bfloat16*>(ohi)[off] = __float2bfloat16_rn(v);
+  } else {
+    float h, l;
+    split_tf32(v, h, l);
+    reinterpret_cast<float*>(ohi)[off] = h;
+    olo[off] = l;
+  }
+}
+
+template <int ACT, int PREC>
 __device__ __forceinline__ void store_block(const GemmParams& p, const float* ep, int row0, int n0, float* cbase,
-                                            const float* rbase, bool vec_c, bool vec_r, float alpha, float bsc,
-                                            bool has_shift, int lane) {
+                                            const float* rbase, void* ohi, float* olo, bool vec_c, bool vec_r,
+                                            float alpha, float bsc, bool has_shift, int lane) {
   const int rsub = lane >> 2, c4 = (lane & 3) * 4;
   const int n = n0 + c4;
   float sc[4], sh[4];
@@ -219,8 +256,8 @@ __device__ __forceinline__ void store_block(const GemmParams& p, const float* ep
   for (int k = 0; k < 4; ++k) a[k] = *reinterpret_cast<const float4*>(ep + (8 * k + rsub) * 20 + c4);
   if (full_n && vec_c && row0 + 32 <= p.M && !rbase) {
     // whole block inside the output, no residual: straight float4 stores
-    float* dst = cbase + (long long)(row0 + rsub) * p.c_sm + n;
-    const long long step = 8 * p.c_sm;
+    const long long c0 = (long long)(row0 + rsub) * p.c_sm + n, cstep = 8 * p.c_sm;
+    const long long o0 = (long long)(row0 + rsub) * p.o_sm + n, ostep = 8 * p.o_sm;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       float v[4] = {a[k].x, a[k].y, a[k].z, a[k].w};
@@ -230,7 +267,8 @@ __device__ __forceinline__ void store_block(const GemmParams& p, const float* ep
         if (has_shift) v[j] = v[j] + sh[j];
         v[j] = act_apply<ACT>(v[j]);
       }
-      *reinterpret_cast<float4*>(dst + k * step) = make_float4(v[0], v[1], v[2], v[3]);
+      if (cbase) *reinterpret_cast<float4*>(cbase + c0 + k * cstep) = make_float4(v[0], v[1], v[2], v[3]);
+      if (ohi) store_operand4<PREC>(ohi, olo, o0 + k * ostep, v);
     }
     return;
   }
@@ -246,6 +284,7 @@ __device__ __forceinline__ void store_block(const GemmParams& p, const float* ep
     }
     if (row >= p.M) continue;
     const long long co = (long long)row * p.c_sm + (long long)n * p.c_sn;
+    const long long oo = (long long)row * p.o_sm + n;
     if (full_n && vec_c) {
       if (rbase) {
         const long long ro = (long long)row * p.r_sm + (long long)n * p.r_sn;
@@ -257,14 +296,16 @@ __device__ __forceinline__ void store_block(const GemmParams& p, const float* ep
           for (int j = 0; j < 4; ++j) v[j] += rbase[ro + (long long)j * p.r_sn];
         }
       }
-      *reinterpret_cast<float4*>(cbase + co) = make_float4(v[0], v[1], v[2], v[3]);
+      if (cbase) *reinterpret_cast<float4*>(cbase + co) = make_float4(v[0], v[1], v[2], v[3]);
+      if (ohi) store_operand4<PREC>(ohi, olo, oo, v);
     } else {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         if (n + j >= p.N) break;
         float w = v[j];
         if (rbase) w += rbase[(long long)row * p.r_sm + (long long)(n + j) * p.r_sn];
-        cbase[co + (long long)j * p.c_sn] = w;
+        if (cbase) cbase[co + (long long)j * p.c_sn] = w;
+        if (ohi) store_operand1<PREC>(ohi, olo, oo + j, w);
       }
     }
   }
@@ -570,10 +611,13 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
       int bz, tm, tn;
       tile_coords(p, t, bz, tm, tn);
       const int m0 = tm * kBM + q * 32, n0 = tn * BN + col0;
-      float* cbase = p.c + (long long)bz * p.c_sb;
+      float* cbase = p.c ? p.c + (long long)bz * p.c_sb : nullptr;
       const float* rbase = p.res ? p.res + (long long)bz * p.r_sb : nullptr;
+      const long long obatch = (long long)bz * p.M * p.o_sm;
+      void* ohi = p.o_hi ? (void*)((char*)p.o_hi + obatch * C::ESZ) : nullptr;
+      float* olo = p.o_lo ? p.o_lo + obatch : nullptr;
       // float4 stores need contiguous, 16-byte aligned rows of the output (and residual)
-      const bool vec_c = p.c_sn == 1 && (p.c_sm & 3) == 0 && (((uintptr_t)cbase) & 15) == 0;
+      const bool vec_c = !cbase || (p.c_sn == 1 && (p.c_sm & 3) == 0 && (((uintptr_t)cbase) & 15) == 0);
       const bool vec_r = rbase && p.r_sn == 1 && (p.r_sm & 3) == 0 && (((uintptr_t)rbase) & 15) == 0;
 #pragma unroll
       for (int cc = 0; cc < HALF; cc += 16) {
@@ -583,12 +627,12 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
           *reinterpret_cast<float4*>(ep + lane * 20 + j) = make_float4(acc[cc + j], acc[cc + j + 1], acc[cc + j + 2], acc[cc + j + 3]);
         __syncwarp();
         switch (p.act) {
-          case 1: store_block<1>(p, ep, m0, n0 + cc, cbase, rbase, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-          case 2: store_block<2>(p, ep, m0, n0 + cc, cbase, rbase, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-          case 3: store_block<3>(p, ep, m0, n0 + cc, cbase, rbase, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-          case 4: store_block<4>(p, ep, m0, n0 + cc, cbase, rbase, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-          case 5: store_block<5>(p, ep, m0, n0 + cc, cbase, rbase, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-          default: store_block<0>(p, ep, m0, n0 + cc, cbase, rbase, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          case 1: store_block<1, PREC>(p, ep, m0, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          case 2: store_block<2, PREC>(p, ep, m0, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          case 3: store_block<3, PREC>(p, ep, m0, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          case 4: store_block<4, PREC>(p, ep, m0, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          case 5: store_block<5, PREC>(p, ep, m0, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          default: store_block<0, PREC>(p, ep, m0, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
         }
         __syncwarp();
       }
@@ -683,6 +727,9 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream) {
   p.num_m = (int)ceil_div(L.M, kBM);
   p.num_n = (int)ceil_div(L.N, BN);
   p.batch = (int)L.batch;
+  p.o_hi = L.out_hi;
+  p.o_lo = L.out_lo;
+  p.o_sm = L.o_sm;
   p.x_hi = L.x_hi;
   p.x_lo = L.x_lo;
   p.H = (int)L.H; p.W = (int)L.W; p.Cp = (int)L.Cp; p.KH = (int)L.KH; p.KW = (int)L.KW;
@@ -712,6 +759,12 @@ void launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
   PFB_CHECK_ARG(L.M > 0 && L.N > 0 && L.batch > 0, "gemm: empty problem");
   PFB_CHECK_ARG(L.M < (1ll << 31) && L.N < (1ll << 31), "gemm: dimension too large");
   PFB_CHECK_ARG(L.err != nullptr, "gemm: error flag pointer required");
+  PFB_CHECK_ARG(L.c || L.out_hi, "gemm: no output");
+  if (L.out_hi) {
+    PFB_CHECK_ARG(L.N % 4 == 0 && L.o_sm % 4 == 0 && L.o_sm >= L.N && ((uintptr_t)L.out_hi & 15) == 0 &&
+                      (L.precision == PFC_PRECISION_BF16 || (L.out_lo && ((uintptr_t)L.out_lo & 15) == 0)),
+                  "gemm: operand output needs 16-byte aligned rows of a multiple of 4 columns");
+  }
   const int64_t kal = L.precision == PFC_PRECISION_BF16 ? 64 : 32;
   PFB_CHECK_ARG(L.kpad % kal == 0 && L.kpad >= L.K, "gemm: kpad must be a multiple of the K tile and >= K");
   if (L.conv) {

@@ -15,8 +15,14 @@ struct GemmLaunch {
   const void* b_lo = nullptr;
   int64_t a_sb = 0, b_sb = 0;  // nonzero: operand has `batch` slices
   int64_t batch = 1, M = 0, N = 0, K = 0, kpad = 0;
-  float* c = nullptr;
+  float* c = nullptr;  // may be null when only the operand outputs are wanted
   int64_t c_sb = 0, c_sm = 0, c_sn = 1;
+  // Operand outputs: the epilogue also writes its values as the tensor-core
+  // operand of a following GEMM (hi/lo split, or bf16 in out_hi): element
+  // (b, m, n) at [(b*M + m)*o_sm + n].  Requires N % 4 == 0, o_sm % 4 == 0.
+  void* out_hi = nullptr;
+  float* out_lo = nullptr;
+  int64_t o_sm = 0;
   float alpha = 1.f;
   const float* alpha_ptr = nullptr;
   const float* bias = nullptr;
@@ -95,6 +101,13 @@ struct PoolLaunch {
   int64_t n = 0, c = 0, h = 0, w = 0, sn = 0, sc = 0, sh = 0, sw = 0;
   int64_t kh = 1, kw = 1, stride_h = 1, stride_w = 1, pad_h = 0, pad_w = 0;
   int64_t oh = 0, ow = 0, osn = 0, osc = 0, osh = 0, osw = 0;
+  // Operand output for an implicit-GEMM Conv2d that reads this pool's
+  // result: the channels-last [N][OH][OW][C] copy as tf32x3 hi/lo (or bf16 in
+  // out_hi), at the offsets of the channels-last output y (osc == 1).  y
+  // itself may then be null.
+  void* out_hi = nullptr;
+  float* out_lo = nullptr;
+  int precision = 0;
 };
 void launch_pool(const PoolLaunch& L, cudaStream_t stream);
 

@@ -9,6 +9,7 @@
 
 #include "../common.hpp"
 #include "kernels.hpp"
+#include "split.cuh"
 
 namespace pfb {
 
@@ -36,18 +37,6 @@ struct View6 {
   long long shape[6];
   long long stride[6];
 };
-
-// tf32x3 split: hi keeps the sign, exponent and top 10 mantissa bits; lo is
-// the exact remainder.  Non-finite values go entirely into hi.
-__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
-  if (!isfinite(x)) {
-    hi = isnan(x) ? __int_as_float(0x7fc00000) : x;
-    lo = 0.f;
-    return;
-  }
-  hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
-  lo = x - hi;
-}
 
 __device__ __forceinline__ long long row_offset(const View6& v, long long row) {
   // rows enumerate dims [0, rank-1) row-major
@@ -238,34 +227,58 @@ __global__ void pool_kernel(PoolLaunch L) {
         out = s / (float)(L.kh * L.kw);  // count includes padding
       }
     }
-    L.y[n * L.osn + c * L.osc + oh * L.osh + ow * L.osw] = out;
+    const long long yo = n * L.osn + c * L.osc + oh * L.osh + ow * L.osw;
+    if (L.y) L.y[yo] = out;
+    if (L.out_hi) {
+      if (L.precision == PFC_PRECISION_BF16) {
+        ((__nv_bfloat16*)L.out_hi)[yo] = __float2bfloat16_rn(out);
+      } else {
+        float hv, lv;
+        split_tf32(out, hv, lv);
+        ((float*)L.out_hi)[yo] = hv;
+        L.out_lo[yo] = lv;
+      }
+    }
    }
   }
 }
 
-// Channels-last copy of a Conv2d input: one thread per output element,
-// channel fastest (coalesced writes; coalesced reads when the input is
-// already channels-last).  IDX is int when every index fits in 32 bits.
+// Channels-last copy of a Conv2d input: one thread per pixel and group of 4
+// channels (float4 stores, coalesced; the 4 reads are coalesced across
+// threads for channels-last and channel-planar inputs alike).  IDX is int
+// when every index fits in 32 bits.
 template <int PREC, typename IDX>
 __global__ void conv_input_kernel(ConvInputLaunch L) {
-  const IDX C = (IDX)L.c, Cp = (IDX)L.cp, H = (IDX)L.h, W = (IDX)L.w;
-  const IDX total = (IDX)L.n * H * W * Cp;
+  const IDX C = (IDX)L.c, G = (IDX)(L.cp / 4), H = (IDX)L.h, W = (IDX)L.w;
+  const IDX total = (IDX)L.n * H * W * G;
   for (IDX i = (IDX)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (IDX)gridDim.x * blockDim.x) {
-    const IDX c = i % Cp;
-    const IDX pix = i / Cp;
+    const IDX g = i % G;
+    const IDX pix = i / G;
     const IDX w = pix % W;
     const IDX hn = pix / W;
     const IDX h = hn % H;
     const IDX n = hn / H;
-    float x = 0.f;
-    if (c < C) x = L.x[(long long)n * L.sn + (long long)c * L.sc + (long long)h * L.sh + (long long)w * L.sw];
+    const float* src = L.x + (long long)n * L.sn + (long long)h * L.sh + (long long)w * L.sw;
+    float x[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const IDX c = 4 * g + j;
+      x[j] = c < C ? src[(long long)c * L.sc] : 0.f;
+    }
     if constexpr (PREC == PFC_PRECISION_BF16) {
-      ((__nv_bfloat16*)L.hi)[i] = __float2bfloat16_rn(x);
+      __nv_bfloat162 a = __floats2bfloat162_rn(x[0], x[1]), b = __floats2bfloat162_rn(x[2], x[3]);
+      uint2 pk;
+      pk.x = *(uint32_t*)&a;
+      pk.y = *(uint32_t*)&b;
+      *(uint2*)((__nv_bfloat16*)L.hi + 4 * i) = pk;
     } else {
-      float hv, lv;
-      split_tf32(x, hv, lv);
-      ((float*)L.hi)[i] = hv;
-      L.lo[i] = lv;
+      float4 hv, lv;
+      split_tf32(x[0], hv.x, lv.x);
+      split_tf32(x[1], hv.y, lv.y);
+      split_tf32(x[2], hv.z, lv.z);
+      split_tf32(x[3], hv.w, lv.w);
+      *(float4*)((float*)L.hi + 4 * i) = hv;
+      *(float4*)(L.lo + 4 * i) = lv;
     }
   }
 }
@@ -365,6 +378,10 @@ void launch_pool(const PoolLaunch& L, cudaStream_t stream) {
   const long long total = L.n * L.c * L.oh * L.ow;
   if (total == 0) return;
   PFB_CHECK_ARG(L.c * L.ow < (1ll << 31), "pool: channels x output width too large");
+  PFB_CHECK_ARG(L.y || L.out_hi, "pool: no output");
+  PFB_CHECK_ARG(!L.out_hi || (L.osc == 1 && L.osw == L.c && L.osh == L.ow * L.c && L.osn == L.oh * L.ow * L.c &&
+                              (L.precision == PFC_PRECISION_BF16 || L.out_lo)),
+                "pool: operand output needs a dense channels-last layout");
   const long long inner = L.c * L.ow, rows = L.n * L.oh;
   dim3 grid((unsigned)ceil_div(inner, 256), (unsigned)std::min<long long>(rows, 65535), 1);
   pool_kernel<<<grid, 256, 0, stream>>>(L);
@@ -373,8 +390,9 @@ void launch_pool(const PoolLaunch& L, cudaStream_t stream) {
 
 void launch_conv_input(const ConvInputLaunch& L, cudaStream_t stream) {
   PFB_CHECK_ARG(L.x && L.hi && (L.precision == PFC_PRECISION_BF16 || L.lo), "conv input: null pointer");
-  PFB_CHECK_ARG(L.cp >= L.c && L.c > 0, "conv input: padded channels must cover the channels");
-  const long long total = L.n * L.h * L.w * L.cp;
+  PFB_CHECK_ARG(L.cp >= L.c && L.c > 0 && L.cp % 4 == 0, "conv input: padded channels must cover the channels");
+  PFB_CHECK_ARG(((uintptr_t)L.hi & 15) == 0 && ((uintptr_t)L.lo & 15) == 0, "conv input: outputs must be 16-byte aligned");
+  const long long total = L.n * L.h * L.w * (L.cp / 4);
   if (total == 0) return;
   const unsigned g = grid_for(total, 256);
   const bool small = total < (1ll << 30);  // i + grid stride stays below 2^31

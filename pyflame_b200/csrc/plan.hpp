@@ -114,6 +114,11 @@ struct GemmArgs {
   int act = 0;
   View residual; bool has_residual = false;
   int64_t r_sb = 0, r_sm = 0, r_sn = 0;
+  // Operand outputs written by the epilogue for a following GEMM (replacing
+  // that GEMM's operand preparation): element (b,m,n) at [(b*M+m)*op_sm + n].
+  int op_hi = -1, op_lo = -1;
+  int64_t op_sm = 0;
+  bool write_c = true;  // false when only the operand outputs are read
   // implicit-GEMM Conv2d: A gathered from the channels-last input x_hi/x_lo
   bool conv = false;
   int x_hi = -1, x_lo = -1;
@@ -125,6 +130,9 @@ struct PoolArgs {
   View y;
   int mode = 0;
   int64_t kh = 1, kw = 1, sh = 1, sw = 1, ph = 0, pw = 0;
+  // channels-last operand copy for a following implicit-GEMM Conv2d
+  int op_hi = -1, op_lo = -1;
+  bool write_y = true;
 };
 
 struct BnFoldArgs {
