@@ -6,13 +6,16 @@
 One step evaluates one batch of the workload's graph.  `value` is whole-job
 samples/s with inputs resident in HBM (CudaExecutor.execute_device, device
 pointers bound to the graph's INPUT nodes, outputs written in place); `e2e`
-is the same metric through the public host-buffer call
-(CudaExecutor.execute) with inputs copied from pinned host memory and all
-outputs read back every step.  Multi-GPU runs (torchrun, one process per GPU)
-give every rank its own full batch (weak scaling): weights are broadcast once
-from rank 0 over NCCL and registered as each rank's resident constants
-(CudaExecutor.set_resident); no collective runs inside the timed region.  `--impl reference` times PyFlame's own CPU code for the path
-on the host cores instead.
+is the same metric through the public host-buffer call with inputs copied
+from pinned host memory and all outputs read back every step:
+CudaExecutor.execute_streamed (the batch as micro-batches whose copies
+overlap compute), and under `e2e.serial` CudaExecutor.execute (one upload,
+compute, download in sequence).  Multi-GPU runs (torchrun, one process per
+GPU) give every rank its own full batch (weak scaling): weights are broadcast
+once from rank 0 over NCCL and registered as each rank's resident constants
+(CudaExecutor.set_resident); no collective runs inside the timed region.
+`--impl reference` times PyFlame's own CPU code for the path on the host
+cores instead.
 """
 from __future__ import annotations
 
@@ -42,6 +45,8 @@ FULL = {
     "encoder": dict(batch=32, seq=512),
     "convstack": dict(batch=256),
 }
+# micro-batches of the end-to-end host-buffer measurement (execute_streamed)
+E2E_CHUNKS = {"fused": 8, "mlp": 1, "gemm_chain": 4, "encoder": 4, "convstack": 8}
 # CPU-baseline samples (bounded, seconds of CPU work)
 CPU_SAMPLE = {
     "fused": dict(rows=8192, cols=4096),
@@ -260,19 +265,38 @@ def run_ours(args):
         g.version += 1  # payload pointers changed: rebuild the native graph description
         pinned_out = [torch.empty(t.shape, dtype=torch.float32).pin_memory() for t in w.outputs]
         out_np = [p.numpy() for p in pinned_out]
+        h2d = sum(t.node().constant_data().nbytes for t in w.inputs.values())
+        d2h = sum(o.nbytes for o in out_np)
+        n_e2e = max(3, min(args.steps, 20))
+        # (a) one execute call per step: upload, compute, download in sequence
         for _ in range(2):
             rr = ex.execute(g, out_ids, out=out_np)
             assert rr.success, rr.error_message
-        n_e2e = max(3, min(args.steps, 20))
         t0 = time.perf_counter()
         for _ in range(n_e2e):
             rr = ex.execute(g, out_ids, out=out_np)
+        dt_serial = time.perf_counter() - t0
+        # (b) execute_streamed: the same batch as micro-batches of one chunk
+        # graph, each chunk's compute overlapping the next upload and the
+        # previous download
+        chunks = E2E_CHUNKS[args.workload]
+        key = next(iter(FULL[args.workload]))  # the batch-size key (rows / batch)
+        cw = build_workload(args.workload, **{**FULL[args.workload], key: FULL[args.workload][key] // chunks})
+        cg = cw.outputs[0].graph()
+        c_in = {cw.inputs[name].node().id(): pinned_in[name].numpy() for name in cw.inputs}
+        c_out = [t.node().id() for t in cw.outputs]
+        for _ in range(2):
+            ex.execute_streamed(cg, c_in, c_out, out_np)
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            ex.execute_streamed(cg, c_in, c_out, out_np)
         dt = time.perf_counter() - t0
-        h2d = sum(t.node().constant_data().nbytes for t in w.inputs.values())
-        d2h = sum(o.nbytes for o in out_np)
         e2e = {"value": w.samples * n_e2e / dt, "unit": "samples/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": dt / n_e2e * 1e3, "steps": n_e2e,
-               "api": "CudaExecutor.execute (pfc_executor_execute), pinned host buffers"}
+               "api": f"CudaExecutor.execute_streamed (pfc_executor_execute_streamed), {chunks} chunks, "
+                      "pinned host buffers",
+               "serial": {"value": w.samples * n_e2e / dt_serial, "ms_per_step": dt_serial / n_e2e * 1e3,
+                          "api": "CudaExecutor.execute (pfc_executor_execute)"}}
 
     if rank == 0:
         pk, pk_kind = peaks()

@@ -220,6 +220,22 @@ PFC_API int pfc_executor_execute_device(pfc_executor* ex, pfc_graph* g, const ui
                                 void* const* out_dev, void* stream,
                                 pfc_execution_result* result);
 
+/* Streamed host-buffer execution for graphs whose rows are independent (no
+ * op mixes rows of dim 0, as for batch sharding): `g` describes one chunk of
+ * rows, and the host arrays hold `n_chunks` chunks back to back (input i of
+ * chunk c at in_host[i] + c * size_bytes(input_ids[i]), outputs likewise).
+ * Chunk c+1's inputs are copied in and chunk c-1's outputs copied out while
+ * chunk c computes (three streams, two device slots per tensor), so a step
+ * costs about the largest of the three instead of their sum.  Host memory
+ * must be pinned for the copies to overlap.  Synchronous: returns when every
+ * output is on the host.  No counterpart in the reference (ROCmExecutor
+ * copies and computes one graph serially, rocm_executor.cpp:66-161). */
+PFC_API int pfc_executor_execute_streamed(pfc_executor* ex, pfc_graph* g, const uint64_t* input_ids,
+                                          int n_inputs, const void* const* in_host,
+                                          const uint64_t* output_ids, int n_outputs,
+                                          void* const* out_host, int n_chunks,
+                                          pfc_execution_result* result);
+
 PFC_API int pfc_executor_get_device_info(pfc_executor* ex, pfc_device_info* info);
 PFC_API int pfc_executor_get_memory_stats(pfc_executor* ex, pfc_memory_stats* stats);
 /* Drop every resident constant and compiled plan. */

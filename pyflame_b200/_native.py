@@ -88,6 +88,9 @@ SIGNATURES = {
     "pfc_executor_execute_device": (C.c_int, [_P, _P, C.POINTER(C.c_uint64), C.c_int, C.POINTER(_P),
                                               C.POINTER(C.c_uint64), C.c_int, C.POINTER(_P), _P,
                                               C.POINTER(ExecutionResultC)]),
+    "pfc_executor_execute_streamed": (C.c_int, [_P, _P, C.POINTER(C.c_uint64), C.c_int, C.POINTER(_P),
+                                                C.POINTER(C.c_uint64), C.c_int, C.POINTER(_P), C.c_int,
+                                                C.POINTER(ExecutionResultC)]),
     "pfc_executor_get_device_info": (C.c_int, [_P, C.POINTER(DeviceInfo)]),
     "pfc_executor_get_memory_stats": (C.c_int, [_P, C.POINTER(MemoryStatsC)]),
     "pfc_executor_release_constants": (C.c_int, [_P]),

@@ -298,6 +298,43 @@ class CudaExecutor:
                                                     out_p, C.c_void_p(stream or None), C.byref(r)))
         return ExecutionResult(True, "", r.compile_time_ms, 0.0, 0.0, r.total_time_ms, {}, r.kernel_launches)
 
+    def execute_streamed(self, chunk_graph: Graph, inputs: Dict[int, np.ndarray], output_ids: Sequence[int],
+                         outputs: Sequence[np.ndarray]) -> ExecutionResult:
+        """Host-buffer execution of a batch in chunks, with the copies of
+        neighbouring chunks overlapping each chunk's compute.  `chunk_graph`
+        computes one chunk of rows; `inputs` maps each of its leaf node ids to
+        a host array holding all chunks back to back along dim 0, `outputs`
+        are host arrays for `output_ids` laid out the same way.  Valid when
+        rows are independent (as for batch sharding).  Pinned arrays (e.g.
+        torch `pin_memory()` views) let the copies overlap.  Raises on
+        failure."""
+        output_ids = [int(i) for i in output_ids]
+        ng = native_graph(chunk_graph, output_ids)
+        items = list(inputs.items())
+        n_chunks = None
+        for nid, arr in items:
+            per = chunk_graph.node(nid).numel() * 4
+            if arr.nbytes % per or not arr.flags.c_contiguous:
+                raise ValueError(f"input {nid}: {arr.nbytes} bytes is not a whole number of {per}-byte chunks")
+            n = arr.nbytes // per
+            if n_chunks not in (None, n):
+                raise ValueError("inputs hold different numbers of chunks")
+            n_chunks = n
+        for oid, arr in zip(output_ids, outputs):
+            per = chunk_graph.node(oid).numel() * 4
+            if not arr.flags.c_contiguous or arr.nbytes != per * (n_chunks or 0):
+                raise ValueError(f"output {oid}: expected {n_chunks} chunks of {per} bytes")
+        k_in, k_out = len(items), len(output_ids)
+        in_ids = (C.c_uint64 * max(1, k_in))(*[i for i, _ in items])
+        in_p = (C.c_void_p * max(1, k_in))(*[a.ctypes.data for _, a in items])
+        out_ids = (C.c_uint64 * max(1, k_out))(*output_ids)
+        out_p = (C.c_void_p * max(1, k_out))(*[a.ctypes.data for a in outputs])
+        r = N.ExecutionResultC()
+        N.check(N.lib().pfc_executor_execute_streamed(self.handle, ng.handle, in_ids, k_in, in_p, out_ids, k_out,
+                                                      out_p, int(n_chunks or 0), C.byref(r)))
+        return ExecutionResult(True, "", r.compile_time_ms, r.transfer_time_ms, r.compute_time_ms, r.total_time_ms,
+                               {}, r.kernel_launches)
+
     def get_device_info(self) -> DeviceInfo:
         i = N.DeviceInfo()
         N.check(N.lib().pfc_executor_get_device_info(self.handle, C.byref(i)))

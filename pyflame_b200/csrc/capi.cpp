@@ -308,6 +308,21 @@ int pfc_executor_execute_device(pfc_executor* ex, pfc_graph* g, const uint64_t* 
   return rc;
 }
 
+int pfc_executor_execute_streamed(pfc_executor* ex, pfc_graph* g, const uint64_t* input_ids, int n_inputs,
+                                  const void* const* in_host, const uint64_t* output_ids, int n_outputs,
+                                  void* const* out_host, int n_chunks, pfc_execution_result* result) {
+  if (result) std::memset(result, 0, sizeof *result);
+  int rc = guarded([&] {
+    PFB_CHECK_ARG(ex && g && result, "null argument");
+    PFB_CHECK_ARG(n_inputs >= 0 && (n_inputs == 0 || (input_ids && in_host)), "bad inputs");
+    PFB_CHECK_ARG(n_outputs > 0 && output_ids && out_host, "bad outputs");
+    std::vector<uint64_t> ins(input_ids, input_ids + n_inputs), outs(output_ids, output_ids + n_outputs);
+    ex->ex->execute_streamed(g->g, ins, in_host, outs, out_host, n_chunks, result);
+  });
+  if (rc != PFC_OK) fill_error(result, rc);
+  return rc;
+}
+
 int pfc_executor_get_device_info(pfc_executor* ex, pfc_device_info* info) {
   return guarded([&] {
     PFB_CHECK_ARG(ex && info, "null argument");

@@ -104,14 +104,18 @@ CudaExecutor::~CudaExecutor() {
   release_constants();
   if (err_dev_) cudaFree(err_dev_);
   pool_.reset();
+  if (copy_in_) cudaStreamDestroy(copy_in_);
+  if (copy_out_) cudaStreamDestroy(copy_out_);
   if (stream_) cudaStreamDestroy(stream_);
 }
 
 void CudaExecutor::release_constants() {
   if (stream_) cudaStreamSynchronize(stream_);
   for (auto& [k, pe] : plans_) {
-    if (pe.gexec) cudaGraphExecDestroy(pe.gexec);
+    for (auto& gr : pe.graphs) cudaGraphExecDestroy(gr.second);
     if (pe.arena) pool_->deallocate(pe.arena, stream_);
+    for (int k2 = 0; k2 < 2; ++k2)
+      for (void* p : pe.slots[k2]) pool_->deallocate(p, stream_);
   }
   plans_.clear();
   for (auto& [k, r] : resident_) {
@@ -531,17 +535,22 @@ int64_t CudaExecutor::run_steps(PlanEntry& pe, const std::vector<void*>& ptrs, c
     return launches;
   }
   bool graph_ok = cfg_.use_cuda_graph && !cfg_.sync_after_launch;
-  if (graph_ok && pe.gexec && pe.gexec_ptrs == ptrs) {
-    PFB_CUDA(cudaGraphLaunch(pe.gexec, s));
-    ++pe.runs;
-    return launches;
+  if (graph_ok) {
+    for (auto& gr : pe.graphs)
+      if (gr.first == ptrs) {
+        PFB_CUDA(cudaGraphLaunch(gr.second, s));
+        ++pe.runs;
+        return launches;
+      }
   }
   if (graph_ok && pe.runs >= 1) {
     // capture once the plan has run eagerly (kernel attributes are set)
-    if (pe.gexec) {
-      cudaGraphExecDestroy(pe.gexec);
-      pe.gexec = nullptr;
+    constexpr size_t kGraphsPerPlan = 4;
+    if (pe.graphs.size() >= kGraphsPerPlan) {
+      cudaGraphExecDestroy(pe.graphs.front().second);
+      pe.graphs.erase(pe.graphs.begin());
     }
+    cudaGraphExec_t gexec = nullptr;
     cudaGraph_t graph;
     PFB_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
     try {
@@ -552,16 +561,15 @@ int64_t CudaExecutor::run_steps(PlanEntry& pe, const std::vector<void*>& ptrs, c
       throw;
     }
     PFB_CUDA(cudaStreamEndCapture(s, &graph));
-    cudaError_t e = cudaGraphInstantiate(&pe.gexec, graph, 0);
+    cudaError_t e = cudaGraphInstantiate(&gexec, graph, 0);
     cudaGraphDestroy(graph);
     if (e != cudaSuccess) {
       cudaGetLastError();
-      pe.gexec = nullptr;
       for (size_t i = 0; i < P.steps.size(); ++i)
         if (!P.steps[i].once) launch_step(pe, i, ptrs, s);
     } else {
-      pe.gexec_ptrs = ptrs;
-      PFB_CUDA(cudaGraphLaunch(pe.gexec, s));
+      pe.graphs.push_back({ptrs, gexec});
+      PFB_CUDA(cudaGraphLaunch(gexec, s));
     }
     ++pe.runs;
     return launches;
@@ -704,6 +712,143 @@ void CudaExecutor::execute_device(Graph& g, const std::vector<uint64_t>& in_ids,
   }
   res->success = 1;
   res->compile_time_ms = compile_ms;
+  res->total_time_ms = ms_since(t0);
+  res->kernel_launches = launches;
+}
+
+void CudaExecutor::execute_streamed(Graph& g, const std::vector<uint64_t>& in_ids, const void* const* in_host,
+                                    const std::vector<uint64_t>& outs, void* const* out_host, int n_chunks,
+                                    pfc_execution_result* res) {
+  std::lock_guard<std::mutex> lock(mu_);
+  auto t0 = std::chrono::steady_clock::now();
+  DeviceGuard dg(cfg_.device_id);
+  if (n_chunks < 1) fail(PFC_ERR_INVALID_ARGUMENT, "n_chunks must be at least 1");
+  std::unordered_set<uint64_t> bindings;
+  std::vector<size_t> in_bytes, out_bytes;
+  for (size_t i = 0; i < in_ids.size(); ++i) {
+    const Node* n = g.find(in_ids[i]);
+    if (!n) fail(PFC_ERR_INVALID_ARGUMENT, "input id " + std::to_string(in_ids[i]) + " is not in the graph");
+    if (n->type == NodeType::OPERATION) fail(PFC_ERR_INVALID_ARGUMENT, "only leaf nodes can be streamed inputs");
+    if (!in_host[i]) fail(PFC_ERR_INVALID_ARGUMENT, "null input buffer");
+    bindings.insert(in_ids[i]);
+    in_bytes.push_back(n->size_bytes());
+  }
+  for (size_t i = 0; i < outs.size(); ++i) {
+    const Node* n = g.find(outs[i]);
+    if (!n) fail(PFC_ERR_INVALID_ARGUMENT, "output id " + std::to_string(outs[i]) + " is not in the graph");
+    if (!out_host[i]) fail(PFC_ERR_INVALID_ARGUMENT, "null output buffer");
+    out_bytes.push_back(n->size_bytes());
+  }
+  double compile_ms = 0;
+  PlanEntry& pe = prepare(g, outs, bindings, &compile_ms);
+  const Plan& P = *pe.plan;
+  if (!copy_in_) PFB_CUDA(cudaStreamCreateWithFlags(&copy_in_, cudaStreamNonBlocking));
+  if (!copy_out_) PFB_CUDA(cudaStreamCreateWithFlags(&copy_out_, cudaStreamNonBlocking));
+  // two device slots per input and output, kept with the plan between calls
+  const cudaStream_t s = stream_;
+  std::vector<size_t> want(in_bytes);
+  want.insert(want.end(), out_bytes.begin(), out_bytes.end());
+  if (pe.slot_bytes != want) {
+    PFB_CUDA(cudaStreamSynchronize(s));
+    for (int k = 0; k < 2; ++k) {
+      for (void* p : pe.slots[k]) pool_->deallocate(p, s);
+      pe.slots[k].clear();
+      for (size_t b : want) pe.slots[k].push_back(pool_->allocate(std::max<size_t>(b, 256), s));
+    }
+    pe.slot_bytes = want;
+  }
+  std::vector<void*> in_slot[2], out_slot[2];
+  for (int k = 0; k < 2; ++k) {
+    in_slot[k].assign(pe.slots[k].begin(), pe.slots[k].begin() + in_bytes.size());
+    out_slot[k].assign(pe.slots[k].begin() + in_bytes.size(), pe.slots[k].end());
+  }
+  cudaEvent_t ready, ev_in[2], ev_comp[2], ev_out[2], e_start, e_end;
+  PFB_CUDA(cudaEventCreateWithFlags(&ready, cudaEventDisableTiming));
+  for (int k = 0; k < 2; ++k) {
+    PFB_CUDA(cudaEventCreateWithFlags(&ev_in[k], cudaEventDisableTiming));
+    PFB_CUDA(cudaEventCreateWithFlags(&ev_comp[k], cudaEventDisableTiming));
+    PFB_CUDA(cudaEventCreateWithFlags(&ev_out[k], cudaEventDisableTiming));
+  }
+  PFB_CUDA(cudaEventCreate(&e_start));
+  PFB_CUDA(cudaEventCreate(&e_end));
+  PFB_CUDA(cudaEventRecord(ready, s));  // slots exist
+  PFB_CUDA(cudaStreamWaitEvent(copy_in_, ready));
+  PFB_CUDA(cudaStreamWaitEvent(copy_out_, ready));
+  PFB_CUDA(cudaEventRecord(e_start, copy_in_));
+  int64_t launches = 0;
+  std::unordered_map<int, int> owner;
+  for (size_t i = 0; i < outs.size(); ++i) owner[P.output_views[i].buf]++;
+  for (int c = 0; c < n_chunks; ++c) {
+    const int k = c & 1;
+    // inputs of chunk c into slot k once chunk c-2 has finished reading it
+    if (c >= 2) PFB_CUDA(cudaStreamWaitEvent(copy_in_, ev_comp[k]));
+    for (size_t i = 0; i < in_ids.size(); ++i)
+      PFB_CUDA(cudaMemcpyAsync(in_slot[k][i], (const char*)in_host[i] + (size_t)c * in_bytes[i], in_bytes[i],
+                               cudaMemcpyHostToDevice, copy_in_));
+    PFB_CUDA(cudaEventRecord(ev_in[k], copy_in_));
+    // compute chunk c once its inputs landed and chunk c-2's outputs left slot k
+    PFB_CUDA(cudaStreamWaitEvent(s, ev_in[k]));
+    if (c >= 2) PFB_CUDA(cudaStreamWaitEvent(s, ev_out[k]));
+    std::unordered_map<uint64_t, const void*> bind;
+    for (size_t i = 0; i < in_ids.size(); ++i) bind[in_ids[i]] = in_slot[k][i];
+    std::vector<std::pair<void*, const Node*>> uploads;
+    std::vector<void*> ptrs = resolve(pe, g, bind, s, &uploads);
+    std::vector<bool> direct(outs.size(), false);
+    for (size_t i = 0; i < outs.size(); ++i) {
+      const View& v = P.output_views[i];
+      const Buffer& b = P.buffers[v.buf];
+      if (b.kind == BufKind::ARENA && v.offset == 0 && owner[v.buf] == 1) {
+        ptrs[v.buf] = out_slot[k][i];
+        direct[i] = true;
+      }
+    }
+    for (auto& [dst, n] : uploads) PFB_CUDA(cudaMemcpyAsync(dst, n->data, n->data_bytes, cudaMemcpyHostToDevice, s));
+    {
+      std::vector<float> table(P.scalars.size());
+      for (size_t i = 0; i < P.scalars.size(); ++i) table[i] = P.scalars[i].value;
+      if (!table.empty() && (table != pe.table || pe.table_ptr != ptrs[P.scalar_buf])) {
+        PFB_CUDA(cudaMemcpyAsync(ptrs[P.scalar_buf], table.data(), table.size() * 4, cudaMemcpyHostToDevice, s));
+        pe.table = table;
+        pe.table_ptr = ptrs[P.scalar_buf];
+      }
+    }
+    launches += run_steps(pe, ptrs, s);
+    for (size_t i = 0; i < outs.size(); ++i) {
+      if (direct[i]) continue;
+      const View& v = P.output_views[i];
+      const void* src = (const char*)ptrs[v.buf] + v.offset * (int64_t)dtype_size(v.dtype);
+      PFB_CUDA(cudaMemcpyAsync(out_slot[k][i], src, out_bytes[i], cudaMemcpyDeviceToDevice, s));
+    }
+    PFB_CUDA(cudaEventRecord(ev_comp[k], s));
+    // outputs of chunk c back to the host
+    PFB_CUDA(cudaStreamWaitEvent(copy_out_, ev_comp[k]));
+    for (size_t i = 0; i < outs.size(); ++i)
+      PFB_CUDA(cudaMemcpyAsync((char*)out_host[i] + (size_t)c * out_bytes[i], out_slot[k][i], out_bytes[i],
+                               cudaMemcpyDeviceToHost, copy_out_));
+    PFB_CUDA(cudaEventRecord(ev_out[k], copy_out_));
+  }
+  PFB_CUDA(cudaEventRecord(e_end, copy_out_));
+  cudaError_t se = cudaStreamSynchronize(copy_out_);
+  if (se == cudaSuccess) se = cudaStreamSynchronize(s);
+  float total = 0;
+  if (se == cudaSuccess) cudaEventElapsedTime(&total, e_start, e_end);
+  // the next call's first copies must not overtake this call's last reads
+  PFB_CUDA(cudaEventRecord(ready, copy_in_));
+  PFB_CUDA(cudaStreamWaitEvent(s, ready));
+  cudaEventDestroy(ready);
+  for (int k = 0; k < 2; ++k) {
+    cudaEventDestroy(ev_in[k]);
+    cudaEventDestroy(ev_comp[k]);
+    cudaEventDestroy(ev_out[k]);
+  }
+  cudaEventDestroy(e_start);
+  cudaEventDestroy(e_end);
+  if (se != cudaSuccess) fail(PFC_ERR_CUDA, std::string("execution failed: ") + cudaGetErrorString(se));
+  check_device_error(s);
+  res->success = 1;
+  res->compile_time_ms = compile_ms;
+  res->transfer_time_ms = total;  // copies overlap compute: the span of the whole pipeline
+  res->compute_time_ms = total;
   res->total_time_ms = ms_since(t0);
   res->kernel_launches = launches;
 }

@@ -38,6 +38,12 @@ class CudaExecutor {
   void execute_device(Graph& g, const std::vector<uint64_t>& in_ids, const void* const* in_dev,
                       const std::vector<uint64_t>& outs, void* const* out_dev, cudaStream_t stream,
                       pfc_execution_result* res);
+  // Streamed host-buffer path: `g` computes one chunk of rows; the inputs
+  // and outputs hold n_chunks chunks back to back.  Copies of chunk c+1 in
+  // and c-1 out overlap the compute of chunk c (three streams, two slots).
+  void execute_streamed(Graph& g, const std::vector<uint64_t>& in_ids, const void* const* in_host,
+                        const std::vector<uint64_t>& outs, void* const* out_host, int n_chunks,
+                        pfc_execution_result* res);
 
   pfc_device_info device_info() const;
   pfc_memory_stats memory_stats() const { return pool_->stats(); }
@@ -53,11 +59,17 @@ class CudaExecutor {
     std::unique_ptr<Plan> plan;
     void* arena = nullptr;
     std::vector<cudaKernel_t> kernels;  // per step (JIT steps)
-    cudaGraphExec_t gexec = nullptr;
-    std::vector<void*> gexec_ptrs;      // buffer pointers the graph was captured with
+    // captured CUDA graphs of the plan, one per set of buffer pointers (a
+    // streamed call alternates between two sets); at most kGraphsPerPlan
+    std::vector<std::pair<std::vector<void*>, cudaGraphExec_t>> graphs;
     int runs = 0;
     std::vector<float> table;           // splat values last uploaded to the scalar table
     void* table_ptr = nullptr;
+    // streamed execution: two device slots per streamed input and output,
+    // kept with the plan (allocating them per call made the pool trim and
+    // re-map memory on every call)
+    std::vector<void*> slots[2];
+    std::vector<size_t> slot_bytes;
   };
   struct Resident {
     void* dev = nullptr;
@@ -76,6 +88,7 @@ class CudaExecutor {
 
   pfc_executor_config cfg_;
   cudaStream_t stream_ = nullptr;
+  cudaStream_t copy_in_ = nullptr, copy_out_ = nullptr;  // streamed execution (created on first use)
   std::unique_ptr<CudaMemoryPool> pool_;
   int* err_dev_ = nullptr;
   int num_sms_ = 148;

@@ -307,6 +307,108 @@ __global__ void conv_weight_kernel(ConvWeightLaunch L) {
   }
 }
 
+// Max / average pool on channels-last data (input and output channel
+// stride 1, C % 4 == 0): grid.y walks output rows (n, oh), threads take 4
+// channels of one output column each (float4 loads and stores, 32-bit index
+// math inside an image, window clipped once).  Same NaN rule and window order
+// as pool_kernel.
+__global__ void pool_cl_kernel(PoolLaunch L) {
+  const int C4 = (int)(L.c / 4), OW = (int)L.ow, OH = (int)L.oh;
+  const int H = (int)L.h, W = (int)L.w, sh = (int)L.sh, sw = (int)L.sw;
+  const int inner = C4 * OW;
+  const int rows = (int)(L.n * L.oh);
+  for (int row = blockIdx.y; row < rows; row += gridDim.y) {
+    const int n = row / OH, oh = row - n * OH;
+    const float* xb = L.x + (long long)n * L.sn;
+    const int hs = oh * (int)L.stride_h - (int)L.pad_h;
+    const int h0 = max(hs, 0), h1 = min(hs + (int)L.kh, H);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < inner; i += gridDim.x * blockDim.x) {
+      const int c = (i % C4) * 4, ow = i / C4;
+      const int ws = ow * (int)L.stride_w - (int)L.pad_w;
+      const int w0 = max(ws, 0), w1 = min(ws + (int)L.kw, W);
+      float r[4];
+      if (L.mode == 0) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) r[j] = -__int_as_float(0x7f800000);
+        for (int h = h0; h < h1; ++h)
+          for (int w = w0; w < w1; ++w) {
+            const float4 v4 = *reinterpret_cast<const float4*>(xb + h * sh + w * sw + c);
+            const float v[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              if (v[j] > r[j] || isnan(v[j])) r[j] = v[j];
+          }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) r[j] = 0.f;
+        for (int h = h0; h < h1; ++h)
+          for (int w = w0; w < w1; ++w) {
+            const float4 v4 = *reinterpret_cast<const float4*>(xb + h * sh + w * sw + c);
+            r[0] += v4.x; r[1] += v4.y; r[2] += v4.z; r[3] += v4.w;
+          }
+        const float cnt = (float)(L.kh * L.kw);  // count includes padding
+#pragma unroll
+        for (int j = 0; j < 4; ++j) r[j] = r[j] / cnt;
+      }
+      const long long yo = (long long)n * L.osn + (long long)oh * L.osh + (long long)ow * L.osw + c;
+      if (L.y) *reinterpret_cast<float4*>(L.y + yo) = make_float4(r[0], r[1], r[2], r[3]);
+      if (L.out_hi) {
+        if (L.precision == PFC_PRECISION_BF16) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) ((__nv_bfloat16*)L.out_hi)[yo + j] = __float2bfloat16_rn(r[j]);
+        } else {
+          float4 hv, lv;
+          split_tf32(r[0], hv.x, lv.x);
+          split_tf32(r[1], hv.y, lv.y);
+          split_tf32(r[2], hv.z, lv.z);
+          split_tf32(r[3], hv.w, lv.w);
+          *reinterpret_cast<float4*>((float*)L.out_hi + yo) = hv;
+          *reinterpret_cast<float4*>(L.out_lo + yo) = lv;
+        }
+      }
+    }
+  }
+}
+
+// Adaptive average pool to 1x1 over a channels-last input: one CTA per
+// (image, 32-channel group); 8 warps take every 8th pixel, lanes are
+// channels (coalesced 128-byte reads); the 8 partial sums meet in shared
+// memory.
+__global__ void global_avg_cl_kernel(PoolLaunch L) {
+  __shared__ float part[8][32];
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const long long n = blockIdx.y, c = (long long)blockIdx.x * 32 + lane;
+  const long long P = L.h * L.w;
+  float s = 0.f;
+  if (c < L.c) {
+    const float* xb = L.x + n * L.sn + c;
+    for (long long p = wp; p < P; p += 8) {
+      const long long h = p / L.w, w = p - h * L.w;
+      s += xb[h * L.sh + w * L.sw];
+    }
+  }
+  part[wp][lane] = s;
+  __syncthreads();
+  if (wp == 0 && c < L.c) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += part[k][lane];
+    const float out = t / (float)P;
+    const long long yo = n * L.osn + c * L.osc;
+    if (L.y) L.y[yo] = out;
+    if (L.out_hi) {
+      if (L.precision == PFC_PRECISION_BF16) {
+        ((__nv_bfloat16*)L.out_hi)[yo] = __float2bfloat16_rn(out);
+      } else {
+        float hv, lv;
+        split_tf32(out, hv, lv);
+        ((float*)L.out_hi)[yo] = hv;
+        L.out_lo[yo] = lv;
+      }
+    }
+  }
+}
+
 __global__ void bn_fold_kernel(BnFoldLaunch L) {
   for (long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x; c < L.channels; c += (long long)gridDim.x * blockDim.x) {
     const float g = L.gamma ? L.gamma[c * L.gs] : L.gamma_c;
@@ -382,7 +484,26 @@ void launch_pool(const PoolLaunch& L, cudaStream_t stream) {
   PFB_CHECK_ARG(!L.out_hi || (L.osc == 1 && L.osw == L.c && L.osh == L.ow * L.c && L.osn == L.oh * L.ow * L.c &&
                               (L.precision == PFC_PRECISION_BF16 || L.out_lo)),
                 "pool: operand output needs a dense channels-last layout");
-  const long long inner = L.c * L.ow, rows = L.n * L.oh;
+  if (L.mode == 2 && L.oh == 1 && L.ow == 1 && L.sc == 1 && L.n < 65536) {
+    dim3 grid((unsigned)ceil_div(L.c, 32), (unsigned)L.n, 1);
+    global_avg_cl_kernel<<<grid, 256, 0, stream>>>(L);
+    PFB_CUDA(cudaGetLastError());
+    return;
+  }
+  const long long rows = L.n * L.oh;
+  const bool cl4 = L.mode != 2 && L.sc == 1 && L.osc == 1 && L.c % 4 == 0 && L.sw % 4 == 0 && L.sh % 4 == 0 &&
+                   L.sn % 4 == 0 && L.osw % 4 == 0 && L.osh % 4 == 0 && L.osn % 4 == 0 &&
+                   ((uintptr_t)L.x & 15) == 0 && (!L.y || ((uintptr_t)L.y & 15) == 0) &&
+                   (!L.out_hi || ((uintptr_t)L.out_hi & 15) == 0) && (!L.out_lo || ((uintptr_t)L.out_lo & 15) == 0) &&
+                   L.h * L.sh < (1ll << 31) && L.w * L.sw < (1ll << 31) && rows < (1ll << 31);
+  if (cl4) {
+    const long long inner = (L.c / 4) * L.ow;
+    dim3 grid((unsigned)ceil_div(inner, 128), (unsigned)std::min<long long>(rows, 65535), 1);
+    pool_cl_kernel<<<grid, 128, 0, stream>>>(L);
+    PFB_CUDA(cudaGetLastError());
+    return;
+  }
+  const long long inner = L.c * L.ow;
   dim3 grid((unsigned)ceil_div(inner, 256), (unsigned)std::min<long long>(rows, 65535), 1);
   pool_kernel<<<grid, 256, 0, stream>>>(L);
   PFB_CUDA(cudaGetLastError());

@@ -299,6 +299,20 @@ def test_batchnorm_alone_and_pools(cuda_executor, oracle_mod, rng):
     close(gpu[3], ref[3], rtol=1e-6, atol=1e-7)
 
 
+def test_pools_channels_last(cuda_executor, oracle_mod, rng):
+    """Pools over a channels-last view (the layout conv outputs have), which
+    takes the float4 channels-last kernel; adaptive 1x1 takes the global one."""
+    data = rng.standard_normal((3, 11, 13, 8)).astype(np.float32)  # N, H, W, C
+    data[0, 2, 3, 1] = np.nan
+    x = pf.tensor(data).transpose(1, 3).transpose(2, 3)  # [N, C, H, W] view, channel stride 1
+    outs = [nn.MaxPool2d(3, 2)(x), nn.MaxPool2d(2, 2, 1)(x), nn.AvgPool2d(3, 2, 1)(x), nn.AdaptiveAvgPool2d(1)(x)]
+    gpu, ref = run(cuda_executor, outs, oracle_mod)
+    bitexact(gpu[0], ref[0])
+    bitexact(gpu[1], ref[1])
+    close(gpu[2], ref[2], rtol=1e-6, atol=1e-7)
+    close(gpu[3], ref[3], rtol=1e-5, atol=1e-6)
+
+
 # ---- attention / encoder block ---------------------------------------------------------
 
 def test_multihead_attention(cuda_executor, oracle_mod, rng):
@@ -395,6 +409,38 @@ def test_device_resident_execution(cuda_executor, oracle_mod):
     ref = oracle_mod.run(g, ids)
     bitexact(outs[2].cpu().numpy(), ref[ids[2]])
     close_rows(outs[3].cpu().numpy(), ref[ids[3]], 1e-5)
+
+
+@pytest.mark.parametrize("chunks", [1, 2, 5])
+def test_streamed_execution(cuda_executor, oracle_mod, chunks):
+    """execute_streamed over `chunks` chunks equals the oracle on the whole
+    batch (rows are independent), for row kernels and a GEMM chain."""
+    import torch
+    from pyflame_b200 import workloads
+    rows, cols = 48, 256
+    full = workloads.fused(rows * chunks, cols)
+    ids_full = [t.node().id() for t in full.outputs]
+    ref = oracle_mod.run(full.outputs[0].graph(), ids_full)
+    xs = torch.from_numpy(full.inputs["x"].node().constant_data().copy()).pin_memory()
+    ys = torch.from_numpy(full.inputs["y"].node().constant_data().copy()).pin_memory()
+    w = workloads.fused(rows, cols)
+    g = w.outputs[0].graph()
+    ids = [t.node().id() for t in w.outputs]
+    outs = [torch.empty((rows * chunks,) + tuple(t.shape[1:])).pin_memory().numpy() for t in w.outputs]
+    for _ in range(2):  # the second call replays captured graphs
+        cuda_executor.execute_streamed(g, {w.inputs["x"].node().id(): xs.numpy(), w.inputs["y"].node().id(): ys.numpy()},
+                                       ids, outs)
+    close(outs[2], ref[ids_full[2]], rtol=1e-5, atol=1e-6, what="max")
+    close_rows(outs[3], ref[ids_full[3]], 1e-5, what="layernorm")
+    mc = workloads.mlp(batch=16)
+    mfull = workloads.mlp(batch=16 * chunks)
+    mids = [t.node().id() for t in mfull.outputs]
+    mref = oracle_mod.run(mfull.outputs[0].graph(), mids)[mids[0]]
+    xin = torch.from_numpy(mfull.inputs["x"].node().constant_data().copy()).pin_memory()
+    mout = torch.empty(mref.shape).pin_memory().numpy()
+    cuda_executor.execute_streamed(mc.outputs[0].graph(), {mc.inputs["x"].node().id(): xin.numpy()},
+                                   [mc.outputs[0].node().id()], [mout])
+    close_rows(mout, mref, RTOL_GEMM_TF32X3, what="mlp streamed")
 
 
 def test_memory_stats_and_release(cuda_executor):
