@@ -1397,7 +1397,7 @@ class Compiler {
   // conv_cp > 0: `src` is a Conv2d weight [O,C,KH,KW] laid out for the
   // implicit GEMM (k = (kh*KW + kw)*conv_cp + c).
   Operand prepare_operand(const View& src, int64_t rows, int64_t cols, int64_t kpad, int prec,
-                          const std::string& label, int at, int64_t conv_cp = 0) {
+                          const std::string& label, int at, int64_t conv_cp = 0, int64_t conv_kwp = 0) {
     if (conv_cp == 0 && !src.is_splat && src.buf >= 0 && src.offset == 0 && src.strides == View::dense_strides(src.shape)) {
       auto pit = pending_.find(std::make_tuple(src.buf, rows, cols, kpad, prec));
       if (pit != pending_.end()) {
@@ -1408,7 +1408,7 @@ class Compiler {
     std::ostringstream sig;
     sig << src.buf << ':' << src.offset << ':' << (int)src.dtype << ':' << src.is_splat << ':' << src.splat_slot;
     for (size_t d = 0; d < src.shape.size(); ++d) sig << ',' << src.shape[d] << '/' << src.strides[d];
-    sig << '|' << rows << ',' << cols << ',' << kpad << ',' << prec << ',' << conv_cp;
+    sig << '|' << rows << ',' << cols << ',' << kpad << ',' << prec << ',' << conv_cp << ',' << conv_kwp;
     auto it = operands_.find(sig.str());
     if (it != operands_.end()) return it->second;
     const size_t esz = prec == PFC_PRECISION_BF16 ? 2 : 4;
@@ -1450,6 +1450,7 @@ class Compiler {
     s.split.out_hi = op.hi;
     s.split.out_lo = op.lo;
     s.split.conv_cp = conv_cp;
+    s.split.conv_kwp = conv_kwp;
     add_step(at, std::move(s));
     operands_.emplace(sig.str(), op);
     return op;
@@ -2355,8 +2356,14 @@ void Compiler::lower_conv(const GemmChain& ch, int at) {
   // a 16-byte chunk), gathered tile by tile inside the GEMM.
   const int64_t chunk = prec == PFC_PRECISION_BF16 ? 8 : 4;
   const int64_t Cp = round_up(Cin, chunk);
-  int64_t K = KH * KW * Cp;
-  int64_t kpad = round_up(K, prec == PFC_PRECISION_BF16 ? 64 : 32);
+  // A filter row of few channels (Cp*KW <= one k-block) is laid out as one
+  // k-block of KWp taps (zero weights past KW) over a zero-padded input, so
+  // each k-block of A is a 128-byte window of one padded input row (TMA-fed).
+  const int64_t bk = prec == PFC_PRECISION_BF16 ? 64 : 32;
+  const bool window = Cp * KW <= bk && bk % Cp == 0 && dl[1] == 1;
+  const int64_t KWp = window ? bk / Cp : KW;
+  int64_t K = KH * KWp * Cp;
+  int64_t kpad = round_up(K, bk);
   size_t esz = prec == PFC_PRECISION_BF16 ? 2 : 4;
   int64_t M = Nimg * OH * OW;
   Step si;
@@ -2366,10 +2373,17 @@ void Compiler::lower_conv(const GemmChain& ch, int at) {
   I.x = x;
   I.cp = Cp;
   I.precision = prec;
-  const size_t xbytes = (size_t)(Nimg * H * W * Cp) * esz;
+  int64_t Hp = 0, Wp = 0;
+  if (window) {
+    Hp = std::max(H + 2 * pd[0], (OH - 1) * st[0] + (KH - 1) * dl[0] + 1);
+    Wp = std::max(W + 2 * pd[1], (OW - 1) * st[1] + KWp);
+    I.hp = Hp; I.wp = Wp; I.ph = pd[0]; I.pw = pd[1];
+    si.label = "conv input (channels-last, padded) " + shape_str(x.shape);
+  }
+  const size_t xbytes = (size_t)(Nimg * (window ? Hp * Wp : H * W) * Cp) * esz;
   I.out_hi = new_buffer(xbytes);
   I.out_lo = prec == PFC_PRECISION_BF16 ? -1 : new_buffer(xbytes);
-  const Operand opw = prepare_operand(w, O, K, kpad, prec, "prepare conv weight", at, Cp);
+  const Operand opw = prepare_operand(w, O, K, kpad, prec, "prepare conv weight", at, Cp, KWp);
   // output NHWC: logical [N,O,OH,OW], strides (OH*OW*O, 1, OW*O, O)
   View c;
   c.shape = {Nimg, O, OH, OW};
@@ -2386,6 +2400,7 @@ void Compiler::lower_conv(const GemmChain& ch, int at) {
   G.x_hi = I.out_hi; G.x_lo = I.out_lo;
   G.H = H; G.W = W; G.Cp = Cp; G.KH = KH; G.KW = KW; G.sh = st[0]; G.sw = st[1];
   G.ph = pd[0]; G.pw = pd[1]; G.dh = dl[0]; G.dw = dl[1]; G.OH = OH; G.OW = OW;
+  G.Nimg = Nimg; G.Hp = Hp; G.Wp = Wp; G.KWp = KWp;
   G.batch = 1; G.M = M; G.N = O; G.K = K; G.kpad = kpad;
   G.c = c; G.c_sm = O; G.c_sn = 1; G.c_sb = 0;
   G.act = ch.act;
@@ -2667,7 +2682,9 @@ void Compiler::emit_operands_at_producers() {
       S[j].label += " +operand";
     } else if (st.kind == StepKind::CONV_INPUT) {
       const View& x = st.convin.x;  // [N,C,H,W]
-      if (x.is_splat || x.buf < 0 || x.offset != 0 || x.shape.size() != 4 || x.shape[1] != st.convin.cp) continue;
+      if (x.is_splat || x.buf < 0 || x.offset != 0 || x.shape.size() != 4 || x.shape[1] != st.convin.cp ||
+          st.convin.hp > 0)
+        continue;
       const int64_t C = x.shape[1], H = x.shape[2], W = x.shape[3];
       if (x.strides != std::vector<int64_t>{H * W * C, 1, W * C, C}) continue;  // channels-last
       const int j = producer(x.buf);

@@ -370,7 +370,7 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
         W.w = L.src;
         W.o = a.src.shape[0]; W.c = a.src.shape[1]; W.kh = a.src.shape[2]; W.kw = a.src.shape[3];
         W.so = L.stride[0]; W.sc = L.stride[1]; W.skh = L.stride[2]; W.skw = L.stride[3];
-        W.cp = a.conv_cp; W.kpad = a.kpad; W.precision = a.precision;
+        W.cp = a.conv_cp; W.kpad = a.kpad; W.precision = a.precision; W.kwp = a.conv_kwp;
         W.hi = L.hi; W.lo = L.lo;
         launch_conv_weight(W, s);
       } else {
@@ -385,6 +385,7 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
       L.n = a.x.shape[0]; L.c = a.x.shape[1]; L.h = a.x.shape[2]; L.w = a.x.shape[3];
       L.sn = a.x.strides[0]; L.sc = a.x.strides[1]; L.sh = a.x.strides[2]; L.sw = a.x.strides[3];
       L.cp = a.cp; L.precision = a.precision;
+      L.hp = a.hp; L.wp = a.wp; L.ph = a.ph; L.pw = a.pw;
       L.hi = bufp(a.out_hi, 0);
       L.lo = (float*)bufp(a.out_lo, 0);
       launch_conv_input(L, s);
@@ -438,6 +439,7 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
         L.x_lo = bufp(a.x_lo, 0);
         L.H = a.H; L.W = a.W; L.Cp = a.Cp; L.KH = a.KH; L.KW = a.KW; L.sh = a.sh; L.sw = a.sw;
         L.ph = a.ph; L.pw = a.pw; L.dh = a.dh; L.dw = a.dw; L.OH = a.OH; L.OW = a.OW;
+        L.batch_images = a.Nimg; L.Hp = a.Hp; L.Wp = a.Wp; L.KWp = a.KWp;
       }
       launch_gemm(L, s);
       break;

@@ -75,10 +75,17 @@ struct GemmParams {
   void* o_hi;           // operand outputs for a following GEMM (or null)
   float* o_lo;
   long long o_sm;
-  // implicit-GEMM Conv2d (CONV kernels): channels-last input [N][H][W][Cp]
+  // implicit-GEMM Conv2d: channels-last input [N][H][W][Cp] (or a zero-padded
+  // [N][Hp][Wp][Cp] copy when Hp > 0), weight k = (kh*KWp + kw)*Cp + c
   const void* x_hi;
   const void* x_lo;
   int H, W, Cp, KH, KW, sh, sw, ph, pw, dh, dw, OH, OW;
+  int Hp, Wp, KWp;
+  // conv_tma: 0 = A rows gathered (CONV kernels) or a plain GEMM;
+  // 1 = A boxes by TMA from the unpadded input, one (tap, 32 channels) per
+  //     k-block; 2 = A windows by TMA from the padded input, one filter row
+  //     per k-block.  Modes 1 and 2 tile the output as TH x TW pixels.
+  int conv_tma, TW, TH, tiles_w, tiles_h;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -148,6 +155,24 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
       "l"((uint64_t)map), "r"(mbar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t mbar, int c0, int c1,
+                                            int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(mbar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, uint32_t mbar, int c0, int c1,
+                                            int c2, int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(mbar), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
       : "memory");
 }
 
@@ -233,10 +258,11 @@ __device__ __forceinline__ void store_operand1(void* ohi, float* olo, long long 
   }
 }
 
+// Rows m_base .. m_base+31 of the output matrix, of which the first nvalid exist.
 template <int ACT, int PREC>
-__device__ __forceinline__ void store_block(const GemmParams& p, const float* ep, int row0, int n0, float* cbase,
-                                            const float* rbase, void* ohi, float* olo, bool vec_c, bool vec_r,
-                                            float alpha, float bsc, bool has_shift, int lane) {
+__device__ __forceinline__ void store_block(const GemmParams& p, const float* ep, long long m_base, int nvalid, int n0,
+                                            float* cbase, const float* rbase, void* ohi, float* olo, bool vec_c,
+                                            bool vec_r, float alpha, float bsc, bool has_shift, int lane) {
   const int rsub = lane >> 2, c4 = (lane & 3) * 4;
   const int n = n0 + c4;
   float sc[4], sh[4];
@@ -254,10 +280,10 @@ __device__ __forceinline__ void store_block(const GemmParams& p, const float* ep
   float4 a[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) a[k] = *reinterpret_cast<const float4*>(ep + (8 * k + rsub) * 20 + c4);
-  if (full_n && vec_c && row0 + 32 <= p.M && !rbase) {
+  if (full_n && vec_c && nvalid == 32 && !rbase) {
     // whole block inside the output, no residual: straight float4 stores
-    const long long c0 = (long long)(row0 + rsub) * p.c_sm + n, cstep = 8 * p.c_sm;
-    const long long o0 = (long long)(row0 + rsub) * p.o_sm + n, ostep = 8 * p.o_sm;
+    const long long c0 = (m_base + rsub) * p.c_sm + n, cstep = 8 * p.c_sm;
+    const long long o0 = (m_base + rsub) * p.o_sm + n, ostep = 8 * p.o_sm;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       float v[4] = {a[k].x, a[k].y, a[k].z, a[k].w};
@@ -274,7 +300,7 @@ __device__ __forceinline__ void store_block(const GemmParams& p, const float* ep
   }
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const int row = row0 + 8 * k + rsub;
+    const long long row = m_base + 8 * k + rsub;
     float v[4] = {a[k].x, a[k].y, a[k].z, a[k].w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -282,12 +308,12 @@ __device__ __forceinline__ void store_block(const GemmParams& p, const float* ep
       if (has_shift) v[j] = v[j] + sh[j];
       v[j] = act_apply<ACT>(v[j]);
     }
-    if (row >= p.M) continue;
-    const long long co = (long long)row * p.c_sm + (long long)n * p.c_sn;
-    const long long oo = (long long)row * p.o_sm + n;
+    if (8 * k + rsub >= nvalid) continue;
+    const long long co = row * p.c_sm + (long long)n * p.c_sn;
+    const long long oo = row * p.o_sm + n;
     if (full_n && vec_c) {
       if (rbase) {
-        const long long ro = (long long)row * p.r_sm + (long long)n * p.r_sn;
+        const long long ro = row * p.r_sm + (long long)n * p.r_sn;
         if (vec_r) {
           const float4 r4 = *reinterpret_cast<const float4*>(rbase + ro);
           v[0] += r4.x; v[1] += r4.y; v[2] += r4.z; v[3] += r4.w;
@@ -303,7 +329,7 @@ __device__ __forceinline__ void store_block(const GemmParams& p, const float* ep
       for (int j = 0; j < 4; ++j) {
         if (n + j >= p.N) break;
         float w = v[j];
-        if (rbase) w += rbase[(long long)row * p.r_sm + (long long)(n + j) * p.r_sn];
+        if (rbase) w += rbase[row * p.r_sm + (long long)(n + j) * p.r_sn];
         if (cbase) cbase[co + (long long)j * p.c_sn] = w;
         if (ohi) store_operand1<PREC>(ohi, olo, oo + j, w);
       }
@@ -371,6 +397,16 @@ __device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& bz,
   const int gsz = min(p.num_m - first_m, group);
   tm = first_m + (r % per_group) % gsz;
   tn = (r % per_group) / gsz;
+}
+
+// Output tile tm of a TMA-fed convolution -> (image, first output row, first
+// output column); the tile is TH x TW output pixels.
+__device__ __forceinline__ void conv_tile(const GemmParams& p, int tm, int& img, int& oh0, int& ow0) {
+  const int per_img = p.tiles_h * p.tiles_w;
+  img = tm / per_img;
+  const int r = tm - img * per_img;
+  oh0 = (r / p.tiles_w) * p.TH;
+  ow0 = (r % p.tiles_w) * p.TW;
 }
 
 // Persistent kernel: each CTA walks tiles blockIdx.x, +gridDim.x, ...
@@ -443,12 +479,14 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
       const bool mok = m < p.M;
       int ih0 = 0, iw0 = 0;
       long long img_base = 0;
+      // a zero-padded input is addressed in padded coordinates (no border checks needed)
+      const int XH = p.Hp > 0 ? p.Hp : p.H, XW = p.Hp > 0 ? p.Wp : p.W;
       if (mok) {
         const int img = m / ohw, rem = m - img * ohw;
         const int oh = rem / p.OW, ow = rem - oh * p.OW;
-        ih0 = oh * p.sh - p.ph;
-        iw0 = ow * p.sw - p.pw;
-        img_base = (long long)img * p.H * p.W * p.Cp;
+        ih0 = oh * p.sh - (p.Hp > 0 ? 0 : p.ph);
+        iw0 = ow * p.sw - (p.Hp > 0 ? 0 : p.pw);
+        img_base = (long long)img * XH * XW * p.Cp;
       }
       int c = 0, kw = 0, kh = 0, tap = 0;  // position of the next chunk along k
       for (int kb = 0; kb < nkb; ++kb, ++g) {
@@ -467,16 +505,16 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int ih = ih0 + kh * p.dh, iw = iw0 + kw * p.dw;
-          const bool in = mok && tap < taps && (unsigned)ih < (unsigned)p.H && (unsigned)iw < (unsigned)p.W;
-          const long long off = in ? (img_base + ((long long)ih * p.W + iw) * p.Cp + c) * C::ESZ : 0;
+          const bool in = mok && tap < taps && kw < p.KW && (unsigned)ih < (unsigned)XH && (unsigned)iw < (unsigned)XW;
+          const long long off = in ? (img_base + ((long long)ih * XW + iw) * p.Cp + c) * C::ESZ : 0;
           const uint32_t sw = (uint32_t)((j ^ (r & 7)) << 4);  // 128-byte swizzle, as TMA writes it
           cp_async16(arow_hi + sw, (const char*)p.x_hi + off, in ? 16u : 0u);
           if constexpr (C::NOPS == 2) cp_async16(arow_lo + sw, (const char*)p.x_lo + off, in ? 16u : 0u);
           c += CH;
           if (c == p.Cp) {
             c = 0;
-            ++tap;
-            if (++kw == p.KW) { kw = 0; ++kh; }
+            if (++kw == p.KWp) { kw = 0; ++kh; }
+            tap = kh * p.KW + kw;
           }
         }
         cp_async_commit();
@@ -513,12 +551,29 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
         const uint32_t fb = smem_u32(&full[s]);
         mbar_expect_tx(fb, C::STAGE);
         const int kc = kb * C::BK;
-        tma_load_3d(smem_u32(st), &ta_hi, fb, kc, m0, ca);
-        tma_load_3d(smem_u32(st + C::A_TILE), &tb_hi, fb, kc, n0, cb);
-        if constexpr (C::NOPS == 2) {
-          tma_load_3d(smem_u32(st + C::A_TILE + C::B_TILE), &ta_lo, fb, kc, m0, ca);
-          tma_load_3d(smem_u32(st + 2 * C::A_TILE + C::B_TILE), &tb_lo, fb, kc, n0, cb);
+        const uint32_t a_hi_dst = smem_u32(st), a_lo_dst = smem_u32(st + C::A_TILE + C::B_TILE);
+        if (p.conv_tma == 1) {
+          // 32 channels of one filter tap: a TH x TW box of the input shifted by the tap
+          const int per_tap = p.Cp / 32;
+          const int tap = kb / per_tap, c0 = (kb - tap * per_tap) * 32;
+          const int kh = tap / p.KW, kw = tap - kh * p.KW;
+          int img, oh0, ow0;
+          conv_tile(p, tm, img, oh0, ow0);
+          const int x0 = ow0 - p.pw + kw * p.dw, y0 = oh0 - p.ph + kh * p.dh;
+          tma_load_4d(a_hi_dst, &ta_hi, fb, c0, x0, y0, img);
+          if constexpr (C::NOPS == 2) tma_load_4d(a_lo_dst, &ta_lo, fb, c0, x0, y0, img);
+        } else if (p.conv_tma == 2) {
+          // filter row kb: for every output pixel a 128-byte window of the padded input
+          int img, oh0, ow0;
+          conv_tile(p, tm, img, oh0, ow0);
+          tma_load_5d(a_hi_dst, &ta_hi, fb, 0, ow0, kb, oh0, img);
+          if constexpr (C::NOPS == 2) tma_load_5d(a_lo_dst, &ta_lo, fb, 0, ow0, kb, oh0, img);
+        } else {
+          tma_load_3d(a_hi_dst, &ta_hi, fb, kc, m0, ca);
+          if constexpr (C::NOPS == 2) tma_load_3d(a_lo_dst, &ta_lo, fb, kc, m0, ca);
         }
+        tma_load_3d(smem_u32(st + C::A_TILE), &tb_hi, fb, kc, n0, cb);
+        if constexpr (C::NOPS == 2) tma_load_3d(smem_u32(st + 2 * C::A_TILE + C::B_TILE), &tb_lo, fb, kc, n0, cb);
       }
     }
     // drain: every issued copy must have landed before the CTA can exit
@@ -610,7 +665,20 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
       if (!ok) break;
       int bz, tm, tn;
       tile_coords(p, t, bz, tm, tn);
-      const int m0 = tm * kBM + q * 32, n0 = tn * BN + col0;
+      const int n0 = tn * BN + col0;
+      // this warp's 32 rows: output matrix rows m_base.., the first nvalid of which exist
+      long long m_base;
+      int nvalid;
+      if (p.conv_tma) {
+        int img, oh0, ow0;
+        conv_tile(p, tm, img, oh0, ow0);
+        const int oh = oh0 + (q * 32) / p.TW, ow = ow0 + (q * 32) % p.TW;  // TW >= 32: one output row
+        m_base = ((long long)img * p.OH + oh) * p.OW + ow;
+        nvalid = oh < p.OH ? max(0, min(32, p.OW - ow)) : 0;
+      } else {
+        m_base = (long long)tm * kBM + q * 32;
+        nvalid = max(0, min(32, p.M - (int)m_base));
+      }
       float* cbase = p.c ? p.c + (long long)bz * p.c_sb : nullptr;
       const float* rbase = p.res ? p.res + (long long)bz * p.r_sb : nullptr;
       const long long obatch = (long long)bz * p.M * p.o_sm;
@@ -627,12 +695,12 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
           *reinterpret_cast<float4*>(ep + lane * 20 + j) = make_float4(acc[cc + j], acc[cc + j + 1], acc[cc + j + 2], acc[cc + j + 3]);
         __syncwarp();
         switch (p.act) {
-          case 1: store_block<1, PREC>(p, ep, m0, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-          case 2: store_block<2, PREC>(p, ep, m0, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-          case 3: store_block<3, PREC>(p, ep, m0, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-          case 4: store_block<4, PREC>(p, ep, m0, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-          case 5: store_block<5, PREC>(p, ep, m0, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-          default: store_block<0, PREC>(p, ep, m0, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          case 1: store_block<1, PREC>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          case 2: store_block<2, PREC>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          case 3: store_block<3, PREC>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          case 4: store_block<4, PREC>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          case 5: store_block<5, PREC>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          default: store_block<0, PREC>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
         }
         __syncwarp();
       }
@@ -685,8 +753,42 @@ CUtensorMap make_map(const void* base, int prec, int64_t kpad, int64_t rows, int
   return m;
 }
 
+// A-operand maps of a TMA-fed convolution (box of TW x TH output pixels).
+// Mode 1: the unpadded input [N][H][W][Cp], box (32 channels, TW, TH, 1).
+// Mode 2: overlapping windows of the padded input [N][Hp][Wp][Cp]: dims
+// (window of 128 bytes, output column at stride sw*Cp, filter row at dh
+// padded input rows, output row at sh padded rows, image), box
+// (window, TW, 1, TH, 1).  False when the driver rejects the map.
+bool make_conv_map(const GemmLaunch& L, int prec, int mode, int TW, int TH, const void* base, CUtensorMap* m) {
+  std::memset(m, 0, sizeof *m);
+  const int esz = prec == PFC_PRECISION_BF16 ? 2 : 4;
+  const CUtensorMapDataType dt = prec == PFC_PRECISION_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const cuuint64_t C = (cuuint64_t)L.Cp;
+  CUresult r;
+  if (mode == 1) {
+    cuuint64_t dims[4] = {C, (cuuint64_t)L.W, (cuuint64_t)L.H, (cuuint64_t)L.batch_images};
+    cuuint64_t strides[3] = {C * esz, C * L.W * esz, C * L.W * L.H * esz};
+    cuuint32_t box[4] = {(cuuint32_t)(128 / esz), (cuuint32_t)TW, (cuuint32_t)TH, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    r = get_encode()(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    const cuuint64_t row = C * L.Wp * esz;  // bytes of one padded input row
+    cuuint64_t dims[5] = {(cuuint64_t)(128 / esz), (cuuint64_t)L.OW, (cuuint64_t)L.KH, (cuuint64_t)L.OH,
+                          (cuuint64_t)L.batch_images};
+    cuuint64_t strides[4] = {(cuuint64_t)(L.sw * C * esz), row * L.dh, row * L.sh, row * L.Hp};
+    cuuint32_t box[5] = {(cuuint32_t)(128 / esz), (cuuint32_t)TW, 1, (cuuint32_t)TH, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    r = get_encode()(m, dt, 5, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
+  return r == CUDA_SUCCESS;
+}
+
 template <int PREC, int BN, bool CONV>
-void launch_t(const GemmLaunch& L, cudaStream_t stream) {
+void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const CUtensorMap* conv_maps = nullptr,
+              int TW = 0) {
   using C = Cfg<PREC, BN>;
   static bool attr_set[64] = {};
   int dev = 0;
@@ -698,10 +800,16 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream) {
   const int64_t a_rows = L.M, b_rows = L.N;
   CUtensorMap tb_hi = make_map(L.b_hi, PREC, L.kpad, b_rows, L.b_sb ? L.batch : 1, BN);
   CUtensorMap tb_lo = PREC == PFC_PRECISION_BF16 ? tb_hi : make_map(L.b_lo, PREC, L.kpad, b_rows, L.b_sb ? L.batch : 1, BN);
-  // CONV gathers A itself: its maps are unused
-  CUtensorMap ta_hi = CONV ? tb_hi : make_map(L.a_hi, PREC, L.kpad, a_rows, L.a_sb ? L.batch : 1, kBM);
-  CUtensorMap ta_lo = CONV || PREC == PFC_PRECISION_BF16 ? ta_hi
-                                                         : make_map(L.a_lo, PREC, L.kpad, a_rows, L.a_sb ? L.batch : 1, kBM);
+  // CONV gathers A itself (its maps are unused); TMA-fed convolutions bring their own maps
+  CUtensorMap ta_hi, ta_lo;
+  if (conv_tma) {
+    ta_hi = conv_maps[0];
+    ta_lo = conv_maps[1];
+  } else {
+    ta_hi = CONV ? tb_hi : make_map(L.a_hi, PREC, L.kpad, a_rows, L.a_sb ? L.batch : 1, kBM);
+    ta_lo = CONV || PREC == PFC_PRECISION_BF16 ? ta_hi
+                                               : make_map(L.a_lo, PREC, L.kpad, a_rows, L.a_sb ? L.batch : 1, kBM);
+  }
   GemmParams p;
   p.M = (int)L.M;
   p.N = (int)L.N;
@@ -735,6 +843,13 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream) {
   p.H = (int)L.H; p.W = (int)L.W; p.Cp = (int)L.Cp; p.KH = (int)L.KH; p.KW = (int)L.KW;
   p.sh = (int)L.sh; p.sw = (int)L.sw; p.ph = (int)L.ph; p.pw = (int)L.pw; p.dh = (int)L.dh; p.dw = (int)L.dw;
   p.OH = (int)L.OH; p.OW = (int)L.OW;
+  p.Hp = (int)L.Hp; p.Wp = (int)L.Wp; p.KWp = (int)(L.KWp > 0 ? L.KWp : L.KW);
+  p.conv_tma = conv_tma;
+  p.TW = TW > 0 ? TW : 128;
+  p.TH = 128 / p.TW;
+  p.tiles_w = conv_tma ? (int)ceil_div(L.OW, p.TW) : 1;
+  p.tiles_h = conv_tma ? (int)ceil_div(L.OH, p.TH) : 1;
+  if (conv_tma) p.num_m = (int)(L.batch_images * p.tiles_h * p.tiles_w);
   if (L.K == 0) p.nkb = 0;
   // accumulation chunks of 512 elements of K (16 tf32 / 8 bf16 k-blocks)
   p.kchunk = 512 / C::BK;
@@ -755,6 +870,22 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream) {
 
 }  // namespace
 
+// Which A feed a convolution can use: 1 or 2 (TMA, maps built) or 0 (gather).
+int conv_tma_mode(const GemmLaunch& L, int prec, CUtensorMap* maps, int* TW) {
+  if (!L.allow_tma_conv || L.OW < 32) return 0;
+  const int esz = prec == PFC_PRECISION_BF16 ? 2 : 4;
+  const int64_t bk = 128 / esz, kwp = L.KWp > 0 ? L.KWp : L.KW;
+  *TW = L.OW > 32 ? 64 : 32;
+  int mode = 0;
+  if (L.Hp == 0 && L.Cp % bk == 0 && L.sh == 1 && L.sw == 1 && kwp == L.KW) mode = 1;
+  else if (L.Hp > 0 && kwp * L.Cp == bk && L.dw == 1 && (L.sw * L.Cp * esz) % 16 == 0) mode = 2;
+  if (!mode) return 0;
+  if (!make_conv_map(L, prec, mode, *TW, 128 / *TW, L.x_hi, &maps[0])) return 0;
+  if (prec == PFC_PRECISION_BF16) maps[1] = maps[0];
+  else if (!make_conv_map(L, prec, mode, *TW, 128 / *TW, L.x_lo, &maps[1])) return 0;
+  return mode;
+}
+
 void launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
   PFB_CHECK_ARG(L.M > 0 && L.N > 0 && L.batch > 0, "gemm: empty problem");
   PFB_CHECK_ARG(L.M < (1ll << 31) && L.N < (1ll << 31), "gemm: dimension too large");
@@ -773,7 +904,11 @@ void launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
     PFB_CHECK_ARG(L.x_hi && ((uintptr_t)L.x_hi & 15) == 0 && (L.precision == PFC_PRECISION_BF16 ||
                                                                (L.x_lo && ((uintptr_t)L.x_lo & 15) == 0)),
                   "conv gemm: channels-last input must be 16-byte aligned");
-    PFB_CHECK_ARG(L.Cp > 0 && L.Cp % ch == 0 && L.K == L.KH * L.KW * L.Cp, "conv gemm: bad channel padding");
+    const int64_t kwp = L.KWp > 0 ? L.KWp : L.KW;
+    PFB_CHECK_ARG(L.Cp > 0 && L.Cp % ch == 0 && kwp >= L.KW && L.K == L.KH * kwp * L.Cp, "conv gemm: bad channel padding");
+    PFB_CHECK_ARG(L.Hp == 0 || (L.Hp >= (L.OH - 1) * L.sh + (L.KH - 1) * L.dh + 1 &&
+                                L.Wp >= (L.OW - 1) * L.sw + (kwp - 1) * L.dw + 1),
+                  "conv gemm: padded input too small");
     PFB_CHECK_ARG(L.M == L.M / (L.OH * L.OW) * L.OH * L.OW && L.H * L.W * L.Cp < (1ll << 40) &&
                       L.OH * L.OW < (1ll << 31) && L.KH * L.KW < (1 << 20),
                   "conv gemm: bad geometry");
@@ -783,7 +918,11 @@ void launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
   PFB_CHECK_ARG(((uintptr_t)L.b_hi & 15) == 0, "gemm: operands must be 16-byte aligned");
   if (L.precision == PFC_PRECISION_BF16) {
     if (L.conv) {
-      launch_t<PFC_PRECISION_BF16, 64, true>(L, stream);
+      CUtensorMap maps[2];
+      int TW = 0;
+      const int mode = conv_tma_mode(L, PFC_PRECISION_BF16, maps, &TW);
+      if (mode) launch_t<PFC_PRECISION_BF16, 64, false>(L, stream, mode, maps, TW);
+      else launch_t<PFC_PRECISION_BF16, 64, true>(L, stream);
     } else {
       if (L.N > 64) launch_t<PFC_PRECISION_BF16, 128, false>(L, stream);
       else launch_t<PFC_PRECISION_BF16, 64, false>(L, stream);
@@ -791,9 +930,13 @@ void launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
   } else {
     PFB_CHECK_ARG(L.b_lo && (L.conv || L.a_lo), "gemm: tf32x3 needs lo operands");
     if (L.conv) {
+      CUtensorMap maps[2];
+      int TW = 0;
+      const int mode = conv_tma_mode(L, PFC_PRECISION_TF32X3, maps, &TW);
+      if (mode) launch_t<PFC_PRECISION_TF32X3, 64, false>(L, stream, mode, maps, TW);
       // 64-column tiles: the gathering warps leave too few registers for a
       // 128-column accumulator (wider convolutions take several column tiles)
-      launch_t<PFC_PRECISION_TF32X3, 64, true>(L, stream);
+      else launch_t<PFC_PRECISION_TF32X3, 64, true>(L, stream);
     } else {
       if (L.N > 64) launch_t<PFC_PRECISION_TF32X3, 128, false>(L, stream);
       else launch_t<PFC_PRECISION_TF32X3, 64, false>(L, stream);

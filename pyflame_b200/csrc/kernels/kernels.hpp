@@ -41,6 +41,12 @@ struct GemmLaunch {
   const void* x_hi = nullptr;
   const void* x_lo = nullptr;
   int64_t H = 0, W = 0, Cp = 0, KH = 1, KW = 1, sh = 1, sw = 1, ph = 0, pw = 0, dh = 1, dw = 1, OH = 0, OW = 0;
+  int64_t batch_images = 1;  // N of the convolution (M = N*OH*OW)
+  // x is a zero-padded copy [N][Hp][Wp][Cp] when Hp > 0 (padding already
+  // applied: padded coordinates are oh*sh + kh*dh, ow*sw + kw*dw)
+  int64_t Hp = 0, Wp = 0;
+  int64_t KWp = 0;  // taps per filter row in the weight layout (>= KW; 0 = KW)
+  bool allow_tma_conv = true;  // TMA-fed A when the geometry allows it
 };
 void launch_gemm(const GemmLaunch& L, cudaStream_t stream);
 
@@ -51,6 +57,8 @@ struct ConvInputLaunch {
   const float* x = nullptr;
   int64_t n = 0, c = 0, h = 0, w = 0, sn = 0, sc = 0, sh = 0, sw = 0;
   int64_t cp = 0;
+  // zero-padded output [N][hp][wp][cp] with the image at (ph, pw); hp = 0: unpadded
+  int64_t hp = 0, wp = 0, ph = 0, pw = 0;
   int precision = 0;
   void* hi = nullptr;
   float* lo = nullptr;
@@ -63,6 +71,7 @@ struct ConvWeightLaunch {
   const float* w = nullptr;
   int64_t o = 0, c = 0, kh = 0, kw = 0, so = 0, sc = 0, skh = 0, skw = 0;
   int64_t cp = 0, kpad = 0;
+  int64_t kwp = 0;  // taps per filter row in the layout (>= kw; 0 = kw): k = (kh*kwp + kw)*cp + c
   int precision = 0;
   void* hi = nullptr;
   float* lo = nullptr;

@@ -249,21 +249,26 @@ __global__ void pool_kernel(PoolLaunch L) {
 // when every index fits in 32 bits.
 template <int PREC, typename IDX>
 __global__ void conv_input_kernel(ConvInputLaunch L) {
+  // output extent: the padded image when hp > 0 (zeros outside the input)
   const IDX C = (IDX)L.c, G = (IDX)(L.cp / 4), H = (IDX)L.h, W = (IDX)L.w;
-  const IDX total = (IDX)L.n * H * W * G;
+  const IDX OHp = L.hp > 0 ? (IDX)L.hp : H, OWp = L.hp > 0 ? (IDX)L.wp : W;
+  const IDX PH = L.hp > 0 ? (IDX)L.ph : 0, PW = L.hp > 0 ? (IDX)L.pw : 0;
+  const IDX total = (IDX)L.n * OHp * OWp * G;
   for (IDX i = (IDX)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (IDX)gridDim.x * blockDim.x) {
     const IDX g = i % G;
     const IDX pix = i / G;
-    const IDX w = pix % W;
-    const IDX hn = pix / W;
-    const IDX h = hn % H;
-    const IDX n = hn / H;
+    const IDX wq = pix % OWp;
+    const IDX hn = pix / OWp;
+    const IDX hq = hn % OHp;
+    const IDX n = hn / OHp;
+    const IDX h = hq - PH, w = wq - PW;
+    const bool inside = h >= 0 && h < H && w >= 0 && w < W;
     const float* src = L.x + (long long)n * L.sn + (long long)h * L.sh + (long long)w * L.sw;
     float x[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const IDX c = 4 * g + j;
-      x[j] = c < C ? src[(long long)c * L.sc] : 0.f;
+      x[j] = (inside && c < C) ? src[(long long)c * L.sc] : 0.f;
     }
     if constexpr (PREC == PFC_PRECISION_BF16) {
       __nv_bfloat162 a = __floats2bfloat162_rn(x[0], x[1]), b = __floats2bfloat162_rn(x[2], x[3]);
@@ -287,15 +292,13 @@ __global__ void conv_input_kernel(ConvInputLaunch L) {
 template <int PREC>
 __global__ void conv_weight_kernel(ConvWeightLaunch L) {
   const long long total = L.o * L.kpad;
-  const long long taps = L.kh * L.kw;
+  const long long kwp = L.kwp > 0 ? L.kwp : L.kw;  // taps per filter row in the layout
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
     const long long o = i / L.kpad, k = i % L.kpad;
-    const long long tap = k / L.cp, c = k % L.cp;
+    const long long slot = k / L.cp, c = k % L.cp;
+    const long long kh = slot / kwp, kw = slot % kwp;
     float x = 0.f;
-    if (tap < taps && c < L.c) {
-      const long long kh = tap / L.kw, kw = tap % L.kw;
-      x = L.w[o * L.so + c * L.sc + kh * L.skh + kw * L.skw];
-    }
+    if (kh < L.kh && kw < L.kw && c < L.c) x = L.w[o * L.so + c * L.sc + kh * L.skh + kw * L.skw];
     if constexpr (PREC == PFC_PRECISION_BF16) {
       ((__nv_bfloat16*)L.hi)[i] = __float2bfloat16_rn(x);
     } else {
@@ -513,7 +516,8 @@ void launch_conv_input(const ConvInputLaunch& L, cudaStream_t stream) {
   PFB_CHECK_ARG(L.x && L.hi && (L.precision == PFC_PRECISION_BF16 || L.lo), "conv input: null pointer");
   PFB_CHECK_ARG(L.cp >= L.c && L.c > 0 && L.cp % 4 == 0, "conv input: padded channels must cover the channels");
   PFB_CHECK_ARG(((uintptr_t)L.hi & 15) == 0 && ((uintptr_t)L.lo & 15) == 0, "conv input: outputs must be 16-byte aligned");
-  const long long total = L.n * L.h * L.w * (L.cp / 4);
+  PFB_CHECK_ARG(L.hp == 0 || (L.hp >= L.h + L.ph && L.wp >= L.w + L.pw), "conv input: padded extent too small");
+  const long long total = L.n * (L.hp > 0 ? L.hp * L.wp : L.h * L.w) * (L.cp / 4);
   if (total == 0) return;
   const unsigned g = grid_for(total, 256);
   const bool small = total < (1ll << 30);  // i + grid stride stays below 2^31
@@ -529,7 +533,9 @@ void launch_conv_input(const ConvInputLaunch& L, cudaStream_t stream) {
 
 void launch_conv_weight(const ConvWeightLaunch& L, cudaStream_t stream) {
   PFB_CHECK_ARG(L.w && L.hi && (L.precision == PFC_PRECISION_BF16 || L.lo), "conv weight: null pointer");
-  PFB_CHECK_ARG(L.cp >= L.c && L.kpad >= L.kh * L.kw * L.cp, "conv weight: bad layout");
+  PFB_CHECK_ARG(L.cp >= L.c && (L.kwp == 0 || L.kwp >= L.kw) &&
+                    L.kpad >= L.kh * (L.kwp > 0 ? L.kwp : L.kw) * L.cp,
+                "conv weight: bad layout");
   const long long total = L.o * L.kpad;
   if (total == 0) return;
   if (L.precision == PFC_PRECISION_BF16) conv_weight_kernel<PFC_PRECISION_BF16><<<grid_for(total, 256), 256, 0, stream>>>(L);

@@ -85,12 +85,14 @@ struct SplitArgs {
   // conv_cp > 0: src is a Conv2d weight [O,C,KH,KW] laid out for the implicit
   // GEMM, k = (kh*KW + kw)*conv_cp + c
   int64_t conv_cp = 0;
+  int64_t conv_kwp = 0;  // taps per filter row in that layout (0 = KW)
 };
 
 struct ConvInputArgs {
   View x;  // [N,C,H,W]
-  int out_hi = -1, out_lo = -1;  // [N][H][W][cp]
+  int out_hi = -1, out_lo = -1;  // [N][H][W][cp], or zero-padded [N][hp][wp][cp] when hp > 0
   int64_t cp = 0;
+  int64_t hp = 0, wp = 0, ph = 0, pw = 0;
   int precision = 0;
 };
 
@@ -123,6 +125,7 @@ struct GemmArgs {
   bool conv = false;
   int x_hi = -1, x_lo = -1;
   int64_t H = 0, W = 0, Cp = 0, KH = 1, KW = 1, sh = 1, sw = 1, ph = 0, pw = 0, dh = 1, dw = 1, OH = 0, OW = 0;
+  int64_t Nimg = 1, Hp = 0, Wp = 0, KWp = 0;
 };
 
 struct PoolArgs {

@@ -259,10 +259,16 @@ def test_gemm_bf16_mode(oracle_mod, rng, native):
 
 @pytest.mark.parametrize("cfg", [dict(n=2, c=3, h=17, w=15, o=8, k=3, s=1, p=1),
                                  dict(n=2, c=3, h=32, w=32, o=16, k=7, s=2, p=3),
-                                 dict(n=1, c=5, h=9, w=11, o=4, k=2, s=3, p=0)])
+                                 dict(n=1, c=5, h=9, w=11, o=4, k=2, s=3, p=0),
+                                 # TMA-fed A (output width >= 32): 32-channel boxes, partial tiles, dilation
+                                 dict(n=2, c=32, h=37, w=45, o=64, k=3, s=1, p=2, d=2),
+                                 dict(n=1, c=64, h=33, w=70, o=96, k=3, s=1, p=1),
+                                 # TMA-fed windows of a padded input: few channels, stride 2, row dilation
+                                 dict(n=2, c=3, h=70, w=83, o=16, k=5, s=2, p=2),
+                                 dict(n=2, c=4, h=40, w=36, o=8, k=3, s=1, p=1, d=(2, 1))])
 def test_conv2d(cuda_executor, oracle_mod, rng, cfg):
     x = rng.random((cfg["n"], cfg["c"], cfg["h"], cfg["w"])).astype(np.float32)
-    conv = nn.Conv2d(cfg["c"], cfg["o"], cfg["k"], cfg["s"], cfg["p"])
+    conv = nn.Conv2d(cfg["c"], cfg["o"], cfg["k"], cfg["s"], cfg["p"], cfg.get("d", 1))
     conv.set_parameter("weight", rng.standard_normal((cfg["o"], cfg["c"], cfg["k"], cfg["k"])).astype(np.float32))
     conv.set_parameter("bias", rng.standard_normal(cfg["o"]).astype(np.float32))
     (g,), (r,) = run(cuda_executor, [conv(pf.tensor(x))], oracle_mod)
