@@ -374,18 +374,18 @@ __global__ void pool_cl_kernel(PoolLaunch L) {
 }
 
 // Adaptive average pool to 1x1 over a channels-last input: one CTA per
-// (image, 32-channel group); 8 warps take every 8th pixel, lanes are
-// channels (coalesced 128-byte reads); the 8 partial sums meet in shared
+// (image, 32-channel group); 32 warps take every 32nd pixel, lanes are
+// channels (coalesced 128-byte reads); the 32 partial sums meet in shared
 // memory.
-__global__ void global_avg_cl_kernel(PoolLaunch L) {
-  __shared__ float part[8][32];
+__global__ void __launch_bounds__(1024) global_avg_cl_kernel(PoolLaunch L) {
+  __shared__ float part[32][33];
   const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
   const long long n = blockIdx.y, c = (long long)blockIdx.x * 32 + lane;
   const long long P = L.h * L.w;
   float s = 0.f;
   if (c < L.c) {
     const float* xb = L.x + n * L.sn + c;
-    for (long long p = wp; p < P; p += 8) {
+    for (long long p = wp; p < P; p += 32) {
       const long long h = p / L.w, w = p - h * L.w;
       s += xb[h * L.sh + w * L.sw];
     }
@@ -395,7 +395,7 @@ __global__ void global_avg_cl_kernel(PoolLaunch L) {
   if (wp == 0 && c < L.c) {
     float t = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) t += part[k][lane];
+    for (int k = 0; k < 32; ++k) t += part[k][lane];
     const float out = t / (float)P;
     const long long yo = n * L.osn + c * L.osc;
     if (L.y) L.y[yo] = out;
@@ -489,7 +489,7 @@ void launch_pool(const PoolLaunch& L, cudaStream_t stream) {
                 "pool: operand output needs a dense channels-last layout");
   if (L.mode == 2 && L.oh == 1 && L.ow == 1 && L.sc == 1 && L.n < 65536) {
     dim3 grid((unsigned)ceil_div(L.c, 32), (unsigned)L.n, 1);
-    global_avg_cl_kernel<<<grid, 256, 0, stream>>>(L);
+    global_avg_cl_kernel<<<grid, 1024, 0, stream>>>(L);
     PFB_CUDA(cudaGetLastError());
     return;
   }
