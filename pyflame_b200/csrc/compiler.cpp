@@ -2361,6 +2361,16 @@ void Compiler::lower_conv(const GemmChain& ch, int at) {
   // each k-block of A is a 128-byte window of one padded input row (TMA-fed).
   const int64_t bk = prec == PFC_PRECISION_BF16 ? 64 : 32;
   const bool window = Cp * KW <= bk && bk % Cp == 0 && dl[1] == 1;
+  // A stride-1 filter over whole k-blocks of channels whose output rows are
+  // narrower than the 32-pixel TMA boxes also reads a zero-padded input:
+  // numbering output pixels in its padded row space turns every tap into a
+  // row offset, so the GEMM stages each tile's input rows (the halo) once per
+  // channel block and enters them per tap.  The halo of 128 pixels must fit
+  // one 256-row copy.  (At 64 output channels the two TMA-fed forms run at the
+  // same rate, and wider rows keep the unpadded input that producers write.)
+  const int64_t reach = (KH - 1) * dl[0] * (W + 2 * pd[1]) + (KW - 1) * dl[1];
+  const bool halo = !window && st[0] == 1 && st[1] == 1 && Cp % bk == 0 && OW < 32 &&
+                    round_up(128 + reach, 8) <= 256;
   const int64_t KWp = window ? bk / Cp : KW;
   int64_t K = KH * KWp * Cp;
   int64_t kpad = round_up(K, bk);
@@ -2374,13 +2384,13 @@ void Compiler::lower_conv(const GemmChain& ch, int at) {
   I.cp = Cp;
   I.precision = prec;
   int64_t Hp = 0, Wp = 0;
-  if (window) {
+  if (window || halo) {
     Hp = std::max(H + 2 * pd[0], (OH - 1) * st[0] + (KH - 1) * dl[0] + 1);
-    Wp = std::max(W + 2 * pd[1], (OW - 1) * st[1] + KWp);
+    Wp = std::max(W + 2 * pd[1], (OW - 1) * st[1] + (KWp - 1) * dl[1] + 1);
     I.hp = Hp; I.wp = Wp; I.ph = pd[0]; I.pw = pd[1];
     si.label = "conv input (channels-last, padded) " + shape_str(x.shape);
   }
-  const size_t xbytes = (size_t)(Nimg * (window ? Hp * Wp : H * W) * Cp) * esz;
+  const size_t xbytes = (size_t)(Nimg * (Hp > 0 ? Hp * Wp : H * W) * Cp) * esz;
   I.out_hi = new_buffer(xbytes);
   I.out_lo = prec == PFC_PRECISION_BF16 ? -1 : new_buffer(xbytes);
   const Operand opw = prepare_operand(w, O, K, kpad, prec, "prepare conv weight", at, Cp, KWp);

@@ -85,7 +85,10 @@ struct GemmParams {
   // 1 = A boxes by TMA from the unpadded input, one (tap, 32 channels) per
   //     k-block; 2 = A windows by TMA from the padded input, one filter row
   //     per k-block.  Modes 1 and 2 tile the output as TH x TW pixels.
+  //     3 = halo-staged (conv_halo_kernel): output pixels numbered in the
+  //     padded row space, halo_rows input rows per 32-channel block.
   int conv_tma, TW, TH, tiles_w, tiles_h;
+  int nimg, halo_rows;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -149,6 +152,14 @@ __device__ __forceinline__ void mbar_wait_own(uint32_t a, uint32_t parity, int* 
   }
 }
 
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t mbar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(mbar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t mbar, int c0, int c1,
                                             int c2) {
   asm volatile(
@@ -187,6 +198,15 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
   d |= (uint64_t)2 << 61;               // SWIZZLE_128B
   return d;
 }
+
+// The 128-byte swizzle is a function of the absolute shared-memory address
+// (chunk bits 4-6 XOR row bits 7-9), for TMA writes and tensor-core reads
+// alike.  So a matrix may start anywhere on a 16-byte boundary of a swizzled
+// buffer: 32 bytes further along K, or a whole number of 128-byte rows
+// further down (a tap's run inside a halo), with the plain descriptor and a
+// base offset of 0 (verified against the oracle).  Offsets are added to a
+// descriptor directly: its low 14 bits hold the address in 16-byte units.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t bytes) { return d + (bytes >> 4); }
 
 // Instruction descriptor for kind::tf32 / kind::f16: D fp32, K-major A and B.
 __host__ __device__ constexpr uint32_t idesc(int M, int N, uint32_t ab_fmt) {
@@ -258,8 +278,20 @@ __device__ __forceinline__ void store_operand1(void* ohi, float* olo, long long 
   }
 }
 
-// Rows m_base .. m_base+31 of the output matrix, of which the first nvalid exist.
-template <int ACT, int PREC>
+// Output row of virtual row v of a halo-staged convolution (pixels numbered
+// (img*Hp + oh)*Wp + ow in the padded row space), or -1 for a padding pixel.
+// (The host keeps N*Hp*Wp + 128 below 2^31, so 32-bit division suffices.)
+__device__ __forceinline__ long long halo_out_row(const GemmParams& p, long long v) {
+  const unsigned hw = (unsigned)(p.Hp * p.Wp), vv = (unsigned)v;
+  const unsigned img = vv / hw, rem = vv - img * hw;
+  const unsigned oh = rem / (unsigned)p.Wp, ow = rem - oh * (unsigned)p.Wp;
+  if (img >= (unsigned)p.nimg || oh >= (unsigned)p.OH || ow >= (unsigned)p.OW) return -1;
+  return ((long long)img * p.OH + oh) * p.OW + ow;
+}
+
+// Rows m_base .. m_base+31 of the output matrix, of which the first nvalid
+// exist; MAPPED: virtual rows m_base .. of a halo-staged convolution.
+template <int ACT, int PREC, bool MAPPED = false>
 __device__ __forceinline__ void store_block(const GemmParams& p, const float* ep, long long m_base, int nvalid, int n0,
                                             float* cbase, const float* rbase, void* ohi, float* olo, bool vec_c,
                                             bool vec_r, float alpha, float bsc, bool has_shift, int lane) {
@@ -280,7 +312,7 @@ __device__ __forceinline__ void store_block(const GemmParams& p, const float* ep
   float4 a[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) a[k] = *reinterpret_cast<const float4*>(ep + (8 * k + rsub) * 20 + c4);
-  if (full_n && vec_c && nvalid == 32 && !rbase) {
+  if (!MAPPED && full_n && vec_c && nvalid == 32 && !rbase) {
     // whole block inside the output, no residual: straight float4 stores
     const long long c0 = (m_base + rsub) * p.c_sm + n, cstep = 8 * p.c_sm;
     const long long o0 = (m_base + rsub) * p.o_sm + n, ostep = 8 * p.o_sm;
@@ -300,7 +332,8 @@ __device__ __forceinline__ void store_block(const GemmParams& p, const float* ep
   }
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const long long row = m_base + 8 * k + rsub;
+    long long row = m_base + 8 * k + rsub;
+    if constexpr (MAPPED) row = halo_out_row(p, row);
     float v[4] = {a[k].x, a[k].y, a[k].z, a[k].w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -308,7 +341,7 @@ __device__ __forceinline__ void store_block(const GemmParams& p, const float* ep
       if (has_shift) v[j] = v[j] + sh[j];
       v[j] = act_apply<ACT>(v[j]);
     }
-    if (8 * k + rsub >= nvalid) continue;
+    if (MAPPED ? row < 0 : 8 * k + rsub >= nvalid) continue;
     const long long co = row * p.c_sm + (long long)n * p.c_sn;
     const long long oo = row * p.o_sm + n;
     if (full_n && vec_c) {
@@ -407,6 +440,87 @@ __device__ __forceinline__ void conv_tile(const GemmParams& p, int tm, int& img,
   const int r = tm - img * per_img;
   oh0 = (r / p.tiles_w) * p.TH;
   ow0 = (r % p.tiles_w) * p.TW;
+}
+
+// Epilogue warp e (0..7) on TMEM lane quarter q: for every tile this CTA
+// owns, sum the chunk accumulators in registers (handing each accumulator
+// back to the MMA warp at once), then apply alpha/bias/folded-BN/activation/
+// residual and store 32 x 16 blocks through this warp's staging area ep.
+// rows(tm, m_base, nvalid) names the warp's 32 output rows.
+template <int PREC, int BN, bool MAPPED, class Rows>
+__device__ __forceinline__ void run_epilogue(const GemmParams& p, uint32_t tmem, uint64_t* acc_full,
+                                             uint64_t* acc_empty, float* ep, int e, int q, int lane, Rows rows) {
+  using C = Cfg<PREC, BN>;
+  constexpr int HALF = BN / 2;  // columns per epilogue warp
+  const int col0 = (e >> 2) * HALF;
+  const int nkb = p.nkb;
+  const int ntiles = p.num_m * p.num_n * p.batch;
+  const float alpha = p.alpha_ptr ? *p.alpha_ptr : p.alpha;
+  const float bsc = p.bias_scalar ? *p.bias_scalar : 0.f;
+  const bool has_shift = p.scale || p.bias || p.bias_scalar;
+  int u = 0;
+  bool ok = true;
+  for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+    // this thread's row of the tile, columns col0..col0+HALF: the sum of the chunk accumulators
+    float acc[HALF];
+#pragma unroll
+    for (int j = 0; j < HALF; ++j) acc[j] = 0.f;
+    for (int ch = 0; ch < p.nchunks; ++ch, ++u) {
+      const int b = u & 1;
+      const uint32_t use = (uint32_t)(u >> 1);
+      if (!mbar_wait(smem_u32(&acc_full[b]), use & 1u, p.err)) { ok = false; break; }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      if (nkb > 0) {
+#pragma unroll
+        for (int cc = 0; cc < HALF; cc += 32) {
+          uint32_t r[32];
+          const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + col0 + cc);
+          tmem_ld16_nowait(ta, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+          tmem_ld16_nowait(ta + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[cc + j] += __uint_as_float(r[j]);
+        }
+      }
+      // the chunk is in registers: hand the accumulator back to the MMA warp
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&acc_empty[b]));
+    }
+    if (!ok) break;
+    int bz, tm, tn;
+    tile_coords(p, t, bz, tm, tn);
+    const int n0 = tn * BN + col0;
+    // this warp's 32 rows: output matrix rows m_base.., the first nvalid of which exist
+    long long m_base;
+    int nvalid;
+    rows(tm, m_base, nvalid);
+    float* cbase = p.c ? p.c + (long long)bz * p.c_sb : nullptr;
+    const float* rbase = p.res ? p.res + (long long)bz * p.r_sb : nullptr;
+    const long long obatch = (long long)bz * p.M * p.o_sm;
+    void* ohi = p.o_hi ? (void*)((char*)p.o_hi + obatch * C::ESZ) : nullptr;
+    float* olo = p.o_lo ? p.o_lo + obatch : nullptr;
+    // float4 stores need contiguous, 16-byte aligned rows of the output (and residual)
+    const bool vec_c = !cbase || (p.c_sn == 1 && (p.c_sm & 3) == 0 && (((uintptr_t)cbase) & 15) == 0);
+    const bool vec_r = rbase && p.r_sn == 1 && (p.r_sm & 3) == 0 && (((uintptr_t)rbase) & 15) == 0;
+#pragma unroll
+    for (int cc = 0; cc < HALF; cc += 16) {
+      // transpose through shared memory: this lane's row in, 8 rows x 16 columns out per pass
+#pragma unroll
+      for (int j = 0; j < 16; j += 4)
+        *reinterpret_cast<float4*>(ep + lane * 20 + j) = make_float4(acc[cc + j], acc[cc + j + 1], acc[cc + j + 2], acc[cc + j + 3]);
+      __syncwarp();
+      switch (p.act) {
+        case 1: store_block<1, PREC, MAPPED>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+        case 2: store_block<2, PREC, MAPPED>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+        case 3: store_block<3, PREC, MAPPED>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+        case 4: store_block<4, PREC, MAPPED>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+        case 5: store_block<5, PREC, MAPPED>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+        default: store_block<0, PREC, MAPPED>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+      }
+      __syncwarp();
+    }
+  }
 }
 
 // Persistent kernel: each CTA walks tiles blockIdx.x, +gridDim.x, ...
@@ -601,19 +715,19 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
           if (!mbar_wait(smem_u32(&full[s]), ph, p.err)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const uint32_t st = smem_u32(smem + s * C::STAGE);
-          const uint32_t a_hi = st, b_hi = st + C::A_TILE;
-          const uint32_t a_lo = st + C::A_TILE + C::B_TILE, b_lo = st + 2 * C::A_TILE + C::B_TILE;
+          const uint64_t da_hi = sdesc(st), db_hi = sdesc(st + C::A_TILE);
+          const uint64_t da_lo = sdesc(st + C::A_TILE + C::B_TILE), db_lo = sdesc(st + 2 * C::A_TILE + C::B_TILE);
 #pragma unroll
           for (int ks = 0; ks < C::KSTEPS; ++ks) {
             const uint32_t koff = ks * 32;  // 32 bytes of K per instruction
             const uint32_t acc = (kb > kb0 || ks > 0) ? 1u : 0u;
             if constexpr (C::NOPS == 2) {
               // small products first, then the leading term
-              umma<PREC>(acc_t, sdesc(a_lo + koff), sdesc(b_hi + koff), C::IDESC, acc);
-              umma<PREC>(acc_t, sdesc(a_hi + koff), sdesc(b_lo + koff), C::IDESC, 1u);
-              umma<PREC>(acc_t, sdesc(a_hi + koff), sdesc(b_hi + koff), C::IDESC, 1u);
+              umma<PREC>(acc_t, desc_add(da_lo, koff), desc_add(db_hi, koff), C::IDESC, acc);
+              umma<PREC>(acc_t, desc_add(da_hi, koff), desc_add(db_lo, koff), C::IDESC, 1u);
+              umma<PREC>(acc_t, desc_add(da_hi, koff), desc_add(db_hi, koff), C::IDESC, 1u);
             } else {
-              umma<PREC>(acc_t, sdesc(a_hi + koff), sdesc(b_hi + koff), C::IDESC, acc);
+              umma<PREC>(acc_t, desc_add(da_hi, koff), desc_add(db_hi, koff), C::IDESC, acc);
             }
           }
           umma_commit(smem_u32(&empty[s]));
@@ -625,88 +739,235 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
     umma_commit(smem_u32(done));
   } else if (warp > PW) {
     // ---------------- epilogue ----------------
-    constexpr int HALF = BN / 2;  // columns per epilogue warp
     const int e = warp - PW - 1;  // 0..7
-    const int q = warp & 3;       // TMEM lane quarter this warp may access
-    const int col0 = (e >> 2) * HALF;
-    float* ep = epi + e * C::EPI_WARP_FLOATS;
-    const float alpha = p.alpha_ptr ? *p.alpha_ptr : p.alpha;
-    const float bsc = p.bias_scalar ? *p.bias_scalar : 0.f;
-    const bool has_shift = p.scale || p.bias || p.bias_scalar;
-    int u = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-      // this thread's row of the tile, columns col0..col0+HALF: the sum of the chunk accumulators
-      float acc[HALF];
-#pragma unroll
-      for (int j = 0; j < HALF; ++j) acc[j] = 0.f;
-      for (int ch = 0; ch < p.nchunks; ++ch, ++u) {
-        const int b = u & 1;
-        const uint32_t use = (uint32_t)(u >> 1);
-        if (!mbar_wait(smem_u32(&acc_full[b]), use & 1u, p.err)) { ok = false; break; }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        if (nkb > 0) {
-#pragma unroll
-          for (int cc = 0; cc < HALF; cc += 32) {
-            uint32_t r[32];
-            const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + col0 + cc);
-            tmem_ld16_nowait(ta, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
-            tmem_ld16_nowait(ta + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-            for (int j = 0; j < 32; ++j) acc[cc + j] += __uint_as_float(r[j]);
-          }
-        }
-        // the chunk is in registers: hand the accumulator back to the MMA warp
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&acc_empty[b]));
-      }
-      if (!ok) break;
-      int bz, tm, tn;
-      tile_coords(p, t, bz, tm, tn);
-      const int n0 = tn * BN + col0;
-      // this warp's 32 rows: output matrix rows m_base.., the first nvalid of which exist
-      long long m_base;
-      int nvalid;
-      if (p.conv_tma) {
-        int img, oh0, ow0;
-        conv_tile(p, tm, img, oh0, ow0);
-        const int oh = oh0 + (q * 32) / p.TW, ow = ow0 + (q * 32) % p.TW;  // TW >= 32: one output row
-        m_base = ((long long)img * p.OH + oh) * p.OW + ow;
-        nvalid = oh < p.OH ? max(0, min(32, p.OW - ow)) : 0;
-      } else {
-        m_base = (long long)tm * kBM + q * 32;
-        nvalid = max(0, min(32, p.M - (int)m_base));
-      }
-      float* cbase = p.c ? p.c + (long long)bz * p.c_sb : nullptr;
-      const float* rbase = p.res ? p.res + (long long)bz * p.r_sb : nullptr;
-      const long long obatch = (long long)bz * p.M * p.o_sm;
-      void* ohi = p.o_hi ? (void*)((char*)p.o_hi + obatch * C::ESZ) : nullptr;
-      float* olo = p.o_lo ? p.o_lo + obatch : nullptr;
-      // float4 stores need contiguous, 16-byte aligned rows of the output (and residual)
-      const bool vec_c = !cbase || (p.c_sn == 1 && (p.c_sm & 3) == 0 && (((uintptr_t)cbase) & 15) == 0);
-      const bool vec_r = rbase && p.r_sn == 1 && (p.r_sm & 3) == 0 && (((uintptr_t)rbase) & 15) == 0;
-#pragma unroll
-      for (int cc = 0; cc < HALF; cc += 16) {
-        // transpose through shared memory: this lane's row in, 8 rows x 16 columns out per pass
-#pragma unroll
-        for (int j = 0; j < 16; j += 4)
-          *reinterpret_cast<float4*>(ep + lane * 20 + j) = make_float4(acc[cc + j], acc[cc + j + 1], acc[cc + j + 2], acc[cc + j + 3]);
-        __syncwarp();
-        switch (p.act) {
-          case 1: store_block<1, PREC>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-          case 2: store_block<2, PREC>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-          case 3: store_block<3, PREC>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-          case 4: store_block<4, PREC>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-          case 5: store_block<5, PREC>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-          default: store_block<0, PREC>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-        }
-        __syncwarp();
-      }
-    }
+    run_epilogue<PREC, BN, false>(p, tmem, acc_full, acc_empty, epi + e * C::EPI_WARP_FLOATS, e, warp & 3, lane,
+                                  [&](int tm, long long& m_base, int& nvalid) {
+                                    const int q = warp & 3;
+                                    if (p.conv_tma) {
+                                      int img, oh0, ow0;
+                                      conv_tile(p, tm, img, oh0, ow0);
+                                      // TW >= 32: the warp's rows lie in one output row
+                                      const int oh = oh0 + (q * 32) / p.TW, ow = ow0 + (q * 32) % p.TW;
+                                      m_base = ((long long)img * p.OH + oh) * p.OW + ow;
+                                      nvalid = oh < p.OH ? max(0, min(32, p.OW - ow)) : 0;
+                                    } else {
+                                      m_base = (long long)tm * kBM + q * 32;
+                                      nvalid = max(0, min(32, p.M - (int)m_base));
+                                    }
+                                  });
   }
   // teardown: wait until every MMA of this CTA retired, then release TMEM
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == PW) {
+    if (lane == 0) mbar_wait_own(smem_u32(done), 0u, p.err);
+    __syncwarp();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)C::TMEM_COLS));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Halo-staged implicit-GEMM convolution (stride 1).
+//
+// The input is the zero-padded channels-last copy [N][Hp][Wp][Cp], seen as
+// N*Hp*Wp rows of Cp channels.  Output pixels are numbered in the same row
+// space, v = (img*Hp + oh)*Wp + ow; pixels with ow >= OW or oh >= OH are
+// computed and dropped.  At stride 1 tap (kh, kw) of pixel v reads input row
+// v + kh*dh*Wp + kw*dw, so the 128 pixels of a tile need one contiguous run of
+// 128 + (KH-1)*dh*Wp + (KW-1)*dw input rows: the halo.  One TMA copy brings
+// the halo of a 32-channel block into shared memory, and the A operand of
+// every tap is the same run entered kh*dh*Wp + kw*dw rows later, so the input
+// crosses L2 once per channel block instead of once per tap.
+// Warps: 0 streams B (one tap x channel block per stage), 1 allocates TMEM and
+// issues the MMAs, 2..9 run the epilogue, 10 loads halos into two buffers.
+template <int PREC, int BN>
+struct HaloCfg {
+  using G = Cfg<PREC, BN>;
+  static constexpr int HROWS = 256;  // halo rows per buffer (one TMA box)
+  static constexpr int H_OP = HROWS * 128;
+  static constexpr int H_BUF = G::NOPS * H_OP;
+  static constexpr int B_STAGE = G::NOPS * G::B_TILE;
+  static constexpr int B_FIT = (G::SMEM_LIMIT - G::EPI_BYTES - 2048 - 2 * H_BUF) / B_STAGE;
+  static constexpr int B_STAGES = B_FIT > 8 ? 8 : B_FIT;
+  static constexpr int SMEM = 2 * H_BUF + B_STAGES * B_STAGE + G::EPI_BYTES + 1024 /*barriers*/ + 1024 /*align*/;
+  static_assert(B_STAGES >= 2, "shared memory too small for the halo kernel");
+};
+constexpr int kHaloThreads = (1 + 1 + kEpiWarps + 1) * 32;
+
+template <int PREC, int BN>
+__global__ void __launch_bounds__(kHaloThreads, 1)
+    conv_halo_kernel(const __grid_constant__ CUtensorMap tx_hi, const __grid_constant__ CUtensorMap tx_lo,
+                     const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
+                     const GemmParams p) {
+  using C = Cfg<PREC, BN>;
+  using H = HaloCfg<PREC, BN>;
+  constexpr int S = H::B_STAGES;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* halo = smem;                    // [2][NOPS][HROWS x 128 B]
+  uint8_t* bst = smem + 2 * H::H_BUF;      // [S][NOPS][BN x 128 B]
+  float* epi = (float*)(bst + S * H::B_STAGE);
+  uint64_t* full = (uint64_t*)((uint8_t*)epi + C::EPI_BYTES);  // [S] B copy landed
+  uint64_t* empty = full + S;                                  // [S] B stage consumed
+  uint64_t* hfull = empty + S;                                 // [2] halo landed
+  uint64_t* hempty = hfull + 2;                                // [2] halo consumed
+  uint64_t* acc_full = hempty + 2;                             // [2] MMA -> epilogue
+  uint64_t* acc_empty = acc_full + 2;                          // [2] epilogue -> MMA
+  uint64_t* done = acc_empty + 2;                              // all MMAs retired
+  uint32_t* tmem_slot = (uint32_t*)(done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ int s_stop;
+  if (threadIdx.x == 0) s_stop = *(volatile int*)p.err;
+  __syncthreads();
+  if (s_stop != 0) return;
+
+  constexpr int PW = 1;  // MMA warp
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&hfull[b]), 1);
+      mbar_init(smem_u32(&hempty[b]), 1);
+      mbar_init(smem_u32(&acc_full[b]), 1);
+      mbar_init(smem_u32(&acc_empty[b]), kEpiWarps);
+    }
+    mbar_init(smem_u32(done), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == PW) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"((uint32_t)C::TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  const int ntiles = p.num_m * p.num_n;
+  const int ncb = p.Cp / C::BK, taps = p.KH * p.KW;
+  if (warp == 0 && lane == 0) {
+    // ---------------- B producer: weight columns (kh*KW + kw)*Cp + 32*cb ----------------
+    int g = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      int bz, tm, tn;
+      tile_coords(p, t, bz, tm, tn);
+      const int n0 = tn * BN;
+      for (int cb = 0; cb < ncb && ok; ++cb) {
+        for (int tap = 0; tap < taps; ++tap, ++g) {
+          const int s = g % S;
+          const uint32_t ph = (uint32_t)(g / S) & 1u;
+          if (g >= S && !mbar_wait(smem_u32(&empty[s]), ph ^ 1u, p.err)) { ok = false; break; }
+          uint8_t* st = bst + s * H::B_STAGE;
+          const uint32_t fb = smem_u32(&full[s]);
+          mbar_expect_tx(fb, H::B_STAGE);
+          const int kc = tap * p.Cp + cb * C::BK;
+          tma_load_3d(smem_u32(st), &tb_hi, fb, kc, n0, 0);
+          if constexpr (C::NOPS == 2) tma_load_3d(smem_u32(st + C::B_TILE), &tb_lo, fb, kc, n0, 0);
+        }
+      }
+    }
+    for (int k = g > S ? g - S : 0; k < g; ++k)
+      mbar_wait_own(smem_u32(&full[k % S]), (uint32_t)(k / S) & 1u, p.err);
+  } else if (warp == PW + 1 + kEpiWarps && lane == 0) {
+    // ---------------- halo producer ----------------
+    int h = 0;
+    bool ok = true;
+    const uint32_t bytes = (uint32_t)p.halo_rows * 128u * C::NOPS;
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      int bz, tm, tn;
+      tile_coords(p, t, bz, tm, tn);
+      for (int cb = 0; cb < ncb; ++cb, ++h) {
+        const int hb = h & 1;
+        const uint32_t ph = (uint32_t)(h >> 1) & 1u;
+        if (h >= 2 && !mbar_wait(smem_u32(&hempty[hb]), ph ^ 1u, p.err)) { ok = false; break; }
+        uint8_t* dst = halo + hb * H::H_BUF;
+        const uint32_t fb = smem_u32(&hfull[hb]);
+        mbar_expect_tx(fb, bytes);
+        tma_load_2d(smem_u32(dst), &tx_hi, fb, cb * C::BK, tm * kBM);
+        if constexpr (C::NOPS == 2) tma_load_2d(smem_u32(dst + H::H_OP), &tx_lo, fb, cb * C::BK, tm * kBM);
+      }
+    }
+    for (int k = h > 2 ? h - 2 : 0; k < h; ++k)
+      mbar_wait_own(smem_u32(&hfull[k & 1]), (uint32_t)(k >> 1) & 1u, p.err);
+  } else if (warp == PW && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    // k-blocks run channel block by channel block, tap by tap within one;
+    // every kchunk k-blocks of a tile go to a fresh accumulator.
+    // The issuing thread keeps its per-k-block work to counters and additions:
+    // any latency here stalls the tensor core.
+    int h = 0, u = 0, s = 0;
+    uint32_t sph = 0;  // phase parity of ring stage s
+    const uint32_t row_step = (uint32_t)(p.dh * p.Wp) * 128u, col_step = (uint32_t)p.dw * 128u;
+    const uint32_t b_base = smem_u32(bst);
+    bool ok = true;
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      int left = 0, j = 0, b = 0;  // k-blocks left in the current accumulation chunk
+      uint32_t acc_t = tmem;
+      for (int cb = 0; cb < ncb && ok; ++cb, ++h) {
+        const int hb = h & 1;
+        if (!mbar_wait(smem_u32(&hfull[hb]), (uint32_t)(h >> 1) & 1u, p.err)) { ok = false; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t x_hi = smem_u32(halo + hb * H::H_BUF);
+        uint32_t arow = 0;
+        for (int kh = 0; kh < p.KH && ok; ++kh, arow += row_step) {
+          uint32_t aoff = arow;
+          for (int kw = 0; kw < p.KW; ++kw, aoff += col_step) {
+            const bool first = left == 0;
+            if (first) {
+              b = u & 1;
+              if (u >= 2 && !mbar_wait(smem_u32(&acc_empty[b]), (uint32_t)((u >> 1) & 1) ^ 1u, p.err)) {
+                ok = false;
+                break;
+              }
+              asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+              acc_t = tmem + (uint32_t)(b * BN);
+              left = min(p.kchunk, p.nkb - j);
+            }
+            if (!mbar_wait(smem_u32(&full[s]), sph, p.err)) { ok = false; break; }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint64_t da_hi = sdesc(x_hi + aoff), da_lo = desc_add(da_hi, H::H_OP);
+            const uint64_t db_hi = sdesc(b_base + (uint32_t)s * H::B_STAGE), db_lo = desc_add(db_hi, C::B_TILE);
+#pragma unroll
+            for (int ks = 0; ks < C::KSTEPS; ++ks) {
+              const uint32_t koff = ks * 32;
+              const uint32_t acc = (!first || ks > 0) ? 1u : 0u;
+              if constexpr (C::NOPS == 2) {
+                umma<PREC>(acc_t, desc_add(da_lo, koff), desc_add(db_hi, koff), C::IDESC, acc);
+                umma<PREC>(acc_t, desc_add(da_hi, koff), desc_add(db_lo, koff), C::IDESC, 1u);
+                umma<PREC>(acc_t, desc_add(da_hi, koff), desc_add(db_hi, koff), C::IDESC, 1u);
+              } else {
+                umma<PREC>(acc_t, desc_add(da_hi, koff), desc_add(db_hi, koff), C::IDESC, acc);
+              }
+            }
+            umma_commit(smem_u32(&empty[s]));
+            if (++s == S) { s = 0; sph ^= 1u; }
+            ++j;
+            if (--left == 0) {
+              umma_commit(smem_u32(&acc_full[b]));
+              ++u;
+            }
+          }
+        }
+        if (!ok) break;
+        umma_commit(smem_u32(&hempty[hb]));
+      }
+    }
+    umma_commit(smem_u32(done));
+  } else if (warp > PW && warp <= PW + kEpiWarps) {
+    // ---------------- epilogue ----------------
+    const int e = warp - PW - 1;
+    run_epilogue<PREC, BN, true>(p, tmem, acc_full, acc_empty, epi + e * C::EPI_WARP_FLOATS, e, warp & 3, lane,
+                                 [&](int tm, long long& m_base, int& nvalid) {
+                                   m_base = (long long)tm * kBM + (warp & 3) * 32;  // virtual rows
+                                   nvalid = -1;
+                                 });
+  }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == PW) {
@@ -786,6 +1047,30 @@ bool make_conv_map(const GemmLaunch& L, int prec, int mode, int TW, int TH, cons
   return r == CUDA_SUCCESS;
 }
 
+// Input rows one halo-staged tile reads: 128 pixels plus the reach of the
+// filter in the padded row space, rounded up to whole 8-row swizzle groups.
+int64_t halo_rows(const GemmLaunch& L) {
+  const int64_t reach = (L.KH - 1) * L.dh * L.Wp + (L.KW - 1) * L.dw;
+  return (kBM + reach + 7) / 8 * 8;
+}
+
+// Mode 3: the padded input [N][Hp][Wp][Cp] as N*Hp*Wp rows, box (32
+// channels, halo rows).  Rows past the end read as zero.
+bool make_halo_map(const GemmLaunch& L, int prec, const void* base, CUtensorMap* m) {
+  std::memset(m, 0, sizeof *m);
+  const int esz = prec == PFC_PRECISION_BF16 ? 2 : 4;
+  const CUtensorMapDataType dt = prec == PFC_PRECISION_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  cuuint64_t dims[2] = {(cuuint64_t)L.Cp, (cuuint64_t)(L.batch_images * L.Hp * L.Wp)};
+  cuuint64_t strides[1] = {(cuuint64_t)(L.Cp * esz)};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / esz), (cuuint32_t)halo_rows(L)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = get_encode()(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 template <int PREC, int BN, bool CONV>
 void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const CUtensorMap* conv_maps = nullptr,
               int TW = 0) {
@@ -795,6 +1080,9 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const 
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
     PFB_CUDA(cudaFuncSetAttribute(gemm_kernel<PREC, BN, CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    if constexpr (!CONV)
+      PFB_CUDA(cudaFuncSetAttribute(conv_halo_kernel<PREC, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    HaloCfg<PREC, BN>::SMEM));
     attr_set[dev & 63] = true;
   }
   const int64_t a_rows = L.M, b_rows = L.N;
@@ -850,6 +1138,14 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const 
   p.tiles_w = conv_tma ? (int)ceil_div(L.OW, p.TW) : 1;
   p.tiles_h = conv_tma ? (int)ceil_div(L.OH, p.TH) : 1;
   if (conv_tma) p.num_m = (int)(L.batch_images * p.tiles_h * p.tiles_w);
+  p.nimg = (int)L.batch_images;
+  p.halo_rows = 0;
+  if (conv_tma == 3) {
+    // halo-staged: tiles of 128 pixels of the padded row space
+    p.num_m = (int)ceil_div(L.batch_images * L.Hp * L.Wp, kBM);
+    p.halo_rows = (int)halo_rows(L);
+    p.batch = 1;
+  }
   if (L.K == 0) p.nkb = 0;
   // accumulation chunks of 512 elements of K (16 tf32 / 8 bf16 k-blocks)
   p.kchunk = 512 / C::BK;
@@ -864,6 +1160,14 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const 
     sms[dev & 63] = v > 0 ? v : 148;
   }
   const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sms[dev & 63]);
+  if constexpr (!CONV) {
+    if (conv_tma == 3) {
+      conv_halo_kernel<PREC, BN><<<grid, kHaloThreads, HaloCfg<PREC, BN>::SMEM, stream>>>(ta_hi, ta_lo, tb_hi,
+                                                                                         tb_lo, p);
+      PFB_CUDA(cudaGetLastError());
+      return;
+    }
+  }
   gemm_kernel<PREC, BN, CONV><<<grid, kThreads<CONV>, C::SMEM, stream>>>(ta_hi, ta_lo, tb_hi, tb_lo, p);
   PFB_CUDA(cudaGetLastError());
 }
@@ -872,9 +1176,20 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const 
 
 // Which A feed a convolution can use: 1 or 2 (TMA, maps built) or 0 (gather).
 int conv_tma_mode(const GemmLaunch& L, int prec, CUtensorMap* maps, int* TW) {
-  if (!L.allow_tma_conv || L.OW < 32) return 0;
+  if (!L.allow_tma_conv) return 0;
   const int esz = prec == PFC_PRECISION_BF16 ? 2 : 4;
   const int64_t bk = 128 / esz, kwp = L.KWp > 0 ? L.KWp : L.KW;
+  // halo-staged: stride 1 over a padded input, whole 32-channel blocks, a
+  // halo that fits one TMA box
+  if (L.Hp > 0 && L.sh == 1 && L.sw == 1 && L.Cp % bk == 0 && kwp == L.KW &&
+      halo_rows(L) <= HaloCfg<PFC_PRECISION_TF32X3, 64>::HROWS &&
+      L.batch_images * L.Hp * L.Wp < (int64_t)INT32_MAX - 2 * kBM) {
+    if (make_halo_map(L, prec, L.x_hi, &maps[0])) {
+      if (prec == PFC_PRECISION_BF16) { maps[1] = maps[0]; return 3; }
+      if (make_halo_map(L, prec, L.x_lo, &maps[1])) return 3;
+    }
+  }
+  if (L.OW < 32) return 0;
   *TW = L.OW > 32 ? 64 : 32;
   int mode = 0;
   if (L.Hp == 0 && L.Cp % bk == 0 && L.sh == 1 && L.sw == 1 && kwp == L.KW) mode = 1;

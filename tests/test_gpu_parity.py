@@ -255,6 +255,24 @@ def test_gemm_bf16_mode(oracle_mod, rng, native):
     ex.close()
 
 
+def test_conv2d_bf16_mode(oracle_mod, rng, native):
+    """bf16 operands through the halo-staged 3x3 (64-channel blocks) and the
+    TMA-window 7x7 / 2 (few channels)."""
+    ex = pf.CudaExecutor(pf.CudaExecutor.Config(precision="bf16"))
+    outs = []
+    for c, o, k, s, p, hw in [(64, 64, 3, 1, 1, (14, 18)), (3, 16, 7, 2, 3, (40, 40))]:
+        x = rng.random((2, c) + hw).astype(np.float32)
+        conv = nn.Conv2d(c, o, k, s, p)
+        conv.set_parameter("weight", (rng.standard_normal((o, c, k, k)) / np.sqrt(c * k * k)).astype(np.float32))
+        conv.set_parameter("bias", np.zeros(o, np.float32))
+        outs.append(conv(pf.tensor(x)))
+    gpu, ref = run(ex, outs, oracle_mod)
+    for g, r in zip(gpu, ref):
+        close_rows(g.reshape(g.shape[0] * g.shape[1], -1), r.reshape(r.shape[0] * r.shape[1], -1), RTOL_GEMM_BF16,
+                   what="bf16 conv")
+    ex.close()
+
+
 # ---- convolution and pooling ---------------------------------------------------------------
 
 @pytest.mark.parametrize("cfg", [dict(n=2, c=3, h=17, w=15, o=8, k=3, s=1, p=1),
@@ -265,7 +283,14 @@ def test_gemm_bf16_mode(oracle_mod, rng, native):
                                  dict(n=1, c=64, h=33, w=70, o=96, k=3, s=1, p=1),
                                  # TMA-fed windows of a padded input: few channels, stride 2, row dilation
                                  dict(n=2, c=3, h=70, w=83, o=16, k=5, s=2, p=2),
-                                 dict(n=2, c=4, h=40, w=36, o=8, k=3, s=1, p=1, d=(2, 1))])
+                                 dict(n=2, c=4, h=40, w=36, o=8, k=3, s=1, p=1, d=(2, 1)),
+                                 # halo-staged (stride 1, whole 32-channel blocks, halo <= 256 rows):
+                                 # 3x3; dilation with a partial column tile; 1x1 over three channel
+                                 # blocks and two column tiles; 5x5
+                                 dict(n=3, c=64, h=20, w=30, o=64, k=3, s=1, p=1),
+                                 dict(n=2, c=32, h=25, w=21, o=48, k=3, s=1, p=2, d=2),
+                                 dict(n=2, c=96, h=9, w=13, o=80, k=1, s=1, p=0),
+                                 dict(n=2, c=32, h=12, w=14, o=64, k=5, s=1, p=2)])
 def test_conv2d(cuda_executor, oracle_mod, rng, cfg):
     x = rng.random((cfg["n"], cfg["c"], cfg["h"], cfg["w"])).astype(np.float32)
     conv = nn.Conv2d(cfg["c"], cfg["o"], cfg["k"], cfg["s"], cfg["p"], cfg.get("d", 1))
@@ -280,17 +305,28 @@ def test_conv_bn_relu_pool_stack(cuda_executor, oracle_mod, rng):
     conv = nn.Conv2d(3, 16, 7, 2, 3)
     bn = nn.BatchNorm2d(16)
     bn.eval()
+    params = {}
     for name, lo, hi in [("weight", 0.5, 1.5), ("bias", -0.5, 0.5), ("running_mean", -0.5, 0.5),
                          ("running_var", 0.5, 2.0)]:
-        bn.set_parameter(name, rng.uniform(lo, hi, 16).astype(np.float32))
+        params[name] = rng.uniform(lo, hi, 16).astype(np.float32)
+        bn.set_parameter(name, params[name])
     pool = nn.MaxPool2d(3, 2)
-    out = pool(pf.relu(bn(conv(x))))
+    c = conv(x)
+    out = pool(pf.relu(bn(c)))
     gap = nn.AdaptiveAvgPool2d(1)(out)
     avg = nn.AvgPool2d(2)(out)
-    gpu, ref = run(cuda_executor, [out, gap, avg], oracle_mod)
-    for g, r in zip(gpu, ref):
-        close_rows(g.reshape(-1, g.shape[-1] * g.shape[-2]), r.reshape(-1, r.shape[-1] * r.shape[-2]),
-                   RTOL_GEMM_TF32X3)
+    gpu, ref = run(cuda_executor, [out, gap, avg, c], oracle_mod)
+    # The folded BatchNorm can cancel most of a channel's conv value, so the
+    # error bound follows the conv output's scale times the channel's BN scale
+    # (the size of the terms accumulated), not the small value left after it.
+    bn_scale = np.abs(params["weight"] / np.sqrt(params["running_var"].astype(np.float64) + 1e-5))
+    conv_rms = np.sqrt(np.mean(ref[3].astype(np.float64) ** 2, axis=(2, 3)))  # [N, C]
+    term_scale = (conv_rms * bn_scale[None, :]).reshape(-1, 1)
+    for g, r in zip(gpu[:3], ref[:3]):
+        g2, r2 = g.reshape(-1, g.shape[-1] * g.shape[-2]), r.reshape(-1, r.shape[-1] * r.shape[-2])
+        close(g2, r2, rtol=RTOL_GEMM_TF32X3, atol=RTOL_GEMM_TF32X3 * term_scale)
+    close_rows(gpu[3].reshape(-1, gpu[3].shape[-1] * gpu[3].shape[-2]),
+               ref[3].reshape(-1, ref[3].shape[-1] * ref[3].shape[-2]), RTOL_GEMM_TF32X3)
 
 
 def test_batchnorm_alone_and_pools(cuda_executor, oracle_mod, rng):
