@@ -10,7 +10,8 @@ is the same metric through the public host-buffer call with inputs copied
 from pinned host memory and all outputs read back every step:
 CudaExecutor.execute_streamed (the batch as micro-batches whose copies
 overlap compute), and under `e2e.serial` CudaExecutor.execute (one upload,
-compute, download in sequence).  Multi-GPU runs (torchrun, one process per
+compute, download in sequence); a batch too small to split (the MLP's 64
+samples) takes execute alone.  Multi-GPU runs (torchrun, one process per
 GPU) give every rank its own full batch (weak scaling): weights are broadcast
 once from rank 0 over NCCL and registered as each rank's resident constants
 (CudaExecutor.set_resident); no collective runs inside the timed region.
@@ -279,24 +280,31 @@ def run_ours(args):
         # (b) execute_streamed: the same batch as micro-batches of one chunk
         # graph, each chunk's compute overlapping the next upload and the
         # previous download
+        serial = {"value": w.samples * n_e2e / dt_serial, "ms_per_step": dt_serial / n_e2e * 1e3,
+                  "api": "CudaExecutor.execute (pfc_executor_execute)"}
         chunks = E2E_CHUNKS[args.workload]
-        key = next(iter(FULL[args.workload]))  # the batch-size key (rows / batch)
-        cw = build_workload(args.workload, **{**FULL[args.workload], key: FULL[args.workload][key] // chunks})
-        cg = cw.outputs[0].graph()
-        c_in = {cw.inputs[name].node().id(): pinned_in[name].numpy() for name in cw.inputs}
-        c_out = [t.node().id() for t in cw.outputs]
-        for _ in range(2):
-            ex.execute_streamed(cg, c_in, c_out, out_np)
-        t0 = time.perf_counter()
-        for _ in range(n_e2e):
-            ex.execute_streamed(cg, c_in, c_out, out_np)
-        dt = time.perf_counter() - t0
-        e2e = {"value": w.samples * n_e2e / dt, "unit": "samples/s", "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": d2h, "ms_per_step": dt / n_e2e * 1e3, "steps": n_e2e,
-               "api": f"CudaExecutor.execute_streamed (pfc_executor_execute_streamed), {chunks} chunks, "
-                      "pinned host buffers",
-               "serial": {"value": w.samples * n_e2e / dt_serial, "ms_per_step": dt_serial / n_e2e * 1e3,
-                          "api": "CudaExecutor.execute (pfc_executor_execute)"}}
+        if chunks > 1:
+            key = next(iter(FULL[args.workload]))  # the batch-size key (rows / batch)
+            cw = build_workload(args.workload, **{**FULL[args.workload], key: FULL[args.workload][key] // chunks})
+            cg = cw.outputs[0].graph()
+            c_in = {cw.inputs[name].node().id(): pinned_in[name].numpy() for name in cw.inputs}
+            c_out = [t.node().id() for t in cw.outputs]
+            for _ in range(2):
+                ex.execute_streamed(cg, c_in, c_out, out_np)
+            t0 = time.perf_counter()
+            for _ in range(n_e2e):
+                ex.execute_streamed(cg, c_in, c_out, out_np)
+            dt = time.perf_counter() - t0
+            e2e = {"value": w.samples * n_e2e / dt, "unit": "samples/s", "h2d_bytes_per_step": h2d,
+                   "d2h_bytes_per_step": d2h, "ms_per_step": dt / n_e2e * 1e3, "steps": n_e2e,
+                   "api": f"CudaExecutor.execute_streamed (pfc_executor_execute_streamed), {chunks} chunks, "
+                          "pinned host buffers",
+                   "serial": serial}
+        else:
+            # a batch too small to split: one execute call per step
+            e2e = {"value": serial["value"], "unit": "samples/s", "h2d_bytes_per_step": h2d,
+                   "d2h_bytes_per_step": d2h, "ms_per_step": serial["ms_per_step"], "steps": n_e2e,
+                   "api": serial["api"] + ", pinned host buffers"}
 
     if rank == 0:
         pk, pk_kind = peaks()
