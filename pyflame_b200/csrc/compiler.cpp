@@ -198,11 +198,15 @@ __device__ __forceinline__ float pf_div(float a, float b) {
   return a / b;
 }
 __device__ __forceinline__ float pf_relu(float x) { return (0.f < x) ? x : 0.f; }
-__device__ __forceinline__ float pf_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+// Sigmoid and SiLU use the hardware exp2 and reciprocal approximations
+// (__expf, __fdividef): within about 1e-6 relative of 1/(1+exp(-x)) for
+// |x| <= 20 and exact at the limits (0, 1, NaN); the chain is a third of the
+// correctly rounded expf and division, which row kernels are bound by.
+__device__ __forceinline__ float pf_sigmoid(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float pf_gelu(float x) {
   return 0.5f * x * (1.0f + tanhf(0.7978845608f * (x + 0.044715f * x * x * x)));
 }
-__device__ __forceinline__ float pf_silu(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ float pf_silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float pf_max(float a, float b) { return fmaxf(a, b); }
 __device__ __forceinline__ float pf_min(float a, float b) { return fminf(a, b); }
 // The 3xTF32 operand split (identical to the precompiled kernels'): hi keeps
