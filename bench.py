@@ -316,7 +316,7 @@ def run_ours(args):
         # share of device time in a profiled step of the same plan.
         if w.flops:
             bound, unit = "tensor", "TFLOP/s"
-            gemm_ms = sum(ms for name, ms in kernels if name.startswith("gemm") or name.startswith("conv gemm"))
+            gemm_ms = sum(ms for name, ms in kernels if name.startswith(("gemm", "conv gemm", "attention")))
             dom_ms = ms_per_step * gemm_ms / total_kernel_ms
             achieved = w.flops / (dom_ms / 1e3) / 1e12 if gemm_ms else 0.0
             # kernels run inside a long loop: the sustained GEMM figure

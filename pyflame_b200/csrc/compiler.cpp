@@ -1297,6 +1297,8 @@ class Compiler {
   std::vector<Region> regions_;
   std::unordered_map<uint64_t, int> chain_of_;       // node -> chain index (mm and absorbed)
   std::vector<GemmChain> chains_;
+  // attention: chain of the PV matmul -> (chain of the QK^T matmul, softmax node)
+  std::unordered_map<int, std::pair<int, uint64_t>> attn_;
   std::unordered_map<uint64_t, int> row_region_;     // row op -> region
   std::vector<std::pair<int, Step>> steps_;
   std::unordered_map<uint64_t, int> splat_slot_;
@@ -1466,6 +1468,7 @@ class Compiler {
 
   void classify();
   void absorb_epilogues();
+  void detect_attention();
   void build_regions();
   void attach_row_ops();
   void lower();
@@ -1474,6 +1477,7 @@ class Compiler {
   void lower_region(int r);
   void lower_row_alone(uint64_t id);
   void lower_chain(int c);
+  void lower_attention(int c);
   void lower_matmul(const GemmChain& ch, int at);
   void lower_conv(const GemmChain& ch, int at);
   void lower_pool(uint64_t id);
@@ -1631,6 +1635,97 @@ void Compiler::absorb_epilogues() {
       cls_[a] = cls_[id];  // absorbed nodes no longer form elementwise regions
     }
   }
+}
+
+// Attention: MATMUL(Q, K^T) (only a scale absorbed) feeding nothing but a
+// softmax over its last dim, which feeds nothing but the A operand of
+// MATMUL(P, V) (nothing absorbed), all batched over the same leading dims,
+// with head dims <= 64, becomes one unit lowered as the fused attention
+// kernel: the scores and probabilities never reach HBM.  This is the core of
+// PyFlame's MultiheadAttention::forward (attention.cpp).
+void Compiler::detect_attention() {
+  if (in_.precision != PFC_PRECISION_TF32X3) return;
+  for (int c2 = 0; c2 < (int)chains_.size(); ++c2) {
+    const GemmChain& ch2 = chains_[c2];
+    if (cls_[ch2.mm] != Cls::GEMM || !ch2.absorbed.empty() || chain_of_.at(ch2.mm) != c2) continue;
+    const Node& mm2 = N(ch2.mm);
+    if (mm2.op != Op::MATMUL || mm2.inputs.size() != 2 || mm2.inputs[0] == mm2.inputs[1]) continue;
+    const uint64_t sm = mm2.inputs[0];
+    const Node& smn = N(sm);
+    if (smn.op != Op::SOFTMAX || cls_[sm] != Cls::ROW || is_out_.count(sm) || users_[sm].size() != 1) continue;
+    const int rank = (int)smn.shape.size();
+    if (rank < 3) continue;
+    int dim = (int)smn.attr_int("dim", -1);
+    if (dim < 0) dim += rank;
+    if (dim != rank - 1) continue;
+    const uint64_t r1 = smn.inputs.at(0);
+    auto it = chain_of_.find(r1);
+    if (it == chain_of_.end()) continue;
+    const int c1 = it->second;
+    const GemmChain& ch1 = chains_[c1];
+    if (ch1.result != r1 || is_out_.count(r1) || users_[r1].size() != 1 || cls_[ch1.mm] != Cls::GEMM) continue;
+    if (ch1.has_bias || ch1.has_bn || ch1.act || ch1.has_residual || attn_.count(c1)) continue;
+    const Node& mm1 = N(ch1.mm);
+    if (mm1.op != Op::MATMUL || mm1.inputs.size() != 2) continue;
+    bool ok = true;
+    for (const Node* x : {&mm1, &mm2})
+      for (uint64_t in : x->inputs) {
+        const Node& o = N(in);
+        ok = ok && o.shape.size() == (size_t)rank && !in_.splats.count(in) && o.dtype == DType::F32;
+        for (int k = 0; ok && k < rank - 2; ++k) ok = o.shape[k] == smn.shape[k];
+      }
+    if (!ok) continue;
+    const int64_t d1 = N(mm1.inputs[0]).shape[rank - 1], d2 = N(mm2.inputs[1]).shape[rank - 1];
+    if (d1 > 64 || d2 > 64 || mm2.shape[rank - 2] != smn.shape[rank - 2]) continue;
+    // every node of the QK^T chain and the softmax join the PV chain's unit
+    std::vector<uint64_t> nodes{ch1.mm, sm};
+    nodes.insert(nodes.end(), ch1.absorbed.begin(), ch1.absorbed.end());
+    for (uint64_t x : nodes) {
+      chain_of_[x] = c2;
+      cls_[x] = Cls::GEMM;
+    }
+    attn_.emplace(c2, std::make_pair(c1, sm));
+  }
+}
+
+void Compiler::lower_attention(int c2) {
+  const GemmChain& ch2 = chains_[c2];
+  const GemmChain& ch1 = chains_[attn_.at(c2).first];
+  const int at = pos_[ch2.result];
+  const Node& mm1 = N(ch1.mm);
+  const Node& mm2 = N(ch2.mm);
+  View q = value(mm1.inputs[0]);   // [batch..., M, d]
+  View kt = value(mm1.inputs[1]);  // [batch..., d, L]
+  View v = value(mm2.inputs[1]);   // [batch..., L, dv]
+  const size_t r = q.shape.size();
+  std::vector<int64_t> batch(q.shape.begin(), q.shape.end() - 2);
+  const int64_t nbatch = prod(batch);
+  const int64_t M = q.shape[r - 2], d = q.shape[r - 1], L = kt.shape[r - 1], dv = v.shape[r - 1];
+  if (kt.shape[r - 2] != d || v.shape[r - 2] != L) fail(PFC_ERR_GRAPH, "matmul: inner dimensions don't match");
+  const int prec = in_.precision;
+  const int64_t kq = round_up(d, 32), kv = round_up(L, 32);
+  // K as [batch..., L, d] and V^T as [batch..., dv, L]: swap the last two dims
+  View k = kt, vt = v;
+  std::swap(k.shape[r - 2], k.shape[r - 1]);
+  std::swap(k.strides[r - 2], k.strides[r - 1]);
+  std::swap(vt.shape[r - 2], vt.shape[r - 1]);
+  std::swap(vt.strides[r - 2], vt.strides[r - 1]);
+  const Operand oq = prepare_operand(q, nbatch * M, d, kq, prec, "prepare Q " + shape_str(q.shape), at);
+  const Operand ok = prepare_operand(k, nbatch * L, d, kq, prec, "prepare K " + shape_str(k.shape), at);
+  const Operand ov = prepare_operand(vt, nbatch * dv, L, kv, prec, "prepare V^T " + shape_str(vt.shape), at);
+  View c = dense(mm2.shape, DType::F32);
+  Step st;
+  st.kind = StepKind::ATTENTION;
+  st.label = "attention " + std::to_string(nbatch) + "x[" + std::to_string(M) + "x" + std::to_string(L) + "x" +
+             std::to_string(dv) + "]";
+  AttnArgs& A = st.attn;
+  A.q_hi = oq.hi; A.q_lo = oq.lo; A.k_hi = ok.hi; A.k_lo = ok.lo; A.vt_hi = ov.hi; A.vt_lo = ov.lo;
+  A.batch = nbatch; A.M = M; A.L = L; A.d = dv; A.kq = kq; A.kv = kv;
+  A.alpha = ch1.alpha;
+  A.alpha_slot = ch1.alpha_slot;
+  A.c = c;
+  add_step(at, std::move(st));
+  val_[ch2.result] = c;
 }
 
 // A set of nodes is convex when no path leaves it and re-enters it; only
@@ -2461,6 +2556,10 @@ void Compiler::lower_conv(const GemmChain& ch, int at) {
 }
 
 void Compiler::lower_chain(int ci) {
+  if (attn_.count(ci)) {
+    lower_attention(ci);
+    return;
+  }
   const GemmChain& ch = chains_[ci];
   int at = pos_[ch.result];
   if (cls_[ch.mm] == Cls::CONV) lower_conv(ch, at);
@@ -2656,6 +2755,12 @@ void Compiler::emit_operands_at_producers() {
         break;
       }
       case StepKind::MEMSET: add(st.memset_buf, i); break;
+      case StepKind::ATTENTION: {
+        const AttnArgs& A = st.attn;
+        add(A.q_hi, i); add(A.q_lo, i); add(A.k_hi, i); add(A.k_lo, i); add(A.vt_hi, i); add(A.vt_lo, i);
+        add(A.c.buf, i);
+        break;
+      }
     }
   }
   std::unordered_set<int> out_bufs;
@@ -2793,6 +2898,12 @@ void Compiler::finish() {
         break;
       }
       case StepKind::MEMSET: use(s.memset_buf, i); break;
+      case StepKind::ATTENTION: {
+        const AttnArgs& A = s.attn;
+        use(A.q_hi, i); use(A.q_lo, i); use(A.k_hi, i); use(A.k_lo, i); use(A.vt_hi, i); use(A.vt_lo, i);
+        use(A.c.buf, i);
+        break;
+      }
     }
   }
   int nsteps = (int)P_->steps.size();
@@ -2854,6 +2965,7 @@ std::unique_ptr<Plan> Compiler::run() {
   P_->scalar_buf = new_buffer(4 * 64);
   classify();
   absorb_epilogues();
+  detect_attention();
   build_regions();
   attach_row_ops();
   lower();

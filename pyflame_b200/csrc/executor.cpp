@@ -404,6 +404,24 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
       launch_im2col(L, s);
       break;
     }
+    case StepKind::ATTENTION: {
+      const AttnArgs& a = st.attn;
+      AttnLaunch L;
+      L.batch = a.batch; L.M = a.M; L.L = a.L; L.d = a.d; L.kq = a.kq; L.kv = a.kv;
+      L.q_hi = bufp(a.q_hi, 0);
+      L.q_lo = (const float*)bufp(a.q_lo, 0);
+      L.k_hi = bufp(a.k_hi, 0);
+      L.k_lo = (const float*)bufp(a.k_lo, 0);
+      L.vt_hi = bufp(a.vt_hi, 0);
+      L.vt_lo = (const float*)bufp(a.vt_lo, 0);
+      L.alpha = a.alpha;
+      L.alpha_ptr = a.alpha_slot >= 0 ? (const float*)bufp(P.scalar_buf, (int64_t)a.alpha_slot * 4) : nullptr;
+      L.c = (float*)viewp(a.c);
+      L.c_sb = a.M * a.d; L.c_sm = a.d; L.c_sn = 1;
+      L.err = err_dev_;
+      launch_attention(L, s);
+      break;
+    }
     case StepKind::GEMM: {
       const GemmArgs& a = st.gemm;
       GemmLaunch L;

@@ -1,0 +1,422 @@
+// Fused attention for sm_100a: O = softmax(alpha * Q K^T) V over batch x head
+// slices, with split-fp32 (3xTF32) operands.
+//
+// Replaces the three passes PyFlame's MultiheadAttention graph costs behind
+// the ROCm executor (rocm_executor.cpp:278-335: a batched GEMM for the
+// scores, the softmax kernel of rocm_kernels.hip, a batched GEMM for the
+// weighted values), in which the [slices, M, L] scores and probabilities make
+// two round trips through HBM.  Here they live in tensor memory only.
+//
+// One persistent CTA per SM walks tiles of (slice, 128 query rows):
+//   warp 0     TMA: Q of the tile once, then key blocks of 64 (K, and in the
+//              second pass V^T) through two-stage rings.
+//   warp 1     TMEM (512 columns) and the MMAs.  S = Q K_j^T goes into one of
+//              two 64-column TMEM buffers (kind::tf32 x3 from shared memory);
+//              O += P_j V_j takes P from TMEM as the A operand.
+//   warps 2-5  one query row per thread (TMEM lane): pass 1 reads each S block
+//              and keeps the row's running max and sum of exp; pass 2 reads S
+//              again, writes P = exp(alpha*s - max) / sum as hi/lo tf32 into
+//              one of two TMEM P buffers, and at the end reads O and stores it.
+// Computing S twice keeps P exactly normalised before it meets V, so the O
+// accumulator is never rescaled.  Keys past L are masked; query rows past M
+// and head columns past d are dropped.  Every wait is bounded by the global
+// timer and reports PFC_ERR_TIMEOUT through *err.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+
+#include "../common.hpp"
+#include "kernels.hpp"
+#include "split.cuh"
+#include "tcgen05.cuh"
+
+namespace pfb {
+
+CUtensorMap make_operand_map(const void* base, int prec, int64_t kpad, int64_t rows, int64_t batch, int box_rows);
+
+namespace {
+
+constexpr int kAQ = 128;          // query rows per tile (one per TMEM lane)
+constexpr int kAK = 64;           // keys per block
+constexpr int kAD = 64;           // head-dim columns of O and rows of V^T
+constexpr int kAThreads = 6 * 32;
+
+constexpr int kQChunk = kAQ * 128;  // 128 rows x 32 tf32
+constexpr int kKChunk = kAK * 128;  // 64 keys x 32 tf32
+constexpr int kVChunk = kAD * 128;  // 64 head-dim rows x 32 keys
+constexpr int kQBytes = 2 * 2 * kQChunk;    // [hi/lo][k-chunk]
+constexpr int kKStage = 2 * 2 * kKChunk;    // [hi/lo][k-chunk]
+constexpr int kVStage = 2 * 2 * kVChunk;    // [hi/lo][key chunk]
+constexpr int kStages = 2;
+constexpr int kASmem = kQBytes + kStages * (kKStage + kVStage) + 1024 /*barriers*/ + 1024 /*align*/;
+// TMEM columns: S buffers at 0 and 64; P buffers (hi 64 | lo 64) at 128 and
+// 256; O at 384.
+constexpr uint32_t kTS = 0, kTP = 128, kTO = 384, kATmemCols = 512;
+constexpr uint32_t kIdesc = idesc(kAQ, 64, 2u);  // M 128, N 64, tf32
+
+struct AttnParams {
+  int batch, M, L, d, nkc, nblk, ntq;
+  float alpha;
+  const float* alpha_ptr;
+  float* c;
+  long long c_sb, c_sm, c_sn;
+  int* err;
+};
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// D (TMEM) += A (TMEM, K-major: lane = row, column = k) x B (shared memory)
+__device__ __forceinline__ void umma_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t db, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(db), "r"(kIdesc), "r"(acc));
+}
+
+// 64 fp32 columns of this warp's TMEM lanes
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+  uint32_t r[64];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) tmem_ld16_nowait(taddr + 16 * i, *reinterpret_cast<uint32_t(*)[16]>(&r[16 * i]));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__global__ void __launch_bounds__(kAThreads, 1)
+    attn_kernel(const __grid_constant__ CUtensorMap tq_hi, const __grid_constant__ CUtensorMap tq_lo,
+                const __grid_constant__ CUtensorMap tk_hi, const __grid_constant__ CUtensorMap tk_lo,
+                const __grid_constant__ CUtensorMap tv_hi, const __grid_constant__ CUtensorMap tv_lo,
+                const AttnParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sq = smem;
+  uint8_t* sk = sq + kQBytes;
+  uint8_t* sv = sk + kStages * kKStage;
+  uint64_t* bars = (uint64_t*)(sv + kStages * kVStage);
+  uint64_t* q_full = bars + 0;
+  uint64_t* q_free = bars + 1;
+  uint64_t* k_full = bars + 2;   // [2]
+  uint64_t* k_free = bars + 4;   // [2]
+  uint64_t* v_full = bars + 6;   // [2]
+  uint64_t* v_free = bars + 8;   // [2]
+  uint64_t* s_full = bars + 10;  // [2] S block in TMEM
+  uint64_t* s_free = bars + 12;  // [2] S block read by the softmax warps
+  uint64_t* p_full = bars + 14;  // [2] P block written
+  uint64_t* p_free = bars + 16;  // [2] P block consumed by its MMAs
+  uint64_t* o_full = bars + 18;
+  uint64_t* o_free = bars + 19;
+  uint64_t* done = bars + 20;
+  uint32_t* tmem_slot = (uint32_t*)(bars + 21);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ int s_stop;
+  if (threadIdx.x == 0) s_stop = *(volatile int*)p.err;
+  __syncthreads();
+  if (s_stop != 0) return;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(q_full), 1);
+    mbar_init(smem_u32(q_free), 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&k_full[i]), 1);
+      mbar_init(smem_u32(&k_free[i]), 1);
+      mbar_init(smem_u32(&v_full[i]), 1);
+      mbar_init(smem_u32(&v_free[i]), 1);
+      mbar_init(smem_u32(&s_full[i]), 1);
+      mbar_init(smem_u32(&s_free[i]), 4);
+      mbar_init(smem_u32(&p_full[i]), 4);
+      mbar_init(smem_u32(&p_free[i]), 1);
+    }
+    mbar_init(smem_u32(o_full), 1);
+    mbar_init(smem_u32(o_free), 4);
+    mbar_init(smem_u32(done), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kATmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  const int ntiles = p.batch * p.ntq;
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    int gk = 0, gv = 0, tc = 0;
+    bool ok = true;
+    const uint32_t kbytes = (uint32_t)(2 * p.nkc * kKChunk);
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
+      const int b = t / p.ntq, q0 = (t - b * p.ntq) * kAQ;
+      if (tc > 0 && !mbar_wait(smem_u32(q_free), (uint32_t)(tc - 1) & 1u, p.err)) { ok = false; break; }
+      mbar_expect_tx(smem_u32(q_full), (uint32_t)(2 * p.nkc * kQChunk));
+      for (int c = 0; c < p.nkc; ++c) {
+        tma_load_3d(smem_u32(sq + c * kQChunk), &tq_hi, smem_u32(q_full), c * 32, q0, b);
+        tma_load_3d(smem_u32(sq + (2 + c) * kQChunk), &tq_lo, smem_u32(q_full), c * 32, q0, b);
+      }
+      for (int pass = 0; pass < 2 && ok; ++pass) {
+        for (int j = 0; j < p.nblk; ++j) {
+          const int s = gk & 1;
+          if (gk >= 2 && !mbar_wait(smem_u32(&k_free[s]), (uint32_t)((gk >> 1) - 1) & 1u, p.err)) { ok = false; break; }
+          uint8_t* kst = sk + s * kKStage;
+          mbar_expect_tx(smem_u32(&k_full[s]), kbytes);
+          for (int c = 0; c < p.nkc; ++c) {
+            tma_load_3d(smem_u32(kst + c * kKChunk), &tk_hi, smem_u32(&k_full[s]), c * 32, j * kAK, b);
+            tma_load_3d(smem_u32(kst + (2 + c) * kKChunk), &tk_lo, smem_u32(&k_full[s]), c * 32, j * kAK, b);
+          }
+          ++gk;
+          if (pass == 1) {
+            const int v = gv & 1;
+            if (gv >= 2 && !mbar_wait(smem_u32(&v_free[v]), (uint32_t)((gv >> 1) - 1) & 1u, p.err)) { ok = false; break; }
+            uint8_t* vst = sv + v * kVStage;
+            mbar_expect_tx(smem_u32(&v_full[v]), (uint32_t)kVStage);
+            for (int c = 0; c < 2; ++c) {
+              tma_load_3d(smem_u32(vst + c * kVChunk), &tv_hi, smem_u32(&v_full[v]), j * kAK + c * 32, 0, b);
+              tma_load_3d(smem_u32(vst + (2 + c) * kVChunk), &tv_lo, smem_u32(&v_full[v]), j * kAK + c * 32, 0, b);
+            }
+            ++gv;
+          }
+        }
+      }
+    }
+    // drain: every copy issued must land before the CTA exits
+    if (tc > 0) mbar_wait_own(smem_u32(q_full), (uint32_t)(tc - 1) & 1u, p.err);
+    for (int k = gk > 2 ? gk - 2 : 0; k < gk; ++k) mbar_wait_own(smem_u32(&k_full[k & 1]), (uint32_t)(k >> 1) & 1u, p.err);
+    for (int k = gv > 2 ? gv - 2 : 0; k < gv; ++k) mbar_wait_own(smem_u32(&v_full[k & 1]), (uint32_t)(k >> 1) & 1u, p.err);
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    int gk = 0, gv = 0, gs = 0, gp = 0, tc = 0;
+    bool ok = true;
+    const uint32_t q_base = smem_u32(sq);
+    // S[gs & 1] = Q K^T of the next K block
+    auto issue_s = [&]() -> bool {
+      const int sb = gs & 1, ks = gk & 1;
+      if (gs >= 2 && !mbar_wait(smem_u32(&s_free[sb]), (uint32_t)((gs >> 1) - 1) & 1u, p.err)) return false;
+      if (!mbar_wait(smem_u32(&k_full[ks]), (uint32_t)(gk >> 1) & 1u, p.err)) return false;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t d = tmem + kTS + (uint32_t)(sb * 64);
+      const uint32_t k_base = smem_u32(sk + ks * kKStage);
+      for (int c = 0; c < p.nkc; ++c) {
+        const uint64_t qh = sdesc(q_base + c * kQChunk), ql = sdesc(q_base + (2 + c) * kQChunk);
+        const uint64_t kh = sdesc(k_base + c * kKChunk), kl = sdesc(k_base + (2 + c) * kKChunk);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t off = kk * 32;
+          const uint32_t acc = (c > 0 || kk > 0) ? 1u : 0u;
+          umma<PFC_PRECISION_TF32X3>(d, desc_add(ql, off), desc_add(kh, off), kIdesc, acc);
+          umma<PFC_PRECISION_TF32X3>(d, desc_add(qh, off), desc_add(kl, off), kIdesc, 1u);
+          umma<PFC_PRECISION_TF32X3>(d, desc_add(qh, off), desc_add(kh, off), kIdesc, 1u);
+        }
+      }
+      umma_commit(smem_u32(&k_free[ks]));
+      umma_commit(smem_u32(&s_full[sb]));
+      ++gk;
+      ++gs;
+      return true;
+    };
+    // O += P V of key block j
+    auto issue_pv = [&](int j) -> bool {
+      const int pb = gp & 1, vs = gv & 1;
+      if (!mbar_wait(smem_u32(&p_full[pb]), (uint32_t)(gp >> 1) & 1u, p.err)) return false;
+      if (!mbar_wait(smem_u32(&v_full[vs]), (uint32_t)(gv >> 1) & 1u, p.err)) return false;
+      if (j == 0 && tc > 0 && !mbar_wait(smem_u32(o_free), (uint32_t)(tc - 1) & 1u, p.err)) return false;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t d = tmem + kTO;
+      const uint32_t ph = tmem + kTP + (uint32_t)(pb * 128), pl = ph + 64;
+      const uint32_t v_base = smem_u32(sv + vs * kVStage);
+      for (int c = 0; c < 2; ++c) {
+        const uint64_t vh = sdesc(v_base + c * kVChunk), vl = sdesc(v_base + (2 + c) * kVChunk);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t col = (uint32_t)(c * 32 + kk * 8), off = kk * 32;
+          const uint32_t acc = (j > 0 || c > 0 || kk > 0) ? 1u : 0u;
+          umma_tmem_a(d, pl + col, desc_add(vh, off), acc);
+          umma_tmem_a(d, ph + col, desc_add(vl, off), 1u);
+          umma_tmem_a(d, ph + col, desc_add(vh, off), 1u);
+        }
+      }
+      umma_commit(smem_u32(&v_free[vs]));
+      umma_commit(smem_u32(&p_free[pb]));
+      ++gv;
+      ++gp;
+      return true;
+    };
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
+      if (!mbar_wait(smem_u32(q_full), (uint32_t)tc & 1u, p.err)) { ok = false; break; }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      for (int j = 0; j < p.nblk && ok; ++j) ok = issue_s();  // pass 1: statistics
+      // pass 2: S of the next block goes in before P V of this one, so the
+      // softmax warps work on one block while the tensor core does the other
+      if (ok) ok = issue_s();
+      for (int j = 0; j < p.nblk && ok; ++j) {
+        if (j + 1 < p.nblk) ok = issue_s();
+        if (ok && j + 1 == p.nblk) umma_commit(smem_u32(q_free));  // the last S of the tile is issued
+        if (ok) ok = issue_pv(j);
+      }
+      if (ok) umma_commit(smem_u32(o_full));
+    }
+    umma_commit(smem_u32(done));
+  } else if (warp >= 2) {
+    // ---------------- softmax and output ----------------
+    const int q = warp & 3;
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    const float scale = (p.alpha_ptr ? *p.alpha_ptr : p.alpha) * 1.4426950408889634f;  // alpha * log2(e)
+    int gs = 0, gp = 0, tc = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
+      const int b = t / p.ntq, q0 = (t - b * p.ntq) * kAQ;
+      float m = -INFINITY, l = 0.f;
+      float v[64];
+      auto read_s = [&]() -> bool {
+        const int sb = gs & 1;
+        if (!mbar_wait(smem_u32(&s_full[sb]), (uint32_t)(gs >> 1) & 1u, p.err)) return false;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        tmem_ld64(lane_base + kTS + (uint32_t)(sb * 64), v);
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&s_free[sb]));
+        ++gs;
+        return true;
+      };
+      // pass 1: running max and sum of exp2(scale * s - max), in log2 units
+      for (int j = 0; j < p.nblk && ok; ++j) {
+        if (!(ok = read_s())) break;
+        const int nk = min(kAK, p.L - j * kAK);
+        float bm = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < 64; ++k)
+          if (k < nk) bm = fmaxf(bm, v[k] * scale);
+        const float mn = fmaxf(m, bm);
+        float sum = 0.f;
+#pragma unroll
+        for (int k = 0; k < 64; ++k)
+          if (k < nk) sum += exp2f(fmaf(v[k], scale, -mn));
+        l = l * exp2f(m - mn) + sum;
+        m = mn;
+      }
+      const float inv = 1.f / l;
+      // pass 2: normalised P as hi/lo tf32 into TMEM
+      for (int j = 0; j < p.nblk && ok; ++j) {
+        if (!(ok = read_s())) break;
+        const int nk = min(kAK, p.L - j * kAK);
+        const int pb = gp & 1;
+        if (gp >= 2 && !(ok = mbar_wait(smem_u32(&p_free[pb]), (uint32_t)((gp >> 1) - 1) & 1u, p.err))) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t pbase = lane_base + kTP + (uint32_t)(pb * 128);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const int kk = 16 * i + k;
+            const float pv = kk < nk ? exp2f(fmaf(v[kk], scale, -m)) * inv : 0.f;
+            float h, lw;
+            split_tf32(pv, h, lw);
+            hi[k] = __float_as_uint(h);
+            lo[k] = __float_as_uint(lw);
+          }
+          tmem_st16(pbase + 16 * i, hi);
+          tmem_st16(pbase + 64 + 16 * i, lo);
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&p_full[pb]));
+        ++gp;
+      }
+      if (!ok) break;
+      // output row
+      if (!(ok = mbar_wait(smem_u32(o_full), (uint32_t)tc & 1u, p.err))) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      tmem_ld64(lane_base + kTO, v);
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(o_free));
+      const int row = q0 + q * 32 + lane;
+      if (row < p.M) {
+        float* out = p.c + (long long)b * p.c_sb + (long long)row * p.c_sm;
+        if (p.c_sn == 1 && p.d == 64 && (((uintptr_t)out) & 15) == 0) {
+#pragma unroll
+          for (int n = 0; n < 64; n += 4) *reinterpret_cast<float4*>(out + n) = make_float4(v[n], v[n + 1], v[n + 2], v[n + 3]);
+        } else {
+#pragma unroll
+          for (int n = 0; n < 64; ++n)
+            if (n < p.d) out[(long long)n * p.c_sn] = v[n];
+        }
+      }
+    }
+  }
+  // teardown: every MMA retired before TMEM is released
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    if (lane == 0) mbar_wait_own(smem_u32(done), 0u, p.err);
+    __syncwarp();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kATmemCols));
+  }
+}
+
+}  // namespace
+
+void launch_attention(const AttnLaunch& L, cudaStream_t stream) {
+  PFB_CHECK_ARG(L.batch > 0 && L.M > 0 && L.L > 0 && L.d > 0, "attention: empty problem");
+  PFB_CHECK_ARG(L.d <= kAD && (L.kq == 32 || L.kq == 64), "attention: head dimensions must be <= 64");
+  PFB_CHECK_ARG(L.kv >= L.L && L.kv % 32 == 0, "attention: V^T operand must cover the keys");
+  PFB_CHECK_ARG(L.batch < (1 << 20) && L.M < (1 << 24) && L.L < (1 << 24), "attention: too large");
+  PFB_CHECK_ARG(L.err && L.c, "attention: null pointer");
+  for (const void* q : {L.q_hi, (const void*)L.q_lo, L.k_hi, (const void*)L.k_lo, L.vt_hi, (const void*)L.vt_lo})
+    PFB_CHECK_ARG(q && ((uintptr_t)q & 15) == 0, "attention: operands must be 16-byte aligned");
+  static bool attr_set[64] = {};
+  static int sms[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    PFB_CUDA(cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kASmem));
+    int v = 0;
+    PFB_CUDA(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev));
+    sms[dev & 63] = v > 0 ? v : 148;
+    attr_set[dev & 63] = true;
+  }
+  const int prec = PFC_PRECISION_TF32X3;
+  const CUtensorMap qh = make_operand_map(L.q_hi, prec, L.kq, L.M, L.batch, kAQ);
+  const CUtensorMap ql = make_operand_map(L.q_lo, prec, L.kq, L.M, L.batch, kAQ);
+  const CUtensorMap kh = make_operand_map(L.k_hi, prec, L.kq, L.L, L.batch, kAK);
+  const CUtensorMap kl = make_operand_map(L.k_lo, prec, L.kq, L.L, L.batch, kAK);
+  const CUtensorMap vh = make_operand_map(L.vt_hi, prec, L.kv, L.d, L.batch, kAD);
+  const CUtensorMap vl = make_operand_map(L.vt_lo, prec, L.kv, L.d, L.batch, kAD);
+  AttnParams p;
+  p.batch = (int)L.batch;
+  p.M = (int)L.M;
+  p.L = (int)L.L;
+  p.d = (int)L.d;
+  p.nkc = (int)(L.kq / 32);
+  p.nblk = (int)ceil_div(L.L, kAK);
+  p.ntq = (int)ceil_div(L.M, kAQ);
+  p.alpha = L.alpha;
+  p.alpha_ptr = L.alpha_ptr;
+  p.c = L.c;
+  p.c_sb = L.c_sb;
+  p.c_sm = L.c_sm;
+  p.c_sn = L.c_sn;
+  p.err = L.err;
+  const int64_t ntiles = (int64_t)p.batch * p.ntq;
+  PFB_CHECK_ARG(ntiles < (1ll << 31), "attention: too many tiles");
+  const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sms[dev & 63]);
+  attn_kernel<<<grid, kAThreads, kASmem, stream>>>(qh, ql, kh, kl, vh, vl, p);
+  PFB_CUDA(cudaGetLastError());
+}
+
+}  // namespace pfb

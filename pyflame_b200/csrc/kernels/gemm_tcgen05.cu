@@ -41,6 +41,7 @@
 #include "../common.hpp"
 #include "kernels.hpp"
 #include "split.cuh"
+#include "tcgen05.cuh"
 
 namespace pfb {
 
@@ -54,7 +55,6 @@ template <bool CONV>
 constexpr int kProdWarps = CONV ? 4 : 1;
 template <bool CONV>
 constexpr int kThreads = (kProdWarps<CONV> + 1 + kEpiWarps) * 32;
-constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s per wait
 
 struct GemmParams {
   int M, N, nkb, a_batched, b_batched;
@@ -90,148 +90,6 @@ struct GemmParams {
   int conv_tma, TW, TH, tiles_w, tiles_h;
   int nimg, halo_rows;
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ unsigned long long gtimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t a, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(a), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(a), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait: false (and *err set) if the phase did not complete in time.
-__device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, int* err) {
-  if (mbar_try(a, parity)) return true;
-  unsigned long long t0 = gtimer();
-  while (true) {
-    for (int i = 0; i < 128; ++i)
-      if (mbar_try(a, parity)) return true;
-    if (*(volatile int*)err != 0) return false;
-    if (gtimer() - t0 > kWaitNs) {
-      atomicCAS(err, 0, PFC_ERR_TIMEOUT);
-      return false;
-    }
-  }
-}
-
-// Wait for this CTA's own asynchronous work (copies in flight, issued MMAs)
-// before its shared memory or TMEM goes away: bounded by time only, even when
-// another role already recorded an error.
-__device__ __forceinline__ void mbar_wait_own(uint32_t a, uint32_t parity, int* err) {
-  if (mbar_try(a, parity)) return;
-  unsigned long long t0 = gtimer();
-  while (true) {
-    for (int i = 0; i < 128; ++i)
-      if (mbar_try(a, parity)) return;
-    if (gtimer() - t0 > kWaitNs) {
-      atomicCAS(err, 0, PFC_ERR_TIMEOUT);
-      return;
-    }
-  }
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t mbar, int c0, int c1) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-      "l"((uint64_t)map), "r"(mbar), "r"(c0), "r"(c1)
-      : "memory");
-}
-
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t mbar, int c0, int c1,
-                                            int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
-      "l"((uint64_t)map), "r"(mbar), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t mbar, int c0, int c1,
-                                            int c2, int c3) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
-      "l"((uint64_t)map), "r"(mbar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-      : "memory");
-}
-
-__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, uint32_t mbar, int c0, int c1,
-                                            int c2, int c3, int c4) {
-  asm volatile(
-      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
-      "l"((uint64_t)map), "r"(mbar), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
-      : "memory");
-}
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
-// 1024 bytes apart (SBO), sm100 descriptor version 1.
-__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
-  d |= (uint64_t)1 << 16;               // LBO (unused for swizzled K-major)
-  d |= (uint64_t)(1024 >> 4) << 32;     // SBO
-  d |= (uint64_t)1 << 46;               // version
-  d |= (uint64_t)2 << 61;               // SWIZZLE_128B
-  return d;
-}
-
-// The 128-byte swizzle is a function of the absolute shared-memory address
-// (chunk bits 4-6 XOR row bits 7-9), for TMA writes and tensor-core reads
-// alike.  So a matrix may start anywhere on a 16-byte boundary of a swizzled
-// buffer: 32 bytes further along K, or a whole number of 128-byte rows
-// further down (a tap's run inside a halo), with the plain descriptor and a
-// base offset of 0 (verified against the oracle).  Offsets are added to a
-// descriptor directly: its low 14 bits hold the address in 16-byte units.
-__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t bytes) { return d + (bytes >> 4); }
-
-// Instruction descriptor for kind::tf32 / kind::f16: D fp32, K-major A and B.
-__host__ __device__ constexpr uint32_t idesc(int M, int N, uint32_t ab_fmt) {
-  return (1u << 4) | (ab_fmt << 7) | (ab_fmt << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-
-template <int PREC>
-__device__ __forceinline__ void umma(uint32_t tmem, uint64_t da, uint64_t db, uint32_t id, uint32_t acc) {
-  if constexpr (PREC == PFC_PRECISION_BF16) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
-        "l"(da), "l"(db), "r"(id), "r"(acc));
-  } else {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
-        "l"(da), "l"(db), "r"(id), "r"(acc));
-  }
-}
-
-__device__ __forceinline__ void umma_commit(uint32_t mbar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar)
-               : "memory");
-}
 
 template <int ACT>
 __device__ __forceinline__ float act_apply(float v) {
@@ -392,18 +250,6 @@ struct Cfg {
   static_assert(STAGES >= 2, "shared memory too small for two stages");
   static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation");
 };
-
-__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
-
-__device__ __forceinline__ void mbar_arrive(uint32_t a) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory");
-}
 
 // 16-byte global->shared copy; src_bytes 0 writes zeros (padding).
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
@@ -1173,6 +1019,12 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const 
 }
 
 }  // namespace
+
+// 3-D operand map [batch][rows][kpad], box (128 bytes of K) x box_rows x 1,
+// for the other tensor-core kernels.
+CUtensorMap make_operand_map(const void* base, int prec, int64_t kpad, int64_t rows, int64_t batch, int box_rows) {
+  return make_map(base, prec, kpad, rows, batch, box_rows);
+}
 
 // Which A feed a convolution can use: 1 or 2 (TMA, maps built) or 0 (gather).
 int conv_tma_mode(const GemmLaunch& L, int prec, CUtensorMap* maps, int* TW) {

@@ -50,6 +50,28 @@ struct GemmLaunch {
 };
 void launch_gemm(const GemmLaunch& L, cudaStream_t stream);
 
+// Fused attention O = softmax(alpha * Q K^T) V over batch slices (3xTF32
+// operands as prepared for the GEMM): Q [batch][M][kq], K [batch][L][kq],
+// V^T [batch][d][kv] hi/lo, K-major; O[b][m][n] at c + b*c_sb + m*c_sm + n*c_sn.
+// Needs d <= 64, kq in {32, 64}, kv >= L.  Replaces the QK^T GEMM, softmax
+// and PV GEMM that rocm_executor.cpp:278-335 and rocm_kernels.hip run as
+// separate passes for PyFlame's MultiheadAttention graphs.
+struct AttnLaunch {
+  int64_t batch = 0, M = 0, L = 0, d = 0, kq = 0, kv = 0;
+  const void* q_hi = nullptr;
+  const float* q_lo = nullptr;
+  const void* k_hi = nullptr;
+  const float* k_lo = nullptr;
+  const void* vt_hi = nullptr;
+  const float* vt_lo = nullptr;
+  float alpha = 1.f;
+  const float* alpha_ptr = nullptr;  // device scalar (a splat slot), overrides alpha
+  float* c = nullptr;
+  int64_t c_sb = 0, c_sm = 0, c_sn = 1;
+  int* err = nullptr;
+};
+void launch_attention(const AttnLaunch& L, cudaStream_t stream);
+
 // Channels-last copy of a Conv2d input for the implicit GEMM: x is a strided
 // [N,C,H,W] view; output [N][H][W][Cp] (Cp >= C, zero channels above C) as
 // tf32x3 hi/lo fp32 pairs, or bf16 in hi when precision is bf16.

@@ -61,6 +61,7 @@ enum class StepKind : uint8_t {
   POOL,       // pfk_pool2d
   BN_FOLD,    // fold BatchNorm(eval) into per-channel scale/shift
   MEMSET,     // zero a buffer range
+  ATTENTION,  // fused softmax(alpha * Q K^T) V (tcgen05)
 };
 
 // Pointer-argument buffer index that resolves to the executor's device error
@@ -147,6 +148,17 @@ struct BnFoldArgs {
   int out_scale = -1, out_shift = -1;
 };
 
+// Fused attention over batch slices: Q [batch][M][kq], K [batch][L][kq] and
+// V^T [batch][d][kv] are prepared tf32 hi/lo operands; O is written to c,
+// dense [batch][M][d].
+struct AttnArgs {
+  int q_hi = -1, q_lo = -1, k_hi = -1, k_lo = -1, vt_hi = -1, vt_lo = -1;
+  int64_t batch = 1, M = 0, L = 0, d = 0, kq = 0, kv = 0;
+  float alpha = 1.f;
+  int alpha_slot = -1;
+  View c;
+};
+
 struct Step {
   StepKind kind = StepKind::JIT;
   bool once = false;           // fills PREPARED buffers: runs only while they are unfilled
@@ -158,6 +170,7 @@ struct Step {
   GemmArgs gemm;
   PoolArgs pool;
   BnFoldArgs bnfold;
+  AttnArgs attn;
   int memset_buf = -1;
 };
 

@@ -366,6 +366,20 @@ def test_multihead_attention(cuda_executor, oracle_mod, rng):
     close_rows(g, r, RTOL_GEMM_TF32X3, what="mha")
 
 
+@pytest.mark.parametrize("b,h,m,l,d,scale", [(2, 3, 300, 200, 64, 0.125), (1, 2, 128, 512, 32, 1.0),
+                                             (3, 1, 50, 70, 40, 4.0)])
+def test_fused_attention(cuda_executor, oracle_mod, rng, b, h, m, l, d, scale):
+    """softmax(scale * Q K^T) V as one fused step: partial query tiles and key
+    blocks, a 32-wide head, and a peaked softmax (logits around +-75)."""
+    q = pf.tensor(rng.standard_normal((b, h, m, d)).astype(np.float32))
+    k = pf.tensor(rng.standard_normal((b, h, l, d)).astype(np.float32))
+    v = pf.tensor(rng.standard_normal((b, h, l, d)).astype(np.float32))
+    out = pf.matmul(pf.softmax(pf.matmul(q, k.transpose(-2, -1)) * scale, -1), v)
+    assert "attention " in cuda_executor.describe_plan(out.graph(), [out.node().id()])
+    (g,), (r,) = run(cuda_executor, [out], oracle_mod)
+    close_rows(g.reshape(-1, d), r.reshape(-1, d), RTOL_GEMM_TF32X3, what="attention")
+
+
 def test_encoder_block_small(cuda_executor, oracle_mod):
     from pyflame_b200 import workloads
     w = workloads.encoder(batch=2, seq=16, d=64, heads=4, ff=256)
@@ -449,7 +463,9 @@ def test_device_resident_execution(cuda_executor, oracle_mod):
                                      [o.data_ptr() for o in outs])
     torch.cuda.synchronize()
     ref = oracle_mod.run(g, ids)
-    bitexact(outs[2].cpu().numpy(), ref[ids[2]])
+    # the row max selects one value of z = sigmoid(x*y+0.5) - relu(x), which
+    # carries the device exp's last-bit difference from the host libm
+    close(outs[2].cpu().numpy(), ref[ids[2]], rtol=1e-5, atol=1e-6)
     close_rows(outs[3].cpu().numpy(), ref[ids[3]], 1e-5)
 
 
