@@ -13,10 +13,13 @@
 //   warp 1     TMEM (512 columns) and the MMAs.  S = Q K_j^T goes into one of
 //              two 64-column TMEM buffers (kind::tf32 x3 from shared memory);
 //              O += P_j V_j takes P from TMEM as the A operand.
-//   warps 2-5  one query row per thread (TMEM lane): pass 1 reads each S block
-//              and keeps the row's running max and sum of exp; pass 2 reads S
+//   warps 2-9  two warps per TMEM lane quarter, each taking 32 of a block's 64
+//              key columns for its 32 query rows: pass 1 reads the S blocks and
+//              keeps the running max and sum of exp (the two halves of a row
+//              combine once per tile through shared memory); pass 2 reads S
 //              again, writes P = exp(alpha*s - max) / sum as hi/lo tf32 into
-//              one of two TMEM P buffers, and at the end reads O and stores it.
+//              one of two TMEM P buffers, and at the end each warp reads and
+//              stores its half of the row of O.
 // Computing S twice keeps P exactly normalised before it meets V, so the O
 // accumulator is never rescaled.  Keys past L are masked; query rows past M
 // and head columns past d are dropped.  Every wait is bounded by the global
@@ -41,7 +44,8 @@ namespace {
 constexpr int kAQ = 128;          // query rows per tile (one per TMEM lane)
 constexpr int kAK = 64;           // keys per block
 constexpr int kAD = 64;           // head-dim columns of O and rows of V^T
-constexpr int kAThreads = 6 * 32;
+constexpr int kSoftWarps = 8;
+constexpr int kAThreads = (2 + kSoftWarps) * 32;
 
 constexpr int kQChunk = kAQ * 128;  // 128 rows x 32 tf32
 constexpr int kKChunk = kAK * 128;  // 64 keys x 32 tf32
@@ -82,14 +86,32 @@ __device__ __forceinline__ void umma_tmem_a(uint32_t d_tmem, uint32_t a_tmem, ui
       "r"(a_tmem), "l"(db), "r"(kIdesc), "r"(acc));
 }
 
-// 64 fp32 columns of this warp's TMEM lanes
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
-  uint32_t r[64];
+// 32 fp32 columns of this warp's TMEM lanes
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) tmem_ld16_nowait(taddr + 16 * i, *reinterpret_cast<uint32_t(*)[16]>(&r[16 * i]));
+  for (int i = 0; i < 2; ++i) tmem_ld16_nowait(taddr + 16 * i, *reinterpret_cast<uint32_t(*)[16]>(&r[16 * i]));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Barrier among the softmax warps only.  Every softmax warp passes the same
+// barriers in the same order, also after a failed wait: a warp never leaves
+// the tile loop except right after softmax_bar_any has told all of them.
+__device__ __forceinline__ void softmax_bar() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kSoftWarps * 32) : "memory");
+}
+// ... and returns whether any softmax thread passed `v` true
+__device__ __forceinline__ bool softmax_bar_any(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(kSoftWarps * 32)
+      : "memory");
+  return r != 0;
 }
 
 __global__ void __launch_bounds__(kAThreads, 1)
@@ -133,12 +155,12 @@ __global__ void __launch_bounds__(kAThreads, 1)
       mbar_init(smem_u32(&v_full[i]), 1);
       mbar_init(smem_u32(&v_free[i]), 1);
       mbar_init(smem_u32(&s_full[i]), 1);
-      mbar_init(smem_u32(&s_free[i]), 4);
-      mbar_init(smem_u32(&p_full[i]), 4);
+      mbar_init(smem_u32(&s_free[i]), kSoftWarps);
+      mbar_init(smem_u32(&p_full[i]), kSoftWarps);
       mbar_init(smem_u32(&p_free[i]), 1);
     }
     mbar_init(smem_u32(o_full), 1);
-    mbar_init(smem_u32(o_free), 4);
+    mbar_init(smem_u32(o_free), kSoftWarps);
     mbar_init(smem_u32(done), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -270,53 +292,67 @@ __global__ void __launch_bounds__(kAThreads, 1)
     umma_commit(smem_u32(done));
   } else if (warp >= 2) {
     // ---------------- softmax and output ----------------
-    const int q = warp & 3;
+    __shared__ float2 row_stat[2][kAQ];  // (max, sum) of each half of a row
+    const int q = warp & 3, hf = (warp - 2) >> 2;
+    const int row_in_tile = q * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
     const float scale = (p.alpha_ptr ? *p.alpha_ptr : p.alpha) * 1.4426950408889634f;  // alpha * log2(e)
     int gs = 0, gp = 0, tc = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tc) {
       const int b = t / p.ntq, q0 = (t - b * p.ntq) * kAQ;
       float m = -INFINITY, l = 0.f;
-      float v[64];
+      float v[32];
       auto read_s = [&]() -> bool {
         const int sb = gs & 1;
         if (!mbar_wait(smem_u32(&s_full[sb]), (uint32_t)(gs >> 1) & 1u, p.err)) return false;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        tmem_ld64(lane_base + kTS + (uint32_t)(sb * 64), v);
+        tmem_ld32(lane_base + kTS + (uint32_t)(sb * 64 + hf * 32), v);
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&s_free[sb]));
         ++gs;
         return true;
       };
-      // pass 1: running max and sum of exp2(scale * s - max), in log2 units
+      // pass 1: running max and sum of exp2(scale * s - max) over this half, in log2 units
       for (int j = 0; j < p.nblk && ok; ++j) {
         if (!(ok = read_s())) break;
-        const int nk = min(kAK, p.L - j * kAK);
+        const int nk = min(32, p.L - j * kAK - hf * 32);
         float bm = -INFINITY;
 #pragma unroll
-        for (int k = 0; k < 64; ++k)
+        for (int k = 0; k < 32; ++k)
           if (k < nk) bm = fmaxf(bm, v[k] * scale);
         const float mn = fmaxf(m, bm);
         float sum = 0.f;
 #pragma unroll
-        for (int k = 0; k < 64; ++k)
+        for (int k = 0; k < 32; ++k)
           if (k < nk) sum += exp2f(fmaf(v[k], scale, -mn));
-        l = l * exp2f(m - mn) + sum;
+        l = (m == -INFINITY ? 0.f : l * exp2f(m - mn)) + sum;
         m = mn;
       }
+      // both halves of the row: combine (a half may hold no keys: max -inf, sum 0)
+      row_stat[hf][row_in_tile] = make_float2(m, l);
+      if (softmax_bar_any(!ok)) break;  // all softmax warps leave together
+      {
+        const float2 o = row_stat[hf ^ 1][row_in_tile];
+        const float mn = fmaxf(m, o.x);
+        l = (m == -INFINITY ? 0.f : l * exp2f(m - mn)) + (o.x == -INFINITY ? 0.f : o.y * exp2f(o.x - mn));
+        m = mn;
+      }
+      softmax_bar();  // row_stat is free for the next tile
       const float inv = 1.f / l;
+      // From here a failed wait skips the rest of this tile; the warp still
+      // meets the others at the next tile's barrier, which ends the loop.
       // pass 2: normalised P as hi/lo tf32 into TMEM
       for (int j = 0; j < p.nblk && ok; ++j) {
         if (!(ok = read_s())) break;
-        const int nk = min(kAK, p.L - j * kAK);
+        const int nk = min(32, p.L - j * kAK - hf * 32);
         const int pb = gp & 1;
         if (gp >= 2 && !(ok = mbar_wait(smem_u32(&p_free[pb]), (uint32_t)((gp >> 1) - 1) & 1u, p.err))) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t pbase = lane_base + kTP + (uint32_t)(pb * 128);
+        const uint32_t pbase = lane_base + kTP + (uint32_t)(pb * 128 + hf * 32);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 2; ++i) {
           uint32_t hi[16], lo[16];
 #pragma unroll
           for (int k = 0; k < 16; ++k) {
@@ -336,24 +372,24 @@ __global__ void __launch_bounds__(kAThreads, 1)
         if (lane == 0) mbar_arrive(smem_u32(&p_full[pb]));
         ++gp;
       }
-      if (!ok) break;
-      // output row
-      if (!(ok = mbar_wait(smem_u32(o_full), (uint32_t)tc & 1u, p.err))) break;
+      if (!ok) continue;
+      // this warp's half of the output row
+      if (!(ok = mbar_wait(smem_u32(o_full), (uint32_t)tc & 1u, p.err))) continue;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      tmem_ld64(lane_base + kTO, v);
+      tmem_ld32(lane_base + kTO + (uint32_t)(hf * 32), v);
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(o_free));
-      const int row = q0 + q * 32 + lane;
+      const int row = q0 + row_in_tile;
       if (row < p.M) {
-        float* out = p.c + (long long)b * p.c_sb + (long long)row * p.c_sm;
+        float* out = p.c + (long long)b * p.c_sb + (long long)row * p.c_sm + (long long)(hf * 32) * p.c_sn;
         if (p.c_sn == 1 && p.d == 64 && (((uintptr_t)out) & 15) == 0) {
 #pragma unroll
-          for (int n = 0; n < 64; n += 4) *reinterpret_cast<float4*>(out + n) = make_float4(v[n], v[n + 1], v[n + 2], v[n + 3]);
+          for (int n = 0; n < 32; n += 4) *reinterpret_cast<float4*>(out + n) = make_float4(v[n], v[n + 1], v[n + 2], v[n + 3]);
         } else {
 #pragma unroll
-          for (int n = 0; n < 64; ++n)
-            if (n < p.d) out[(long long)n * p.c_sn] = v[n];
+          for (int n = 0; n < 32; ++n)
+            if (hf * 32 + n < p.d) out[(long long)n * p.c_sn] = v[n];
         }
       }
     }
