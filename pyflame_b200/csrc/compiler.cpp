@@ -1654,7 +1654,7 @@ void Compiler::detect_attention() {
     const Node& smn = N(sm);
     if (smn.op != Op::SOFTMAX || cls_[sm] != Cls::ROW || is_out_.count(sm) || users_[sm].size() != 1) continue;
     const int rank = (int)smn.shape.size();
-    if (rank < 3) continue;
+    if (rank < 3 || rank > 4) continue;  // [slices, M, L] or [B, H, M, L]
     int dim = (int)smn.attr_int("dim", -1);
     if (dim < 0) dim += rank;
     if (dim != rank - 1) continue;
@@ -1713,7 +1713,14 @@ void Compiler::lower_attention(int c2) {
   const Operand oq = prepare_operand(q, nbatch * M, d, kq, prec, "prepare Q " + shape_str(q.shape), at);
   const Operand ok = prepare_operand(k, nbatch * L, d, kq, prec, "prepare K " + shape_str(k.shape), at);
   const Operand ov = prepare_operand(vt, nbatch * dv, L, kv, prec, "prepare V^T " + shape_str(vt.shape), at);
+  // O [batch..., M, dv], stored with the heads innermost when there is a
+  // head dim ([B][M][H][dv] for [B, H, M, dv]): merging the heads back,
+  // transpose(1, 2) + reshape, is then a view of a dense [B*M, H*dv] matrix.
   View c = dense(mm2.shape, DType::F32);
+  if (r == 4) {
+    const int64_t H = mm2.shape[1];
+    c.strides = {M * H * dv, dv, H * dv, 1};
+  }
   Step st;
   st.kind = StepKind::ATTENTION;
   st.label = "attention " + std::to_string(nbatch) + "x[" + std::to_string(M) + "x" + std::to_string(L) + "x" +
@@ -2758,7 +2765,7 @@ void Compiler::emit_operands_at_producers() {
       case StepKind::ATTENTION: {
         const AttnArgs& A = st.attn;
         add(A.q_hi, i); add(A.q_lo, i); add(A.k_hi, i); add(A.k_lo, i); add(A.vt_hi, i); add(A.vt_lo, i);
-        add(A.c.buf, i);
+        add(A.c.buf, i); add(A.op_hi, i); add(A.op_lo, i);
         break;
       }
     }
@@ -2771,6 +2778,7 @@ void Compiler::emit_operands_at_producers() {
       const Step& st = S[j];
       if (st.kind == StepKind::GEMM && st.gemm.c.buf == b && st.gemm.write_c) return j;
       if (st.kind == StepKind::POOL && st.pool.y.buf == b && st.pool.write_y) return j;
+      if (st.kind == StepKind::ATTENTION && st.attn.c.buf == b && st.attn.write_c) return j;
     }
     return -1;
   };
@@ -2785,12 +2793,50 @@ void Compiler::emit_operands_at_producers() {
     Step& st = S[i];
     if (st.kind == StepKind::SPLIT && !st.once && st.split.conv_cp == 0) {
       const View& v = st.split.src;
-      if (v.is_splat || v.buf < 0 || v.offset != 0 || v.strides != View::dense_strides(v.shape)) continue;
+      if (v.is_splat || v.buf < 0 || v.offset != 0) continue;
+      const bool dense_src = v.strides == View::dense_strides(v.shape);
       const int j = producer(v.buf);
+      if (j >= 0 && j < i && S[j].kind == StepKind::ATTENTION && dense_src) {
+        // the attention's O as a dense [rows, cols] matrix (heads merged)
+        AttnArgs& A = S[j].attn;
+        const size_t r = A.c.shape.size();
+        const int64_t H = r == 4 ? A.c.shape[1] : 1;
+        const int64_t cols = H * A.d, rows = A.batch / H * A.M;
+        const bool merged = r == 4 ? A.c.strides == std::vector<int64_t>{A.M * cols, A.d, cols, 1}
+                                   : A.c.strides == View::dense_strides(A.c.shape);
+        if (A.op_hi >= 0 || !merged || A.c.offset != 0 || st.split.cols != cols || st.split.kpad != cols ||
+            st.split.rows != rows || cols % 4 != 0)
+          continue;
+        A.op_hi = st.split.out_hi;
+        A.op_lo = st.split.out_lo;
+        drop[i] = true;
+        A.write_c = others_read(v.buf, j, i);
+        S[j].label += " +operand";
+        continue;
+      }
       if (j < 0 || j > i || S[j].kind != StepKind::GEMM) continue;
       GemmArgs& G = S[j].gemm;
       const bool dense_c = G.c.offset == 0 && G.c_sn == 1 && G.c_sm == G.N && (G.batch == 1 || G.c_sb == G.M * G.N);
-      if (G.op_hi >= 0 || !dense_c || st.split.cols != G.N || st.split.kpad != G.N || G.N % 4 != 0 ||
+      // the per-head split of a projection, [B, H, L, D] over a dense [B*L, H*D]
+      // output (what attention reads as Q and K): the epilogue writes it head-split
+      if (st.split.src.shape.size() == 4 && !G.conv && G.batch == 1 && dense_c && G.op_hi < 0) {
+        const std::vector<int64_t>& sh = st.split.src.shape;
+        const int64_t B = sh[0], H = sh[1], L = sh[2], D = sh[3];
+        const std::vector<int64_t> want{L * H * D, D, H * D, 1};
+        if (st.split.src.strides == want && B * L == G.M && H * D == G.N && st.split.cols == D &&
+            st.split.kpad == D && st.split.rows == B * H * L && D % 16 == 0 && L % 32 == 0) {
+          G.op_hi = st.split.out_hi;
+          G.op_lo = st.split.out_lo;
+          G.op_sm = D;
+          G.op_heads = H;
+          G.op_rows = L;
+          drop[i] = true;
+          G.write_c = others_read(v.buf, j, i);
+          S[j].label += " +heads";
+        }
+        continue;
+      }
+      if (!dense_src || G.op_hi >= 0 || !dense_c || st.split.cols != G.N || st.split.kpad != G.N || G.N % 4 != 0 ||
           st.split.rows != G.batch * G.M)
         continue;
       G.op_hi = st.split.out_hi;
@@ -2901,7 +2947,8 @@ void Compiler::finish() {
       case StepKind::ATTENTION: {
         const AttnArgs& A = s.attn;
         use(A.q_hi, i); use(A.q_lo, i); use(A.k_hi, i); use(A.k_lo, i); use(A.vt_hi, i); use(A.vt_lo, i);
-        use(A.c.buf, i);
+        if (A.write_c) use(A.c.buf, i);
+        use(A.op_hi, i); use(A.op_lo, i);
         break;
       }
     }

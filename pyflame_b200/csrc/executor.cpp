@@ -416,8 +416,18 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
       L.vt_lo = (const float*)bufp(a.vt_lo, 0);
       L.alpha = a.alpha;
       L.alpha_ptr = a.alpha_slot >= 0 ? (const float*)bufp(P.scalar_buf, (int64_t)a.alpha_slot * 4) : nullptr;
-      L.c = (float*)viewp(a.c);
-      L.c_sb = a.M * a.d; L.c_sm = a.d; L.c_sn = 1;
+      const size_t r = a.c.shape.size();
+      L.c = a.write_c ? (float*)viewp(a.c) : nullptr;
+      L.heads = r == 4 ? a.c.shape[1] : 1;
+      L.c_sb = a.c.strides[0];
+      L.c_sh = r == 4 ? a.c.strides[1] : 0;
+      L.c_sm = a.c.strides[r - 2];
+      L.c_sn = a.c.strides[r - 1];
+      if (a.op_hi >= 0) {
+        // operand buffers share the element offsets of c
+        L.o_hi = (float*)bufp(a.op_hi, a.c.offset * 4);
+        L.o_lo = (float*)bufp(a.op_lo, a.c.offset * 4);
+      }
       L.err = err_dev_;
       launch_attention(L, s);
       break;
@@ -451,6 +461,8 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
       L.out_hi = bufp(a.op_hi, 0);
       L.out_lo = (float*)bufp(a.op_lo, 0);
       L.o_sm = a.op_sm;
+      L.o_heads = a.op_heads;
+      L.o_rows = a.op_rows;
       if (a.conv) {
         L.conv = true;
         L.x_hi = bufp(a.x_hi, 0);

@@ -64,8 +64,11 @@ struct AttnParams {
   int batch, M, L, d, nkc, nblk, ntq;
   float alpha;
   const float* alpha_ptr;
-  float* c;
-  long long c_sb, c_sm, c_sn;
+  float* c;  // O of slice s = b*heads + h at c + b*c_sb + h*c_sh + m*c_sm + n*c_sn
+  int heads;
+  long long c_sb, c_sh, c_sm, c_sn;
+  float* o_hi;  // O as tf32 hi/lo at the same element offsets (or null)
+  float* o_lo;
   int* err;
 };
 
@@ -382,14 +385,42 @@ __global__ void __launch_bounds__(kAThreads, 1)
       if (lane == 0) mbar_arrive(smem_u32(o_free));
       const int row = q0 + row_in_tile;
       if (row < p.M) {
-        float* out = p.c + (long long)b * p.c_sb + (long long)row * p.c_sm + (long long)(hf * 32) * p.c_sn;
-        if (p.c_sn == 1 && p.d == 64 && (((uintptr_t)out) & 15) == 0) {
+        const int bb = b / p.heads, hh = b - bb * p.heads;
+        const long long off = (long long)bb * p.c_sb + (long long)hh * p.c_sh + (long long)row * p.c_sm +
+                              (long long)(hf * 32) * p.c_sn;
+        const bool vec = p.c_sn == 1 && p.d == 64 && (off & 3) == 0;
+        if (p.c) {
+          float* out = p.c + off;
+          if (vec) {
 #pragma unroll
-          for (int n = 0; n < 32; n += 4) *reinterpret_cast<float4*>(out + n) = make_float4(v[n], v[n + 1], v[n + 2], v[n + 3]);
-        } else {
+            for (int n = 0; n < 32; n += 4)
+              *reinterpret_cast<float4*>(out + n) = make_float4(v[n], v[n + 1], v[n + 2], v[n + 3]);
+          } else {
 #pragma unroll
-          for (int n = 0; n < 32; ++n)
-            if (hf * 32 + n < p.d) out[(long long)n * p.c_sn] = v[n];
+            for (int n = 0; n < 32; ++n)
+              if (hf * 32 + n < p.d) out[(long long)n * p.c_sn] = v[n];
+          }
+        }
+        if (p.o_hi) {
+#pragma unroll
+          for (int n = 0; n < 32; n += 4) {
+            float4 h, lw;
+            split_tf32(v[n], h.x, lw.x);
+            split_tf32(v[n + 1], h.y, lw.y);
+            split_tf32(v[n + 2], h.z, lw.z);
+            split_tf32(v[n + 3], h.w, lw.w);
+            if (vec) {
+              *reinterpret_cast<float4*>(p.o_hi + off + n) = h;
+              *reinterpret_cast<float4*>(p.o_lo + off + n) = lw;
+            } else {
+              const float hs[4] = {h.x, h.y, h.z, h.w}, ls[4] = {lw.x, lw.y, lw.z, lw.w};
+              for (int k = 0; k < 4; ++k)
+                if (hf * 32 + n + k < p.d) {
+                  p.o_hi[off + (long long)(n + k) * p.c_sn] = hs[k];
+                  p.o_lo[off + (long long)(n + k) * p.c_sn] = ls[k];
+                }
+            }
+          }
         }
       }
     }
@@ -412,7 +443,9 @@ void launch_attention(const AttnLaunch& L, cudaStream_t stream) {
   PFB_CHECK_ARG(L.d <= kAD && (L.kq == 32 || L.kq == 64), "attention: head dimensions must be <= 64");
   PFB_CHECK_ARG(L.kv >= L.L && L.kv % 32 == 0, "attention: V^T operand must cover the keys");
   PFB_CHECK_ARG(L.batch < (1 << 20) && L.M < (1 << 24) && L.L < (1 << 24), "attention: too large");
-  PFB_CHECK_ARG(L.err && L.c, "attention: null pointer");
+  PFB_CHECK_ARG(L.err && (L.c || L.o_hi) && (!L.o_hi || L.o_lo) && L.heads > 0 && L.batch % L.heads == 0,
+                "attention: null pointer or bad head count");
+  PFB_CHECK_ARG(!L.o_hi || (((uintptr_t)L.o_hi | (uintptr_t)L.o_lo) & 15) == 0, "attention: operand output must be 16-byte aligned");
   for (const void* q : {L.q_hi, (const void*)L.q_lo, L.k_hi, (const void*)L.k_lo, L.vt_hi, (const void*)L.vt_lo})
     PFB_CHECK_ARG(q && ((uintptr_t)q & 15) == 0, "attention: operands must be 16-byte aligned");
   static bool attr_set[64] = {};
@@ -444,9 +477,13 @@ void launch_attention(const AttnLaunch& L, cudaStream_t stream) {
   p.alpha = L.alpha;
   p.alpha_ptr = L.alpha_ptr;
   p.c = L.c;
+  p.heads = (int)L.heads;
   p.c_sb = L.c_sb;
+  p.c_sh = L.c_sh;
   p.c_sm = L.c_sm;
   p.c_sn = L.c_sn;
+  p.o_hi = L.o_hi;
+  p.o_lo = L.o_lo;
   p.err = L.err;
   const int64_t ntiles = (int64_t)p.batch * p.ntq;
   PFB_CHECK_ARG(ntiles < (1ll << 31), "attention: too many tiles");

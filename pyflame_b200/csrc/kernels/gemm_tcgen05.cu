@@ -75,6 +75,7 @@ struct GemmParams {
   void* o_hi;           // operand outputs for a following GEMM (or null)
   float* o_lo;
   long long o_sm;
+  int o_heads, o_rows;  // head-split operand output (GemmLaunch::o_heads)
   // implicit-GEMM Conv2d: channels-last input [N][H][W][Cp] (or a zero-padded
   // [N][Hp][Wp][Cp] copy when Hp > 0), weight k = (kh*KWp + kw)*Cp + c
   const void* x_hi;
@@ -147,6 +148,15 @@ __device__ __forceinline__ long long halo_out_row(const GemmParams& p, long long
   return ((long long)img * p.OH + oh) * p.OW + ow;
 }
 
+// Element offset of operand output (row, n): row-major with pitch o_sm, or
+// head-split [(b*heads + h)*rows + l][d] for row = b*rows + l, n = h*o_sm + d.
+__device__ __forceinline__ long long op_offset(const GemmParams& p, long long row, int n) {
+  if (p.o_heads == 0) return row * p.o_sm + n;
+  const long long b = row / p.o_rows, l = row - b * p.o_rows;
+  const int h = n / (int)p.o_sm, d = n - h * (int)p.o_sm;
+  return ((b * p.o_heads + h) * p.o_rows + l) * p.o_sm + d;
+}
+
 // Rows m_base .. m_base+31 of the output matrix, of which the first nvalid
 // exist; MAPPED: virtual rows m_base .. of a halo-staged convolution.
 template <int ACT, int PREC, bool MAPPED = false>
@@ -173,7 +183,8 @@ __device__ __forceinline__ void store_block(const GemmParams& p, const float* ep
   if (!MAPPED && full_n && vec_c && nvalid == 32 && !rbase) {
     // whole block inside the output, no residual: straight float4 stores
     const long long c0 = (m_base + rsub) * p.c_sm + n, cstep = 8 * p.c_sm;
-    const long long o0 = (m_base + rsub) * p.o_sm + n, ostep = 8 * p.o_sm;
+    // (a head-split operand keeps 32-row blocks inside one batch: same step)
+    const long long o0 = ohi ? op_offset(p, m_base + rsub, n) : 0, ostep = 8 * p.o_sm;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       float v[4] = {a[k].x, a[k].y, a[k].z, a[k].w};
@@ -201,7 +212,7 @@ __device__ __forceinline__ void store_block(const GemmParams& p, const float* ep
     }
     if (MAPPED ? row < 0 : 8 * k + rsub >= nvalid) continue;
     const long long co = row * p.c_sm + (long long)n * p.c_sn;
-    const long long oo = row * p.o_sm + n;
+    const long long oo = ohi ? op_offset(p, row, n) : 0;
     if (full_n && vec_c) {
       if (rbase) {
         const long long ro = row * p.r_sm + (long long)n * p.r_sn;
@@ -972,6 +983,8 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const 
   p.o_hi = L.out_hi;
   p.o_lo = L.out_lo;
   p.o_sm = L.o_sm;
+  p.o_heads = (int)L.o_heads;
+  p.o_rows = (int)L.o_rows;
   p.x_hi = L.x_hi;
   p.x_lo = L.x_lo;
   p.H = (int)L.H; p.W = (int)L.W; p.Cp = (int)L.Cp; p.KH = (int)L.KH; p.KW = (int)L.KW;
@@ -1058,8 +1071,13 @@ void launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
   PFB_CHECK_ARG(L.M < (1ll << 31) && L.N < (1ll << 31), "gemm: dimension too large");
   PFB_CHECK_ARG(L.err != nullptr, "gemm: error flag pointer required");
   PFB_CHECK_ARG(L.c || L.out_hi, "gemm: no output");
+  if (L.out_hi && L.o_heads > 0) {
+    PFB_CHECK_ARG(L.batch == 1 && L.o_sm % 16 == 0 && L.o_heads * L.o_sm == L.N && L.o_rows % 32 == 0 &&
+                      L.M % L.o_rows == 0 && !L.conv,
+                  "gemm: head-split operand output needs 16-column heads, 32-row groups and batch 1");
+  }
   if (L.out_hi) {
-    PFB_CHECK_ARG(L.N % 4 == 0 && L.o_sm % 4 == 0 && L.o_sm >= L.N && ((uintptr_t)L.out_hi & 15) == 0 &&
+    PFB_CHECK_ARG(L.N % 4 == 0 && L.o_sm % 4 == 0 && (L.o_heads > 0 || L.o_sm >= L.N) && ((uintptr_t)L.out_hi & 15) == 0 &&
                       (L.precision == PFC_PRECISION_BF16 || (L.out_lo && ((uintptr_t)L.out_lo & 15) == 0)),
                   "gemm: operand output needs 16-byte aligned rows of a multiple of 4 columns");
   }

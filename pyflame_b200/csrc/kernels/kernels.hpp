@@ -23,6 +23,10 @@ struct GemmLaunch {
   void* out_hi = nullptr;
   float* out_lo = nullptr;
   int64_t o_sm = 0;
+  // o_heads > 0 (batch 1): head-split operand, element (m, n) at
+  // [((m / o_rows)*o_heads + n / o_sm)*o_rows + m % o_rows][n % o_sm], row
+  // pitch o_sm; needs o_sm % 16 == 0, o_heads*o_sm == N, o_rows % 32 == 0
+  int64_t o_heads = 0, o_rows = 0;
   float alpha = 1.f;
   const float* alpha_ptr = nullptr;
   const float* bias = nullptr;
@@ -66,8 +70,12 @@ struct AttnLaunch {
   const float* vt_lo = nullptr;
   float alpha = 1.f;
   const float* alpha_ptr = nullptr;  // device scalar (a splat slot), overrides alpha
-  float* c = nullptr;
-  int64_t c_sb = 0, c_sm = 0, c_sn = 1;
+  // O of slice s = b*heads + h at c + b*c_sb + h*c_sh + m*c_sm + n*c_sn
+  float* c = nullptr;  // may be null when only the operand is written
+  int64_t heads = 1, c_sb = 0, c_sh = 0, c_sm = 0, c_sn = 1;
+  // O also as tf32 hi/lo at the same element offsets (or null)
+  float* o_hi = nullptr;
+  float* o_lo = nullptr;
   int* err = nullptr;
 };
 void launch_attention(const AttnLaunch& L, cudaStream_t stream);

@@ -121,6 +121,10 @@ struct GemmArgs {
   // that GEMM's operand preparation): element (b,m,n) at [(b*M+m)*op_sm + n].
   int op_hi = -1, op_lo = -1;
   int64_t op_sm = 0;
+  // op_heads > 0: head-split operand instead, element (m, n) of a batch-1
+  // GEMM at [((m / op_rows)*op_heads + n / op_sm)*op_rows + m % op_rows][n % op_sm]
+  // (row pitch op_sm): the [B, H, L, D] per-head layout attention reads
+  int64_t op_heads = 0, op_rows = 0;
   bool write_c = true;  // false when only the operand outputs are read
   // implicit-GEMM Conv2d: A gathered from the channels-last input x_hi/x_lo
   bool conv = false;
@@ -149,14 +153,19 @@ struct BnFoldArgs {
 };
 
 // Fused attention over batch slices: Q [batch][M][kq], K [batch][L][kq] and
-// V^T [batch][d][kv] are prepared tf32 hi/lo operands; O is written to c,
-// dense [batch][M][d].
+// V^T [batch][d][kv] are prepared tf32 hi/lo operands; O is written to the
+// view c ([batch..., M, d], rank 3 or 4: slice s = (b, h) of a 4-D view is at
+// b*strides[0] + h*strides[1]).  op_hi/op_lo >= 0: O is also written as a
+// GEMM operand (hi/lo) at the same element offsets as c (then write_c says
+// whether the fp32 value is still needed).
 struct AttnArgs {
   int q_hi = -1, q_lo = -1, k_hi = -1, k_lo = -1, vt_hi = -1, vt_lo = -1;
   int64_t batch = 1, M = 0, L = 0, d = 0, kq = 0, kv = 0;
   float alpha = 1.f;
   int alpha_slot = -1;
   View c;
+  int op_hi = -1, op_lo = -1;
+  bool write_c = true;
 };
 
 struct Step {
