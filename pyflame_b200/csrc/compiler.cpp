@@ -1703,16 +1703,14 @@ void Compiler::lower_attention(int c2) {
   const int64_t M = q.shape[r - 2], d = q.shape[r - 1], L = kt.shape[r - 1], dv = v.shape[r - 1];
   if (kt.shape[r - 2] != d || v.shape[r - 2] != L) fail(PFC_ERR_GRAPH, "matmul: inner dimensions don't match");
   const int prec = in_.precision;
-  const int64_t kq = round_up(d, 32), kv = round_up(L, 32);
-  // K as [batch..., L, d] and V^T as [batch..., dv, L]: swap the last two dims
-  View k = kt, vt = v;
+  const int64_t kq = round_up(d, 32), kv = round_up(dv, 32);
+  // K as [batch..., L, d]: swap the last two dims of K^T (V is used as stored)
+  View k = kt;
   std::swap(k.shape[r - 2], k.shape[r - 1]);
   std::swap(k.strides[r - 2], k.strides[r - 1]);
-  std::swap(vt.shape[r - 2], vt.shape[r - 1]);
-  std::swap(vt.strides[r - 2], vt.strides[r - 1]);
   const Operand oq = prepare_operand(q, nbatch * M, d, kq, prec, "prepare Q " + shape_str(q.shape), at);
   const Operand ok = prepare_operand(k, nbatch * L, d, kq, prec, "prepare K " + shape_str(k.shape), at);
-  const Operand ov = prepare_operand(vt, nbatch * dv, L, kv, prec, "prepare V^T " + shape_str(vt.shape), at);
+  const Operand ov = prepare_operand(v, nbatch * L, dv, kv, prec, "prepare V " + shape_str(v.shape), at);
   // O [batch..., M, dv], stored with the heads innermost when there is a
   // head dim ([B][M][H][dv] for [B, H, M, dv]): merging the heads back,
   // transpose(1, 2) + reshape, is then a view of a dense [B*M, H*dv] matrix.
@@ -1726,7 +1724,7 @@ void Compiler::lower_attention(int c2) {
   st.label = "attention " + std::to_string(nbatch) + "x[" + std::to_string(M) + "x" + std::to_string(L) + "x" +
              std::to_string(dv) + "]";
   AttnArgs& A = st.attn;
-  A.q_hi = oq.hi; A.q_lo = oq.lo; A.k_hi = ok.hi; A.k_lo = ok.lo; A.vt_hi = ov.hi; A.vt_lo = ov.lo;
+  A.q_hi = oq.hi; A.q_lo = oq.lo; A.k_hi = ok.hi; A.k_lo = ok.lo; A.v_hi = ov.hi; A.v_lo = ov.lo;
   A.batch = nbatch; A.M = M; A.L = L; A.d = dv; A.kq = kq; A.kv = kv;
   A.alpha = ch1.alpha;
   A.alpha_slot = ch1.alpha_slot;
@@ -2764,7 +2762,7 @@ void Compiler::emit_operands_at_producers() {
       case StepKind::MEMSET: add(st.memset_buf, i); break;
       case StepKind::ATTENTION: {
         const AttnArgs& A = st.attn;
-        add(A.q_hi, i); add(A.q_lo, i); add(A.k_hi, i); add(A.k_lo, i); add(A.vt_hi, i); add(A.vt_lo, i);
+        add(A.q_hi, i); add(A.q_lo, i); add(A.k_hi, i); add(A.k_lo, i); add(A.v_hi, i); add(A.v_lo, i);
         add(A.c.buf, i); add(A.op_hi, i); add(A.op_lo, i);
         break;
       }
@@ -2946,7 +2944,7 @@ void Compiler::finish() {
       case StepKind::MEMSET: use(s.memset_buf, i); break;
       case StepKind::ATTENTION: {
         const AttnArgs& A = s.attn;
-        use(A.q_hi, i); use(A.q_lo, i); use(A.k_hi, i); use(A.k_lo, i); use(A.vt_hi, i); use(A.vt_lo, i);
+        use(A.q_hi, i); use(A.q_lo, i); use(A.k_hi, i); use(A.k_lo, i); use(A.v_hi, i); use(A.v_lo, i);
         if (A.write_c) use(A.c.buf, i);
         use(A.op_hi, i); use(A.op_lo, i);
         break;

@@ -412,8 +412,8 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
       L.q_lo = (const float*)bufp(a.q_lo, 0);
       L.k_hi = bufp(a.k_hi, 0);
       L.k_lo = (const float*)bufp(a.k_lo, 0);
-      L.vt_hi = bufp(a.vt_hi, 0);
-      L.vt_lo = (const float*)bufp(a.vt_lo, 0);
+      L.v_hi = bufp(a.v_hi, 0);
+      L.v_lo = (const float*)bufp(a.v_lo, 0);
       L.alpha = a.alpha;
       L.alpha_ptr = a.alpha_slot >= 0 ? (const float*)bufp(P.scalar_buf, (int64_t)a.alpha_slot * 4) : nullptr;
       const size_t r = a.c.shape.size();

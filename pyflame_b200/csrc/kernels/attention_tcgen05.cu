@@ -9,10 +9,11 @@
 //
 // One persistent CTA per SM walks tiles of (slice, 128 query rows):
 //   warp 0     TMA: Q of the tile once, then key blocks of 64 (K, and in the
-//              second pass V^T) through two-stage rings.
+//              second pass V) through two-stage rings.
 //   warp 1     TMEM (512 columns) and the MMAs.  S = Q K_j^T goes into one of
 //              two 64-column TMEM buffers (kind::tf32 x3 from shared memory);
-//              O += P_j V_j takes P from TMEM as the A operand.
+//              O += P_j V_j takes P from TMEM as the A operand and V as an
+//              MN-major B operand (its rows are keys, as stored).
 //   warps 2-9  two warps per TMEM lane quarter, each taking 32 of a block's 64
 //              key columns for its 32 query rows: pass 1 reads the S blocks and
 //              keeps the running max and sum of exp (the two halves of a row
@@ -37,7 +38,8 @@
 
 namespace pfb {
 
-CUtensorMap make_operand_map(const void* base, int prec, int64_t kpad, int64_t rows, int64_t batch, int box_rows);
+CUtensorMap make_operand_map(const void* base, int prec, int64_t kpad, int64_t rows, int64_t batch, int box_rows,
+                             bool mn32 = false);
 
 namespace {
 
@@ -49,16 +51,31 @@ constexpr int kAThreads = (2 + kSoftWarps) * 32;
 
 constexpr int kQChunk = kAQ * 128;  // 128 rows x 32 tf32
 constexpr int kKChunk = kAK * 128;  // 64 keys x 32 tf32
-constexpr int kVChunk = kAD * 128;  // 64 head-dim rows x 32 keys
+constexpr int kVChunk = kAK * 128;  // 64 keys x 32 head-dim columns
 constexpr int kQBytes = 2 * 2 * kQChunk;    // [hi/lo][k-chunk]
 constexpr int kKStage = 2 * 2 * kKChunk;    // [hi/lo][k-chunk]
-constexpr int kVStage = 2 * 2 * kVChunk;    // [hi/lo][key chunk]
+constexpr int kVStage = 2 * 2 * kVChunk;    // [hi/lo][head-dim chunk]
 constexpr int kStages = 2;
 constexpr int kASmem = kQBytes + kStages * (kKStage + kVStage) + 1024 /*barriers*/ + 1024 /*align*/;
 // TMEM columns: S buffers at 0 and 64; P buffers (hi 64 | lo 64) at 128 and
 // 256; O at 384.
 constexpr uint32_t kTS = 0, kTP = 128, kTO = 384, kATmemCols = 512;
 constexpr uint32_t kIdesc = idesc(kAQ, 64, 2u);  // M 128, N 64, tf32
+constexpr uint32_t kIdescMnB = kIdesc | (1u << 16);  // ... with B MN-major
+
+// Shared-memory descriptor of an MN-major tf32 operand, the one layout
+// tcgen05 takes for it: the 128-byte swizzle with 32-byte atoms.  Rows of 32
+// N-elements (128 bytes) per K index, 4 K-rows per 512-byte atom (SBO to the
+// next 4), the next 32 N-elements `lbo` bytes on.
+__device__ __forceinline__ uint64_t sdesc_mn(uint32_t saddr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)(lbo >> 4) << 16;      // LBO: next 32 N-elements
+  d |= (uint64_t)(512 >> 4) << 32;      // SBO: next 4 K-rows
+  d |= (uint64_t)1 << 46;               // version
+  d |= (uint64_t)1 << 61;               // SWIZZLE_128B_BASE32B
+  return d;
+}
 
 struct AttnParams {
   int batch, M, L, d, nkc, nblk, ntq;
@@ -81,12 +98,12 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 
-// D (TMEM) += A (TMEM, K-major: lane = row, column = k) x B (shared memory)
+// D (TMEM) += A (TMEM, K-major: lane = row, column = k) x B (shared memory, MN-major)
 __device__ __forceinline__ void umma_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t db, uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(db), "r"(kIdesc), "r"(acc));
+      "r"(a_tmem), "l"(db), "r"(kIdescMnB), "r"(acc));
 }
 
 // 32 fp32 columns of this warp's TMEM lanes
@@ -207,9 +224,9 @@ __global__ void __launch_bounds__(kAThreads, 1)
             if (gv >= 2 && !mbar_wait(smem_u32(&v_free[v]), (uint32_t)((gv >> 1) - 1) & 1u, p.err)) { ok = false; break; }
             uint8_t* vst = sv + v * kVStage;
             mbar_expect_tx(smem_u32(&v_full[v]), (uint32_t)kVStage);
-            for (int c = 0; c < 2; ++c) {
-              tma_load_3d(smem_u32(vst + c * kVChunk), &tv_hi, smem_u32(&v_full[v]), j * kAK + c * 32, 0, b);
-              tma_load_3d(smem_u32(vst + (2 + c) * kVChunk), &tv_lo, smem_u32(&v_full[v]), j * kAK + c * 32, 0, b);
+            for (int c = 0; c < 2; ++c) {  // head-dim columns 32c..32c+31 of keys j*64..
+              tma_load_3d(smem_u32(vst + c * kVChunk), &tv_hi, smem_u32(&v_full[v]), c * 32, j * kAK, b);
+              tma_load_3d(smem_u32(vst + (2 + c) * kVChunk), &tv_lo, smem_u32(&v_full[v]), c * 32, j * kAK, b);
             }
             ++gv;
           }
@@ -261,16 +278,16 @@ __global__ void __launch_bounds__(kAThreads, 1)
       const uint32_t d = tmem + kTO;
       const uint32_t ph = tmem + kTP + (uint32_t)(pb * 128), pl = ph + 64;
       const uint32_t v_base = smem_u32(sv + vs * kVStage);
-      for (int c = 0; c < 2; ++c) {
-        const uint64_t vh = sdesc(v_base + c * kVChunk), vl = sdesc(v_base + (2 + c) * kVChunk);
+      // V block [64 keys][64 head dims] as two 32-column chunks: K-step kk
+      // takes keys 8kk..8kk+7 (one 1024-byte atom row group further down)
+      const uint64_t vh = sdesc_mn(v_base, kVChunk), vl = sdesc_mn(v_base + 2 * kVChunk, kVChunk);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint32_t col = (uint32_t)(c * 32 + kk * 8), off = kk * 32;
-          const uint32_t acc = (j > 0 || c > 0 || kk > 0) ? 1u : 0u;
-          umma_tmem_a(d, pl + col, desc_add(vh, off), acc);
-          umma_tmem_a(d, ph + col, desc_add(vl, off), 1u);
-          umma_tmem_a(d, ph + col, desc_add(vh, off), 1u);
-        }
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t col = (uint32_t)(kk * 8), off = kk * 1024;
+        const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
+        umma_tmem_a(d, pl + col, desc_add(vh, off), acc);
+        umma_tmem_a(d, ph + col, desc_add(vl, off), 1u);
+        umma_tmem_a(d, ph + col, desc_add(vh, off), 1u);
       }
       umma_commit(smem_u32(&v_free[vs]));
       umma_commit(smem_u32(&p_free[pb]));
@@ -441,12 +458,12 @@ __global__ void __launch_bounds__(kAThreads, 1)
 void launch_attention(const AttnLaunch& L, cudaStream_t stream) {
   PFB_CHECK_ARG(L.batch > 0 && L.M > 0 && L.L > 0 && L.d > 0, "attention: empty problem");
   PFB_CHECK_ARG(L.d <= kAD && (L.kq == 32 || L.kq == 64), "attention: head dimensions must be <= 64");
-  PFB_CHECK_ARG(L.kv >= L.L && L.kv % 32 == 0, "attention: V^T operand must cover the keys");
+  PFB_CHECK_ARG(L.kv == 32 || L.kv == 64, "attention: V operand must have 32 or 64 padded head-dim columns");
   PFB_CHECK_ARG(L.batch < (1 << 20) && L.M < (1 << 24) && L.L < (1 << 24), "attention: too large");
   PFB_CHECK_ARG(L.err && (L.c || L.o_hi) && (!L.o_hi || L.o_lo) && L.heads > 0 && L.batch % L.heads == 0,
                 "attention: null pointer or bad head count");
   PFB_CHECK_ARG(!L.o_hi || (((uintptr_t)L.o_hi | (uintptr_t)L.o_lo) & 15) == 0, "attention: operand output must be 16-byte aligned");
-  for (const void* q : {L.q_hi, (const void*)L.q_lo, L.k_hi, (const void*)L.k_lo, L.vt_hi, (const void*)L.vt_lo})
+  for (const void* q : {L.q_hi, (const void*)L.q_lo, L.k_hi, (const void*)L.k_lo, L.v_hi, (const void*)L.v_lo})
     PFB_CHECK_ARG(q && ((uintptr_t)q & 15) == 0, "attention: operands must be 16-byte aligned");
   static bool attr_set[64] = {};
   static int sms[64] = {};
@@ -464,8 +481,8 @@ void launch_attention(const AttnLaunch& L, cudaStream_t stream) {
   const CUtensorMap ql = make_operand_map(L.q_lo, prec, L.kq, L.M, L.batch, kAQ);
   const CUtensorMap kh = make_operand_map(L.k_hi, prec, L.kq, L.L, L.batch, kAK);
   const CUtensorMap kl = make_operand_map(L.k_lo, prec, L.kq, L.L, L.batch, kAK);
-  const CUtensorMap vh = make_operand_map(L.vt_hi, prec, L.kv, L.d, L.batch, kAD);
-  const CUtensorMap vl = make_operand_map(L.vt_lo, prec, L.kv, L.d, L.batch, kAD);
+  const CUtensorMap vh = make_operand_map(L.v_hi, prec, L.kv, L.L, L.batch, kAK, true);
+  const CUtensorMap vl = make_operand_map(L.v_lo, prec, L.kv, L.L, L.batch, kAK, true);
   AttnParams p;
   p.batch = (int)L.batch;
   p.M = (int)L.M;

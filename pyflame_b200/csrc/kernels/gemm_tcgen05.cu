@@ -1034,9 +1034,23 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const 
 }  // namespace
 
 // 3-D operand map [batch][rows][kpad], box (128 bytes of K) x box_rows x 1,
-// for the other tensor-core kernels.
-CUtensorMap make_operand_map(const void* base, int prec, int64_t kpad, int64_t rows, int64_t batch, int box_rows) {
-  return make_map(base, prec, kpad, rows, batch, box_rows);
+// for the other tensor-core kernels.  mn32: the 128-byte swizzle with 32-byte
+// atoms, the shared-memory layout tcgen05 reads an MN-major tf32 operand from.
+CUtensorMap make_operand_map(const void* base, int prec, int64_t kpad, int64_t rows, int64_t batch, int box_rows,
+                             bool mn32) {
+  if (!mn32) return make_map(base, prec, kpad, rows, batch, box_rows);
+  CUtensorMap m;
+  std::memset(&m, 0, sizeof m);
+  cuuint64_t dims[3] = {(cuuint64_t)kpad, (cuuint64_t)rows, (cuuint64_t)std::max<int64_t>(batch, 1)};
+  cuuint64_t strides[2] = {(cuuint64_t)(kpad * 4), (cuuint64_t)(kpad * rows * 4)};
+  cuuint32_t box[3] = {32, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  PFB_CHECK_ARG(prec == PFC_PRECISION_TF32X3, "MN-major operand maps are tf32 only");
+  CUresult r = get_encode()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) fail(PFC_ERR_CUDA, "cuTensorMapEncodeTiled (32-byte atoms) failed: " + std::to_string((int)r));
+  return m;
 }
 
 // Which A feed a convolution can use: 1 or 2 (TMA, maps built) or 0 (gather).

@@ -55,9 +55,9 @@ struct GemmLaunch {
 void launch_gemm(const GemmLaunch& L, cudaStream_t stream);
 
 // Fused attention O = softmax(alpha * Q K^T) V over batch slices (3xTF32
-// operands as prepared for the GEMM): Q [batch][M][kq], K [batch][L][kq],
-// V^T [batch][d][kv] hi/lo, K-major; O[b][m][n] at c + b*c_sb + m*c_sm + n*c_sn.
-// Needs d <= 64, kq in {32, 64}, kv >= L.  Replaces the QK^T GEMM, softmax
+// operands as prepared for the GEMM): Q [batch][M][kq], K [batch][L][kq] and
+// V [batch][L][kv] hi/lo, rows of head-dim columns (padded to kq, kv).
+// Needs d <= 64 and kq, kv in {32, 64}.  Replaces the QK^T GEMM, softmax
 // and PV GEMM that rocm_executor.cpp:278-335 and rocm_kernels.hip run as
 // separate passes for PyFlame's MultiheadAttention graphs.
 struct AttnLaunch {
@@ -66,8 +66,8 @@ struct AttnLaunch {
   const float* q_lo = nullptr;
   const void* k_hi = nullptr;
   const float* k_lo = nullptr;
-  const void* vt_hi = nullptr;
-  const float* vt_lo = nullptr;
+  const void* v_hi = nullptr;
+  const float* v_lo = nullptr;
   float alpha = 1.f;
   const float* alpha_ptr = nullptr;  // device scalar (a splat slot), overrides alpha
   // O of slice s = b*heads + h at c + b*c_sb + h*c_sh + m*c_sm + n*c_sn

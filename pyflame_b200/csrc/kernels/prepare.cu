@@ -412,6 +412,61 @@ __global__ void __launch_bounds__(1024) global_avg_cl_kernel(PoolLaunch L) {
   }
 }
 
+// Adaptive average pool to 1x1 over a dense channels-last image ([H*W][C],
+// C % 4 == 0, C <= 1024): one 256-thread CTA per image.  Thread t takes the
+// float4 of channels 4*(t % C4) of pixels t / C4, t / C4 + R, ... (R = 256 /
+// C4 pixels per pass, four loads in flight), then the R partial sums of each
+// channel combine through shared memory in a fixed order.
+__global__ void __launch_bounds__(256) global_avg_cl4_kernel(PoolLaunch L) {
+  __shared__ float4 part[256];
+  const int C4 = (int)(L.c / 4), R = 256 / C4;
+  const int t = threadIdx.x, j = t % C4, r = t / C4;
+  const long long n = blockIdx.x;
+  const int P = (int)(L.h * L.w);
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (r < R) {
+    const float4* xb = reinterpret_cast<const float4*>(L.x + n * L.sn) + j;
+    int p = r;
+    for (; p + 3 * R < P; p += 4 * R) {
+      const float4 a = xb[(long long)p * C4], b = xb[(long long)(p + R) * C4];
+      const float4 c = xb[(long long)(p + 2 * R) * C4], d = xb[(long long)(p + 3 * R) * C4];
+      s.x += a.x + b.x + c.x + d.x;
+      s.y += a.y + b.y + c.y + d.y;
+      s.z += a.z + b.z + c.z + d.z;
+      s.w += a.w + b.w + c.w + d.w;
+    }
+    for (; p < P; p += R) {
+      const float4 a = xb[(long long)p * C4];
+      s.x += a.x; s.y += a.y; s.z += a.z; s.w += a.w;
+    }
+  }
+  part[t] = s;
+  __syncthreads();
+  if (r == 0) {
+    for (int k = 1; k < R; ++k) {
+      const float4 o = part[k * C4 + j];
+      s.x += o.x; s.y += o.y; s.z += o.z; s.w += o.w;
+    }
+    const float inv = 1.f / (float)P;
+    const float out[4] = {s.x * inv, s.y * inv, s.z * inv, s.w * inv};
+    for (int q = 0; q < 4; ++q) {
+      const long long c = 4 * j + q;
+      const long long yo = n * L.osn + c * L.osc;
+      if (L.y) L.y[yo] = out[q];
+      if (L.out_hi) {
+        if (L.precision == PFC_PRECISION_BF16) {
+          ((__nv_bfloat16*)L.out_hi)[yo] = __float2bfloat16_rn(out[q]);
+        } else {
+          float hv, lv;
+          split_tf32(out[q], hv, lv);
+          ((float*)L.out_hi)[yo] = hv;
+          L.out_lo[yo] = lv;
+        }
+      }
+    }
+  }
+}
+
 __global__ void bn_fold_kernel(BnFoldLaunch L) {
   for (long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x; c < L.channels; c += (long long)gridDim.x * blockDim.x) {
     const float g = L.gamma ? L.gamma[c * L.gs] : L.gamma_c;
@@ -487,6 +542,12 @@ void launch_pool(const PoolLaunch& L, cudaStream_t stream) {
   PFB_CHECK_ARG(!L.out_hi || (L.osc == 1 && L.osw == L.c && L.osh == L.ow * L.c && L.osn == L.oh * L.ow * L.c &&
                               (L.precision == PFC_PRECISION_BF16 || L.out_lo)),
                 "pool: operand output needs a dense channels-last layout");
+  if (L.mode == 2 && L.oh == 1 && L.ow == 1 && L.sc == 1 && L.sw == L.c && L.sh == L.w * L.c && L.c % 4 == 0 &&
+      L.c <= 1024 && L.sn % 4 == 0 && ((uintptr_t)L.x & 15) == 0 && L.h * L.w < (1ll << 30) && L.n < (1ll << 31)) {
+    global_avg_cl4_kernel<<<(unsigned)L.n, 256, 0, stream>>>(L);
+    PFB_CUDA(cudaGetLastError());
+    return;
+  }
   if (L.mode == 2 && L.oh == 1 && L.ow == 1 && L.sc == 1 && L.n < 65536) {
     dim3 grid((unsigned)ceil_div(L.c, 32), (unsigned)L.n, 1);
     global_avg_cl_kernel<<<grid, 1024, 0, stream>>>(L);

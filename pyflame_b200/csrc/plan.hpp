@@ -153,13 +153,13 @@ struct BnFoldArgs {
 };
 
 // Fused attention over batch slices: Q [batch][M][kq], K [batch][L][kq] and
-// V^T [batch][d][kv] are prepared tf32 hi/lo operands; O is written to the
+// V [batch][L][kv] are prepared tf32 hi/lo operands; O is written to the
 // view c ([batch..., M, d], rank 3 or 4: slice s = (b, h) of a 4-D view is at
 // b*strides[0] + h*strides[1]).  op_hi/op_lo >= 0: O is also written as a
 // GEMM operand (hi/lo) at the same element offsets as c (then write_c says
 // whether the fp32 value is still needed).
 struct AttnArgs {
-  int q_hi = -1, q_lo = -1, k_hi = -1, k_lo = -1, vt_hi = -1, vt_lo = -1;
+  int q_hi = -1, q_lo = -1, k_hi = -1, k_lo = -1, v_hi = -1, v_lo = -1;
   int64_t batch = 1, M = 0, L = 0, d = 0, kq = 0, kv = 0;
   float alpha = 1.f;
   int alpha_slot = -1;
