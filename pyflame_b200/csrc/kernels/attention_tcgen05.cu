@@ -8,23 +8,25 @@
 // two round trips through HBM.  Here they live in tensor memory only.
 //
 // One persistent CTA per SM walks tiles of (slice, 128 query rows):
-//   warp 0     TMA: Q of the tile once, then key blocks of 64 (K, and in the
-//              second pass V) through two-stage rings.
+//   warp 0     TMA: Q of the tile once, then key blocks of 64 (K and V)
+//              through two-stage rings.
 //   warp 1     TMEM (512 columns) and the MMAs.  S = Q K_j^T goes into one of
 //              two 64-column TMEM buffers (kind::tf32 x3 from shared memory);
-//              O += P_j V_j takes P from TMEM as the A operand and V as an
-//              MN-major B operand (its rows are keys, as stored).
-//   warps 2-9  two warps per TMEM lane quarter, each taking 32 of a block's 64
-//              key columns for its 32 query rows: pass 1 reads the S blocks and
-//              keeps the running max and sum of exp (the two halves of a row
-//              combine once per tile through shared memory); pass 2 reads S
-//              again, writes P = exp(alpha*s - max) / sum as hi/lo tf32 into
-//              one of two TMEM P buffers, and at the end each warp reads and
-//              stores its half of the row of O.
-// Computing S twice keeps P exactly normalised before it meets V, so the O
-// accumulator is never rescaled.  Keys past L are masked; query rows past M
-// and head columns past d are dropped.  Every wait is bounded by the global
-// timer and reports PFC_ERR_TIMEOUT through *err.
+//              O_h += P_j,h V_j,h for the two 32-key halves h of the block takes
+//              P from TMEM as the A operand and V as an MN-major B operand (its
+//              rows are keys, as stored), into one of two O accumulators.
+//   warps 2-9  two warps per TMEM lane quarter; warp half h owns keys
+//              32h..32h+31 of every block for its 32 query rows: it reads S,
+//              keeps a running max m_h and sum l_h, and writes
+//              P = exp2(alpha*log2(e)*s - m_h) as hi/lo tf32 into one of two
+//              TMEM P buffers.  m_h moves only when a block's max exceeds it
+//              by more than 2^8 (P stays below 256); then O_h and l_h are
+//              rescaled once the previous block's P*V has retired.  At the end
+//              of a tile the halves combine, O = (O_0 a_0 + O_1 a_1) /
+//              (l_0 a_0 + l_1 a_1) with a_h = 2^(m_h - max(m_0, m_1)).
+// Keys past L are masked; query rows past M and head columns past d are
+// dropped.  Every wait is bounded by the global timer and reports
+// PFC_ERR_TIMEOUT through *err.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -58,8 +60,9 @@ constexpr int kVStage = 2 * 2 * kVChunk;    // [hi/lo][head-dim chunk]
 constexpr int kStages = 2;
 constexpr int kASmem = kQBytes + kStages * (kKStage + kVStage) + 1024 /*barriers*/ + 1024 /*align*/;
 // TMEM columns: S buffers at 0 and 64; P buffers (hi 64 | lo 64) at 128 and
-// 256; O at 384.
+// 256; O accumulators of the two key halves at 384 and 448.
 constexpr uint32_t kTS = 0, kTP = 128, kTO = 384, kATmemCols = 512;
+constexpr float kRescaleLog2 = 8.f;  // P < 2^8 between rescales
 constexpr uint32_t kIdesc = idesc(kAQ, 64, 2u);  // M 128, N 64, tf32
 constexpr uint32_t kIdescMnB = kIdesc | (1u << 16);  // ... with B MN-major
 
@@ -104,6 +107,13 @@ __device__ __forceinline__ void umma_tmem_a(uint32_t d_tmem, uint32_t a_tmem, ui
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(db), "r"(kIdescMnB), "r"(acc));
+}
+
+// Bounded wait taken by every lane of a warp, with one outcome for all of
+// them: the warp-collective TMEM accesses that follow run on all lanes or
+// none.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t a, uint32_t parity, int* err) {
+  return __all_sync(0xffffffffu, mbar_wait(a, parity, err));
 }
 
 // 32 fp32 columns of this warp's TMEM lanes
@@ -208,7 +218,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
         tma_load_3d(smem_u32(sq + c * kQChunk), &tq_hi, smem_u32(q_full), c * 32, q0, b);
         tma_load_3d(smem_u32(sq + (2 + c) * kQChunk), &tq_lo, smem_u32(q_full), c * 32, q0, b);
       }
-      for (int pass = 0; pass < 2 && ok; ++pass) {
+      {
         for (int j = 0; j < p.nblk; ++j) {
           const int s = gk & 1;
           if (gk >= 2 && !mbar_wait(smem_u32(&k_free[s]), (uint32_t)((gk >> 1) - 1) & 1u, p.err)) { ok = false; break; }
@@ -219,7 +229,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
             tma_load_3d(smem_u32(kst + (2 + c) * kKChunk), &tk_lo, smem_u32(&k_full[s]), c * 32, j * kAK, b);
           }
           ++gk;
-          if (pass == 1) {
+          {
             const int v = gv & 1;
             if (gv >= 2 && !mbar_wait(smem_u32(&v_free[v]), (uint32_t)((gv >> 1) - 1) & 1u, p.err)) { ok = false; break; }
             uint8_t* vst = sv + v * kVStage;
@@ -275,19 +285,23 @@ __global__ void __launch_bounds__(kAThreads, 1)
       if (!mbar_wait(smem_u32(&v_full[vs]), (uint32_t)(gv >> 1) & 1u, p.err)) return false;
       if (j == 0 && tc > 0 && !mbar_wait(smem_u32(o_free), (uint32_t)(tc - 1) & 1u, p.err)) return false;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t d = tmem + kTO;
       const uint32_t ph = tmem + kTP + (uint32_t)(pb * 128), pl = ph + 64;
       const uint32_t v_base = smem_u32(sv + vs * kVStage);
       // V block [64 keys][64 head dims] as two 32-column chunks: K-step kk
-      // takes keys 8kk..8kk+7 (one 1024-byte atom row group further down)
+      // takes keys 8kk..8kk+7 (one 1024-byte row group further down); keys
+      // 32h.. go to accumulator O_h
       const uint64_t vh = sdesc_mn(v_base, kVChunk), vl = sdesc_mn(v_base + 2 * kVChunk, kVChunk);
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t col = (uint32_t)(kk * 8), off = kk * 1024;
-        const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
-        umma_tmem_a(d, pl + col, desc_add(vh, off), acc);
-        umma_tmem_a(d, ph + col, desc_add(vl, off), 1u);
-        umma_tmem_a(d, ph + col, desc_add(vh, off), 1u);
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t d = tmem + kTO + (uint32_t)(h * 64);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t col = (uint32_t)(h * 32 + kk * 8), off = (uint32_t)(h * 4 + kk) * 1024u;
+          const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
+          umma_tmem_a(d, pl + col, desc_add(vh, off), acc);
+          umma_tmem_a(d, ph + col, desc_add(vl, off), 1u);
+          umma_tmem_a(d, ph + col, desc_add(vh, off), 1u);
+        }
       }
       umma_commit(smem_u32(&v_free[vs]));
       umma_commit(smem_u32(&p_free[pb]));
@@ -298,10 +312,9 @@ __global__ void __launch_bounds__(kAThreads, 1)
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
       if (!mbar_wait(smem_u32(q_full), (uint32_t)tc & 1u, p.err)) { ok = false; break; }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      for (int j = 0; j < p.nblk && ok; ++j) ok = issue_s();  // pass 1: statistics
-      // pass 2: S of the next block goes in before P V of this one, so the
-      // softmax warps work on one block while the tensor core does the other
-      if (ok) ok = issue_s();
+      // S of the next block goes in before P V of this one, so the softmax
+      // warps work on one block while the tensor core does the other
+      ok = issue_s();
       for (int j = 0; j < p.nblk && ok; ++j) {
         if (j + 1 < p.nblk) ok = issue_s();
         if (ok && j + 1 == p.nblk) umma_commit(smem_u32(q_free));  // the last S of the tile is issued
@@ -325,7 +338,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
       float v[32];
       auto read_s = [&]() -> bool {
         const int sb = gs & 1;
-        if (!mbar_wait(smem_u32(&s_full[sb]), (uint32_t)(gs >> 1) & 1u, p.err)) return false;
+        if (!mbar_wait_warp(smem_u32(&s_full[sb]), (uint32_t)(gs >> 1) & 1u, p.err)) return false;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         tmem_ld32(lane_base + kTS + (uint32_t)(sb * 64 + hf * 32), v);
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -334,7 +347,8 @@ __global__ void __launch_bounds__(kAThreads, 1)
         ++gs;
         return true;
       };
-      // pass 1: running max and sum of exp2(scale * s - max) over this half, in log2 units
+      // one pass: this half's keys, running max m (log2 units, moved lazily)
+      // and sum l of P = exp2(scale * s - m)
       for (int j = 0; j < p.nblk && ok; ++j) {
         if (!(ok = read_s())) break;
         const int nk = min(32, p.L - j * kAK - hf * 32);
@@ -342,42 +356,43 @@ __global__ void __launch_bounds__(kAThreads, 1)
 #pragma unroll
         for (int k = 0; k < 32; ++k)
           if (k < nk) bm = fmaxf(bm, v[k] * scale);
-        const float mn = fmaxf(m, bm);
-        float sum = 0.f;
+        const bool first = m == -INFINITY;
+        const bool move = bm > (first ? -INFINITY : m + kRescaleLog2);
+        const float mn = move ? bm : m;
+        if (__any_sync(0xffffffffu, move && !first && j > 0)) {
+          // O_h holds blocks up to j-1: wait for their P*V, then rescale
+          const int prev = gp - 1;
+          if (!(ok = mbar_wait_warp(smem_u32(&p_free[prev & 1]), (uint32_t)(prev >> 1) & 1u, p.err))) break;
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const float a = (move && !first) ? exp2f(m - mn) : 1.f;
+          const uint32_t oaddr = lane_base + kTO + (uint32_t)(hf * 64);
+          float o[32];
 #pragma unroll
-        for (int k = 0; k < 32; ++k)
-          if (k < nk) sum += exp2f(fmaf(v[k], scale, -mn));
-        l = (m == -INFINITY ? 0.f : l * exp2f(m - mn)) + sum;
+          for (int c = 0; c < 64; c += 32) {
+            tmem_ld32(oaddr + c, o);
+            uint32_t w[32];
+#pragma unroll
+            for (int k = 0; k < 32; ++k) w[k] = __float_as_uint(o[k] * a);
+            tmem_st16(oaddr + c, *reinterpret_cast<const uint32_t(*)[16]>(&w[0]));
+            tmem_st16(oaddr + c + 16, *reinterpret_cast<const uint32_t(*)[16]>(&w[16]));
+          }
+          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        }
+        if (move && !first) l *= exp2f(m - mn);
         m = mn;
-      }
-      // both halves of the row: combine (a half may hold no keys: max -inf, sum 0)
-      row_stat[hf][row_in_tile] = make_float2(m, l);
-      if (softmax_bar_any(!ok)) break;  // all softmax warps leave together
-      {
-        const float2 o = row_stat[hf ^ 1][row_in_tile];
-        const float mn = fmaxf(m, o.x);
-        l = (m == -INFINITY ? 0.f : l * exp2f(m - mn)) + (o.x == -INFINITY ? 0.f : o.y * exp2f(o.x - mn));
-        m = mn;
-      }
-      softmax_bar();  // row_stat is free for the next tile
-      const float inv = 1.f / l;
-      // From here a failed wait skips the rest of this tile; the warp still
-      // meets the others at the next tile's barrier, which ends the loop.
-      // pass 2: normalised P as hi/lo tf32 into TMEM
-      for (int j = 0; j < p.nblk && ok; ++j) {
-        if (!(ok = read_s())) break;
-        const int nk = min(32, p.L - j * kAK - hf * 32);
         const int pb = gp & 1;
-        if (gp >= 2 && !(ok = mbar_wait(smem_u32(&p_free[pb]), (uint32_t)((gp >> 1) - 1) & 1u, p.err))) break;
+        if (gp >= 2 && !(ok = mbar_wait_warp(smem_u32(&p_free[pb]), (uint32_t)((gp >> 1) - 1) & 1u, p.err))) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t pbase = lane_base + kTP + (uint32_t)(pb * 128 + hf * 32);
+        float sum = 0.f;
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
           uint32_t hi[16], lo[16];
 #pragma unroll
           for (int k = 0; k < 16; ++k) {
             const int kk = 16 * i + k;
-            const float pv = kk < nk ? exp2f(fmaf(v[kk], scale, -m)) * inv : 0.f;
+            const float pv = kk < nk ? exp2f(fmaf(v[kk], scale, -m)) : 0.f;
+            sum += pv;
             float h, lw;
             split_tf32(pv, h, lw);
             hi[k] = __float_as_uint(h);
@@ -386,17 +401,39 @@ __global__ void __launch_bounds__(kAThreads, 1)
           tmem_st16(pbase + 16 * i, hi);
           tmem_st16(pbase + 64 + 16 * i, lo);
         }
+        l += sum;
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&p_full[pb]));
         ++gp;
       }
+      // the two halves of the row: weights a_h = 2^(m_h - m) (0 for a half without keys)
+      row_stat[hf][row_in_tile] = make_float2(m, l);
+      if (softmax_bar_any(!ok)) break;  // all softmax warps leave together
+      float a_self, a_other, inv;
+      {
+        const float2 o = row_stat[hf ^ 1][row_in_tile];
+        const float mx = fmaxf(m, o.x);
+        a_self = m == -INFINITY ? 0.f : exp2f(m - mx);
+        a_other = o.x == -INFINITY ? 0.f : exp2f(o.x - mx);
+        inv = 1.f / (l * a_self + o.y * a_other);
+      }
+      softmax_bar();  // row_stat is free for the next tile
+      const float a0 = (hf == 0 ? a_self : a_other) * inv, a1 = (hf == 0 ? a_other : a_self) * inv;
+      // From here a failed wait skips the rest of this tile; the warp still
+      // meets the others at the next tile's barrier, which ends the loop.
       if (!ok) continue;
       // this warp's half of the output row
-      if (!(ok = mbar_wait(smem_u32(o_full), (uint32_t)tc & 1u, p.err))) continue;
+      if (!(ok = mbar_wait_warp(smem_u32(o_full), (uint32_t)tc & 1u, p.err))) continue;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      tmem_ld32(lane_base + kTO + (uint32_t)(hf * 32), v);
+      {
+        float o1[32];
+        tmem_ld32(lane_base + kTO + (uint32_t)(hf * 32), v);        // O_0, this warp's 32 columns
+        tmem_ld32(lane_base + kTO + 64u + (uint32_t)(hf * 32), o1);  // O_1, the same columns
+#pragma unroll
+        for (int n = 0; n < 32; ++n) v[n] = v[n] * a0 + o1[n] * a1;
+      }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(o_free));
