@@ -330,7 +330,25 @@ __global__ void pool_cl_kernel(PoolLaunch L) {
       const int ws = ow * (int)L.stride_w - (int)L.pad_w;
       const int w0 = max(ws, 0), w1 = min(ws + (int)L.kw, W);
       float r[4];
-      if (L.mode == 0) {
+      if (L.mode == 0 && h1 - h0 == 3 && w1 - w0 == 3) {
+        // a whole 3x3 window: all nine loads in flight, then the same
+        // NaN-aware max in the same (h, w) order
+        const float* base = xb + h0 * sh + w0 * sw + c;
+        float4 v4[9];
+#pragma unroll
+        for (int a = 0; a < 3; ++a)
+#pragma unroll
+          for (int e = 0; e < 3; ++e) v4[a * 3 + e] = *reinterpret_cast<const float4*>(base + a * sh + e * sw);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) r[j] = -__int_as_float(0x7f800000);
+#pragma unroll
+        for (int k = 0; k < 9; ++k) {
+          const float v[4] = {v4[k].x, v4[k].y, v4[k].z, v4[k].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (v[j] > r[j] || isnan(v[j])) r[j] = v[j];
+        }
+      } else if (L.mode == 0) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) r[j] = -__int_as_float(0x7f800000);
         for (int h = h0; h < h1; ++h)
