@@ -343,6 +343,14 @@ PFC_API int pfk_pool2d(const float* x, float* y, const pfk_pool_params* p, void*
 PFC_API int pfk_matmul_tf32x3_static(const float* a, const float* b, float* c, int64_t M, int64_t N,
                                      int64_t K, int* err, void* stream);
 
+/* Self-check of the failure path every tensor-core kernel shares: launches
+ * one CTA whose mbarrier wait can never complete, bounded by the global timer
+ * like all device waits here; after `limit_us` (at most 5 s) it records
+ * PFC_ERR_TIMEOUT in the device int *err (left as is if already non-zero)
+ * and the kernel returns.  Nothing faults or hangs and the context stays
+ * usable.  No counterpart in the reference. */
+PFC_API int pfk_check_bounded_wait(int* err, int64_t limit_us, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -105,6 +105,7 @@ SIGNATURES = {
     "pfk_im2col": (C.c_int, [_P] + [_I64] * 18 + [_P, _P, _P, _I64, _P]),
     "pfk_pool2d": (C.c_int, [_P, _P, C.POINTER(PoolParamsC), _P]),
     "pfk_matmul_tf32x3_static": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, _P]),
+    "pfk_check_bounded_wait": (C.c_int, [_P, _I64, _P]),
 }
 
 _lib = None

@@ -410,6 +410,10 @@ int pfc_executor_last_profile(pfc_executor* ex, char (*names)[64], double* ms, i
 }
 
 // ---- kernel entry points ---------------------------------------------------------
+int pfk_check_bounded_wait(int* err, int64_t limit_us, void* stream) {
+  return guarded([&] { pfb::launch_wait_check(err, limit_us, (cudaStream_t)stream); });
+}
+
 int pfk_split_tf32(const float* src, int64_t batch, int64_t rows, int64_t cols, int64_t sb, int64_t sr, int64_t sk,
                    float* hi, float* lo, int64_t kpad, void* stream) {
   return guarded([&] {

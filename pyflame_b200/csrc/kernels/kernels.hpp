@@ -80,6 +80,10 @@ struct AttnLaunch {
 };
 void launch_attention(const AttnLaunch& L, cudaStream_t stream);
 
+// One CTA whose bounded mbarrier wait can never complete: after limit_us it
+// records PFC_ERR_TIMEOUT in *err and returns (a test of the failure path).
+void launch_wait_check(int* err, int64_t limit_us, cudaStream_t stream);
+
 // Channels-last copy of a Conv2d input for the implicit GEMM: x is a strided
 // [N,C,H,W] view; output [N][H][W][Cp] (Cp >= C, zero channels above C) as
 // tf32x3 hi/lo fp32 pairs, or bf16 in hi when precision is bf16.

@@ -42,19 +42,23 @@ __device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: false (and *err set) if the phase did not complete in time.
-__device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, int* err) {
+// Bounded wait: false (and *err set) if the phase did not complete within
+// limit_ns, or if another thread already recorded an error.
+__device__ __forceinline__ bool mbar_wait_for(uint32_t a, uint32_t parity, int* err, unsigned long long limit_ns) {
   if (mbar_try(a, parity)) return true;
   unsigned long long t0 = gtimer();
   while (true) {
     for (int i = 0; i < 128; ++i)
       if (mbar_try(a, parity)) return true;
     if (*(volatile int*)err != 0) return false;
-    if (gtimer() - t0 > kWaitNs) {
+    if (gtimer() - t0 > limit_ns) {
       atomicCAS(err, 0, PFC_ERR_TIMEOUT);
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, int* err) {
+  return mbar_wait_for(a, parity, err, kWaitNs);
 }
 
 // Wait for this CTA's own asynchronous work (copies in flight, issued MMAs)
