@@ -256,11 +256,13 @@ def test_gemm_bf16_mode(oracle_mod, rng, native):
 
 
 def test_conv2d_bf16_mode(oracle_mod, rng, native):
-    """bf16 operands through the halo-staged 3x3 (64-channel blocks) and the
-    TMA-window 7x7 / 2 (few channels)."""
+    """bf16 operands through the halo-staged 3x3 (64-channel blocks), the
+    TMA-window 7x7 / 2 (few channels) and TMA boxes (64 channels per k-block)
+    with 128- and 64-column tiles."""
     ex = pf.CudaExecutor(pf.CudaExecutor.Config(precision="bf16"))
     outs = []
-    for c, o, k, s, p, hw in [(64, 64, 3, 1, 1, (14, 18)), (3, 16, 7, 2, 3, (40, 40))]:
+    for c, o, k, s, p, hw in [(64, 64, 3, 1, 1, (14, 18)), (3, 16, 7, 2, 3, (40, 40)), (64, 128, 3, 1, 1, (16, 40)),
+                              (64, 64, 3, 1, 1, (12, 36))]:
         x = rng.random((2, c) + hw).astype(np.float32)
         conv = nn.Conv2d(c, o, k, s, p)
         conv.set_parameter("weight", (rng.standard_normal((o, c, k, k)) / np.sqrt(c * k * k)).astype(np.float32))
@@ -290,7 +292,10 @@ def test_conv2d_bf16_mode(oracle_mod, rng, native):
                                  dict(n=3, c=64, h=20, w=30, o=64, k=3, s=1, p=1),
                                  dict(n=2, c=32, h=25, w=21, o=48, k=3, s=1, p=2, d=2),
                                  dict(n=2, c=96, h=9, w=13, o=80, k=1, s=1, p=0),
-                                 dict(n=2, c=32, h=12, w=14, o=64, k=5, s=1, p=2)])
+                                 dict(n=2, c=32, h=12, w=14, o=64, k=5, s=1, p=2),
+                                 # TMA boxes with 128-column tiles: 128 channels; 192 (a partial tile)
+                                 dict(n=2, c=64, h=20, w=40, o=128, k=3, s=1, p=1),
+                                 dict(n=1, c=32, h=18, w=37, o=192, k=3, s=1, p=1)])
 def test_conv2d(cuda_executor, oracle_mod, rng, cfg):
     x = rng.random((cfg["n"], cfg["c"], cfg["h"], cfg["w"])).astype(np.float32)
     conv = nn.Conv2d(cfg["c"], cfg["o"], cfg["k"], cfg["s"], cfg["p"], cfg.get("d", 1))
