@@ -97,6 +97,51 @@ class ClockSampler:
         self.gpu = gpu
         self.proc = None
         self.lines = []
+        self.nvml = []  # (sm MHz, max MHz, clock-event reason bits) read in-process
+        self._stop = threading.Event()
+        self._poller = None
+
+    # NVML clock-event reason bits (nvml.h: nvmlClocksEventReason*)
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40}
+
+    def start_polling(self):
+        """Read the SM clock and clock-event reasons through NVML about every
+        half millisecond until stop_polling(): a timed region of a few
+        milliseconds still gets samples (nvidia-smi's own interval is 50 ms).
+        Read-only queries; no GPU setting is touched."""
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            try:
+                # the CUDA device's own NVML handle (NVML ignores CUDA_VISIBLE_DEVICES)
+                pr = torch.cuda.get_device_properties(self.gpu)
+                h = pynvml.nvmlDeviceGetHandleByPciBusId(
+                    f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0".encode())
+            except Exception:
+                h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        except Exception:
+            return
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    self.nvml.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), mx, reasons(h)))
+                except Exception:
+                    return
+                time.sleep(0.0005)
+
+        self._poller = threading.Thread(target=run, daemon=True)
+        self._poller.start()
+
+    def stop_polling(self):
+        self._stop.set()
+        if self._poller:
+            self._poller.join(timeout=2)
 
     def __enter__(self):
         try:
@@ -143,6 +188,12 @@ class ClockSampler:
                 continue
             for n, v in zip(names, f[5:9]):
                 if v.lower() == "active":
+                    reasons.add(n)
+        for clk, cmax, bits in self.nvml:
+            sm.append(float(clk))
+            mx = max(mx, float(cmax))
+            for n, b in self.REASON_BITS.items():
+                if bits & b:
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
                 "reasons": sorted(reasons), "samples": len(sm)}
@@ -230,11 +281,13 @@ def run_ours(args):
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     with ClockSampler(local) as clk:
         clk.wait_first_sample()
+        clk.start_polling()
         ev[0].record(stream)
         for i in range(args.steps):
             step()
             ev[i + 1].record(stream)
         torch.cuda.synchronize()
+        clk.stop_polling()
     per_step = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
     total_ms = ev[0].elapsed_time(ev[-1])
     if world > 1:
