@@ -262,7 +262,7 @@ def test_conv2d_bf16_mode(oracle_mod, rng, native):
     ex = pf.CudaExecutor(pf.CudaExecutor.Config(precision="bf16"))
     outs = []
     for c, o, k, s, p, hw in [(64, 64, 3, 1, 1, (14, 18)), (3, 16, 7, 2, 3, (40, 40)), (64, 128, 3, 1, 1, (16, 40)),
-                              (64, 64, 3, 1, 1, (12, 36))]:
+                              (64, 64, 3, 1, 1, (12, 36)), (64, 192, 3, 1, 1, (10, 33))]:
         x = rng.random((2, c) + hw).astype(np.float32)
         conv = nn.Conv2d(c, o, k, s, p)
         conv.set_parameter("weight", (rng.standard_normal((o, c, k, k)) / np.sqrt(c * k * k)).astype(np.float32))
