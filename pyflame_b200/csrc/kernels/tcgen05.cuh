@@ -61,6 +61,24 @@ __device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, int* err)
   return mbar_wait_for(a, parity, err, kWaitNs);
 }
 
+// Bounded wait for a role off the critical path (an epilogue waiting for its
+// accumulator): sleeps between tries instead of spinning, which leaves the
+// SMSP's issue slots to the warps that share it (the MMA issuer among them).
+// Same outcome as mbar_wait: false (and *err set) on timeout or a recorded error.
+__device__ __forceinline__ bool mbar_wait_backoff(uint32_t a, uint32_t parity, int* err) {
+  if (mbar_try(a, parity)) return true;
+  const unsigned long long t0 = gtimer();
+  while (true) {
+    __nanosleep(256);
+    if (mbar_try(a, parity)) return true;
+    if (*(volatile int*)err != 0) return false;
+    if (gtimer() - t0 > kWaitNs) {
+      atomicCAS(err, 0, PFC_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // Wait for this CTA's own asynchronous work (copies in flight, issued MMAs)
 // before its shared memory or TMEM goes away: bounded by time only, even when
 // another role already recorded an error.
