@@ -47,7 +47,8 @@ FULL = {
     "convstack": dict(batch=256),
 }
 # micro-batches of the end-to-end host-buffer measurement (execute_streamed)
-E2E_CHUNKS = {"fused": 8, "mlp": 1, "gemm_chain": 4, "encoder": 4, "convstack": 8}
+# chunks of the batch in the streamed e2e measurement, each the best of 2/4/8 measured on B200
+E2E_CHUNKS = {"fused": 8, "mlp": 1, "gemm_chain": 8, "encoder": 2, "convstack": 8}
 # CPU-baseline samples (bounded, seconds of CPU work)
 CPU_SAMPLE = {
     "fused": dict(rows=8192, cols=4096),
