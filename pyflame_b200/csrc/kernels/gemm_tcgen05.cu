@@ -200,6 +200,30 @@ __device__ __forceinline__ void store_block(const GemmParams& p, const float* ep
     }
     return;
   }
+  if (!MAPPED && full_n && vec_c && vec_r && nvalid == 32 && rbase) {
+    // whole block with a float4 residual: all four residual loads in flight
+    // before the first store (one memory latency per block, not four)
+    const long long c0 = (m_base + rsub) * p.c_sm + n, cstep = 8 * p.c_sm;
+    const long long r0 = (m_base + rsub) * p.r_sm + n, rstep = 8 * p.r_sm;
+    const long long o0 = ohi ? op_offset(p, m_base + rsub, n) : 0, ostep = 8 * p.o_sm;
+    float4 r[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) r[k] = *reinterpret_cast<const float4*>(rbase + r0 + k * rstep);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float v[4] = {a[k].x, a[k].y, a[k].z, a[k].w};
+      const float rr[4] = {r[k].x, r[k].y, r[k].z, r[k].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[j] = v[j] * sc[j];
+        if (has_shift) v[j] = v[j] + sh[j];
+        v[j] = act_apply<ACT>(v[j]) + rr[j];
+      }
+      if (cbase) *reinterpret_cast<float4*>(cbase + c0 + k * cstep) = make_float4(v[0], v[1], v[2], v[3]);
+      if (ohi) store_operand4<PREC>(ohi, olo, o0 + k * ostep, v);
+    }
+    return;
+  }
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     long long row = m_base + 8 * k + rsub;
