@@ -976,9 +976,16 @@ std::string gen_row(const RowSpec& rs, const std::string& name, int num_sms, int
             << "[off + q * (" << ity << ")" << st.back() << "] = y[q];\n";
       }
       if (op.op_hi >= 0) {
-        // dense row-major `out`: the operand element shares its offset
-        o << "          for (int q = 0; q < " << VEC << "; ++q) if (cl + q < (" << ity << ")" << L.C
-          << ") { float h, l; pf_split(y[q], h, l); oph" << r << "[off + q] = h; opl" << r << "[off + q] = l; }\n";
+        // dense row-major `out`: the operand element shares its offset.  With
+        // whole, 16-byte aligned 4-element chunks (as the float4 store of `out`
+        // above needs) hi and lo go out as one float4 each, not eight scalars.
+        if (VEC == 4 && st.back() == 1)
+          o << "          { float4 h4, l4;\n            pf_split(y[0], h4.x, l4.x); pf_split(y[1], h4.y, l4.y);\n"
+            << "            pf_split(y[2], h4.z, l4.z); pf_split(y[3], h4.w, l4.w);\n            *(float4*)(oph" << r
+            << " + off) = h4;\n            *(float4*)(opl" << r << " + off) = l4; }\n";
+        else
+          o << "          for (int q = 0; q < " << VEC << "; ++q) if (cl + q < (" << ity << ")" << L.C
+            << ") { float h, l; pf_split(y[q], h, l); oph" << r << "[off + q] = h; opl" << r << "[off + q] = l; }\n";
       }
       o << "        } }\n";
     }
