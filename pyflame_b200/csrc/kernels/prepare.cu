@@ -101,6 +101,32 @@ __global__ void prepare_vec4(const float* __restrict__ src, View6 v, long long r
   }
 }
 
+// Dense row-major source with kpad == K: the operand is the source split
+// element for element, one float4 per thread step and no index arithmetic
+// (the general path's 64-bit row/column divisions made it instruction-bound).
+template <int PREC>
+__global__ void prepare_flat4(const float4* __restrict__ src, long long n4, void* __restrict__ hi,
+                              float* __restrict__ lo) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    const float4 x = src[i];
+    if constexpr (PREC == PFC_PRECISION_BF16) {
+      __nv_bfloat162 a = __floats2bfloat162_rn(x.x, x.y), b = __floats2bfloat162_rn(x.z, x.w);
+      uint2 pk;
+      pk.x = *(uint32_t*)&a;
+      pk.y = *(uint32_t*)&b;
+      reinterpret_cast<uint2*>(hi)[i] = pk;
+    } else {
+      float4 h, l;
+      split_tf32(x.x, h.x, l.x);
+      split_tf32(x.y, h.y, l.y);
+      split_tf32(x.z, h.z, l.z);
+      split_tf32(x.w, h.w, l.w);
+      reinterpret_cast<float4*>(hi)[i] = h;
+      reinterpret_cast<float4*>(lo)[i] = l;
+    }
+  }
+}
+
 // Transposed source: the last row dim is contiguous (stride 1) and K is
 // strided.  32x32 tiles through shared memory keep both sides coalesced.
 template <int PREC>
@@ -524,7 +550,20 @@ void launch_prepare(const PrepLaunch& L, cudaStream_t stream) {
   bool vec = sk == 1 && K % 4 == 0 && ((uintptr_t)L.src & 15) == 0;
   for (int d = 0; d + 1 < v.rank && vec; ++d) vec = (v.stride[d] % 4) == 0 || v.shape[d] == 1;
   const bool trans = !vec && sk != 1 && v.stride[v.rank - 2] == 1 && v.shape[v.rank - 2] > 1;
-  if (vec) {
+  bool dense = vec && L.kpad == K;
+  {
+    long long expect = K;
+    for (int d = v.rank - 2; d >= 0 && dense; --d) {
+      if (v.shape[d] != 1 && v.stride[d] != expect) dense = false;
+      expect *= v.shape[d];
+    }
+  }
+  if (dense) {
+    const long long n4 = rows * K / 4;
+    unsigned g = grid_for(n4, 256);
+    if (bf) prepare_flat4<PFC_PRECISION_BF16><<<g, 256, 0, stream>>>((const float4*)L.src, n4, L.hi, L.lo);
+    else prepare_flat4<PFC_PRECISION_TF32X3><<<g, 256, 0, stream>>>((const float4*)L.src, n4, L.hi, L.lo);
+  } else if (vec) {
     unsigned g = grid_for(rows * (L.kpad / 4), 256);
     if (bf) prepare_vec4<PFC_PRECISION_BF16><<<g, 256, 0, stream>>>(L.src, v, rows, L.kpad, L.hi, L.lo);
     else prepare_vec4<PFC_PRECISION_TF32X3><<<g, 256, 0, stream>>>(L.src, v, rows, L.kpad, L.hi, L.lo);
