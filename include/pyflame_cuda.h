@@ -182,6 +182,8 @@ typedef struct pfc_execution_result {
     double compute_time_ms;
     double total_time_ms;
     int64_t kernel_launches; /* device launches issued by this call */
+    uint64_t h2d_bytes;      /* host->device bytes this call copied (inputs, constants not yet resident) */
+    uint64_t d2h_bytes;      /* device->host bytes this call copied (outputs) */
 } pfc_execution_result;
 
 /* rocm::MemoryStats (rocm_memory.hpp:14-21) */
@@ -328,13 +330,14 @@ typedef struct pfk_pool_params {
 } pfk_pool_params;
 PFC_API int pfk_pool2d(const float* x, float* y, const pfk_pool_params* p, void* stream);
 
-/* C[M,N] = A[M,K] @ B[K,N] (fp32, row-major; MATMUL as matmul.cpp:12-31) on
- * the 3xTF32 tcgen05 GEMM, allocating nothing: the split operands and the
- * wait-timeout flag live in a fixed 64 MiB device array inside the library
- * (one per device), for hosts that cannot grant the library device memory or
- * must not call cudaMalloc/cudaFree on this path.  No counterpart in the
- * reference (its kernels take caller-allocated buffers, rocm_kernels.hip:740-806).
- * Needs 256 + 2*ru(4*M*Kp) + 2*ru(4*N*Kp) bytes, Kp = K rounded up to 32,
+/* C[M,N] = A[M,K] @ B[K,N], all fp32 dense row-major, on the 3xTF32 tcgen05
+ * GEMM, allocating nothing: the split operands and the wait-timeout flag live
+ * in a fixed 64 MiB device array inside the library (one per device), for
+ * hosts that cannot grant the library device memory or must not call
+ * cudaMalloc/cudaFree on this path.  It has no counterpart in the reference.
+ * The array occupies 64 MiB on every device once this library's device code
+ * is loaded there (under CUDA_MODULE_LOADING=EAGER, at context creation),
+ * whether or not this entry point is ever called.  Needs 256 + 2*ru(4*M*Kp) + 2*ru(4*N*Kp) bytes, Kp = K rounded up to 32,
  * ru = round up to 256; larger problems return PFC_ERR_INVALID_ARGUMENT.
  * All calls share the array, so overlapping calls race: serialise them (one
  * stream).  The first call on a device sets up the array's address; make it

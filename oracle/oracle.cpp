@@ -103,14 +103,17 @@ struct Tensor {
   std::vector<T> v;
 };
 
-// Worker threads: ORACLE_THREADS, else every hardware thread.
+// Worker threads of the calling host thread: set by orc_set_threads (per
+// host thread, so concurrent callers can each ask for one), else
+// ORACLE_THREADS, else every hardware thread.
+thread_local int tl_threads = 0;
 int oracle_threads() {
   static int n = [] {
     const char* e = std::getenv("ORACLE_THREADS");
     int v = e ? std::atoi(e) : (int)std::thread::hardware_concurrency();
     return v > 0 ? v : 1;
   }();
-  return n;
+  return tl_threads > 0 ? tl_threads : n;
 }
 
 // Runs f(i) for i in [0, n) on contiguous chunks; each i runs exactly once,
@@ -267,12 +270,17 @@ class Eval {
       // constants / inputs / parameters: payload or zeros (the ROCm executor zero-fills, rocm_executor.cpp:99-102)
       out.v.assign(n.numel(), T(0));
       if (n.has_data) {
+        const int64_t ne = n.numel(), blk = 1 << 16;
         if (n.dtype == 0) {
           const float* p = (const float*)n.data.data();
-          for (int64_t i = 0; i < n.numel(); ++i) out.v[i] = (T)p[i];
+          parallel_for((ne + blk - 1) / blk, [&](int64_t b) {
+            for (int64_t i = b * blk; i < std::min(ne, (b + 1) * blk); ++i) out.v[i] = (T)p[i];
+          });
         } else if (n.dtype == 7) {
           const double* p = (const double*)n.data.data();
-          for (int64_t i = 0; i < n.numel(); ++i) out.v[i] = (T)p[i];
+          parallel_for((ne + blk - 1) / blk, [&](int64_t b) {
+            for (int64_t i = b * blk; i < std::min(ne, (b + 1) * blk); ++i) out.v[i] = (T)p[i];
+          });
         } else {
           throw std::runtime_error("oracle evaluates float32/float64 payloads only");
         }
@@ -284,7 +292,10 @@ class Eval {
         op == LAYOUT_TRANSFORM) {
       const auto& x = in(n, 0);
       out.v.resize(x.v.size());
-      for (size_t i = 0; i < x.v.size(); ++i) out.v[i] = unary<T>(op, x.v[i]);
+      const int64_t ne = (int64_t)x.v.size(), blk = 1 << 14;
+      parallel_for((ne + blk - 1) / blk, [&](int64_t b) {
+        for (int64_t i = b * blk; i < std::min(ne, (b + 1) * blk); ++i) out.v[i] = unary<T>(op, x.v[i]);
+      });
       return out;
     }
     if ((op >= 100 && op < 200) || (op >= 800 && op <= 806) || op == MAXIMUM || op == MINIMUM) {
@@ -296,7 +307,10 @@ class Eval {
       auto ia = bcast_index<T>(a.shape, os), ib = bcast_index<T>(b.shape, os);
       out.shape = os;
       out.v.resize(prod(os));
-      for (size_t i = 0; i < out.v.size(); ++i) out.v[i] = binary<T>(op, a.v[ia[i]], b.v[ib[i]]);
+      const int64_t ne = (int64_t)out.v.size(), blk = 1 << 14;
+      parallel_for((ne + blk - 1) / blk, [&](int64_t bk) {
+        for (int64_t i = bk * blk; i < std::min(ne, (bk + 1) * blk); ++i) out.v[i] = binary<T>(op, a.v[ia[i]], b.v[ib[i]]);
+      });
       return out;
     }
     switch (op) {
@@ -485,13 +499,14 @@ class Eval {
   // (2-D) / batch_matmul_cpu (matmul.cpp:124-145); shapes per infer_matmul_spec
   // (shape_inference.hpp:146-217) including broadcast batch dims and 1-D operands.
   Tensor<T> matmul(const Node& n) {
-    Tensor<T> a = in(n, 0), b = in(n, 1);
-    bool a1 = a.shape.size() == 1, b1 = b.shape.size() == 1;
-    if (a1) a.shape.insert(a.shape.begin(), 1);
-    if (b1) b.shape.push_back(1);
-    int64_t M = a.shape[a.shape.size() - 2], K = a.shape.back(), N = b.shape.back();
-    if (b.shape[b.shape.size() - 2] != K) throw std::runtime_error("matmul: inner dimensions don't match");
-    std::vector<int64_t> ab(a.shape.begin(), a.shape.end() - 2), bb(b.shape.begin(), b.shape.end() - 2);
+    const Tensor<T>& a = in(n, 0);
+    const Tensor<T>& b = in(n, 1);
+    std::vector<int64_t> as = a.shape, bs = b.shape;
+    if (as.size() == 1) as.insert(as.begin(), 1);
+    if (bs.size() == 1) bs.push_back(1);
+    int64_t M = as[as.size() - 2], K = as.back(), N = bs.back();
+    if (bs[bs.size() - 2] != K) throw std::runtime_error("matmul: inner dimensions don't match");
+    std::vector<int64_t> ab(as.begin(), as.end() - 2), bb(bs.begin(), bs.end() - 2);
     std::vector<int64_t> batch = bcast(ab, bb);
     int64_t B = prod(batch);
     auto ia = bcast_index<T>(ab.empty() ? std::vector<int64_t>{1} : ab, batch.empty() ? std::vector<int64_t>{1} : batch);
@@ -621,16 +636,19 @@ class Eval {
     std::swap(out.shape[d0], out.shape[d1]);
     auto ost = strides_of(out.shape);
     out.v.resize(x.v.size());
-    for (int64_t l = 0; l < (int64_t)out.v.size(); ++l) {
-      int64_t rem = l, src = 0;
-      for (int d = 0; d < nd; ++d) {
-        int64_t c = rem / ost[d];
-        rem %= ost[d];
-        int sd = d == d0 ? d1 : (d == d1 ? d0 : d);
-        src += c * ist[sd];
+    const int64_t ne = (int64_t)out.v.size(), blk = 1 << 14;
+    parallel_for((ne + blk - 1) / blk, [&](int64_t b) {
+      for (int64_t l = b * blk; l < std::min(ne, (b + 1) * blk); ++l) {
+        int64_t rem = l, src = 0;
+        for (int d = 0; d < nd; ++d) {
+          int64_t c = rem / ost[d];
+          rem %= ost[d];
+          int sd = d == d0 ? d1 : (d == d1 ? d0 : d);
+          src += c * ist[sd];
+        }
+        out.v[l] = x.v[src];
       }
-      out.v[l] = x.v[src];
-    }
+    });
     return out;
   }
 
@@ -761,5 +779,7 @@ int orc_execute(void* gp, const uint64_t* ids, int n, void* const* outs, int pre
 }
 
 int orc_num_threads(void) { return oracle_threads(); }
+// Worker threads for later calls from the calling host thread (0: the default).
+void orc_set_threads(int n) { tl_threads = n > 0 ? n : 0; }
 
 }  // extern "C"

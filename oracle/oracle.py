@@ -16,6 +16,7 @@ module.
 from __future__ import annotations
 
 import ctypes as C
+import os
 import subprocess
 from pathlib import Path
 from typing import Dict, Sequence
@@ -30,12 +31,14 @@ _lib = None
 _ref = None
 
 
-def build(with_reference: bool = True) -> None:
-    """Compile liboracle.so (and the reference shim when the reference
-    sources are present)."""
+def build(with_reference: bool = True, reference_tree: str = "") -> None:
+    """Compile liboracle.so, and the reference shim when a PyFlame source
+    tree is given (`reference_tree`, else the PYFLAME_REFERENCE environment
+    variable) and present."""
     subprocess.run(["make", "-s", "-C", str(HERE), "all"], check=True)
-    if with_reference and Path("/root/reference/src").exists():
-        subprocess.run(["make", "-s", "-j8", "-C", str(HERE), "ref"], check=True)
+    tree = reference_tree or os.environ.get("PYFLAME_REFERENCE", "")
+    if with_reference and tree and Path(tree, "src").exists():
+        subprocess.run(["make", "-s", "-j8", "-C", str(HERE), "ref", f"REF={tree}"], check=True)
 
 
 def lib():
@@ -117,6 +120,14 @@ def num_threads() -> int:
     L = lib()
     L.orc_num_threads.restype = C.c_int
     return L.orc_num_threads()
+
+
+def set_threads(n: int) -> None:
+    """Worker threads of later oracle calls made from the calling Python
+    thread (0 restores the default: ORACLE_THREADS or every host thread)."""
+    L = lib()
+    L.orc_set_threads.argtypes = [C.c_int]
+    L.orc_set_threads(int(n))
 
 
 class Reference:

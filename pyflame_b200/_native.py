@@ -40,7 +40,7 @@ class ExecutorConfigC(C.Structure):
 class ExecutionResultC(C.Structure):
     _fields_ = [("success", C.c_int), ("error_message", C.c_char * 1024), ("compile_time_ms", C.c_double),
                 ("transfer_time_ms", C.c_double), ("compute_time_ms", C.c_double), ("total_time_ms", C.c_double),
-                ("kernel_launches", C.c_int64)]
+                ("kernel_launches", C.c_int64), ("h2d_bytes", C.c_uint64), ("d2h_bytes", C.c_uint64)]
 
 
 class MemoryStatsC(C.Structure):

@@ -59,6 +59,8 @@ class ExecutionResult:
     total_time_ms: float = 0.0
     outputs: Dict[int, np.ndarray] = field(default_factory=dict)
     kernel_launches: int = 0
+    h2d_bytes: int = 0   # host->device bytes the call copied (inputs, constants not yet resident)
+    d2h_bytes: int = 0   # device->host bytes the call copied (outputs)
 
 
 @dataclass
@@ -268,6 +270,7 @@ class CudaExecutor:
             res.compile_time_ms, res.transfer_time_ms = r.compile_time_ms, r.transfer_time_ms
             res.compute_time_ms, res.total_time_ms = r.compute_time_ms, r.total_time_ms
             res.kernel_launches = r.kernel_launches
+            res.h2d_bytes, res.d2h_bytes = r.h2d_bytes, r.d2h_bytes
             if rc != 0:
                 res.success = False
                 res.error_message = r.error_message.decode(errors="replace")
@@ -296,7 +299,8 @@ class CudaExecutor:
         r = N.ExecutionResultC()
         N.check(N.lib().pfc_executor_execute_device(self.handle, ng.handle, in_ids, k_in, in_p, out_ids, k_out,
                                                     out_p, C.c_void_p(stream or None), C.byref(r)))
-        return ExecutionResult(True, "", r.compile_time_ms, 0.0, 0.0, r.total_time_ms, {}, r.kernel_launches)
+        return ExecutionResult(True, "", r.compile_time_ms, 0.0, 0.0, r.total_time_ms, {}, r.kernel_launches,
+                               r.h2d_bytes, r.d2h_bytes)
 
     def execute_streamed(self, chunk_graph: Graph, inputs: Dict[int, np.ndarray], output_ids: Sequence[int],
                          outputs: Sequence[np.ndarray]) -> ExecutionResult:
@@ -333,7 +337,7 @@ class CudaExecutor:
         N.check(N.lib().pfc_executor_execute_streamed(self.handle, ng.handle, in_ids, k_in, in_p, out_ids, k_out,
                                                       out_p, int(n_chunks or 0), C.byref(r)))
         return ExecutionResult(True, "", r.compile_time_ms, r.transfer_time_ms, r.compute_time_ms, r.total_time_ms,
-                               {}, r.kernel_launches)
+                               {}, r.kernel_launches, r.h2d_bytes, r.d2h_bytes)
 
     def get_device_info(self) -> DeviceInfo:
         i = N.DeviceInfo()

@@ -340,7 +340,7 @@ int pfc_executor_get_memory_stats(pfc_executor* ex, pfc_memory_stats* stats) {
 int pfc_executor_release_constants(pfc_executor* ex) {
   return guarded([&] {
     PFB_CHECK_ARG(ex, "null executor");
-    ex->ex->release_constants();
+    PFB_CUDA(ex->ex->release_constants());
   });
 }
 

@@ -3,6 +3,7 @@
 
 #include <cstdint>
 #include <cstdio>
+#include <mutex>
 #include <stdexcept>
 #include <string>
 
@@ -40,5 +41,27 @@ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline int64_t round_up(int64_t a, int64_t b) { return ceil_div(a, b) * b; }
 
 void set_last_error(const std::string& msg);
+
+// The calling thread's current device, checked (kernel set-up caches are
+// indexed by it and hold 64 devices).
+inline int current_device() {
+  int dev = 0;
+  PFB_CUDA(cudaGetDevice(&dev));
+  PFB_CHECK_ARG(dev >= 0 && dev < 64, "device index above 63");
+  return dev;
+}
+
+// Multiprocessor count of `dev`, queried once per device under std::call_once,
+// so host threads launching at the same time never read a half-written entry.
+inline int device_sm_count(int dev) {
+  static std::once_flag once[64];
+  static int sms[64];
+  std::call_once(once[dev & 63], [dev] {
+    int v = 0;
+    PFB_CUDA(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev));
+    sms[dev & 63] = v > 0 ? v : 148;
+  });
+  return sms[dev & 63];
+}
 
 }  // namespace pfb

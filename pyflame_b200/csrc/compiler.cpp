@@ -198,15 +198,40 @@ __device__ __forceinline__ float pf_div(float a, float b) {
   return a / b;
 }
 __device__ __forceinline__ float pf_relu(float x) { return (0.f < x) ? x : 0.f; }
-// Sigmoid and SiLU use the hardware exp2 and reciprocal approximations
-// (__expf, __fdividef): within about 1e-6 relative of 1/(1+exp(-x)) for
-// |x| <= 20 and exact at the limits (0, 1, NaN); the chain is a third of the
-// correctly rounded expf and division, which row kernels are bound by.
-__device__ __forceinline__ float pf_sigmoid(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+// exp(y) from the hardware exp2 (ex2.approx, about 2 ulp over its range)
+// with the argument split in the manner of Cody and Waite: p = fl(y*L2E) and
+// its rounding error r = (y*L2E - p) + y*L2E_LO (one fma) are kept apart and
+// exp(y) = 2^p * 2^r ~= 2^p * (1 + r*ln2), |r| <= 2^-17 for |y| <= 88.8.  A
+// plain exp2(fl(y*log2e)) instead loses |y|*2^-24*ln2 of relative accuracy
+// (about 4e-6 at |y| = 88).  L2E + L2E_LO = log2(e) to about 2^-50.  Where
+// 2^p already saturates (|p| >= 256), infinities or NaN, r is left out.
+__device__ __forceinline__ float pf_exp_split(float y) {
+  const float L2E = 1.44269502162933349609375f, L2E_LO = 1.925962991e-08f;
+  const float p = y * L2E;
+  const float r = fabsf(p) < 256.0f ? fmaf(y, L2E, -p) + y * L2E_LO : 0.0f;
+  float e;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(e) : "f"(p));
+  return e * fmaf(r, 0.693147180559945309f, 1.0f);
+}
+// n / (1 + exp(-x)) with the fast divide (__fdividef, exact to about 2 ulp
+// for divisors up to 2^126).  Divisors above 2^126 (x < -87.34, up to the
+// infinity of exp's overflow) are scaled by 1/4 on both sides first, so
+// results below FLT_MIN still come out as the correctly signed subnormal
+// (or zero) that the reference's division gives, and SiLU's normal-range
+// outputs for -88.72 < x < -87.34 are kept.
+__device__ __forceinline__ float pf_over_1pexp(float n, float x) {
+  const float d = 1.0f + pf_exp_split(-x);
+  const float s = d > 8.50705917e+37f ? 0.25f : 1.0f;  // 2^126
+  return __fdividef(n * s, d * s);
+}
+// Sigmoid 1/(1+exp(-x)) (executor.cpp:398-403) and SiLU x/(1+exp(-x))
+// (executor.cpp:411-416): within a few ulp of the exact value over every
+// output at or above FLT_MIN, and exact at the limits (0, 1, NaN).
+__device__ __forceinline__ float pf_sigmoid(float x) { return pf_over_1pexp(1.0f, x); }
 __device__ __forceinline__ float pf_gelu(float x) {
   return 0.5f * x * (1.0f + tanhf(0.7978845608f * (x + 0.044715f * x * x * x)));
 }
-__device__ __forceinline__ float pf_silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float pf_silu(float x) { return pf_over_1pexp(x, x); }
 __device__ __forceinline__ float pf_max(float a, float b) { return fmaxf(a, b); }
 __device__ __forceinline__ float pf_min(float a, float b) { return fminf(a, b); }
 // The 3xTF32 operand split (identical to the precompiled kernels'): hi keeps

@@ -101,7 +101,7 @@ CudaExecutor::CudaExecutor(const pfc_executor_config& cfg) : cfg_(cfg) {
 CudaExecutor::~CudaExecutor() {
   DeviceGuard dg(cfg_.device_id);
   if (stream_) cudaStreamSynchronize(stream_);
-  release_constants();
+  (void)release_constants();  // nothing to report to from a destructor
   if (err_dev_) cudaFree(err_dev_);
   pool_.reset();
   if (copy_in_) cudaStreamDestroy(copy_in_);
@@ -109,28 +109,34 @@ CudaExecutor::~CudaExecutor() {
   if (stream_) cudaStreamDestroy(stream_);
 }
 
-void CudaExecutor::release_constants() {
-  if (stream_) cudaStreamSynchronize(stream_);
+cudaError_t CudaExecutor::release_constants() {
+  // everything is released even after a failure; the first error is returned
+  cudaError_t first = cudaSuccess;
+  auto note = [&first](cudaError_t e) {
+    if (first == cudaSuccess && e != cudaSuccess) first = e;
+  };
+  if (stream_) note(cudaStreamSynchronize(stream_));
   for (auto& [k, pe] : plans_) {
-    for (auto& gr : pe.graphs) cudaGraphExecDestroy(gr.second);
-    if (pe.arena) pool_->deallocate(pe.arena, stream_);
+    for (auto& gr : pe.graphs) note(cudaGraphExecDestroy(gr.second));
+    if (pe.arena) note(pool_->deallocate(pe.arena, stream_));
     for (int k2 = 0; k2 < 2; ++k2)
-      for (void* p : pe.slots[k2]) pool_->deallocate(p, stream_);
+      for (void* p : pe.slots[k2]) note(pool_->deallocate(p, stream_));
   }
   plans_.clear();
   for (auto& [k, r] : resident_) {
     if (!r.owned) continue;
-    pool_->deallocate(r.dev, stream_);
+    note(pool_->deallocate(r.dev, stream_));
     pool_->add_resident(-(long long)r.bytes);
   }
   resident_.clear();
   resident_splat_.clear();
   for (auto& [k, pr] : prepared_) {
-    pool_->deallocate(pr.dev, stream_);
+    note(pool_->deallocate(pr.dev, stream_));
     pool_->add_resident(-(long long)pr.bytes);
   }
   prepared_.clear();
-  if (stream_) cudaStreamSynchronize(stream_);
+  if (stream_) note(cudaStreamSynchronize(stream_));
+  return first;
 }
 
 void CudaExecutor::set_resident(uint64_t cache_key, const void* dev, size_t bytes) {
@@ -142,7 +148,7 @@ void CudaExecutor::set_resident(uint64_t cache_key, const void* dev, size_t byte
   auto it = resident_.find(key);
   if (it != resident_.end() && it->second.owned) {
     if (stream_) PFB_CUDA(cudaStreamSynchronize(stream_));
-    pool_->deallocate(it->second.dev, stream_);
+    PFB_CUDA(pool_->deallocate(it->second.dev, stream_));
     pool_->add_resident(-(long long)it->second.bytes);
   }
   Resident r;
@@ -301,6 +307,7 @@ std::vector<void*> CudaExecutor::resolve(PlanEntry& pe, const Graph& g,
             r.bytes = n.data_bytes;
             r.dev = pool_->allocate(n.data_bytes, s);
             PFB_CUDA(cudaMemcpyAsync(r.dev, n.data, n.data_bytes, cudaMemcpyHostToDevice, s));
+            h2d_ += n.data_bytes;
             pool_->add_resident((long long)r.bytes);
             it = resident_.emplace(key, r).first;
           }
@@ -628,6 +635,7 @@ void CudaExecutor::execute(Graph& g, const std::vector<uint64_t>& outs, void* co
   std::lock_guard<std::mutex> lock(mu_);
   auto t0 = std::chrono::steady_clock::now();
   DeviceGuard dg(cfg_.device_id);
+  h2d_ = 0;
   for (size_t i = 0; i < outs.size(); ++i) {
     const Node* n = g.find(outs[i]);
     if (!n) fail(PFC_ERR_INVALID_ARGUMENT, "output id " + std::to_string(outs[i]) + " is not in the graph");
@@ -649,13 +657,17 @@ void CudaExecutor::execute(Graph& g, const std::vector<uint64_t>& outs, void* co
   PFB_CUDA(cudaEventRecord(e0, s));
   std::vector<std::pair<void*, const Node*>> uploads;
   std::vector<void*> ptrs = resolve(pe, g, {}, s, &uploads);
-  for (auto& [dst, n] : uploads) PFB_CUDA(cudaMemcpyAsync(dst, n->data, n->data_bytes, cudaMemcpyHostToDevice, s));
+  for (auto& [dst, n] : uploads) {
+    PFB_CUDA(cudaMemcpyAsync(dst, n->data, n->data_bytes, cudaMemcpyHostToDevice, s));
+    h2d_ += n->data_bytes;
+  }
   {
     // splat values live in a small device table; upload only when they change
     std::vector<float> table(P.scalars.size());
     for (size_t i = 0; i < P.scalars.size(); ++i) table[i] = P.scalars[i].value;
     if (!table.empty() && (table != pe.table || pe.table_ptr != ptrs[P.scalar_buf])) {
       PFB_CUDA(cudaMemcpyAsync(ptrs[P.scalar_buf], table.data(), table.size() * 4, cudaMemcpyHostToDevice, s));
+      h2d_ += table.size() * 4;
       pe.table = table;
       pe.table_ptr = ptrs[P.scalar_buf];
     }
@@ -686,6 +698,12 @@ void CudaExecutor::execute(Graph& g, const std::vector<uint64_t>& outs, void* co
   res->compute_time_ms = comp;
   res->total_time_ms = ms_since(t0);
   res->kernel_launches = launches;
+  res->h2d_bytes = h2d_;
+  res->d2h_bytes = [&] {
+    uint64_t b = 0;
+    for (size_t i = 0; i < outs.size(); ++i) b += out_bytes[i];
+    return b;
+  }();
 }
 
 void CudaExecutor::execute_device(Graph& g, const std::vector<uint64_t>& in_ids, const void* const* in_dev,
@@ -694,6 +712,7 @@ void CudaExecutor::execute_device(Graph& g, const std::vector<uint64_t>& in_ids,
   std::lock_guard<std::mutex> lock(mu_);
   auto t0 = std::chrono::steady_clock::now();
   DeviceGuard dg(cfg_.device_id);
+  h2d_ = 0;
   std::unordered_set<uint64_t> bindings;
   std::unordered_map<uint64_t, const void*> bind;
   for (size_t i = 0; i < in_ids.size(); ++i) {
@@ -724,13 +743,17 @@ void CudaExecutor::execute_device(Graph& g, const std::vector<uint64_t>& in_ids,
       direct[i] = true;
     }
   }
-  for (auto& [dst, n] : uploads) PFB_CUDA(cudaMemcpyAsync(dst, n->data, n->data_bytes, cudaMemcpyHostToDevice, s));
+  for (auto& [dst, n] : uploads) {
+    PFB_CUDA(cudaMemcpyAsync(dst, n->data, n->data_bytes, cudaMemcpyHostToDevice, s));
+    h2d_ += n->data_bytes;
+  }
   {
     // splat values live in a small device table; upload only when they change
     std::vector<float> table(P.scalars.size());
     for (size_t i = 0; i < P.scalars.size(); ++i) table[i] = P.scalars[i].value;
     if (!table.empty() && (table != pe.table || pe.table_ptr != ptrs[P.scalar_buf])) {
       PFB_CUDA(cudaMemcpyAsync(ptrs[P.scalar_buf], table.data(), table.size() * 4, cudaMemcpyHostToDevice, s));
+      h2d_ += table.size() * 4;
       pe.table = table;
       pe.table_ptr = ptrs[P.scalar_buf];
     }
@@ -746,6 +769,8 @@ void CudaExecutor::execute_device(Graph& g, const std::vector<uint64_t>& in_ids,
   res->compile_time_ms = compile_ms;
   res->total_time_ms = ms_since(t0);
   res->kernel_launches = launches;
+  res->h2d_bytes = h2d_;
+  res->d2h_bytes = 0;
 }
 
 void CudaExecutor::execute_streamed(Graph& g, const std::vector<uint64_t>& in_ids, const void* const* in_host,
@@ -754,6 +779,7 @@ void CudaExecutor::execute_streamed(Graph& g, const std::vector<uint64_t>& in_id
   std::lock_guard<std::mutex> lock(mu_);
   auto t0 = std::chrono::steady_clock::now();
   DeviceGuard dg(cfg_.device_id);
+  h2d_ = 0;
   if (n_chunks < 1) fail(PFC_ERR_INVALID_ARGUMENT, "n_chunks must be at least 1");
   std::unordered_set<uint64_t> bindings;
   std::vector<size_t> in_bytes, out_bytes;
@@ -783,7 +809,7 @@ void CudaExecutor::execute_streamed(Graph& g, const std::vector<uint64_t>& in_id
   if (pe.slot_bytes != want) {
     PFB_CUDA(cudaStreamSynchronize(s));
     for (int k = 0; k < 2; ++k) {
-      for (void* p : pe.slots[k]) pool_->deallocate(p, s);
+      for (void* p : pe.slots[k]) PFB_CUDA(pool_->deallocate(p, s));
       pe.slots[k].clear();
       for (size_t b : want) pe.slots[k].push_back(pool_->allocate(std::max<size_t>(b, 256), s));
     }
@@ -815,8 +841,11 @@ void CudaExecutor::execute_streamed(Graph& g, const std::vector<uint64_t>& in_id
     // inputs of chunk c into slot k once chunk c-2 has finished reading it
     if (c >= 2) PFB_CUDA(cudaStreamWaitEvent(copy_in_, ev_comp[k]));
     for (size_t i = 0; i < in_ids.size(); ++i)
+    {
       PFB_CUDA(cudaMemcpyAsync(in_slot[k][i], (const char*)in_host[i] + (size_t)c * in_bytes[i], in_bytes[i],
                                cudaMemcpyHostToDevice, copy_in_));
+      h2d_ += in_bytes[i];
+    }
     PFB_CUDA(cudaEventRecord(ev_in[k], copy_in_));
     // compute chunk c once its inputs landed and chunk c-2's outputs left slot k
     PFB_CUDA(cudaStreamWaitEvent(s, ev_in[k]));
@@ -834,12 +863,16 @@ void CudaExecutor::execute_streamed(Graph& g, const std::vector<uint64_t>& in_id
         direct[i] = true;
       }
     }
-    for (auto& [dst, n] : uploads) PFB_CUDA(cudaMemcpyAsync(dst, n->data, n->data_bytes, cudaMemcpyHostToDevice, s));
+    for (auto& [dst, n] : uploads) {
+    PFB_CUDA(cudaMemcpyAsync(dst, n->data, n->data_bytes, cudaMemcpyHostToDevice, s));
+    h2d_ += n->data_bytes;
+  }
     {
       std::vector<float> table(P.scalars.size());
       for (size_t i = 0; i < P.scalars.size(); ++i) table[i] = P.scalars[i].value;
       if (!table.empty() && (table != pe.table || pe.table_ptr != ptrs[P.scalar_buf])) {
         PFB_CUDA(cudaMemcpyAsync(ptrs[P.scalar_buf], table.data(), table.size() * 4, cudaMemcpyHostToDevice, s));
+      h2d_ += table.size() * 4;
         pe.table = table;
         pe.table_ptr = ptrs[P.scalar_buf];
       }
@@ -883,6 +916,12 @@ void CudaExecutor::execute_streamed(Graph& g, const std::vector<uint64_t>& in_id
   res->compute_time_ms = total;
   res->total_time_ms = ms_since(t0);
   res->kernel_launches = launches;
+  res->h2d_bytes = h2d_;
+  res->d2h_bytes = [&] {
+    uint64_t b = 0;
+    for (size_t i = 0; i < outs.size(); ++i) b += out_bytes[i];
+    return b * (uint64_t)n_chunks;
+  }();
 }
 
 std::string CudaExecutor::describe(Graph& g, const std::vector<uint64_t>& outs) {

@@ -47,7 +47,7 @@ class CudaExecutor {
 
   pfc_device_info device_info() const;
   pfc_memory_stats memory_stats() const { return pool_->stats(); }
-  void release_constants();
+  cudaError_t release_constants();  // first CUDA error met while releasing
   // Caller-owned device memory holding the payload of constants keyed
   // (cache_key, bytes): used in place of an upload, never written or freed.
   void set_resident(uint64_t cache_key, const void* dev, size_t bytes);
@@ -55,6 +55,9 @@ class CudaExecutor {
   const std::vector<std::pair<std::string, double>>& last_profile() const { return profile_; }
 
  private:
+  // host->device bytes copied during the current call (resident uploads, per-call
+  // constants, inputs, the splat table); reported in pfc_execution_result
+  uint64_t h2d_ = 0;
   struct PlanEntry {
     std::unique_ptr<Plan> plan;
     void* arena = nullptr;

@@ -502,17 +502,13 @@ void launch_attention(const AttnLaunch& L, cudaStream_t stream) {
   PFB_CHECK_ARG(!L.o_hi || (((uintptr_t)L.o_hi | (uintptr_t)L.o_lo) & 15) == 0, "attention: operand output must be 16-byte aligned");
   for (const void* q : {L.q_hi, (const void*)L.q_lo, L.k_hi, (const void*)L.k_lo, L.v_hi, (const void*)L.v_lo})
     PFB_CHECK_ARG(q && ((uintptr_t)q & 15) == 0, "attention: operands must be 16-byte aligned");
-  static bool attr_set[64] = {};
-  static int sms[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
+  // per-device set-up once, safe when several host threads launch at once
+  static std::once_flag attr_once[64];
+  const int dev = current_device();
+  std::call_once(attr_once[dev], [] {
     PFB_CUDA(cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kASmem));
-    int v = 0;
-    PFB_CUDA(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev));
-    sms[dev & 63] = v > 0 ? v : 148;
-    attr_set[dev & 63] = true;
-  }
+  });
+  const int n_sms = device_sm_count(dev);
   const int prec = PFC_PRECISION_TF32X3;
   const CUtensorMap qh = make_operand_map(L.q_hi, prec, L.kq, L.M, L.batch, kAQ);
   const CUtensorMap ql = make_operand_map(L.q_lo, prec, L.kq, L.M, L.batch, kAQ);
@@ -541,7 +537,7 @@ void launch_attention(const AttnLaunch& L, cudaStream_t stream) {
   p.err = L.err;
   const int64_t ntiles = (int64_t)p.batch * p.ntq;
   PFB_CHECK_ARG(ntiles < (1ll << 31), "attention: too many tiles");
-  const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sms[dev & 63]);
+  const unsigned grid = (unsigned)std::min<int64_t>(ntiles, n_sms);
   attn_kernel<<<grid, kAThreads, kASmem, stream>>>(qh, ql, kh, kl, vh, vl, p);
   PFB_CUDA(cudaGetLastError());
 }

@@ -960,16 +960,15 @@ template <int PREC, int BN, bool CONV>
 void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const CUtensorMap* conv_maps = nullptr,
               int TW = 0) {
   using C = Cfg<PREC, BN>;
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
+  // per-device set-up once, safe when several host threads launch at once
+  static std::once_flag attr_once[64];
+  const int dev = current_device();
+  std::call_once(attr_once[dev], [] {
     PFB_CUDA(cudaFuncSetAttribute(gemm_kernel<PREC, BN, CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     if constexpr (!CONV)
       PFB_CUDA(cudaFuncSetAttribute(conv_halo_kernel<PREC, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     HaloCfg<PREC, BN>::SMEM));
-    attr_set[dev & 63] = true;
-  }
+  });
   const int64_t a_rows = L.M, b_rows = L.N;
   CUtensorMap tb_hi = make_map(L.b_hi, PREC, L.kpad, b_rows, L.b_sb ? L.batch : 1, BN);
   CUtensorMap tb_lo = PREC == PFC_PRECISION_BF16 ? tb_hi : make_map(L.b_lo, PREC, L.kpad, b_rows, L.b_sb ? L.batch : 1, BN);
@@ -1040,13 +1039,7 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const 
   const int64_t ntiles = (int64_t)p.num_m * p.num_n * L.batch;
   PFB_CHECK_ARG(ntiles < (1ll << 31), "gemm: too many tiles");
   // persistent: one CTA per SM (the shared-memory ring admits one), never more CTAs than tiles
-  static int sms[64] = {};
-  if (!sms[dev & 63]) {
-    int v = 0;
-    PFB_CUDA(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev));
-    sms[dev & 63] = v > 0 ? v : 148;
-  }
-  const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sms[dev & 63]);
+  const unsigned grid = (unsigned)std::min<int64_t>(ntiles, device_sm_count(dev));
   if constexpr (!CONV) {
     if (conv_tma == 3) {
       conv_halo_kernel<PREC, BN><<<grid, kHaloThreads, HaloCfg<PREC, BN>::SMEM, stream>>>(ta_hi, ta_lo, tb_hi,

@@ -2,7 +2,7 @@
 // device memory.
 //
 // pfk_matmul_tf32x3_static computes C = A @ B (A [M,K], B [K,N], C [M,N],
-// all fp32 row-major, PyFlame's MATMUL contract, matmul.cpp:12-31) with the
+// all fp32 dense row-major) with the
 // same 3xTF32 tcgen05 GEMM and operand split as pfk_split_tf32 + pfk_gemm.
 // Those entry points need the caller to supply device buffers for the split
 // operands and the error flag; this one takes them from a fixed scratch array
@@ -23,6 +23,9 @@
 //  - Every call in the process shares the one array (one copy per device),
 //    so calls that overlap in time race on it: serialise them, for example
 //    by issuing them on one stream.
+//  - The array holds 64 MiB on every device where this library's device
+//    code is loaded (with CUDA_MODULE_LOADING=EAGER: at context creation),
+//    called or not.
 //  - The first call on a device looks the array's device address up
 //    (cudaGetSymbolAddress, which may load this file's device code into the
 //    context).  Make that first call before any stream capture begins.

@@ -15,17 +15,7 @@ namespace pfb {
 
 namespace {
 
-int num_sms() {
-  static int sms[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!sms[dev & 63]) {
-    int v = 0;
-    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-    sms[dev & 63] = v > 0 ? v : 148;
-  }
-  return sms[dev & 63];
-}
+int num_sms() { return device_sm_count(current_device()); }
 
 unsigned grid_for(int64_t work, int block) {
   int64_t g = ceil_div(std::max<int64_t>(work, 1), block);

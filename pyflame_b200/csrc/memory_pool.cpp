@@ -45,15 +45,15 @@ void* CudaMemoryPool::allocate(size_t bytes, cudaStream_t stream) {
   return p;
 }
 
-void CudaMemoryPool::deallocate(void* p, cudaStream_t stream) {
-  if (!p) return;
+cudaError_t CudaMemoryPool::deallocate(void* p, cudaStream_t stream) {
+  if (!p) return cudaSuccess;
   std::lock_guard<std::mutex> lock(mu_);
   auto it = sizes_.find(p);
-  if (it == sizes_.end()) return;
+  if (it == sizes_.end()) return cudaSuccess;
   allocated_ -= it->second;
   sizes_.erase(it);
   ++n_free_;
-  cudaFreeAsync(p, stream);
+  return cudaFreeAsync(p, stream);
 }
 
 pfc_memory_stats CudaMemoryPool::stats() const {

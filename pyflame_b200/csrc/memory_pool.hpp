@@ -29,7 +29,9 @@ class CudaMemoryPool {
   CudaMemoryPool& operator=(const CudaMemoryPool&) = delete;
 
   void* allocate(size_t bytes, cudaStream_t stream);
-  void deallocate(void* p, cudaStream_t stream);
+  // Stream-ordered free; returns cudaFreeAsync's status (destructor paths
+  // may ignore it, every other caller checks it).
+  cudaError_t deallocate(void* p, cudaStream_t stream);
   pfc_memory_stats stats() const;
   void add_resident(long long delta) { resident_ += delta; }
 

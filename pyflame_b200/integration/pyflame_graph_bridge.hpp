@@ -3,9 +3,10 @@
 // Header-only, compiled inside the PyFlame tree (it includes PyFlame's IR
 // headers).  It turns a live pyflame::ir::Graph into the C ABI's graph
 // description and runs it through the CUDA executor, filling the fields of
-// PyFlame's ExecutionResult (src/backend/executor.cpp:148-160).  The
-// maintainer-facing integration (the Backend::CUDA branch of
-// backend::Executor) is shown in INTEGRATION.md.
+// PyFlame's ExecutionResult (src/backend/executor.cpp:148-160).  A
+// Backend::CUDA branch of backend::Executor (executor.cpp:171-194) holds a
+// cuda::CudaExecutor (below) and calls its execute() where execute_rocm
+// (executor.cpp:557-582) calls rocm::ROCmExecutor::execute.
 #pragma once
 
 #include <cstring>

@@ -34,6 +34,29 @@ class Workload:
     bytes: float = 0.0             # algorithmic HBM bytes per graph
     meta: dict = field(default_factory=dict)
 
+    def graph(self):
+        return self.outputs[0].graph()
+
+    def output_ids(self) -> List[int]:
+        return [t.node().id() for t in self.outputs]
+
+    def weights(self) -> Dict[int, np.ndarray]:
+        """Constant leaves a serving host keeps on the device (weights and
+        biases), by node id: every payload-carrying leaf that is not a batch
+        input, except constants whose elements are all equal, which the
+        executor turns into scalar-table slots and never materialises."""
+        g = self.graph()
+        input_ids = {t.node().id() for t in self.inputs.values()}
+        out = {}
+        for n in g.topological_order([t.node() for t in self.outputs]):
+            if n.is_operation() or n.id() in input_ids or not n.has_constant_data() or n.numel() <= 1:
+                continue
+            a = n.constant_data()
+            if np.all(a == a.flat[0]):
+                continue
+            out[n.id()] = a
+        return out
+
 
 def _normal(seed, shape, std):
     return (np.random.default_rng(seed).standard_normal(shape) * std).astype(np.float32)

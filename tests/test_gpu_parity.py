@@ -62,6 +62,60 @@ def test_unary(cuda_executor, oracle_mod, rng, fn):
         bitexact(g, r)
 
 
+FLT_MIN = float(np.finfo(np.float32).tiny)
+
+# Inputs per function over which the output spans its whole normal range.
+# Sigmoid/SiLU stop short of -88.72, where the reference's exp(-x) overflows
+# (its semantics there are checked separately below).
+_REL_DOMAIN = {
+    "sigmoid": (-88.70, 40.0), "silu": (-88.70, 40.0), "exp": (-87.3, 88.7), "tanh": (-12.0, 12.0),
+    "log": (1e-37, 3e38), "sqrt": (1e-37, 3e38), "sin": (-200.0, 200.0), "cos": (-200.0, 200.0),
+}
+_F64 = {"sigmoid": lambda x: 1.0 / (1.0 + np.exp(-x)), "silu": lambda x: x / (1.0 + np.exp(-x)), "exp": np.exp,
+        "tanh": np.tanh, "log": np.log, "sqrt": np.sqrt, "sin": np.sin, "cos": np.cos}
+
+
+@pytest.mark.parametrize("fn", sorted(_REL_DOMAIN))
+def test_unary_relative_over_normal_range(cuda_executor, oracle_mod, rng, fn):
+    """1e-5 relative, with no absolute floor, against the exact (fp64) value
+    and against the fp32 reference, for every output at or above FLT_MIN;
+    outputs below FLT_MIN within FLT_MIN.  Covers the tails where a fast
+    exp loses accuracy (sigmoid and SiLU for x in [-88.7, -20])."""
+    lo, hi = _REL_DOMAIN[fn]
+    if lo > 0:  # log-spaced positive inputs
+        data = np.exp(rng.uniform(np.log(lo), np.log(hi), 8192))
+    else:
+        data = np.concatenate([np.linspace(lo, hi, 8192), rng.uniform(lo, hi, 4096)])
+    if fn in ("sigmoid", "silu"):
+        data = np.concatenate([data, rng.uniform(-88.7, -20.0, 4096), np.linspace(-88.7, -87.0, 1024)])
+    if fn == "tanh":
+        data = np.concatenate([data, np.exp(rng.uniform(np.log(1e-30), 0.0, 1024))])
+    data = data.astype(np.float32)
+    f = getattr(pf, fn)
+    (g,), (r,) = run(cuda_executor, [f(pf.tensor(data))], oracle_mod)
+    exact = _F64[fn](data.astype(np.float64))
+    for what, want in (("fp64", exact), ("reference fp32", r.astype(np.float64))):
+        got = g.astype(np.float64)
+        normal = np.abs(exact) >= FLT_MIN
+        rel = np.abs(got[normal] - want[normal]) / np.abs(want[normal])
+        assert rel.max() <= 1e-5, f"{fn} vs {what}: max rel {rel.max():.3g} at x={data[normal][rel.argmax()]!r}"
+        assert np.all(np.abs(got[~normal] - want[~normal]) <= FLT_MIN), f"{fn} vs {what}: sub-FLT_MIN outputs"
+
+
+def test_sigmoid_silu_past_exp_overflow(cuda_executor, oracle_mod):
+    """Below x = -88.72 the reference's exp(-x) is +inf, so sigmoid is +0 and
+    SiLU is -0 (x / inf); the device gives the same values, bit for bit.
+    Between -88.72 and -87.34 SiLU's outputs are still normal numbers."""
+    x = np.concatenate([np.linspace(-200.0, -88.75, 512), [-1e30, -np.inf]]).astype(np.float32)
+    (gs, gl), (rs, rl) = run(cuda_executor, [pf.sigmoid(pf.tensor(x)), pf.silu(pf.tensor(x))], oracle_mod)
+    assert np.all(np.abs(gs) <= FLT_MIN) and np.all(np.abs(rs) <= FLT_MIN)
+    bitexact(gl, rl)
+    near = np.linspace(-88.7, -87.34, 256).astype(np.float32)
+    (g,), (r,) = run(cuda_executor, [pf.silu(pf.tensor(near))], oracle_mod)
+    assert np.all(np.abs(r) >= FLT_MIN)
+    np.testing.assert_allclose(g, r, rtol=1e-5, atol=0)
+
+
 @pytest.mark.parametrize("shapes", [((37, 129), (37, 129)), ((64, 256), (256,)), ((64, 256), (64, 1)),
                                     ((2, 5, 7, 3), (1, 5, 1, 1)), ((3, 1, 8), (4, 1)), ((1000,), ())])
 @pytest.mark.parametrize("op", ["add", "sub", "mul", "div"])
@@ -493,6 +547,10 @@ def test_streamed_execution(cuda_executor, oracle_mod, chunks):
     for _ in range(2):  # the second call replays captured graphs
         cuda_executor.execute_streamed(g, {w.inputs["x"].node().id(): xs.numpy(), w.inputs["y"].node().id(): ys.numpy()},
                                        ids, outs)
+    z = full.outputs[0].node().inputs()[0]
+    zabs = np.abs(oracle_mod.run(full.outputs[0].graph(), [z.id()])[z.id()]).sum(1)
+    close_sum(outs[0], ref[ids_full[0]], zabs, what="sum")
+    close_sum(outs[1], ref[ids_full[1]], zabs / cols, what="mean")
     close(outs[2], ref[ids_full[2]], rtol=1e-5, atol=1e-6, what="max")
     close_rows(outs[3], ref[ids_full[3]], 1e-5, what="layernorm")
     mc = workloads.mlp(batch=16)
@@ -504,6 +562,35 @@ def test_streamed_execution(cuda_executor, oracle_mod, chunks):
     cuda_executor.execute_streamed(mc.outputs[0].graph(), {mc.inputs["x"].node().id(): xin.numpy()},
                                    [mc.outputs[0].node().id()], [mout])
     close_rows(mout, mref, RTOL_GEMM_TF32X3, what="mlp streamed")
+
+
+@pytest.mark.parametrize("fail_at", [1, 2, 4])
+def test_injected_allocation_failure(native, oracle_mod, fail_at):
+    """An allocation that fails (injected on the host at the fail_at-th
+    allocation) comes back as success=False naming the injection, never as an
+    exception; releasing the executor's memory leaves nothing allocated; a
+    fresh executor then runs the same graph correctly."""
+    from pyflame_b200 import workloads
+    from pyflame_b200.backend import CudaExecutor
+    w = workloads.gemm_chain(rows=64, d=256, h=512)
+    g, ids = w.graph(), w.output_ids()
+    ex = CudaExecutor(CudaExecutor.Config(fail_after_n_allocations=fail_at))
+    try:
+        r = ex.execute(g, ids)
+        assert not r.success and "injected allocation failure" in r.error_message, r.error_message
+        assert ex.get_memory_stats().total_allocations == fail_at - 1
+        ex.release_constants()
+        s = ex.get_memory_stats()
+        assert s.total_allocated == 0 and s.resident_constant_bytes == 0, s
+    finally:
+        ex.close()
+    ok = CudaExecutor(CudaExecutor.Config())
+    try:
+        r = ok.execute(g, ids)
+        assert r.success, r.error_message
+        close_rows(r.outputs[ids[0]], oracle_mod.run(g, ids)[ids[0]], RTOL_GEMM_TF32X3, what="after injection")
+    finally:
+        ok.close()
 
 
 def test_memory_stats_and_release(cuda_executor):
