@@ -22,6 +22,7 @@
 // The executor class lives in a .cpp (no header): include it.
 #include "src/backend/executor.cpp"
 
+#include "pyflame/autograd/autograd.hpp"
 #include "pyflame/core/tensor.hpp"
 #include "pyflame/core/tensor_impl.hpp"
 #include "pyflame/nn/attention.hpp"
@@ -102,7 +103,7 @@ std::string attr_text(const std::any& a) {
 static const char* kAttrNames[] = {"dim", "keepdim", "new_shape", "dim0", "dim1", "start", "end", "stride", "padding",
                                    "dilation", "groups", "eps", "momentum", "training", "affine",
                                    "track_running_stats", "normalized_shape", "elementwise_affine", "kernel_size",
-                                   "output_size"};
+                                   "output_size", "target_shape"};
 
 extern "C" {
 
@@ -278,6 +279,24 @@ int ref_build(int kind, char* buf, size_t len) {
       nn::AvgPool2d ap(2);
       nn::AdaptiveAvgPool2d gp(1);
       out = gp.forward(ap.forward(x));
+    } else if (kind == 6) {
+      // backward graph of an MLP loss (autograd.cpp:421-480)
+      auto x = Tensor::from_data(d.data(), {4, 8}, DType::Float32, MeshLayout::SinglePE(), 4 * 8 * 4);
+      nn::Linear l1(8, 6), l2(6, 3);
+      auto loss = softmax(l2.forward(relu(l1.forward(x))), -1).sum();
+      autograd::AutogradEngine::backward(loss.node(), nullptr, graph);
+      out = loss;
+    } else if (kind == 7) {
+      // backward graph of an elementwise chain with a broadcast bias and row reductions
+      auto x = Tensor::from_data(d.data(), {4, 8}, DType::Float32, MeshLayout::SinglePE(), 4 * 8 * 4);
+      auto y = Tensor::from_data(d.data(), {4, 8}, DType::Float32, MeshLayout::SinglePE(), 4 * 8 * 4);
+      auto b = Tensor::from_data(d.data(), {8}, DType::Float32, MeshLayout::SinglePE(), 8 * 4);
+      auto a = x * y + b;
+      auto h = tanh(a) * sigmoid(x) - exp(y) / (abs(x) + 1.0f);
+      auto z = sqrt(h * h + 1.0f).sum(1, true);
+      auto loss = (log(z) + sin(x).sum(1, true) * cos(y).mean(1, true)).sum();
+      autograd::AutogradEngine::backward(loss.node(), nullptr, graph);
+      out = loss;
     } else {
       g_err = "unknown kind";
       return -1;

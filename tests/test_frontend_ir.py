@@ -13,7 +13,7 @@ import numpy as np
 import pytest
 
 import pyflame_b200 as pf
-from pyflame_b200 import ir, nn
+from pyflame_b200 import autograd, ir, nn
 from oracle import oracle as O
 
 DUMP = O.HERE / "_ref" / "ref_dump"
@@ -21,7 +21,7 @@ pytestmark = pytest.mark.skipif(not DUMP.exists(), reason="PyFlame reference fro
 
 ATTR_ORDER = ["dim", "keepdim", "new_shape", "dim0", "dim1", "start", "end", "stride", "padding", "dilation", "groups",
               "eps", "momentum", "training", "affine", "track_running_stats", "normalized_shape",
-              "elementwise_affine", "kernel_size", "output_size"]
+              "elementwise_affine", "kernel_size", "output_size", "target_shape"]
 CT = {ir.A_INT: "int", ir.A_INT64: "int64", ir.A_FLOAT: "float", ir.A_DOUBLE: "double", ir.A_BOOL: "bool",
       ir.A_INT64_VEC: "vec64", ir.A_INT_VEC: "vec32"}
 
@@ -110,12 +110,26 @@ def build(kind):
     elif kind == 5:
         x = pf.Tensor.from_data(D[:2 * 3 * 64], [2, 3, 8, 8])
         nn.AdaptiveAvgPool2d(1)(nn.AvgPool2d(2)(x))
+    elif kind == 6:
+        x = pf.Tensor.from_data(D[:32], [4, 8])
+        l1, l2 = nn.Linear(8, 6), nn.Linear(6, 3)
+        autograd.backward(pf.softmax(l2(pf.relu(l1(x))), -1).sum())
+    elif kind == 7:
+        x = pf.Tensor.from_data(D[:32], [4, 8])
+        y = pf.Tensor.from_data(D[:32], [4, 8])
+        b = pf.Tensor.from_data(D[:8], [8])
+        a = x * y + b
+        h = pf.tanh(a) * pf.sigmoid(x) - pf.exp(y) / (pf.abs(x) + 1.0)
+        z = pf.sqrt(h * h + 1.0).sum(1, True)
+        autograd.backward((pf.log(z) + pf.sin(x).sum(1, True) * pf.cos(y).mean(1, True)).sum())
     return pf.get_current_graph()
 
 
 @pytest.mark.parametrize("kind,what", [(0, "Linear"), (1, "Conv2d+BatchNorm2d+ReLU+MaxPool2d"),
                                        (2, "LayerNorm+softmax"), (3, "MultiheadAttention"),
-                                       (4, "fused elementwise + row reductions"), (5, "AvgPool2d+AdaptiveAvgPool2d")])
+                                       (4, "fused elementwise + row reductions"), (5, "AvgPool2d+AdaptiveAvgPool2d"),
+                                       (6, "MLP loss + AutogradEngine::backward"),
+                                       (7, "elementwise chain + AutogradEngine::backward")])
 def test_same_ir_as_pyflame(kind, what):
     ref = canonical(reference(kind))
     ours = canonical(python_nodes(build(kind)))
