@@ -304,6 +304,14 @@ class SharedPinned:
             self.path.unlink(missing_ok=True)
 
 
+def _shm_free() -> int:
+    try:
+        st = os.statvfs("/dev/shm")
+        return st.f_bavail * st.f_frsize
+    except OSError:
+        return 0
+
+
 def _chunks_for(name, shard):
     c = max(1, min(E2E_CHUNKS[name], shard // MIN_CHUNK[name]))
     while shard % c:
@@ -369,13 +377,13 @@ def measure(name, args, d: Dist, precision="tf32x3", with_e2e=True, with_cpu=Tru
     ex = pf.CudaExecutor(pf.CudaExecutor.Config(device_id=d.local, precision=precision))
     bind, keep = {}, []
     for t in w.inputs.values():
-        dv = torch.from_numpy(np.ascontiguousarray(t.node().constant_data())).cuda()
+        dv = torch.from_numpy(np.array(t.node().constant_data(), copy=True)).cuda()
         keep.append(dv)
         bind[t.node().id()] = dv.data_ptr()
     # weights: rank 0's copy broadcast once over NCCL, then each rank's resident constants
     weights = {}
     for nid, arr in sorted(w.weights().items()):
-        dv = torch.from_numpy(np.ascontiguousarray(arr)).cuda() if rank == 0 else \
+        dv = torch.from_numpy(np.array(arr, copy=True)).cuda() if rank == 0 else \
             torch.empty(arr.shape, dtype=torch.float32, device="cuda")
         d.broadcast(dv)
         weights[nid] = dv
@@ -462,8 +470,13 @@ def measure_e2e(name, args, d: Dist, w, ex, shard, strong, weights):
                  for iname, t in w.inputs.items()}
     shared = []
     out_np = []
+    # one shared result needs room for every rank's outputs in /dev/shm (the
+    # same free space seen by every rank); otherwise each rank writes its rows
+    # into its own pinned buffer
+    need = sum(int(np.prod(t.shape)) * 4 * world for t in w.outputs)
+    use_shared = world > 1 and d.max(0.0 if _shm_free() >= need + (64 << 20) else 1.0) == 0.0
     for k, t in enumerate(w.outputs):
-        if world > 1:
+        if use_shared:
             full_shape = [t.shape[0] * world, *t.shape[1:]]
             sh = SharedPinned(d, f"{name}_{k}", full_shape, d.rank * t.shape[0], (d.rank + 1) * t.shape[0])
             shared.append(sh)
@@ -491,8 +504,10 @@ def measure_e2e(name, args, d: Dist, w, ex, shard, strong, weights):
     e2e = {"value": glob_samples * n_e2e / dt, "unit": "samples/s", "h2d_bytes_per_step": h2d * world,
            "d2h_bytes_per_step": d2h * world, "ms_per_step": dt / n_e2e * 1e3, "steps": n_e2e,
            "chunks_per_gpu": chunks,
-           "api": "CudaExecutor.execute_streamed (pfc_executor_execute_streamed), pinned host buffers" +
-                  (", every rank's outputs into one shared pinned host result" if world > 1 else "")}
+           "api": "CudaExecutor.execute_streamed (pfc_executor_execute_streamed), pinned host buffers",
+           "gather": ("every rank's outputs into its rows of one shared pinned host result" if use_shared else
+                      "each rank's outputs into its own pinned host buffer (/dev/shm too small for one result)"
+                      if world > 1 else "single GPU")}
     if world == 1:
         # the plain host-buffer call for comparison: upload, compute, download in sequence
         for iname, t in w.inputs.items():

@@ -5,7 +5,7 @@ tensors, graph nodes, ops, nn modules, device selection and `eval`, with
 'cuda[:N]' as the device.  Evaluation runs on sm_100a GPUs through
 libpyflame_cuda.so (include/pyflame_cuda.h); there is no CPU evaluation path.
 """
-from . import autograd, ir, nn
+from . import autograd, ir, nn, serving
 from .backend import (Backend, CudaExecutor, DeviceInfo, ExecutionResult, Executor, ExecutorConfig, MemoryStats,
                       cuda_device_count, cuda_get_device, cuda_get_device_info, cuda_is_available, cuda_set_device,
                       cuda_synchronize)

@@ -14,6 +14,7 @@ from __future__ import annotations
 
 import ctypes as C
 import enum
+import threading
 import weakref
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional, Sequence
@@ -184,22 +185,32 @@ class NativeGraph:
         N.check(L.pfc_graph_set_attr(self.handle, nid, k, ct, C.byref(v), cnt))
 
 
+_native_lock = threading.Lock()
+
+
 def native_graph(graph: Graph, output_ids: Sequence[int]) -> NativeGraph:
-    """Build (or reuse) the native description of the subgraph for `output_ids`."""
-    cache = graph.__dict__.setdefault("_native_cache", {})
-    key = (graph.version, tuple(output_ids))
-    ng = cache.get(key)
-    if ng is None:
-        roots = []
-        for i in output_ids:
-            n = graph.node(i)
-            if n is None:
-                raise KeyError(f"output id {i} is not in the graph")
-            roots.append(n)
-        ng = NativeGraph(graph, roots)
-        cache.clear()
-        cache[key] = ng
-    return ng
+    """Build (or reuse) the native description of the subgraph for
+    `output_ids`.  Descriptions of the graph's current version are kept per
+    output set (up to 8), so callers that evaluate several subgraphs of one
+    graph in turn, or from several threads, reuse theirs."""
+    with _native_lock:
+        cache = graph.__dict__.setdefault("_native_cache", {})
+        key = (graph.version, tuple(output_ids))
+        ng = cache.get(key)
+        if ng is None:
+            roots = []
+            for i in output_ids:
+                n = graph.node(i)
+                if n is None:
+                    raise KeyError(f"output id {i} is not in the graph")
+                roots.append(n)
+            ng = NativeGraph(graph, roots)
+            for k in [k for k in cache if k[0] != graph.version]:
+                del cache[k]
+            while len(cache) >= 8:
+                del cache[next(iter(cache))]
+            cache[key] = ng
+        return ng
 
 
 # ---------------------------------------------------------------------------

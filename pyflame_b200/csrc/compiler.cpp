@@ -11,8 +11,10 @@
 //   5. decide which values are materialised, build strided views for shape
 //      ops, emit steps, plan buffer liveness and the arena.
 #include "compiler.hpp"
+#include "kernels/kernels.hpp"
 
 #include <algorithm>
+#include <array>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -1288,6 +1290,8 @@ std::string gen_full(const RowSpec& rs, const std::string& name, int num_sms, in
 // The compiler
 // ---------------------------------------------------------------------------
 
+static bool collapse_batch(const View& v, int nb, int64_t* stride);
+
 struct Region {
   std::vector<uint64_t> nodes;        // topo order
   std::vector<uint64_t> row_ops;      // attached row operations
@@ -1331,6 +1335,9 @@ class Compiler {
   std::vector<GemmChain> chains_;
   // attention: chain of the PV matmul -> (chain of the QK^T matmul, softmax node)
   std::unordered_map<int, std::pair<int, uint64_t>> attn_;
+  // small-batch Linear layers on the CUDA cores: chain of the (last) layer ->
+  // (chain of the first layer or -1, fused softmax/log-softmax node or 0)
+  std::unordered_map<int, std::pair<int, uint64_t>> small_;
   std::unordered_map<uint64_t, int> row_region_;     // row op -> region
   std::vector<std::pair<int, Step>> steps_;
   std::unordered_map<uint64_t, int> splat_slot_;
@@ -1501,6 +1508,8 @@ class Compiler {
   void classify();
   void absorb_epilogues();
   void detect_attention();
+  void detect_small();
+  bool small_eligible(int ci, int64_t* pm, int64_t* pn, int64_t* pk);
   void build_regions();
   void attach_row_ops();
   void lower();
@@ -1510,6 +1519,7 @@ class Compiler {
   void lower_row_alone(uint64_t id);
   void lower_chain(int c);
   void lower_attention(int c);
+  void lower_small(int c);
   void lower_matmul(const GemmChain& ch, int at);
   void lower_conv(const GemmChain& ch, int at);
   void lower_pool(uint64_t id);
@@ -1718,6 +1728,156 @@ void Compiler::detect_attention() {
     }
     attn_.emplace(c2, std::make_pair(c1, sm));
   }
+}
+
+// A Linear layer of a small batch, evaluated on the CUDA cores (small_gemm.cu)
+// instead of the tensor cores: MATMUL(x, TRANSPOSE(w)) of a 2-D leaf weight
+// w [N, K] (PyFlame's Linear, linear.cpp:36-44) with at most kSmallMaxRows
+// rows of x and at most 64 MFLOP, optional alpha/bias/activation epilogue.
+bool Compiler::small_eligible(int ci, int64_t* pm, int64_t* pn, int64_t* pk) {
+  const GemmChain& ch = chains_[ci];
+  if (cls_[ch.mm] != Cls::GEMM || chain_of_.at(ch.mm) != ci || attn_.count(ci)) return false;
+  if (ch.has_bn || ch.has_residual) return false;
+  const Node& mm = N(ch.mm);
+  if (mm.op != Op::MATMUL || mm.inputs.size() != 2 || mm.inputs[0] == mm.inputs[1]) return false;
+  const Node& a = N(mm.inputs[0]);
+  const Node& bt = N(mm.inputs[1]);
+  if (a.shape.empty() || bt.shape.size() != 2 || bt.op != Op::TRANSPOSE || bt.inputs.size() != 1) return false;
+  const Node& w = N(bt.inputs[0]);
+  if (w.type == NodeType::OPERATION || w.shape.size() != 2 || in_.splats.count(bt.inputs[0]) ||
+      in_.bindings.count(bt.inputs[0]) || w.dtype != DType::F32 || a.dtype != DType::F32)
+    return false;
+  const int64_t k = a.shape.back(), n = bt.shape[1];
+  if (w.shape[0] != n || w.shape[1] != k || bt.shape[0] != k) return false;  // [K, N] = w^T
+  const int64_t m = prod(a.shape) / std::max<int64_t>(k, 1);
+  if (m < 1 || m > kSmallMaxRows || k < 1 || n < 1 || 2.0 * m * n * k > 64e6) return false;
+  *pm = m;
+  *pn = n;
+  *pk = k;
+  return true;
+}
+
+// Linear -> (activation) -> Linear -> (softmax) on a small batch becomes one
+// launch (PyFlame's MLP graph, nn/linear.cpp); any other small Linear runs
+// alone on the CUDA cores.
+void Compiler::detect_small() {
+  std::unordered_map<int, std::array<int64_t, 3>> ok;
+  for (int ci = 0; ci < (int)chains_.size(); ++ci) {
+    int64_t m, n, k;
+    if (small_eligible(ci, &m, &n, &k)) ok[ci] = {m, n, k};
+  }
+  std::set<int> taken;
+  for (int c1 = 0; c1 < (int)chains_.size(); ++c1) {
+    if (!ok.count(c1) || taken.count(c1)) continue;
+    const GemmChain& ch1 = chains_[c1];
+    const uint64_t r1 = ch1.result;
+    if (is_out_.count(r1) || users_[r1].size() != 1) continue;
+    auto it = chain_of_.find(users_[r1][0]);
+    if (it == chain_of_.end()) continue;
+    const int c2 = it->second;
+    const GemmChain& ch2 = chains_[c2];
+    if (c2 == c1 || !ok.count(c2) || taken.count(c2) || users_[r1][0] != ch2.mm || N(ch2.mm).inputs[0] != r1) continue;
+    const int64_t M = ok[c1][0], N1 = ok[c1][1], N2 = ok[c2][1];
+    if (ok[c2][0] != M || N1 > 4096 || 2.0 * M * N1 * N2 > 4e6) continue;
+    // an optional row softmax over the last dim, its only reader
+    uint64_t sm = 0;
+    const uint64_t r2 = ch2.result;
+    if (!is_out_.count(r2) && users_[r2].size() == 1) {
+      const uint64_t u = users_[r2][0];
+      const Node& un = N(u);
+      if ((un.op == Op::SOFTMAX || un.op == Op::LOG_SOFTMAX) && cls_[u] == Cls::ROW && un.inputs[0] == r2) {
+        int dim = (int)un.attr_int("dim", -1);
+        if (dim < 0) dim += (int)un.shape.size();
+        if (dim == (int)un.shape.size() - 1) sm = u;
+      }
+    }
+    std::vector<uint64_t> nodes{ch1.mm};
+    nodes.insert(nodes.end(), ch1.absorbed.begin(), ch1.absorbed.end());
+    if (sm) nodes.push_back(sm);
+    for (uint64_t x : nodes) {
+      chain_of_[x] = c2;
+      cls_[x] = Cls::GEMM;
+    }
+    small_[c2] = {c1, sm};
+    taken.insert(c1);
+    taken.insert(c2);
+  }
+  for (auto& [ci, dims] : ok)
+    if (!taken.count(ci)) small_[ci] = {-1, 0};
+}
+
+void Compiler::lower_small(int ci) {
+  const auto [first, sm] = small_.at(ci);
+  const GemmChain& last = chains_[ci];
+  const GemmChain& c1 = first >= 0 ? chains_[first] : last;
+  const uint64_t result = sm ? sm : last.result;
+  const int at = pos_[result];
+  Step st;
+  st.kind = StepKind::SMALL;
+  SmallArgs& S = st.small;
+  // rows of x with K contiguous (copied when the view does not have that form)
+  View a = value(N(c1.mm).inputs[0]);
+  const int64_t K1 = a.shape.back(), M = a.numel() / std::max<int64_t>(K1, 1);
+  int64_t lda = K1;
+  {
+    int64_t rs = K1;
+    const bool rows_ok = !a.is_splat && a.strides.back() == 1 &&
+                         (a.shape.size() == 1 || collapse_batch(a, (int)a.shape.size() - 1, &rs));
+    if (!rows_ok) a = materialize_copy(a, at, "contiguous rows for a small GEMM");
+    else lda = a.shape.size() == 1 ? K1 : rs;
+    if (a.shape.size() >= 2 && !rows_ok) lda = K1;
+  }
+  S.a = a;
+  S.lda = lda;
+  S.M = M;
+  auto layer = [&](const GemmChain& ch, SmallLayerArgs& L) {
+    const Node& bt = N(N(ch.mm).inputs[1]);
+    const View w = value(bt.inputs[0]);  // the [N, K] weight leaf, dense
+    if (w.is_splat || w.strides.back() != 1) fail(PFC_ERR_INTERNAL, "small GEMM weight is not dense rows");
+    L.w_buf = w.buf;
+    L.w_off = w.offset;
+    L.N = w.shape[0];
+    L.K = w.shape[1];
+    L.ldw = w.strides[0];
+    L.alpha = ch.alpha;
+    L.alpha_slot = ch.alpha_slot;
+    L.act = ch.act;
+    if (ch.has_bias) {
+      View b = value(ch.bias);
+      int64_t sn = 0;
+      for (size_t d = 0; d < b.shape.size(); ++d)
+        if (b.shape[d] != 1) sn = b.strides[d];
+      if (b.is_splat) sn = 0;
+      L.bias = b;
+      L.bstride = sn;
+      L.has_bias = true;
+    }
+  };
+  layer(c1, S.l1);
+  std::string label = "small gemm [" + std::to_string(M) + "x" + std::to_string(S.l1.N) + "x" + std::to_string(K1) + "]";
+  if (first >= 0) {
+    S.layers = 2;
+    layer(last, S.l2);
+    S.h_buf = new_buffer((size_t)M * S.l1.N * 4);
+    S.counter_buf = new_buffer(8);
+    Step ms;
+    ms.kind = StepKind::MEMSET;
+    ms.label = "zero small-GEMM arrival counter";
+    ms.memset_buf = S.counter_buf;
+    add_step(at, ms);
+    label = "small mlp [" + std::to_string(M) + "x" + std::to_string(S.l1.N) + "x" + std::to_string(K1) + " -> " +
+            std::to_string(S.l2.N) + "]";
+  }
+  if (sm) {
+    S.softmax = N(sm).op == Op::SOFTMAX ? 1 : 2;
+    label += S.softmax == 1 ? " +softmax" : " +log_softmax";
+  }
+  const int64_t nout = S.layers == 2 ? S.l2.N : S.l1.N;
+  S.out = dense(N(result).shape, DType::F32);
+  S.ldo = nout;
+  st.label = label;
+  add_step(at, st);
+  val_[result] = S.out;
 }
 
 void Compiler::lower_attention(int c2) {
@@ -2597,6 +2757,10 @@ void Compiler::lower_chain(int ci) {
     lower_attention(ci);
     return;
   }
+  if (small_.count(ci)) {
+    lower_small(ci);
+    return;
+  }
   const GemmChain& ch = chains_[ci];
   int at = pos_[ch.result];
   if (cls_[ch.mm] == Cls::CONV) lower_conv(ch, at);
@@ -2798,6 +2962,14 @@ void Compiler::emit_operands_at_producers() {
         add(A.c.buf, i); add(A.op_hi, i); add(A.op_lo, i);
         break;
       }
+      case StepKind::SMALL: {
+        const SmallArgs& Sm = st.small;
+        add(Sm.a.buf, i); add(Sm.l1.w_buf, i); add(Sm.l2.w_buf, i); add(Sm.h_buf, i); add(Sm.counter_buf, i);
+        add(Sm.out.buf, i);
+        if (Sm.l1.has_bias) add(Sm.l1.bias.buf, i);
+        if (Sm.l2.has_bias) add(Sm.l2.bias.buf, i);
+        break;
+      }
     }
   }
   std::unordered_set<int> out_bufs;
@@ -2981,6 +3153,14 @@ void Compiler::finish() {
         use(A.op_hi, i); use(A.op_lo, i);
         break;
       }
+      case StepKind::SMALL: {
+        const SmallArgs& Sm = s.small;
+        use(Sm.a.buf, i); use(Sm.l1.w_buf, i); use(Sm.l2.w_buf, i); use(Sm.h_buf, i); use(Sm.counter_buf, i);
+        use(Sm.out.buf, i);
+        if (Sm.l1.has_bias) use(Sm.l1.bias.buf, i);
+        if (Sm.l2.has_bias) use(Sm.l2.bias.buf, i);
+        break;
+      }
     }
   }
   int nsteps = (int)P_->steps.size();
@@ -3043,6 +3223,7 @@ std::unique_ptr<Plan> Compiler::run() {
   classify();
   absorb_epilogues();
   detect_attention();
+  detect_small();
   build_regions();
   attach_row_ops();
   lower();

@@ -526,6 +526,39 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
     case StepKind::MEMSET:
       PFB_CUDA(cudaMemsetAsync(bufp(st.memset_buf, 0), 0, P.buffers[st.memset_buf].bytes, s));
       break;
+    case StepKind::SMALL: {
+      const SmallArgs& a = st.small;
+      SmallMlpLaunch L;
+      L.layers = a.layers;
+      L.a = viewp(a.a);
+      L.lda = a.lda;
+      L.M = a.M;
+      auto layer = [&](const SmallLayerArgs& l, const float** w, int64_t* ldw, const float** bias, int64_t* bstride,
+                       float* alpha, const float** alpha_ptr, int* act) {
+        *w = (const float*)bufp(l.w_buf, l.w_off * 4);
+        *ldw = l.ldw;
+        *bias = l.has_bias ? viewp(l.bias) : nullptr;
+        *bstride = l.bstride;
+        *alpha = l.alpha;
+        *alpha_ptr = l.alpha_slot >= 0 ? (const float*)bufp(P.scalar_buf, (int64_t)l.alpha_slot * 4) : nullptr;
+        *act = l.act;
+      };
+      layer(a.l1, &L.w1, &L.ldw1, &L.bias1, &L.bstride1, &L.alpha1, &L.alpha1_ptr, &L.act1);
+      L.N1 = a.l1.N;
+      L.K1 = a.l1.K;
+      if (a.layers == 2) {
+        layer(a.l2, &L.w2, &L.ldw2, &L.bias2, &L.bstride2, &L.alpha2, &L.alpha2_ptr, &L.act2);
+        L.N2 = a.l2.N;
+        L.h = (float*)bufp(a.h_buf, 0);
+        L.ldh = a.l1.N;
+        L.counter = (unsigned long long*)bufp(a.counter_buf, 0);
+      }
+      L.out = (float*)viewp(a.out);
+      L.ldo = a.ldo;
+      L.softmax = a.softmax;
+      launch_small_mlp(L, s);
+      break;
+    }
   }
   if (cfg_.sync_after_launch) {
     PFB_CUDA(cudaStreamSynchronize(s));

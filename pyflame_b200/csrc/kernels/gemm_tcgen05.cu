@@ -41,6 +41,7 @@
 #include "../common.hpp"
 #include "kernels.hpp"
 #include "split.cuh"
+#include "act.cuh"
 #include "tcgen05.cuh"
 
 namespace pfb {
@@ -93,15 +94,6 @@ struct GemmParams {
   int nimg, halo_rows;
 };
 
-template <int ACT>
-__device__ __forceinline__ float act_apply(float v) {
-  if constexpr (ACT == 1) return (0.f < v) ? v : 0.f;
-  else if constexpr (ACT == 2) return 0.5f * v * (1.0f + tanhf(0.7978845608f * (v + 0.044715f * v * v * v)));
-  else if constexpr (ACT == 3) return 1.0f / (1.0f + expf(-v));
-  else if constexpr (ACT == 4) return tanhf(v);
-  else if constexpr (ACT == 5) return v / (1.0f + expf(-v));
-  else return v;
-}
 
 // Store one 32-row x 16-column block of a tile.  `ep` holds it row-major
 // with a 20-float row pitch; each pass a warp writes 8 rows x 16 columns,

@@ -154,6 +154,40 @@ struct PoolLaunch {
 };
 void launch_pool(const PoolLaunch& L, cudaStream_t stream);
 
+// Linear layers of a small batch (M <= kSmallMaxRows rows) on the CUDA cores:
+// layer 1 out1[m][n] = act1(alpha1 * sum_k a[m][k] * w1[n][k] + bias1[n]), with
+// w1 rows as Linear stores its weight ([out, in], pitch ldw1).  layers == 2
+// adds out[m][n] = act2(alpha2 * sum_j h[m][j] * w2[n][j] + bias2[n]) over
+// the layer-1 rows h, and softmax (1) or log-softmax (2) over each output
+// row, all in one launch; `counter` (8 bytes) must be zero at the launch.
+constexpr int64_t kSmallMaxRows = 256;
+struct SmallMlpLaunch {
+  int layers = 1;
+  const float* a = nullptr;
+  int64_t lda = 0, M = 0;
+  const float* w1 = nullptr;
+  int64_t ldw1 = 0, N1 = 0, K1 = 0;
+  const float* bias1 = nullptr;  // bias1[n * bstride1] (stride 0: one value)
+  int64_t bstride1 = 0;
+  float alpha1 = 1.f;
+  const float* alpha1_ptr = nullptr;
+  int act1 = 0;
+  const float* w2 = nullptr;  // [N2][ldw2], K2 = N1
+  int64_t ldw2 = 0, N2 = 0;
+  const float* bias2 = nullptr;
+  int64_t bstride2 = 0;
+  float alpha2 = 1.f;
+  const float* alpha2_ptr = nullptr;
+  int act2 = 0;
+  float* h = nullptr;  // layer-1 rows [M][ldh] (layers == 2)
+  int64_t ldh = 0;
+  float* out = nullptr;  // final rows [M][ldo]
+  int64_t ldo = 0;
+  int softmax = 0;
+  unsigned long long* counter = nullptr;
+};
+void launch_small_mlp(const SmallMlpLaunch& L, cudaStream_t stream);
+
 struct BnFoldLaunch {
   const float* gamma = nullptr; int64_t gs = 0;  // strides in elements (0 = splat)
   const float* beta = nullptr;  int64_t bs = 0;

@@ -1,0 +1,237 @@
+// small_gemm.cu — Linear layers of small batches on the CUDA cores, and a
+// two-layer perceptron (Linear, activation, Linear, optional softmax) in one
+// launch.
+//
+// With M <= 256 rows a tensor-core GEMM has at most two 128-row tiles per
+// output column block: a 64-row batch through Linear 784->256 keeps 2 of 148
+// SMs busy for the whole K loop, and the chain Linear -> ReLU -> Linear ->
+// softmax costs four launches whose latency dwarfs the 26 MFLOP of work.
+// Here every warp of a grid that covers the device computes a 4 x 4 block of
+// outputs, its 32 lanes splitting K (float4 loads, coalesced along the
+// weight rows), and reduces the 16 partial sums with shuffles; the bias,
+// scale and activation are applied by the lane that holds each result.  For
+// two layers, the CTA that finishes layer 1 last (an arrival counter zeroed
+// before the launch; no CTA waits on another) computes layer 2 from the
+// layer-1 rows in L2 and then the row softmax, so the whole chain is one
+// launch with no grid-wide barrier.  Products accumulate in fp32 FMAs, in a
+// different order than PyFlame's sequential sums (matmul.cpp:12-31): within
+// a few ulp times sqrt(K) of them.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+
+#include "../common.hpp"
+#include "act.cuh"
+#include "kernels.hpp"
+
+namespace pfb {
+
+namespace {
+
+constexpr int kSWarps = 8;  // warps per CTA
+
+struct SLayer {
+  const float* w;  // weight rows W[n][k] (Linear's [out, in] weight), row pitch ldw
+  long long ldw;
+  const float* bias;  // bias[n * bstride] or null
+  long long bstride;
+  float alpha;
+  const float* alpha_ptr;
+  int N, K, act;
+  int vec;  // float4 loads along K
+};
+
+struct SParams {
+  const float* a;
+  long long lda;
+  int M;
+  SLayer l1, l2;
+  int layers;
+  float* h;  // layer-1 rows when layers == 2
+  long long ldh;
+  float* out;
+  long long ldo;
+  int softmax;  // 0 none, 1 softmax, 2 log-softmax over the last layer's row
+  unsigned long long* counter;
+};
+
+template <bool CG>
+__device__ __forceinline__ float4 ld4(const float* p) {
+  if constexpr (CG) return __ldcg(reinterpret_cast<const float4*>(p));
+  else return __ldg(reinterpret_cast<const float4*>(p));
+}
+template <bool CG>
+__device__ __forceinline__ float ld1(const float* p) {
+  if constexpr (CG) return __ldcg(p);
+  else return __ldg(p);
+}
+
+// Warp `wid` of `nwarps`: 4 x 4 output blocks of act(alpha * x W^T + bias)
+// for the M rows of x (pitch ldx), written to dst[m * ldd + n].  CG: x was
+// written earlier in this launch by other CTAs (read through L2).
+template <bool VEC, bool CG>
+__device__ void layer_tiles(const float* x, long long ldx, int M, const SLayer& L, float* dst, long long ldd, int wid,
+                            int nwarps, int lane) {
+  const int tm = (M + 3) >> 2, tn = (L.N + 3) >> 2;
+  const float alpha = L.alpha_ptr ? *L.alpha_ptr : L.alpha;
+  for (int t = wid; t < tm * tn; t += nwarps) {
+    const int m0 = (t / tn) * 4, n0 = (t % tn) * 4;
+    const float* xr[4];
+    const float* wr[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      xr[i] = x + (long long)min(m0 + i, M - 1) * ldx;  // rows past the end repeat the last (not stored)
+      wr[i] = L.w + (long long)min(n0 + i, L.N - 1) * L.ldw;
+    }
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    if constexpr (VEC) {
+      for (int k = lane * 4; k < L.K; k += 128) {
+        float4 xa[4], wb[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          xa[i] = ld4<CG>(xr[i] + k);
+          wb[i] = ld4<false>(wr[i] + k);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            acc[i][j] = fmaf(xa[i].x, wb[j].x, acc[i][j]);
+            acc[i][j] = fmaf(xa[i].y, wb[j].y, acc[i][j]);
+            acc[i][j] = fmaf(xa[i].z, wb[j].z, acc[i][j]);
+            acc[i][j] = fmaf(xa[i].w, wb[j].w, acc[i][j]);
+          }
+      }
+    } else {
+      for (int k = lane; k < L.K; k += 32) {
+        float xa[4], wb[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          xa[i] = ld1<CG>(xr[i] + k);
+          wb[i] = ld1<false>(wr[i] + k);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xa[i], wb[j], acc[i][j]);
+      }
+    }
+    float mine = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float v = acc[i][j];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        if (lane == i * 4 + j) mine = v;
+      }
+    if (lane < 16) {
+      const int m = m0 + (lane >> 2), n = n0 + (lane & 3);
+      if (m < M && n < L.N) {
+        float v = mine * alpha;
+        if (L.bias) v += L.bias[(long long)n * L.bstride];
+        dst[(long long)m * ldd + n] = act_apply_rt(L.act, v);
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kSWarps * 32) small_mlp_kernel(SParams p) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int gw = blockIdx.x * kSWarps + warp, nw = gridDim.x * kSWarps;
+  float* dst1 = p.layers == 2 ? p.h : p.out;
+  const long long ld1 = p.layers == 2 ? p.ldh : p.ldo;
+  if (p.l1.vec) layer_tiles<true, false>(p.a, p.lda, p.M, p.l1, dst1, ld1, gw, nw, lane);
+  else layer_tiles<false, false>(p.a, p.lda, p.M, p.l1, dst1, ld1, gw, nw, lane);
+  if (p.layers == 1) return;
+  // The last CTA to arrive runs layer 2: its layer-1 rows are complete and,
+  // after the fences, visible in L2 (read with ld.global.cg below).
+  __shared__ int last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(p.counter, 1ull) == (unsigned long long)(gridDim.x - 1);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  if (p.l2.vec) layer_tiles<true, true>(p.h, p.ldh, p.M, p.l2, p.out, p.ldo, warp, kSWarps, lane);
+  else layer_tiles<false, true>(p.h, p.ldh, p.M, p.l2, p.out, p.ldo, warp, kSWarps, lane);
+  if (!p.softmax) return;
+  __syncthreads();  // this CTA's layer-2 stores are visible to all its threads
+  const int N = p.l2.N;
+  for (int m = warp; m < p.M; m += kSWarps) {
+    float* row = p.out + (long long)m * p.ldo;
+    float mx = -__int_as_float(0x7f800000);
+    for (int n = lane; n < N; n += 32) mx = fmaxf(mx, row[n]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float s = 0.f;
+    for (int n = lane; n < N; n += 32) s += expf(row[n] - mx);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (p.softmax == 1) {
+      for (int n = lane; n < N; n += 32) row[n] = expf(row[n] - mx) / s;
+    } else {
+      const float ls = logf(s);
+      for (int n = lane; n < N; n += 32) row[n] = row[n] - mx - ls;
+    }
+  }
+}
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+}  // namespace
+
+void launch_small_mlp(const SmallMlpLaunch& L, cudaStream_t stream) {
+  PFB_CHECK_ARG(L.M > 0 && L.M <= kSmallMaxRows, "small GEMM: 1..256 rows");
+  PFB_CHECK_ARG(L.layers == 1 || L.layers == 2, "small GEMM: one or two layers");
+  PFB_CHECK_ARG(L.a && L.w1 && L.out && L.N1 > 0 && L.K1 > 0 && L.lda >= L.K1 && L.ldw1 >= L.K1,
+                "small GEMM: bad layer-1 operands");
+  PFB_CHECK_ARG(L.K1 < (1 << 24) && L.N1 < (1 << 20), "small GEMM: layer too large");
+  SParams p{};
+  p.a = L.a;
+  p.lda = L.lda;
+  p.M = (int)L.M;
+  p.layers = L.layers;
+  p.out = L.out;
+  p.ldo = L.ldo;
+  p.softmax = L.softmax;
+  auto layer = [](SLayer& s, const float* w, int64_t ldw, const float* bias, int64_t bstride, float alpha,
+                  const float* alpha_ptr, int64_t N, int64_t K, int act, const float* x, int64_t ldx) {
+    s.w = w;
+    s.ldw = ldw;
+    s.bias = bias;
+    s.bstride = bstride;
+    s.alpha = alpha;
+    s.alpha_ptr = alpha_ptr;
+    s.N = (int)N;
+    s.K = (int)K;
+    s.act = act;
+    s.vec = K % 4 == 0 && ldw % 4 == 0 && ldx % 4 == 0 && aligned16(w) && aligned16(x);
+  };
+  layer(p.l1, L.w1, L.ldw1, L.bias1, L.bstride1, L.alpha1, L.alpha1_ptr, L.N1, L.K1, L.act1, L.a, L.lda);
+  if (L.layers == 2) {
+    PFB_CHECK_ARG(L.w2 && L.h && L.counter && L.N2 > 0 && L.ldw2 >= L.N1 && L.ldh >= L.N1 && L.N2 < (1 << 20),
+                  "small GEMM: bad layer-2 operands");
+    layer(p.l2, L.w2, L.ldw2, L.bias2, L.bstride2, L.alpha2, L.alpha2_ptr, L.N2, L.N1, L.act2, L.h, L.ldh);
+    p.h = L.h;
+    p.ldh = L.ldh;
+    p.counter = L.counter;
+    PFB_CHECK_ARG(L.ldo >= L.N2, "small GEMM: output pitch below the row length");
+  } else {
+    PFB_CHECK_ARG(L.softmax == 0, "small GEMM: a fused softmax needs two layers");
+    PFB_CHECK_ARG(L.ldo >= L.N1, "small GEMM: output pitch below the row length");
+  }
+  const int64_t tiles = ((L.M + 3) / 4) * ((L.N1 + 3) / 4);
+  const int64_t sms = device_sm_count(current_device());
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((tiles + kSWarps - 1) / kSWarps, 4 * sms));
+  small_mlp_kernel<<<grid, kSWarps * 32, 0, stream>>>(p);
+  PFB_CUDA(cudaGetLastError());
+}
+
+}  // namespace pfb

@@ -62,6 +62,7 @@ enum class StepKind : uint8_t {
   BN_FOLD,    // fold BatchNorm(eval) into per-channel scale/shift
   MEMSET,     // zero a buffer range
   ATTENTION,  // fused softmax(alpha * Q K^T) V (tcgen05)
+  SMALL,      // Linear layers of a small batch on the CUDA cores (one or two layers, optional softmax)
 };
 
 // Pointer-argument buffer index that resolves to the executor's device error
@@ -168,6 +169,31 @@ struct AttnArgs {
   bool write_c = true;
 };
 
+// One or two Linear layers of a small batch: a [M, K1] rows (pitch lda) times
+// the transposed weights w1 [N1][K1] (pitch ldw1), epilogue alpha/bias/act;
+// with two layers, the layer-1 rows go to `h` and the last CTA runs layer 2
+// and an optional softmax (1) / log-softmax (2) into `out`.
+struct SmallLayerArgs {
+  int w_buf = -1;
+  int64_t w_off = 0, ldw = 0, N = 0, K = 0;
+  View bias;
+  bool has_bias = false;
+  int64_t bstride = 0;
+  float alpha = 1.f;
+  int alpha_slot = -1;
+  int act = 0;
+};
+struct SmallArgs {
+  View a;
+  int64_t lda = 0, M = 0;
+  int layers = 1;
+  SmallLayerArgs l1, l2;
+  int h_buf = -1, counter_buf = -1;
+  View out;
+  int64_t ldo = 0;
+  int softmax = 0;
+};
+
 struct Step {
   StepKind kind = StepKind::JIT;
   bool once = false;           // fills PREPARED buffers: runs only while they are unfilled
@@ -180,6 +206,7 @@ struct Step {
   PoolArgs pool;
   BnFoldArgs bnfold;
   AttnArgs attn;
+  SmallArgs small;
   int memset_buf = -1;
 };
 

@@ -51,7 +51,8 @@ def test_workload_plans_compile(native, name, kw, precision):
     if name == "fused":
         assert desc.count("row kernel") == 1 and "fused elementwise" not in desc
     if name == "mlp":
-        assert desc.count("gemm") == 2 and "fused elementwise" not in desc
+        # Linear, ReLU, Linear and softmax of a 64-sample batch: one launch
+        assert "small mlp [64x256x784 -> 10] +softmax" in desc and "row kernel" not in desc, desc
     if name == "convstack":
         assert "fold batch_norm" in desc and desc.count("conv gemm") == 3
 

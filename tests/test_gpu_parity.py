@@ -283,7 +283,40 @@ def test_linear_relu_softmax_mlp(cuda_executor, oracle_mod):
     (g,), (r,) = run(cuda_executor, w.outputs, oracle_mod)
     close(g, r, rtol=1e-4, atol=1e-6, what="mlp softmax")
     plan = cuda_executor.describe_plan(w.outputs[0].graph(), [w.outputs[0].node().id()])
-    assert plan.count("gemm") == 2, plan  # bias + relu fused into the GEMM epilogues
+    # Linear, ReLU, Linear and softmax in one launch (the arrival-counter reset is a memset)
+    assert "small mlp [64x256x784 -> 10] +softmax" in plan and "row kernel" not in plan, plan
+
+
+@pytest.mark.parametrize("m,k,n1,n2,act,soft", [(64, 784, 256, 10, "relu", "softmax"), (1, 7, 5, 3, "tanh", "log"),
+                                                (256, 130, 96, 70, "gelu", "softmax"), (33, 64, 48, 17, "sigmoid", ""),
+                                                (200, 64, 1000, 0, "", ""), (5, 12, 9, 0, "silu", "")])
+def test_small_batch_linear_layers(cuda_executor, oracle_mod, rng, m, k, n1, n2, act, soft):
+    """Small batches of Linear layers run on the CUDA cores: one layer alone,
+    or Linear -> activation -> Linear (-> softmax / log-softmax) as one
+    launch; scalar loads when K is not a multiple of 4, rows past 32 in the
+    softmax, single rows."""
+    x = pf.tensor(rng.standard_normal((m, k)).astype(np.float32))
+    with nn.deferred_init():
+        l1 = nn.Linear(k, n1)
+        l2 = nn.Linear(n1, max(n2, 1))
+    l1.set_parameter("weight", (rng.standard_normal((n1, k)) / np.sqrt(k)).astype(np.float32))
+    l1.set_parameter("bias", rng.standard_normal(n1).astype(np.float32))
+    l2.set_parameter("weight", (rng.standard_normal((max(n2, 1), n1)) / np.sqrt(n1)).astype(np.float32))
+    fn = {"relu": pf.relu, "tanh": pf.tanh, "gelu": pf.gelu, "sigmoid": pf.sigmoid, "silu": pf.silu,
+          "": lambda t: t}[act]
+    y = fn(l1(x))
+    if n2:
+        y = l2(y)
+        if soft:
+            y = (pf.softmax if soft == "softmax" else pf.log_softmax)(y, -1)
+    plan = cuda_executor.describe_plan(y.graph(), [y.node().id()])
+    assert ("small mlp" if n2 else "small gemm") in plan and "row kernel" not in plan, plan
+    (g,), (r,) = run(cuda_executor, [y], oracle_mod)
+    close_rows(g, r, RTOL_GEMM_TF32X3, what="small batch layers")
+    # scaled product without a bias
+    z = pf.matmul(x, l1.p("weight").transpose(0, 1)) * 0.125
+    (g,), (r,) = run(cuda_executor, [z], oracle_mod)
+    close_rows(g, r, RTOL_GEMM_TF32X3, what="scaled small gemm")
 
 
 def test_gemm_epilogues(cuda_executor, oracle_mod, rng):
