@@ -20,6 +20,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <mutex>
 
 #include "../common.hpp"
 #include "act.cuh"
@@ -54,7 +55,10 @@ struct SParams {
   long long ldo;
   int softmax;  // 0 none, 1 softmax, 2 log-softmax over the last layer's row
   unsigned long long* counter;
+  int l2_smem;  // layer 2 from shared-memory copies of h and w2 (dynamic shared memory)
 };
+
+constexpr size_t kSmallSmemMax = 160 * 1024;  // largest staging of layer 2
 
 template <bool CG>
 __device__ __forceinline__ float4 ld4(const float* p) {
@@ -90,6 +94,7 @@ __device__ void layer_tiles(const float* x, long long ldx, int M, const SLayer& 
 #pragma unroll
       for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
     if constexpr (VEC) {
+#pragma unroll 2
       for (int k = lane * 4; k < L.K; k += 128) {
         float4 xa[4], wb[4];
 #pragma unroll
@@ -142,13 +147,67 @@ __device__ void layer_tiles(const float* x, long long ldx, int M, const SLayer& 
   }
 }
 
+// The same for short rows (K <= kShortK): warp `wid` takes 4 rows x 32
+// columns, lane = column; each lane runs the K loop over its weight row
+// (float4) against the 4 rows of x, which all lanes read at the same address
+// (one broadcast transaction).  No cross-lane reduction; no idle lanes when K
+// is shorter than a warp's 128-element stride.
+template <bool VEC>
+__device__ void layer_rows32(const float* x, long long ldx, int M, const SLayer& L, float* dst, long long ldd, int wid,
+                             int nwarps, int lane) {
+  const int tm = (M + 3) >> 2, tn = (L.N + 31) >> 5;
+  const float alpha = L.alpha_ptr ? *L.alpha_ptr : L.alpha;
+  for (int t = wid; t < tm * tn; t += nwarps) {
+    const int m0 = (t / tn) * 4, n = (t % tn) * 32 + lane;
+    const float* wr = L.w + (long long)min(n, L.N - 1) * L.ldw;
+    const float* xr[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) xr[i] = x + (long long)min(m0 + i, M - 1) * ldx;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    if constexpr (VEC) {
+#pragma unroll 4
+      for (int k = 0; k < L.K; k += 4) {
+        const float4 w = __ldg(reinterpret_cast<const float4*>(wr + k));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 a = __ldg(reinterpret_cast<const float4*>(xr[i] + k));
+          acc[i] = fmaf(a.x, w.x, acc[i]);
+          acc[i] = fmaf(a.y, w.y, acc[i]);
+          acc[i] = fmaf(a.z, w.z, acc[i]);
+          acc[i] = fmaf(a.w, w.w, acc[i]);
+        }
+      }
+    } else {
+      for (int k = 0; k < L.K; ++k) {
+        const float w = __ldg(wr + k);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[i] = fmaf(__ldg(xr[i] + k), w, acc[i]);
+      }
+    }
+    if (n < L.N) {
+      const float b = L.bias ? L.bias[(long long)n * L.bstride] : 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (m0 + i < M) dst[(long long)(m0 + i) * ldd + n] = act_apply_rt(L.act, acc[i] * alpha + b);
+    }
+  }
+}
+
+constexpr int kShortK = 256;
+
 __global__ void __launch_bounds__(kSWarps * 32) small_mlp_kernel(SParams p) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gw = blockIdx.x * kSWarps + warp, nw = gridDim.x * kSWarps;
   float* dst1 = p.layers == 2 ? p.h : p.out;
   const long long ld1 = p.layers == 2 ? p.ldh : p.ldo;
-  if (p.l1.vec) layer_tiles<true, false>(p.a, p.lda, p.M, p.l1, dst1, ld1, gw, nw, lane);
-  else layer_tiles<false, false>(p.a, p.lda, p.M, p.l1, dst1, ld1, gw, nw, lane);
+  if (p.l1.K <= kShortK) {
+    if (p.l1.vec) layer_rows32<true>(p.a, p.lda, p.M, p.l1, dst1, ld1, gw, nw, lane);
+    else layer_rows32<false>(p.a, p.lda, p.M, p.l1, dst1, ld1, gw, nw, lane);
+  } else if (p.l1.vec) {
+    layer_tiles<true, false>(p.a, p.lda, p.M, p.l1, dst1, ld1, gw, nw, lane);
+  } else {
+    layer_tiles<false, false>(p.a, p.lda, p.M, p.l1, dst1, ld1, gw, nw, lane);
+  }
   if (p.layers == 1) return;
   // The last CTA to arrive runs layer 2: its layer-1 rows are complete and,
   // after the fences, visible in L2 (read with ld.global.cg below).
@@ -159,8 +218,40 @@ __global__ void __launch_bounds__(kSWarps * 32) small_mlp_kernel(SParams p) {
   __syncthreads();
   if (!last) return;
   __threadfence();
-  if (p.l2.vec) layer_tiles<true, true>(p.h, p.ldh, p.M, p.l2, p.out, p.ldo, warp, kSWarps, lane);
-  else layer_tiles<false, true>(p.h, p.ldh, p.M, p.l2, p.out, p.ldo, warp, kSWarps, lane);
+  if (p.l2_smem) {
+    // Stage the layer-1 rows and the layer-2 weight in shared memory (rows
+    // padded by one float so threads on different rows hit different banks),
+    // then every thread computes whole outputs: one memory round trip
+    // instead of one per 4x4 block.
+    extern __shared__ float sm[];
+    const int K2 = p.l2.K, ld = K2 + 1, N2 = p.l2.N;
+    float* hs = sm;
+    float* ws = sm + (size_t)p.M * ld;
+    for (int i = threadIdx.x; i < p.M * K2; i += blockDim.x) {
+      const int m = i / K2, k = i - m * K2;
+      hs[m * ld + k] = __ldcg(p.h + (long long)m * p.ldh + k);
+    }
+    for (int i = threadIdx.x; i < N2 * K2; i += blockDim.x) {
+      const int n = i / K2, k = i - n * K2;
+      ws[n * ld + k] = __ldg(p.l2.w + (long long)n * p.l2.ldw + k);
+    }
+    __syncthreads();
+    const float alpha = p.l2.alpha_ptr ? *p.l2.alpha_ptr : p.l2.alpha;
+    for (int o = threadIdx.x; o < p.M * N2; o += blockDim.x) {
+      const int m = o / N2, n = o - m * N2;
+      const float* hr = hs + m * ld;
+      const float* wr = ws + n * ld;
+      float acc = 0.f;
+      for (int k = 0; k < K2; ++k) acc = fmaf(hr[k], wr[k], acc);
+      float v = acc * alpha;
+      if (p.l2.bias) v += p.l2.bias[(long long)n * p.l2.bstride];
+      p.out[(long long)m * p.ldo + n] = act_apply_rt(p.l2.act, v);
+    }
+  } else if (p.l2.vec) {
+    layer_tiles<true, true>(p.h, p.ldh, p.M, p.l2, p.out, p.ldo, warp, kSWarps, lane);
+  } else {
+    layer_tiles<false, true>(p.h, p.ldh, p.M, p.l2, p.out, p.ldo, warp, kSWarps, lane);
+  }
   if (!p.softmax) return;
   __syncthreads();  // this CTA's layer-2 stores are visible to all its threads
   const int N = p.l2.N;
@@ -227,10 +318,23 @@ void launch_small_mlp(const SmallMlpLaunch& L, cudaStream_t stream) {
     PFB_CHECK_ARG(L.softmax == 0, "small GEMM: a fused softmax needs two layers");
     PFB_CHECK_ARG(L.ldo >= L.N1, "small GEMM: output pitch below the row length");
   }
-  const int64_t tiles = ((L.M + 3) / 4) * ((L.N1 + 3) / 4);
-  const int64_t sms = device_sm_count(current_device());
+  size_t smem = 0;
+  if (L.layers == 2) {
+    const size_t need = (size_t)(L.M + L.N2) * (size_t)(L.N1 + 1) * sizeof(float);
+    if (need <= kSmallSmemMax) {
+      p.l2_smem = 1;
+      smem = need;
+    }
+  }
+  const int dev = current_device();
+  static std::once_flag attr_once[64];
+  std::call_once(attr_once[dev], [] {
+    PFB_CUDA(cudaFuncSetAttribute(small_mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmallSmemMax));
+  });
+  const int64_t tiles = ((L.M + 3) / 4) * (L.K1 <= kShortK ? (L.N1 + 31) / 32 : (L.N1 + 3) / 4);
+  const int64_t sms = device_sm_count(dev);
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((tiles + kSWarps - 1) / kSWarps, 4 * sms));
-  small_mlp_kernel<<<grid, kSWarps * 32, 0, stream>>>(p);
+  small_mlp_kernel<<<grid, kSWarps * 32, smem, stream>>>(p);
   PFB_CUDA(cudaGetLastError());
 }
 

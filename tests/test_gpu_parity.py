@@ -289,12 +289,16 @@ def test_linear_relu_softmax_mlp(cuda_executor, oracle_mod):
 
 @pytest.mark.parametrize("m,k,n1,n2,act,soft", [(64, 784, 256, 10, "relu", "softmax"), (1, 7, 5, 3, "tanh", "log"),
                                                 (256, 130, 96, 70, "gelu", "softmax"), (33, 64, 48, 17, "sigmoid", ""),
-                                                (200, 64, 1000, 0, "", ""), (5, 12, 9, 0, "silu", "")])
+                                                (200, 64, 1000, 0, "", ""), (5, 12, 9, 0, "silu", ""),
+                                                (17, 301, 40, 9, "relu", "softmax"),
+                                                (256, 300, 200, 20, "gelu", "log")])
 def test_small_batch_linear_layers(cuda_executor, oracle_mod, rng, m, k, n1, n2, act, soft):
     """Small batches of Linear layers run on the CUDA cores: one layer alone,
     or Linear -> activation -> Linear (-> softmax / log-softmax) as one
-    launch; scalar loads when K is not a multiple of 4, rows past 32 in the
-    softmax, single rows."""
+    launch; short rows (lane per column) and long rows (lanes split K), float4
+    and scalar loads (K not a multiple of 4), layer 2 from shared memory or,
+    when h and the weight do not fit there, from L2; softmax rows past 32;
+    single rows."""
     x = pf.tensor(rng.standard_normal((m, k)).astype(np.float32))
     with nn.deferred_init():
         l1 = nn.Linear(k, n1)
