@@ -327,7 +327,7 @@ def _roofline(name, w, kernels, ms_per_step, precision, pk, pk_kind):
     top = max(kernels, key=lambda k: k[1]) if kernels else ("", 0.0)
     if w.flops:
         bound, unit = "tensor", "TFLOP/s"
-        dom = sum(ms for n, ms in kernels if n.startswith(("gemm", "conv gemm", "attention")))
+        dom = sum(ms for n, ms in kernels if n.startswith(("gemm", "conv gemm", "attention", "small")))
         dom_ms = ms_per_step * dom / total
         achieved = w.flops / (dom_ms / 1e3) / 1e12 if dom else 0.0
         peak = pk.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])

@@ -635,3 +635,18 @@ def test_memory_stats_and_release(cuda_executor):
     assert s.total_allocations >= 1
     info = cuda_executor.get_device_info()
     assert info.architecture.startswith("sm_10")
+
+
+def test_empty_and_degenerate_shapes(cuda_executor, oracle_mod, rng):
+    """Zero-row batches, a reduction over a length-1 dim, a 1x1 matmul and a
+    single-element softmax row: the executor returns correctly shaped (and,
+    where defined, exact) results instead of failing a launch."""
+    e = pf.tensor(np.zeros((0, 8), np.float32))
+    w = pf.tensor(rng.standard_normal((8, 4)).astype(np.float32))
+    one = pf.tensor(rng.standard_normal((5, 1)).astype(np.float32))
+    outs = [pf.relu(e) * 2.0, pf.matmul(e, w), one.sum(1), one.max(1), pf.softmax(one, -1),
+            pf.matmul(pf.tensor([[3.0]]), pf.tensor([[-2.0]]))]
+    gpu, ref = run(cuda_executor, outs, oracle_mod)
+    assert gpu[0].shape == (0, 8) and gpu[1].shape == (0, 4)
+    for g_, r_ in zip(gpu[2:], ref[2:]):
+        bitexact(g_, r_)
