@@ -2557,6 +2557,11 @@ void Compiler::lower_matmul(const GemmChain& ch, int at) {
   }
   int64_t gbatch = b_batched ? nbatch : 1;
   int64_t gM = b_batched ? M : nbatch * M;
+  if (gM == 0 || Nn == 0 || nbatch == 0) {
+    // an empty product: nothing to compute, the (empty) output needs no launch
+    val_[ch.result] = dense(mm.shape, DType::F32);
+    return;
+  }
   // prepared operands
   int64_t arows = nbatch * M, brows = (b_batched ? nbatch : 1) * Nn;
   const Operand opa = prepare_operand(av, arows, K, kpad, prec, "prepare A " + shape_str(afull), at);

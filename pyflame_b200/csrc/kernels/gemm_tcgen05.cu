@@ -266,6 +266,18 @@ struct Cfg {
   static constexpr int A_TILE = kBM * 128;
   static constexpr int B_TILE = BN * 128;
   static constexpr int STAGE = NOPS * (A_TILE + B_TILE);
+  // stage layout [A_hi][A_lo][B_hi][B_lo]: B_hi and B_lo adjacent, so one
+  // descriptor spans both as a 2*BN-row operand
+  static constexpr int A_LO_OFF = A_TILE;
+  static constexpr int B_HI_OFF = NOPS * A_TILE;
+  static constexpr int B_LO_OFF = B_HI_OFF + B_TILE;
+  // 64-column 3xTF32 tiles issue A_hi x [B_hi | B_lo] as ONE N = 128
+  // instruction (64 cycles, against 2 x 48 for two N = 64 ones, and A_hi
+  // read once instead of twice), then A_lo x B_hi (N = 64) into the first
+  // half; the epilogue adds the two halves.  Wider tiles keep three products
+  // into one accumulator.
+  static constexpr bool CAT = NOPS == 2 && BN == 64;
+  static constexpr int ACC_COLS = CAT ? 2 * BN : BN;
   // epilogue staging: per epilogue warp a 32 x 33 fp32 tile (padded: no bank conflicts)
   static constexpr int EPI_WARP_FLOATS = 32 * 20;  // a 32 x 16 block, 20-float pitch
   static constexpr int EPI_BYTES = kEpiWarps * EPI_WARP_FLOATS * 4;
@@ -273,8 +285,9 @@ struct Cfg {
   static constexpr int STAGES_FIT = (SMEM_LIMIT - EPI_BYTES - 2048) / STAGE;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int SMEM = STAGES * STAGE + EPI_BYTES + 1024 /*barriers*/ + 1024 /*align*/;
-  static constexpr int TMEM_COLS = 2 * BN;  // two accumulators: epilogue of tile i overlaps MMAs of tile i+1
+  static constexpr int TMEM_COLS = 2 * ACC_COLS;  // two accumulators: epilogue of tile i overlaps MMAs of tile i+1
   static constexpr uint32_t IDESC = idesc(kBM, BN, PREC == PFC_PRECISION_BF16 ? 1u : 2u);
+  static constexpr uint32_t IDESC_CAT = idesc(kBM, 2 * BN, 2u);
   static_assert(STAGES >= 2, "shared memory too small for two stages");
   static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation");
 };
@@ -350,12 +363,22 @@ __device__ __forceinline__ void run_epilogue(const GemmParams& p, uint32_t tmem,
 #pragma unroll
         for (int cc = 0; cc < HALF; cc += 32) {
           uint32_t r[32];
-          const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + col0 + cc);
+          const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * C::ACC_COLS + col0 + cc);
           tmem_ld16_nowait(ta, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
           tmem_ld16_nowait(ta + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
-          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          if constexpr (C::CAT) {
+            // the A_hi x B_lo half of a concatenated accumulator
+            uint32_t r2[32];
+            tmem_ld16_nowait(ta + BN, *reinterpret_cast<uint32_t(*)[16]>(&r2[0]));
+            tmem_ld16_nowait(ta + BN + 16, *reinterpret_cast<uint32_t(*)[16]>(&r2[16]));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[cc + j] += __uint_as_float(r[j]);
+            for (int j = 0; j < 32; ++j) acc[cc + j] += __uint_as_float(r[j]) + __uint_as_float(r2[j]);
+          } else {
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[cc + j] += __uint_as_float(r[j]);
+          }
         }
       }
       // the chunk is in registers: hand the accumulator back to the MMA warp
@@ -487,11 +510,11 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
         if (r == 0) {
           const uint32_t fb = smem_u32(&full[s]);
           mbar_expect_tx(fb, C::NOPS * C::B_TILE);
-          tma_load_3d(smem_u32(st + C::A_TILE), &tb_hi, fb, kb * C::BK, n0, 0);
-          if constexpr (C::NOPS == 2) tma_load_3d(smem_u32(st + 2 * C::A_TILE + C::B_TILE), &tb_lo, fb, kb * C::BK, n0, 0);
+          tma_load_3d(smem_u32(st + C::B_HI_OFF), &tb_hi, fb, kb * C::BK, n0, 0);
+          if constexpr (C::NOPS == 2) tma_load_3d(smem_u32(st + C::B_LO_OFF), &tb_lo, fb, kb * C::BK, n0, 0);
         }
         const uint32_t arow_hi = smem_u32(st) + (uint32_t)r * 128u;
-        const uint32_t arow_lo = smem_u32(st + C::A_TILE + C::B_TILE) + (uint32_t)r * 128u;
+        const uint32_t arow_lo = smem_u32(st + C::A_LO_OFF) + (uint32_t)r * 128u;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int ih = ih0 + kh * p.dh, iw = iw0 + kw * p.dw;
@@ -541,7 +564,7 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
         const uint32_t fb = smem_u32(&full[s]);
         mbar_expect_tx(fb, C::STAGE);
         const int kc = kb * C::BK;
-        const uint32_t a_hi_dst = smem_u32(st), a_lo_dst = smem_u32(st + C::A_TILE + C::B_TILE);
+        const uint32_t a_hi_dst = smem_u32(st), a_lo_dst = smem_u32(st + C::A_LO_OFF);
         if (p.conv_tma == 1) {
           // BK channels (128 bytes) of one filter tap: a TH x TW box of the input
           // shifted by the tap
@@ -563,8 +586,8 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
           tma_load_3d(a_hi_dst, &ta_hi, fb, kc, m0, ca);
           if constexpr (C::NOPS == 2) tma_load_3d(a_lo_dst, &ta_lo, fb, kc, m0, ca);
         }
-        tma_load_3d(smem_u32(st + C::A_TILE), &tb_hi, fb, kc, n0, cb);
-        if constexpr (C::NOPS == 2) tma_load_3d(smem_u32(st + 2 * C::A_TILE + C::B_TILE), &tb_lo, fb, kc, n0, cb);
+        tma_load_3d(smem_u32(st + C::B_HI_OFF), &tb_hi, fb, kc, n0, cb);
+        if constexpr (C::NOPS == 2) tma_load_3d(smem_u32(st + C::B_LO_OFF), &tb_lo, fb, kc, n0, cb);
       }
     }
     // drain: every issued copy must have landed before the CTA can exit
@@ -584,7 +607,7 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
         const uint32_t use = (uint32_t)(u >> 1);
         if (u >= 2 && !mbar_wait(smem_u32(&acc_empty[b]), (use & 1u) ^ 1u, p.err)) { ok = false; break; }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t acc_t = tmem + (uint32_t)(b * BN);
+        const uint32_t acc_t = tmem + (uint32_t)(b * C::ACC_COLS);
         const int kb0 = ch * p.kchunk, kb1 = min(nkb, kb0 + p.kchunk);
         for (int kb = kb0; kb < kb1; ++kb, ++g) {
           const int s = g % C::STAGES;
@@ -592,13 +615,17 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
           if (!mbar_wait(smem_u32(&full[s]), ph, p.err)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const uint32_t st = smem_u32(smem + s * C::STAGE);
-          const uint64_t da_hi = sdesc(st), db_hi = sdesc(st + C::A_TILE);
-          const uint64_t da_lo = sdesc(st + C::A_TILE + C::B_TILE), db_lo = sdesc(st + 2 * C::A_TILE + C::B_TILE);
+          const uint64_t da_hi = sdesc(st), db_hi = sdesc(st + C::B_HI_OFF);
+          const uint64_t da_lo = sdesc(st + C::A_LO_OFF), db_lo = sdesc(st + C::B_LO_OFF);
 #pragma unroll
           for (int ks = 0; ks < C::KSTEPS; ++ks) {
             const uint32_t koff = ks * 32;  // 32 bytes of K per instruction
             const uint32_t acc = (kb > kb0 || ks > 0) ? 1u : 0u;
-            if constexpr (C::NOPS == 2) {
+            if constexpr (C::CAT) {
+              // [A_hi B_hi | A_hi B_lo] (starts both halves), then + A_lo B_hi
+              umma<PREC>(acc_t, desc_add(da_hi, koff), desc_add(db_hi, koff), C::IDESC_CAT, acc);
+              umma<PREC>(acc_t, desc_add(da_lo, koff), desc_add(db_hi, koff), C::IDESC, 1u);
+            } else if constexpr (C::NOPS == 2) {
               // small products first, then the leading term
               umma<PREC>(acc_t, desc_add(da_lo, koff), desc_add(db_hi, koff), C::IDESC, acc);
               umma<PREC>(acc_t, desc_add(da_hi, koff), desc_add(db_lo, koff), C::IDESC, 1u);
@@ -803,7 +830,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
                 break;
               }
               asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-              acc_t = tmem + (uint32_t)(b * BN);
+              acc_t = tmem + (uint32_t)(b * C::ACC_COLS);
               left = min(p.kchunk, p.nkb - j);
             }
             if (!mbar_wait(smem_u32(&full[s]), sph, p.err)) { ok = false; break; }
@@ -814,7 +841,11 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
             for (int ks = 0; ks < C::KSTEPS; ++ks) {
               const uint32_t koff = ks * 32;
               const uint32_t acc = (!first || ks > 0) ? 1u : 0u;
-              if constexpr (C::NOPS == 2) {
+              if constexpr (C::CAT) {
+                // [B_hi | B_lo] are adjacent in the stage: one N = 128 instruction
+                umma<PREC>(acc_t, desc_add(da_hi, koff), desc_add(db_hi, koff), C::IDESC_CAT, acc);
+                umma<PREC>(acc_t, desc_add(da_lo, koff), desc_add(db_hi, koff), C::IDESC, 1u);
+              } else if constexpr (C::NOPS == 2) {
                 umma<PREC>(acc_t, desc_add(da_lo, koff), desc_add(db_hi, koff), C::IDESC, acc);
                 umma<PREC>(acc_t, desc_add(da_hi, koff), desc_add(db_lo, koff), C::IDESC, 1u);
                 umma<PREC>(acc_t, desc_add(da_hi, koff), desc_add(db_hi, koff), C::IDESC, 1u);

@@ -227,13 +227,30 @@ __global__ void __launch_bounds__(kSWarps * 32) small_mlp_kernel(SParams p) {
     const int K2 = p.l2.K, ld = K2 + 1, N2 = p.l2.N;
     float* hs = sm;
     float* ws = sm + (size_t)p.M * ld;
-    for (int i = threadIdx.x; i < p.M * K2; i += blockDim.x) {
-      const int m = i / K2, k = i - m * K2;
-      hs[m * ld + k] = __ldcg(p.h + (long long)m * p.ldh + k);
-    }
-    for (int i = threadIdx.x; i < N2 * K2; i += blockDim.x) {
-      const int n = i / K2, k = i - n * K2;
-      ws[n * ld + k] = __ldg(p.l2.w + (long long)n * p.l2.ldw + k);
+    // eight loads in flight per thread before their stores (one L2 round
+    // trip per eight elements, not per element)
+    constexpr int kBatch = 8;
+    const int nh = p.M * K2, nall = nh + N2 * K2;
+    for (int i0 = threadIdx.x; i0 < nall; i0 += blockDim.x * kBatch) {
+      float v[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int i = i0 + u * blockDim.x;
+        v[u] = 0.f;
+        if (i < nh) {
+          const int m = i / K2;
+          v[u] = __ldcg(p.h + (long long)m * p.ldh + (i - m * K2));
+        } else if (i < nall) {
+          const int n = (i - nh) / K2;
+          v[u] = __ldg(p.l2.w + (long long)n * p.l2.ldw + (i - nh - n * K2));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int i = i0 + u * blockDim.x;
+        if (i < nh) hs[(i / K2) * ld + i % K2] = v[u];
+        else if (i < nall) ws[((i - nh) / K2) * ld + (i - nh) % K2] = v[u];
+      }
     }
     __syncthreads();
     const float alpha = p.l2.alpha_ptr ? *p.l2.alpha_ptr : p.l2.alpha;
