@@ -92,6 +92,13 @@ struct GemmParams {
   //     block.
   int conv_tma, TW, TH, tiles_w, tiles_h;
   int nimg, halo_rows;
+  // 64-column 3xTF32 tiles: issue A_hi x [B_hi | B_lo] as one 128-column
+  // instruction (Cfg::CAT) for this launch.  Chosen when a tile has enough
+  // k-blocks that the MMAs, not the epilogue, set the pace: the concatenated
+  // accumulator doubles the epilogue's TMEM reads, which a 7-k-block tile
+  // (the 7x7 stem convolution) cannot hide (measured 0.96 -> 1.20 ms), while
+  // 18-k-block tiles gain (3x3 convolutions, 0.54 -> 0.45 ms).
+  int cat;
 };
 
 
@@ -271,13 +278,13 @@ struct Cfg {
   static constexpr int A_LO_OFF = A_TILE;
   static constexpr int B_HI_OFF = NOPS * A_TILE;
   static constexpr int B_LO_OFF = B_HI_OFF + B_TILE;
-  // 64-column 3xTF32 tiles issue A_hi x [B_hi | B_lo] as ONE N = 128
+  // 64-column 3xTF32 tiles may issue A_hi x [B_hi | B_lo] as ONE N = 128
   // instruction (64 cycles, against 2 x 48 for two N = 64 ones, and A_hi
   // read once instead of twice), then A_lo x B_hi (N = 64) into the first
-  // half; the epilogue adds the two halves.  Wider tiles keep three products
-  // into one accumulator.
+  // half; the epilogue adds the two halves (GemmParams::cat picks it per
+  // launch).  Wider tiles keep three products into one accumulator.
   static constexpr bool CAT = NOPS == 2 && BN == 64;
-  static constexpr int ACC_COLS = CAT ? 2 * BN : BN;
+  static constexpr int ACC_COLS = CAT ? 2 * BN : BN;  // columns reserved per accumulator
   // epilogue staging: per epilogue warp a 32 x 33 fp32 tile (padded: no bank conflicts)
   static constexpr int EPI_WARP_FLOATS = 32 * 20;  // a 32 x 16 block, 20-float pitch
   static constexpr int EPI_BYTES = kEpiWarps * EPI_WARP_FLOATS * 4;
@@ -366,7 +373,7 @@ __device__ __forceinline__ void run_epilogue(const GemmParams& p, uint32_t tmem,
           const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * C::ACC_COLS + col0 + cc);
           tmem_ld16_nowait(ta, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
           tmem_ld16_nowait(ta + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
-          if constexpr (C::CAT) {
+          if (C::CAT && p.cat) {
             // the A_hi x B_lo half of a concatenated accumulator
             uint32_t r2[32];
             tmem_ld16_nowait(ta + BN, *reinterpret_cast<uint32_t(*)[16]>(&r2[0]));
@@ -621,7 +628,7 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
           for (int ks = 0; ks < C::KSTEPS; ++ks) {
             const uint32_t koff = ks * 32;  // 32 bytes of K per instruction
             const uint32_t acc = (kb > kb0 || ks > 0) ? 1u : 0u;
-            if constexpr (C::CAT) {
+            if (C::CAT && p.cat) {
               // [A_hi B_hi | A_hi B_lo] (starts both halves), then + A_lo B_hi
               umma<PREC>(acc_t, desc_add(da_hi, koff), desc_add(db_hi, koff), C::IDESC_CAT, acc);
               umma<PREC>(acc_t, desc_add(da_lo, koff), desc_add(db_hi, koff), C::IDESC, 1u);
@@ -841,7 +848,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
             for (int ks = 0; ks < C::KSTEPS; ++ks) {
               const uint32_t koff = ks * 32;
               const uint32_t acc = (!first || ks > 0) ? 1u : 0u;
-              if constexpr (C::CAT) {
+              if (C::CAT && p.cat) {
                 // [B_hi | B_lo] are adjacent in the stage: one N = 128 instruction
                 umma<PREC>(acc_t, desc_add(da_hi, koff), desc_add(db_hi, koff), C::IDESC_CAT, acc);
                 umma<PREC>(acc_t, desc_add(da_lo, koff), desc_add(db_hi, koff), C::IDESC, 1u);
@@ -1056,6 +1063,7 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const 
     p.batch = 1;
   }
   if (L.K == 0) p.nkb = 0;
+  p.cat = (C::CAT && p.nkb >= 12) ? 1 : 0;  // see GemmParams::cat
   // accumulation chunks of 512 elements of K (16 tf32 / 8 bf16 k-blocks)
   p.kchunk = 512 / C::BK;
   p.nchunks = p.nkb > 0 ? (p.nkb + p.kchunk - 1) / p.kchunk : 1;
