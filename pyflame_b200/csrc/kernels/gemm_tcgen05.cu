@@ -92,13 +92,6 @@ struct GemmParams {
   //     block.
   int conv_tma, TW, TH, tiles_w, tiles_h;
   int nimg, halo_rows;
-  // 64-column 3xTF32 tiles: issue A_hi x [B_hi | B_lo] as one 128-column
-  // instruction (Cfg::CAT) for this launch.  Chosen when a tile has enough
-  // k-blocks that the MMAs, not the epilogue, set the pace: the concatenated
-  // accumulator doubles the epilogue's TMEM reads, which a 7-k-block tile
-  // (the 7x7 stem convolution) cannot hide (measured 0.96 -> 1.20 ms), while
-  // 18-k-block tiles gain (3x3 convolutions, 0.54 -> 0.45 ms).
-  int cat;
 };
 
 
@@ -263,7 +256,7 @@ __device__ __forceinline__ void store_block(const GemmParams& p, const float* ep
   }
 }
 
-template <int PREC, int BN>
+template <int PREC, int BN, bool CAT_ = false>
 struct Cfg {
   static constexpr int ESZ = PREC == PFC_PRECISION_BF16 ? 2 : 4;
   static constexpr int BK = 128 / ESZ;  // K elements per 128-byte swizzle row
@@ -278,13 +271,13 @@ struct Cfg {
   static constexpr int A_LO_OFF = A_TILE;
   static constexpr int B_HI_OFF = NOPS * A_TILE;
   static constexpr int B_LO_OFF = B_HI_OFF + B_TILE;
-  // 64-column 3xTF32 tiles may issue A_hi x [B_hi | B_lo] as ONE N = 128
+  // CAT (64-column 3xTF32 tiles): A_hi x [B_hi | B_lo] as ONE N = 128
   // instruction (64 cycles, against 2 x 48 for two N = 64 ones, and A_hi
   // read once instead of twice), then A_lo x B_hi (N = 64) into the first
-  // half; the epilogue adds the two halves (GemmParams::cat picks it per
-  // launch).  Wider tiles keep three products into one accumulator.
-  static constexpr bool CAT = NOPS == 2 && BN == 64;
-  static constexpr int ACC_COLS = CAT ? 2 * BN : BN;  // columns reserved per accumulator
+  // half; the epilogue adds the two halves.  A separate kernel
+  // instantiation, so the MMA issue loop carries no branch.
+  static constexpr bool CAT = CAT_ && NOPS == 2 && BN == 64;
+  static constexpr int ACC_COLS = CAT ? 2 * BN : BN;  // columns per accumulator
   // epilogue staging: per epilogue warp a 32 x 33 fp32 tile (padded: no bank conflicts)
   static constexpr int EPI_WARP_FLOATS = 32 * 20;  // a 32 x 16 block, 20-float pitch
   static constexpr int EPI_BYTES = kEpiWarps * EPI_WARP_FLOATS * 4;
@@ -341,10 +334,10 @@ __device__ __forceinline__ void conv_tile(const GemmParams& p, int tm, int& img,
 // back to the MMA warp at once), then apply alpha/bias/folded-BN/activation/
 // residual and store 32 x 16 blocks through this warp's staging area ep.
 // rows(tm, m_base, nvalid) names the warp's 32 output rows.
-template <int PREC, int BN, bool MAPPED, class Rows>
+template <int PREC, int BN, bool CAT, bool MAPPED, class Rows>
 __device__ __forceinline__ void run_epilogue(const GemmParams& p, uint32_t tmem, uint64_t* acc_full,
                                              uint64_t* acc_empty, float* ep, int e, int q, int lane, Rows rows) {
-  using C = Cfg<PREC, BN>;
+  using C = Cfg<PREC, BN, CAT>;
   constexpr int HALF = BN / 2;  // columns per epilogue warp
   const int col0 = (e >> 2) * HALF;
   const int nkb = p.nkb;
@@ -373,7 +366,7 @@ __device__ __forceinline__ void run_epilogue(const GemmParams& p, uint32_t tmem,
           const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * C::ACC_COLS + col0 + cc);
           tmem_ld16_nowait(ta, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
           tmem_ld16_nowait(ta + 16, *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
-          if (C::CAT && p.cat) {
+          if constexpr (C::CAT) {
             // the A_hi x B_lo half of a concatenated accumulator
             uint32_t r2[32];
             tmem_ld16_nowait(ta + BN, *reinterpret_cast<uint32_t(*)[16]>(&r2[0]));
@@ -432,12 +425,12 @@ __device__ __forceinline__ void run_epilogue(const GemmParams& p, uint32_t tmem,
 // Persistent kernel: each CTA walks tiles blockIdx.x, +gridDim.x, ...
 // CONV: the A operand is gathered by four producer warps from a channels-last
 // input (implicit-GEMM Conv2d) instead of loaded by TMA.
-template <int PREC, int BN, bool CONV>
+template <int PREC, int BN, bool CONV, bool CAT>
 __global__ void __launch_bounds__(kThreads<CONV>, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
                 const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
                 const GemmParams p) {
-  using C = Cfg<PREC, BN>;
+  using C = Cfg<PREC, BN, CAT>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   float* epi = (float*)(smem + C::STAGES * C::STAGE);
@@ -628,7 +621,7 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
           for (int ks = 0; ks < C::KSTEPS; ++ks) {
             const uint32_t koff = ks * 32;  // 32 bytes of K per instruction
             const uint32_t acc = (kb > kb0 || ks > 0) ? 1u : 0u;
-            if (C::CAT && p.cat) {
+            if constexpr (C::CAT) {
               // [A_hi B_hi | A_hi B_lo] (starts both halves), then + A_lo B_hi
               umma<PREC>(acc_t, desc_add(da_hi, koff), desc_add(db_hi, koff), C::IDESC_CAT, acc);
               umma<PREC>(acc_t, desc_add(da_lo, koff), desc_add(db_hi, koff), C::IDESC, 1u);
@@ -651,7 +644,7 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
   } else if (warp > PW) {
     // ---------------- epilogue ----------------
     const int e = warp - PW - 1;  // 0..7
-    run_epilogue<PREC, BN, false>(p, tmem, acc_full, acc_empty, epi + e * C::EPI_WARP_FLOATS, e, warp & 3, lane,
+    run_epilogue<PREC, BN, CAT, false>(p, tmem, acc_full, acc_empty, epi + e * C::EPI_WARP_FLOATS, e, warp & 3, lane,
                                   [&](int tm, long long& m_base, int& nvalid) {
                                     const int q = warp & 3;
                                     if (p.conv_tma) {
@@ -694,7 +687,7 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
 // issues the MMAs, 2..9 run the epilogue, 10 loads halos into two buffers.
 template <int PREC, int BN>
 struct HaloCfg {
-  using G = Cfg<PREC, BN>;
+  using G = Cfg<PREC, BN>;  // the stage layout and sizes do not depend on CAT
   static constexpr int HROWS = 256;  // halo rows per buffer (one TMA box)
   static constexpr int H_OP = HROWS * 128;
   static constexpr int H_BUF = G::NOPS * H_OP;
@@ -706,12 +699,12 @@ struct HaloCfg {
 };
 constexpr int kHaloThreads = (1 + 1 + kEpiWarps + 1) * 32;
 
-template <int PREC, int BN>
+template <int PREC, int BN, bool CAT>
 __global__ void __launch_bounds__(kHaloThreads, 1)
     conv_halo_kernel(const __grid_constant__ CUtensorMap tx_hi, const __grid_constant__ CUtensorMap tx_lo,
                      const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
                      const GemmParams p) {
-  using C = Cfg<PREC, BN>;
+  using C = Cfg<PREC, BN, CAT>;
   using H = HaloCfg<PREC, BN>;
   constexpr int S = H::B_STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -848,7 +841,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
             for (int ks = 0; ks < C::KSTEPS; ++ks) {
               const uint32_t koff = ks * 32;
               const uint32_t acc = (!first || ks > 0) ? 1u : 0u;
-              if (C::CAT && p.cat) {
+              if constexpr (C::CAT) {
                 // [B_hi | B_lo] are adjacent in the stage: one N = 128 instruction
                 umma<PREC>(acc_t, desc_add(da_hi, koff), desc_add(db_hi, koff), C::IDESC_CAT, acc);
                 umma<PREC>(acc_t, desc_add(da_lo, koff), desc_add(db_hi, koff), C::IDESC, 1u);
@@ -877,7 +870,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
   } else if (warp > PW && warp <= PW + kEpiWarps) {
     // ---------------- epilogue ----------------
     const int e = warp - PW - 1;
-    run_epilogue<PREC, BN, true>(p, tmem, acc_full, acc_empty, epi + e * C::EPI_WARP_FLOATS, e, warp & 3, lane,
+    run_epilogue<PREC, BN, CAT, true>(p, tmem, acc_full, acc_empty, epi + e * C::EPI_WARP_FLOATS, e, warp & 3, lane,
                                  [&](int tm, long long& m_base, int& nvalid) {
                                    m_base = (long long)tm * kBM + (warp & 3) * 32;  // virtual rows
                                    nvalid = -1;
@@ -994,10 +987,17 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const 
   static std::once_flag attr_once[64];
   const int dev = current_device();
   std::call_once(attr_once[dev], [] {
-    PFB_CUDA(cudaFuncSetAttribute(gemm_kernel<PREC, BN, CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    if constexpr (!CONV)
-      PFB_CUDA(cudaFuncSetAttribute(conv_halo_kernel<PREC, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    PFB_CUDA(cudaFuncSetAttribute(gemm_kernel<PREC, BN, CONV, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    if constexpr (Cfg<PREC, BN, true>::CAT)
+      PFB_CUDA(cudaFuncSetAttribute(gemm_kernel<PREC, BN, CONV, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    C::SMEM));
+    if constexpr (!CONV) {
+      PFB_CUDA(cudaFuncSetAttribute(conv_halo_kernel<PREC, BN, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     HaloCfg<PREC, BN>::SMEM));
+      if constexpr (Cfg<PREC, BN, true>::CAT)
+        PFB_CUDA(cudaFuncSetAttribute(conv_halo_kernel<PREC, BN, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      HaloCfg<PREC, BN>::SMEM));
+    }
   });
   const int64_t a_rows = L.M, b_rows = L.N;
   CUtensorMap tb_hi = make_map(L.b_hi, PREC, L.kpad, b_rows, L.b_sb ? L.batch : 1, BN);
@@ -1063,7 +1063,12 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const 
     p.batch = 1;
   }
   if (L.K == 0) p.nkb = 0;
-  p.cat = (C::CAT && p.nkb >= 12) ? 1 : 0;  // see GemmParams::cat
+  // The concatenated-B instantiation (Cfg::CAT) where a tile has enough
+  // k-blocks that the MMAs, not the epilogue, set the pace: it doubles the
+  // epilogue's TMEM reads, which a 7-k-block tile (the 7x7 stem convolution)
+  // does not hide (measured 0.96 -> 1.20 ms), while 18-k-block tiles gain
+  // (3x3 convolutions, 0.54 -> 0.45 ms).
+  const bool cat = Cfg<PREC, BN, true>::CAT && p.nkb >= 12;
   // accumulation chunks of 512 elements of K (16 tf32 / 8 bf16 k-blocks)
   p.kchunk = 512 / C::BK;
   p.nchunks = p.nkb > 0 ? (p.nkb + p.kchunk - 1) / p.kchunk : 1;
@@ -1073,13 +1078,28 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const 
   const unsigned grid = (unsigned)std::min<int64_t>(ntiles, device_sm_count(dev));
   if constexpr (!CONV) {
     if (conv_tma == 3) {
-      conv_halo_kernel<PREC, BN><<<grid, kHaloThreads, HaloCfg<PREC, BN>::SMEM, stream>>>(ta_hi, ta_lo, tb_hi,
+      if constexpr (Cfg<PREC, BN, true>::CAT) {
+        if (cat) {
+          conv_halo_kernel<PREC, BN, true><<<grid, kHaloThreads, HaloCfg<PREC, BN>::SMEM, stream>>>(ta_hi, ta_lo, tb_hi,
+                                                                                         tb_lo, p);
+          PFB_CUDA(cudaGetLastError());
+          return;
+        }
+      }
+      conv_halo_kernel<PREC, BN, false><<<grid, kHaloThreads, HaloCfg<PREC, BN>::SMEM, stream>>>(ta_hi, ta_lo, tb_hi,
                                                                                          tb_lo, p);
       PFB_CUDA(cudaGetLastError());
       return;
     }
   }
-  gemm_kernel<PREC, BN, CONV><<<grid, kThreads<CONV>, C::SMEM, stream>>>(ta_hi, ta_lo, tb_hi, tb_lo, p);
+  if constexpr (Cfg<PREC, BN, true>::CAT) {
+    if (cat) {
+      gemm_kernel<PREC, BN, CONV, true><<<grid, kThreads<CONV>, C::SMEM, stream>>>(ta_hi, ta_lo, tb_hi, tb_lo, p);
+      PFB_CUDA(cudaGetLastError());
+      return;
+    }
+  }
+  gemm_kernel<PREC, BN, CONV, false><<<grid, kThreads<CONV>, C::SMEM, stream>>>(ta_hi, ta_lo, tb_hi, tb_lo, p);
   PFB_CUDA(cudaGetLastError());
 }
 

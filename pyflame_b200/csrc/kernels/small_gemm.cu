@@ -60,21 +60,25 @@ struct SParams {
 
 constexpr size_t kSmallSmemMax = 160 * 1024;  // largest staging of layer 2
 
-template <bool CG>
+// Loads by source: 0 global read-only (__ldg), 1 global through L2 (data
+// written earlier in this launch by other CTAs), 2 shared memory.
+template <int SRC>
 __device__ __forceinline__ float4 ld4(const float* p) {
-  if constexpr (CG) return __ldcg(reinterpret_cast<const float4*>(p));
+  if constexpr (SRC == 1) return __ldcg(reinterpret_cast<const float4*>(p));
+  else if constexpr (SRC == 2) return *reinterpret_cast<const float4*>(p);
   else return __ldg(reinterpret_cast<const float4*>(p));
 }
-template <bool CG>
+template <int SRC>
 __device__ __forceinline__ float ld1(const float* p) {
-  if constexpr (CG) return __ldcg(p);
+  if constexpr (SRC == 1) return __ldcg(p);
+  else if constexpr (SRC == 2) return *p;
   else return __ldg(p);
 }
 
 // Warp `wid` of `nwarps`: 4 x 4 output blocks of act(alpha * x W^T + bias)
-// for the M rows of x (pitch ldx), written to dst[m * ldd + n].  CG: x was
-// written earlier in this launch by other CTAs (read through L2).
-template <bool VEC, bool CG>
+// for the M rows of x (pitch ldx), written to dst[m * ldd + n].  XS / WS:
+// where x and the weight rows are read from (ld4 / ld1 sources).
+template <bool VEC, int XS, int WS>
 __device__ void layer_tiles(const float* x, long long ldx, int M, const SLayer& L, float* dst, long long ldd, int wid,
                             int nwarps, int lane) {
   const int tm = (M + 3) >> 2, tn = (L.N + 3) >> 2;
@@ -99,8 +103,8 @@ __device__ void layer_tiles(const float* x, long long ldx, int M, const SLayer& 
         float4 xa[4], wb[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          xa[i] = ld4<CG>(xr[i] + k);
-          wb[i] = ld4<false>(wr[i] + k);
+          xa[i] = ld4<XS>(xr[i] + k);
+          wb[i] = ld4<WS>(wr[i] + k);
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i)
@@ -117,8 +121,8 @@ __device__ void layer_tiles(const float* x, long long ldx, int M, const SLayer& 
         float xa[4], wb[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          xa[i] = ld1<CG>(xr[i] + k);
-          wb[i] = ld1<false>(wr[i] + k);
+          xa[i] = ld1<XS>(xr[i] + k);
+          wb[i] = ld1<WS>(wr[i] + k);
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i)
@@ -204,9 +208,9 @@ __global__ void __launch_bounds__(kSWarps * 32) small_mlp_kernel(SParams p) {
     if (p.l1.vec) layer_rows32<true>(p.a, p.lda, p.M, p.l1, dst1, ld1, gw, nw, lane);
     else layer_rows32<false>(p.a, p.lda, p.M, p.l1, dst1, ld1, gw, nw, lane);
   } else if (p.l1.vec) {
-    layer_tiles<true, false>(p.a, p.lda, p.M, p.l1, dst1, ld1, gw, nw, lane);
+    layer_tiles<true, 0, 0>(p.a, p.lda, p.M, p.l1, dst1, ld1, gw, nw, lane);
   } else {
-    layer_tiles<false, false>(p.a, p.lda, p.M, p.l1, dst1, ld1, gw, nw, lane);
+    layer_tiles<false, 0, 0>(p.a, p.lda, p.M, p.l1, dst1, ld1, gw, nw, lane);
   }
   if (p.layers == 1) return;
   // The last CTA to arrive runs layer 2: its layer-1 rows are complete and,
@@ -219,55 +223,90 @@ __global__ void __launch_bounds__(kSWarps * 32) small_mlp_kernel(SParams p) {
   if (!last) return;
   __threadfence();
   if (p.l2_smem) {
-    // Stage the layer-1 rows and the layer-2 weight in shared memory (rows
-    // padded by one float so threads on different rows hit different banks),
-    // then every thread computes whole outputs: one memory round trip
-    // instead of one per 4x4 block.
-    extern __shared__ float sm[];
-    const int K2 = p.l2.K, ld = K2 + 1, N2 = p.l2.N;
-    float* hs = sm;
-    float* ws = sm + (size_t)p.M * ld;
-    // eight loads in flight per thread before their stores (one L2 round
-    // trip per eight elements, not per element)
+    // Layer 2 from shared memory: stage the layer-1 rows h [M][K2] and the
+    // weight w2 [N2][K2] (eight loads in flight per thread), compute the
+    // [M][N2] outputs with the warps' 4x4 blocks reading shared memory, then
+    // the softmax reads them there too.
+    extern __shared__ __align__(16) float sm[];
+    const int K2 = p.l2.K, N2 = p.l2.N, M = p.M;
+    float* hs = sm;                    // [M][K2]
+    float* ws = hs + (size_t)M * K2;   // [N2][K2]
+    float* zs = ws + (size_t)N2 * K2;  // [M][N2]
     constexpr int kBatch = 8;
-    const int nh = p.M * K2, nall = nh + N2 * K2;
-    for (int i0 = threadIdx.x; i0 < nall; i0 += blockDim.x * kBatch) {
-      float v[kBatch];
+    if (p.l2.vec) {
+      const int q = K2 >> 2, nh = M * q, nall = nh + N2 * q;
+      for (int i0 = threadIdx.x; i0 < nall; i0 += blockDim.x * kBatch) {
+        float4 v[kBatch];
 #pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        const int i = i0 + u * blockDim.x;
-        v[u] = 0.f;
-        if (i < nh) {
-          const int m = i / K2;
-          v[u] = __ldcg(p.h + (long long)m * p.ldh + (i - m * K2));
-        } else if (i < nall) {
-          const int n = (i - nh) / K2;
-          v[u] = __ldg(p.l2.w + (long long)n * p.l2.ldw + (i - nh - n * K2));
+        for (int u = 0; u < kBatch; ++u) {
+          const int i = i0 + u * blockDim.x;
+          if (i < nh) {
+            const int m = i / q;
+            v[u] = __ldcg(reinterpret_cast<const float4*>(p.h + (long long)m * p.ldh) + (i - m * q));
+          } else if (i < nall) {
+            const int n = (i - nh) / q;
+            v[u] = __ldg(reinterpret_cast<const float4*>(p.l2.w + (long long)n * p.l2.ldw) + (i - nh - n * q));
+          }
         }
-      }
 #pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        const int i = i0 + u * blockDim.x;
-        if (i < nh) hs[(i / K2) * ld + i % K2] = v[u];
-        else if (i < nall) ws[((i - nh) / K2) * ld + (i - nh) % K2] = v[u];
+        for (int u = 0; u < kBatch; ++u)
+          if (i0 + u * blockDim.x < nall) reinterpret_cast<float4*>(sm)[i0 + u * blockDim.x] = v[u];
+      }
+    } else {
+      const int nh = M * K2, nall = nh + N2 * K2;
+      for (int i0 = threadIdx.x; i0 < nall; i0 += blockDim.x * kBatch) {
+        float v[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          const int i = i0 + u * blockDim.x;
+          v[u] = 0.f;
+          if (i < nh) {
+            const int m = i / K2;
+            v[u] = __ldcg(p.h + (long long)m * p.ldh + (i - m * K2));
+          } else if (i < nall) {
+            const int n = (i - nh) / K2;
+            v[u] = __ldg(p.l2.w + (long long)n * p.l2.ldw + (i - nh - n * K2));
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u)
+          if (i0 + u * blockDim.x < nall) sm[i0 + u * blockDim.x] = v[u];
       }
     }
     __syncthreads();
-    const float alpha = p.l2.alpha_ptr ? *p.l2.alpha_ptr : p.l2.alpha;
-    for (int o = threadIdx.x; o < p.M * N2; o += blockDim.x) {
-      const int m = o / N2, n = o - m * N2;
-      const float* hr = hs + m * ld;
-      const float* wr = ws + n * ld;
-      float acc = 0.f;
-      for (int k = 0; k < K2; ++k) acc = fmaf(hr[k], wr[k], acc);
-      float v = acc * alpha;
-      if (p.l2.bias) v += p.l2.bias[(long long)n * p.l2.bstride];
-      p.out[(long long)m * p.ldo + n] = act_apply_rt(p.l2.act, v);
+    SLayer l2s = p.l2;
+    l2s.w = ws;
+    l2s.ldw = K2;
+    if (l2s.vec) layer_tiles<true, 2, 2>(hs, K2, M, l2s, zs, N2, warp, kSWarps, lane);
+    else layer_tiles<false, 2, 2>(hs, K2, M, l2s, zs, N2, warp, kSWarps, lane);
+    __syncthreads();
+    for (int m = warp; m < M; m += kSWarps) {
+      const float* zr = zs + m * N2;
+      float* row = p.out + (long long)m * p.ldo;
+      if (!p.softmax) {
+        for (int n = lane; n < N2; n += 32) row[n] = zr[n];
+        continue;
+      }
+      float mx = -__int_as_float(0x7f800000);
+      for (int n = lane; n < N2; n += 32) mx = fmaxf(mx, zr[n]);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      float sum = 0.f;
+      for (int n = lane; n < N2; n += 32) sum += expf(zr[n] - mx);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      if (p.softmax == 1) {
+        for (int n = lane; n < N2; n += 32) row[n] = expf(zr[n] - mx) / sum;
+      } else {
+        const float ls = logf(sum);
+        for (int n = lane; n < N2; n += 32) row[n] = zr[n] - mx - ls;
+      }
     }
+    return;
   } else if (p.l2.vec) {
-    layer_tiles<true, true>(p.h, p.ldh, p.M, p.l2, p.out, p.ldo, warp, kSWarps, lane);
+    layer_tiles<true, 1, 0>(p.h, p.ldh, p.M, p.l2, p.out, p.ldo, warp, kSWarps, lane);
   } else {
-    layer_tiles<false, true>(p.h, p.ldh, p.M, p.l2, p.out, p.ldo, warp, kSWarps, lane);
+    layer_tiles<false, 1, 0>(p.h, p.ldh, p.M, p.l2, p.out, p.ldo, warp, kSWarps, lane);
   }
   if (!p.softmax) return;
   __syncthreads();  // this CTA's layer-2 stores are visible to all its threads
@@ -337,7 +376,7 @@ void launch_small_mlp(const SmallMlpLaunch& L, cudaStream_t stream) {
   }
   size_t smem = 0;
   if (L.layers == 2) {
-    const size_t need = (size_t)(L.M + L.N2) * (size_t)(L.N1 + 1) * sizeof(float);
+    const size_t need = ((size_t)(L.M + L.N2) * (size_t)L.N1 + (size_t)L.M * (size_t)L.N2) * sizeof(float);
     if (need <= kSmallSmemMax) {
       p.l2_smem = 1;
       smem = need;
