@@ -299,17 +299,25 @@ class CudaExecutor:
         pointer (dense row-major); `outputs` are device pointers for
         `output_ids`.  Issued on `stream` (0 = the executor's own stream) and
         not synchronised.  Raises on failure."""
-        output_ids = [int(i) for i in output_ids]
-        ng = native_graph(graph, output_ids)
-        ins = list(inputs.items())
-        k_in, k_out = len(ins), len(output_ids)
-        in_ids = (C.c_uint64 * max(1, k_in))(*[i for i, _ in ins])
-        in_p = (C.c_void_p * max(1, k_in))(*[p for _, p in ins])
-        out_ids = (C.c_uint64 * max(1, k_out))(*output_ids)
-        out_p = (C.c_void_p * max(1, k_out))(*outputs)
+        # a loop of calls with the same arguments (serving, the bench) reuses
+        # the ctypes argument block of the previous call
+        key = (id(graph), graph.version, tuple(inputs.items()), tuple(output_ids), tuple(outputs), stream)
+        cached = self.__dict__.get("_dev_args")
+        if cached is not None and cached[0] == key:
+            args = cached[1]
+        else:
+            output_ids = [int(i) for i in output_ids]
+            ng = native_graph(graph, output_ids)
+            ins = list(inputs.items())
+            k_in, k_out = len(ins), len(output_ids)
+            args = (ng, (C.c_uint64 * max(1, k_in))(*[i for i, _ in ins]), k_in,
+                    (C.c_void_p * max(1, k_in))(*[p for _, p in ins]), (C.c_uint64 * max(1, k_out))(*output_ids),
+                    k_out, (C.c_void_p * max(1, k_out))(*outputs), C.c_void_p(stream or None))
+            self._dev_args = (key, args)
+        ng, in_ids, k_in, in_p, out_ids, k_out, out_p, sp = args
         r = N.ExecutionResultC()
         N.check(N.lib().pfc_executor_execute_device(self.handle, ng.handle, in_ids, k_in, in_p, out_ids, k_out,
-                                                    out_p, C.c_void_p(stream or None), C.byref(r)))
+                                                    out_p, sp, C.byref(r)))
         return ExecutionResult(True, "", r.compile_time_ms, 0.0, 0.0, r.total_time_ms, {}, r.kernel_launches,
                                r.h2d_bytes, r.d2h_bytes)
 

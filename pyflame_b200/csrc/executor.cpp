@@ -123,6 +123,7 @@ cudaError_t CudaExecutor::release_constants() {
       for (void* p : pe.slots[k2]) note(pool_->deallocate(p, stream_));
   }
   plans_.clear();
+  last_ = LastPrepared();
   for (auto& [k, r] : resident_) {
     if (!r.owned) continue;
     note(pool_->deallocate(r.dev, stream_));
@@ -227,14 +228,34 @@ std::unordered_map<uint64_t, float> CudaExecutor::detect_splats(const Graph& g, 
 CudaExecutor::PlanEntry& CudaExecutor::prepare(Graph& g, const std::vector<uint64_t>& outs,
                                                const std::unordered_set<uint64_t>& bindings, double* compile_ms) {
   auto t0 = std::chrono::steady_clock::now();
+  std::vector<uint64_t> bsorted(bindings.begin(), bindings.end());
+  std::sort(bsorted.begin(), bsorted.end());
+  if (last_.pe && last_.graph_uid == g.uid && last_.version == g.version && last_.outs == outs &&
+      last_.bindings == bsorted) {
+    // same graph, unchanged: only per-call payloads can differ.  A splat leaf
+    // whose payload is per call (not resident) must still hold equal values.
+    bool same = true;
+    for (auto& sc : last_.pe->plan->scalars) {
+      const Node& n = g.at(sc.node);
+      if (!n.has_data() || (n.data_flags & PFC_CONST_RESIDENT)) continue;
+      float v = 0.f;
+      if (!all_equal_f32((const float*)n.data, n.numel(), &v)) {
+        same = false;
+        break;
+      }
+      sc.value = v;
+    }
+    if (same) {
+      if (compile_ms) *compile_ms = ms_since(t0);
+      return *last_.pe;
+    }
+  }
   validate_graph(g);
   std::vector<uint64_t> order = topo_order(g, outs);
   auto splats = detect_splats(g, order, bindings);
   uint64_t key = structural_hash(g, outs);
   key = mix(key, (uint64_t)cfg_.precision);
-  std::vector<uint64_t> b(bindings.begin(), bindings.end());
-  std::sort(b.begin(), b.end());
-  for (uint64_t x : b) key = mix(key, x ^ 0xb1b1);
+  for (uint64_t x : bsorted) key = mix(key, x ^ 0xb1b1);
   std::vector<uint64_t> sp;
   for (auto& [id, v] : splats) sp.push_back(id);
   std::sort(sp.begin(), sp.end());
@@ -279,6 +300,11 @@ CudaExecutor::PlanEntry& CudaExecutor::prepare(Graph& g, const std::vector<uint6
     // refresh the splat values seen by this call (the structure is unchanged)
     for (auto& sc : it->second.plan->scalars) sc.value = splats.at(sc.node);
   }
+  last_.graph_uid = g.uid;
+  last_.version = g.version;
+  last_.outs = outs;
+  last_.bindings = bsorted;
+  last_.pe = &it->second;
   if (compile_ms) *compile_ms = ms_since(t0);
   return it->second;
 }

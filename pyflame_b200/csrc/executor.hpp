@@ -74,6 +74,15 @@ class CudaExecutor {
     std::vector<void*> slots[2];
     std::vector<size_t> slot_bytes;
   };
+  // The last (graph, version, outputs, bindings) prepared and its plan: a
+  // repeated call on an unchanged graph skips validation, the topological
+  // walk, splat detection and the structural hash (its per-call splat leaves
+  // are re-checked).
+  struct LastPrepared {
+    uint64_t graph_uid = 0, version = 0;
+    std::vector<uint64_t> outs, bindings;
+    PlanEntry* pe = nullptr;
+  } last_;
   struct Resident {
     void* dev = nullptr;
     size_t bytes = 0;

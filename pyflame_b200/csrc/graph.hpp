@@ -2,6 +2,7 @@
 // (include/pyflame/ir/graph.hpp:17-215) in a flat, pointer-free form.
 #pragma once
 
+#include <atomic>
 #include <cstdint>
 #include <map>
 #include <string>
@@ -88,6 +89,12 @@ struct Graph {
   std::unordered_map<uint64_t, size_t> index;
   std::vector<uint64_t> outputs;
   uint64_t version = 0;  // bumped on every mutation
+  // process-unique identity (never reused, unlike the object's address)
+  const uint64_t uid = next_uid();
+  static uint64_t next_uid() {
+    static std::atomic<uint64_t> n{1};
+    return n.fetch_add(1);
+  }
 
   Node* find(uint64_t id);
   const Node* find(uint64_t id) const;

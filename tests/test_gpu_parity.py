@@ -650,3 +650,22 @@ def test_empty_and_degenerate_shapes(cuda_executor, oracle_mod, rng):
     assert gpu[0].shape == (0, 8) and gpu[1].shape == (0, 4)
     for g_, r_ in zip(gpu[2:], ref[2:]):
         bitexact(g_, r_)
+
+
+def test_repeated_call_sees_changed_input_values(cuda_executor, oracle_mod, rng):
+    """A repeated call on an unchanged graph skips re-analysis, but an INPUT
+    whose values were all equal (a scalar in the plan) and then change in
+    place must be read again, not served from the old plan."""
+    g = pf.get_current_graph()
+    data = np.full((16, 64), 2.0, np.float32)
+    x = pf.Tensor(g, g.create_input(pf.TensorSpec([16, 64])))
+    x.node().set_constant_data(data, copy=False)
+    y = pf.relu(x) * 3.0 + 1.0
+    r1 = cuda_executor.execute(g, [y.node().id()])
+    assert r1.success and np.all(r1.outputs[y.node().id()] == 7.0)
+    data[...] = rng.standard_normal((16, 64)).astype(np.float32)  # same array, same graph version
+    r2 = cuda_executor.execute(g, [y.node().id()])
+    assert r2.success
+    np.testing.assert_array_equal(r2.outputs[y.node().id()], oracle_mod.run(g, [y.node().id()])[y.node().id()])
+    r3 = cuda_executor.execute(g, [y.node().id()])
+    np.testing.assert_array_equal(r3.outputs[y.node().id()], r2.outputs[y.node().id()])
