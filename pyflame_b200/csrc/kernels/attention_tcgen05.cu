@@ -10,20 +10,27 @@
 // One persistent CTA per SM walks tiles of (slice, 128 query rows):
 //   warp 0     TMA: Q of the tile once, then key blocks of 64 (K and V)
 //              through two-stage rings.
-//   warp 1     TMEM (512 columns) and the MMAs.  S = Q K_j^T goes into one of
-//              two 64-column TMEM buffers (kind::tf32 x3 from shared memory);
-//              O_h += P_j,h V_j,h for the two 32-key halves h of the block takes
-//              P from TMEM as the A operand and V as an MN-major B operand (its
+//   warp 1     TMEM (512 columns) and the MMAs, all tf32 x3.  S = Q K_j^T
+//              takes Q from TMEM as the A operand and K from shared memory,
+//              into one of two 128-column S/P buffers.  O_h += P_j,h V_j,h
+//              for the two 32-key halves h of the block takes P from the same
+//              buffer as the A operand and V as an MN-major B operand (its
 //              rows are keys, as stored), into one of two O accumulators.
-//   warps 2-9  two warps per TMEM lane quarter; warp half h owns keys
-//              32h..32h+31 of every block for its 32 query rows: it reads S,
-//              keeps a running max m_h and sum l_h, and writes
-//              P = exp2(alpha*log2(e)*s - m_h) as hi/lo tf32 into one of two
-//              TMEM P buffers.  m_h moves only when a block's max exceeds it
-//              by more than 2^8 (P stays below 256); then O_h and l_h are
-//              rescaled once the previous block's P*V has retired.  At the end
-//              of a tile the halves combine, O = (O_0 a_0 + O_1 a_1) /
-//              (l_0 a_0 + l_1 a_1) with a_h = 2^(m_h - max(m_0, m_1)).
+//              The MMAs of a CTA run in issue order, so S_j+2 may be issued
+//              into the buffer that P_j*V_j, issued before it, reads.
+//   warps 2-9  two warps per TMEM lane quarter.  At the start of a tile they
+//              copy Q (hi / lo) from shared memory into TMEM.  Warp half h
+//              owns keys 32h..32h+31 of every block for its 32 query rows:
+//              it reads S, keeps a running max m_h and sum l_h, and writes
+//              P = exp2(alpha*log2(e)*s - m_h) as hi/lo tf32 over the S it
+//              read (hi) and beside it (lo).  m_h moves only when a block's
+//              max exceeds it by more than 2^8 (P stays below 256); then O_h
+//              and l_h are rescaled once the previous block's P*V has
+//              retired.  At the end of a tile the halves combine,
+//              O = (O_0 a_0 + O_1 a_1) / (l_0 a_0 + l_1 a_1) with
+//              a_h = 2^(m_h - max(m_0, m_1)).
+// Operands from TMEM leave shared memory to the K and V tiles: per key block
+// the tensor core reads 64 KB there instead of 192 KB.
 // Keys past L are masked; query rows past M and head columns past d are
 // dropped.  Every wait is bounded by the global timer and reports
 // PFC_ERR_TIMEOUT through *err.
@@ -59,9 +66,10 @@ constexpr int kKStage = 2 * 2 * kKChunk;    // [hi/lo][k-chunk]
 constexpr int kVStage = 2 * 2 * kVChunk;    // [hi/lo][head-dim chunk]
 constexpr int kStages = 2;
 constexpr int kASmem = kQBytes + kStages * (kKStage + kVStage) + 1024 /*barriers*/ + 1024 /*align*/;
-// TMEM columns: S buffers at 0 and 64; P buffers (hi 64 | lo 64) at 128 and
-// 256; O accumulators of the two key halves at 384 and 448.
-constexpr uint32_t kTS = 0, kTP = 128, kTO = 384, kATmemCols = 512;
+// TMEM columns: S/P buffers at 0 and 128 (S, then P hi, in the first 64
+// columns; P lo in the next 64); O accumulators of the two key halves at 256
+// and 320; Q hi at 384, Q lo at 448.
+constexpr uint32_t kTS = 0, kTO = 256, kTQ = 384, kATmemCols = 512;
 constexpr float kRescaleLog2 = 8.f;  // P < 2^8 between rescales
 constexpr uint32_t kIdesc = idesc(kAQ, 64, 2u);  // M 128, N 64, tf32
 constexpr uint32_t kIdescMnB = kIdesc | (1u << 16);  // ... with B MN-major
@@ -101,12 +109,14 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 
-// D (TMEM) += A (TMEM, K-major: lane = row, column = k) x B (shared memory, MN-major)
+// D (TMEM) += A (TMEM, K-major: lane = row, column = k) x B (shared memory,
+// K-major for IDESC = kIdesc, MN-major for kIdescMnB)
+template <uint32_t IDESC>
 __device__ __forceinline__ void umma_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t db, uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(db), "r"(kIdescMnB), "r"(acc));
+      "r"(a_tmem), "l"(db), "n"(IDESC), "r"(acc));
 }
 
 // Bounded wait taken by every lane of a warp, with one outcome for all of
@@ -124,6 +134,27 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 2^x by the tensor-free special-function unit; results below 2^-126 flush
+// to 0 (they are below P's rounding in the sum of a row).
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// max of 32 values as a tree (depth 5 instead of a chain of 31); NaN
+// entries are ignored as fmaxf ignores them
+__device__ __forceinline__ float max32(const float (&v)[32]) {
+  float a[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) a[k] = fmaxf(v[k], v[k + 16]);
+#pragma unroll
+  for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+    for (int k = 0; k < w; ++k) a[k] = fmaxf(a[k], a[k + w]);
+  return a[0];
 }
 
 // Barrier among the softmax warps only.  Every softmax warp passes the same
@@ -156,13 +187,12 @@ __global__ void __launch_bounds__(kAThreads, 1)
   uint8_t* sv = sk + kStages * kKStage;
   uint64_t* bars = (uint64_t*)(sv + kStages * kVStage);
   uint64_t* q_full = bars + 0;
-  uint64_t* q_free = bars + 1;
+  uint64_t* q_tmem = bars + 1;   // Q copied into TMEM (and its shared memory free)
   uint64_t* k_full = bars + 2;   // [2]
   uint64_t* k_free = bars + 4;   // [2]
   uint64_t* v_full = bars + 6;   // [2]
   uint64_t* v_free = bars + 8;   // [2]
   uint64_t* s_full = bars + 10;  // [2] S block in TMEM
-  uint64_t* s_free = bars + 12;  // [2] S block read by the softmax warps
   uint64_t* p_full = bars + 14;  // [2] P block written
   uint64_t* p_free = bars + 16;  // [2] P block consumed by its MMAs
   uint64_t* o_full = bars + 18;
@@ -178,14 +208,13 @@ __global__ void __launch_bounds__(kAThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(q_full), 1);
-    mbar_init(smem_u32(q_free), 1);
+    mbar_init(smem_u32(q_tmem), kSoftWarps);
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&k_full[i]), 1);
       mbar_init(smem_u32(&k_free[i]), 1);
       mbar_init(smem_u32(&v_full[i]), 1);
       mbar_init(smem_u32(&v_free[i]), 1);
       mbar_init(smem_u32(&s_full[i]), 1);
-      mbar_init(smem_u32(&s_free[i]), kSoftWarps);
       mbar_init(smem_u32(&p_full[i]), kSoftWarps);
       mbar_init(smem_u32(&p_free[i]), 1);
     }
@@ -212,7 +241,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
     const uint32_t kbytes = (uint32_t)(2 * p.nkc * kKChunk);
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
       const int b = t / p.ntq, q0 = (t - b * p.ntq) * kAQ;
-      if (tc > 0 && !mbar_wait(smem_u32(q_free), (uint32_t)(tc - 1) & 1u, p.err)) { ok = false; break; }
+      if (tc > 0 && !mbar_wait(smem_u32(q_tmem), (uint32_t)(tc - 1) & 1u, p.err)) { ok = false; break; }
       mbar_expect_tx(smem_u32(q_full), (uint32_t)(2 * p.nkc * kQChunk));
       for (int c = 0; c < p.nkc; ++c) {
         tma_load_3d(smem_u32(sq + c * kQChunk), &tq_hi, smem_u32(q_full), c * 32, q0, b);
@@ -251,25 +280,24 @@ __global__ void __launch_bounds__(kAThreads, 1)
     // ---------------- MMA issuer ----------------
     int gk = 0, gv = 0, gs = 0, gp = 0, tc = 0;
     bool ok = true;
-    const uint32_t q_base = smem_u32(sq);
-    // S[gs & 1] = Q K^T of the next K block
+    const uint32_t qh_t = tmem + kTQ, ql_t = tmem + kTQ + 64;
+    // S[gs & 1] = Q K^T of the next K block.  Its buffer last held P of
+    // block gs-2, whose P*V MMAs were issued before these.
     auto issue_s = [&]() -> bool {
       const int sb = gs & 1, ks = gk & 1;
-      if (gs >= 2 && !mbar_wait(smem_u32(&s_free[sb]), (uint32_t)((gs >> 1) - 1) & 1u, p.err)) return false;
       if (!mbar_wait(smem_u32(&k_full[ks]), (uint32_t)(gk >> 1) & 1u, p.err)) return false;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t d = tmem + kTS + (uint32_t)(sb * 64);
+      const uint32_t d = tmem + kTS + (uint32_t)(sb * 128);
       const uint32_t k_base = smem_u32(sk + ks * kKStage);
       for (int c = 0; c < p.nkc; ++c) {
-        const uint64_t qh = sdesc(q_base + c * kQChunk), ql = sdesc(q_base + (2 + c) * kQChunk);
         const uint64_t kh = sdesc(k_base + c * kKChunk), kl = sdesc(k_base + (2 + c) * kKChunk);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          const uint32_t off = kk * 32;
+          const uint32_t off = kk * 32, col = (uint32_t)(c * 32 + kk * 8);
           const uint32_t acc = (c > 0 || kk > 0) ? 1u : 0u;
-          umma<PFC_PRECISION_TF32X3>(d, desc_add(ql, off), desc_add(kh, off), kIdesc, acc);
-          umma<PFC_PRECISION_TF32X3>(d, desc_add(qh, off), desc_add(kl, off), kIdesc, 1u);
-          umma<PFC_PRECISION_TF32X3>(d, desc_add(qh, off), desc_add(kh, off), kIdesc, 1u);
+          umma_tmem_a<kIdesc>(d, ql_t + col, desc_add(kh, off), acc);
+          umma_tmem_a<kIdesc>(d, qh_t + col, desc_add(kl, off), 1u);
+          umma_tmem_a<kIdesc>(d, qh_t + col, desc_add(kh, off), 1u);
         }
       }
       umma_commit(smem_u32(&k_free[ks]));
@@ -285,7 +313,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
       if (!mbar_wait(smem_u32(&v_full[vs]), (uint32_t)(gv >> 1) & 1u, p.err)) return false;
       if (j == 0 && tc > 0 && !mbar_wait(smem_u32(o_free), (uint32_t)(tc - 1) & 1u, p.err)) return false;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t ph = tmem + kTP + (uint32_t)(pb * 128), pl = ph + 64;
+      const uint32_t ph = tmem + kTS + (uint32_t)(pb * 128), pl = ph + 64;
       const uint32_t v_base = smem_u32(sv + vs * kVStage);
       // V block [64 keys][64 head dims] as two 32-column chunks: K-step kk
       // takes keys 8kk..8kk+7 (one 1024-byte row group further down); keys
@@ -298,9 +326,9 @@ __global__ void __launch_bounds__(kAThreads, 1)
         for (int kk = 0; kk < 4; ++kk) {
           const uint32_t col = (uint32_t)(h * 32 + kk * 8), off = (uint32_t)(h * 4 + kk) * 1024u;
           const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
-          umma_tmem_a(d, pl + col, desc_add(vh, off), acc);
-          umma_tmem_a(d, ph + col, desc_add(vl, off), 1u);
-          umma_tmem_a(d, ph + col, desc_add(vh, off), 1u);
+          umma_tmem_a<kIdescMnB>(d, pl + col, desc_add(vh, off), acc);
+          umma_tmem_a<kIdescMnB>(d, ph + col, desc_add(vl, off), 1u);
+          umma_tmem_a<kIdescMnB>(d, ph + col, desc_add(vh, off), 1u);
         }
       }
       umma_commit(smem_u32(&v_free[vs]));
@@ -310,14 +338,13 @@ __global__ void __launch_bounds__(kAThreads, 1)
       return true;
     };
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
-      if (!mbar_wait(smem_u32(q_full), (uint32_t)tc & 1u, p.err)) { ok = false; break; }
+      if (!mbar_wait(smem_u32(q_tmem), (uint32_t)tc & 1u, p.err)) { ok = false; break; }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       // S of the next block goes in before P V of this one, so the softmax
       // warps work on one block while the tensor core does the other
       ok = issue_s();
       for (int j = 0; j < p.nblk && ok; ++j) {
         if (j + 1 < p.nblk) ok = issue_s();
-        if (ok && j + 1 == p.nblk) umma_commit(smem_u32(q_free));  // the last S of the tile is issued
         if (ok) ok = issue_pv(j);
       }
       if (ok) umma_commit(smem_u32(o_full));
@@ -332,6 +359,33 @@ __global__ void __launch_bounds__(kAThreads, 1)
     const float scale = (p.alpha_ptr ? *p.alpha_ptr : p.alpha) * 1.4426950408889634f;  // alpha * log2(e)
     int gs = 0, gp = 0, tc = 0;
     bool ok = true;
+    // Q of the CTA's tile number `tq` from shared memory (as TMA wrote it:
+    // 128-byte rows, 16-byte units swizzled by row & 7) into TMEM: this
+    // warp's 32 rows, hi (warp half 0) or lo (half 1), 32 head dims per
+    // chunk.  Its arrival frees the shared copy and starts the tile's MMAs.
+    auto copy_q = [&](int tq) -> bool {
+      if (!mbar_wait_warp(smem_u32(q_full), (uint32_t)tq & 1u, p.err)) return false;
+      const uint8_t* src = sq + hf * 2 * kQChunk + row_in_tile * 128;
+      for (int c = 0; c < p.nkc; ++c) {
+        uint32_t r[32];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const uint4 x = *reinterpret_cast<const uint4*>(src + c * kQChunk + ((u ^ (row_in_tile & 7)) << 4));
+          r[4 * u] = x.x;
+          r[4 * u + 1] = x.y;
+          r[4 * u + 2] = x.z;
+          r[4 * u + 3] = x.w;
+        }
+        const uint32_t dst = lane_base + kTQ + (uint32_t)(hf * 64 + c * 32);
+        tmem_st16(dst, *reinterpret_cast<const uint32_t(*)[16]>(&r[0]));
+        tmem_st16(dst + 16, *reinterpret_cast<const uint32_t(*)[16]>(&r[16]));
+      }
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(q_tmem));
+      return true;
+    };
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tc) {
       const int b = t / p.ntq, q0 = (t - b * p.ntq) * kAQ;
       float m = -INFINITY, l = 0.f;
@@ -340,22 +394,28 @@ __global__ void __launch_bounds__(kAThreads, 1)
         const int sb = gs & 1;
         if (!mbar_wait_warp(smem_u32(&s_full[sb]), (uint32_t)(gs >> 1) & 1u, p.err)) return false;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        tmem_ld32(lane_base + kTS + (uint32_t)(sb * 64 + hf * 32), v);
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&s_free[sb]));
+        tmem_ld32(lane_base + kTS + (uint32_t)(sb * 128 + hf * 32), v);
         ++gs;
         return true;
       };
+      if (tc == 0 && !(ok = copy_q(0))) {
+        // fall through to the tile's barrier with ok false
+      }
       // one pass: this half's keys, running max m (log2 units, moved lazily)
       // and sum l of P = exp2(scale * s - m)
       for (int j = 0; j < p.nblk && ok; ++j) {
         if (!(ok = read_s())) break;
         const int nk = min(32, p.L - j * kAK - hf * 32);
-        float bm = -INFINITY;
+        // scores in log2 units; keys past L (last block only) drop out of
+        // the max and get P = 2^-inf = 0
 #pragma unroll
-        for (int k = 0; k < 32; ++k)
-          if (k < nk) bm = fmaxf(bm, v[k] * scale);
+        for (int k = 0; k < 32; ++k) v[k] *= scale;
+        if (nk < 32) {
+#pragma unroll
+          for (int k = 0; k < 32; ++k)
+            if (k >= nk) v[k] = -INFINITY;
+        }
+        const float bm = max32(v);
         const bool first = m == -INFINITY;
         const bool move = bm > (first ? -INFINITY : m + kRescaleLog2);
         const float mn = move ? bm : m;
@@ -380,34 +440,37 @@ __global__ void __launch_bounds__(kAThreads, 1)
         }
         if (move && !first) l *= exp2f(m - mn);
         m = mn;
+        // P over the S just read (hi) and beside it (lo); the buffer's
+        // previous P was consumed before this S was computed into it
         const int pb = gp & 1;
-        if (gp >= 2 && !(ok = mbar_wait_warp(smem_u32(&p_free[pb]), (uint32_t)((gp >> 1) - 1) & 1u, p.err))) break;
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t pbase = lane_base + kTP + (uint32_t)(pb * 128 + hf * 32);
-        float sum = 0.f;
+        const uint32_t pbase = lane_base + kTS + (uint32_t)(pb * 128 + hf * 32);
+        const float msub = m == -INFINITY ? 0.f : m;  // a half with no keys yet: every P is 0
+        float sum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
           uint32_t hi[16], lo[16];
 #pragma unroll
           for (int k = 0; k < 16; ++k) {
-            const int kk = 16 * i + k;
-            const float pv = kk < nk ? exp2f(fmaf(v[kk], scale, -m)) : 0.f;
-            sum += pv;
-            float h, lw;
-            split_tf32(pv, h, lw);
-            hi[k] = __float_as_uint(h);
-            lo[k] = __float_as_uint(lw);
+            const float pv = ex2_ftz(v[16 * i + k] - msub);
+            sum[k & 3] += pv;
+            // P is finite here (0 <= P < 2^8 between rescales); a NaN or
+            // infinite score makes lo NaN and with it the row's output
+            hi[k] = __float_as_uint(pv) & 0xFFFFE000u;
+            lo[k] = __float_as_uint(pv - __uint_as_float(hi[k]));
           }
           tmem_st16(pbase + 16 * i, hi);
           tmem_st16(pbase + 64 + 16 * i, lo);
         }
-        l += sum;
+        l += (sum[0] + sum[1]) + (sum[2] + sum[3]);
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&p_full[pb]));
         ++gp;
       }
+      // every S MMA of this tile has completed (its last S was read): Q of
+      // the next tile may replace it while the last P*V runs
+      if (ok && t + (int)gridDim.x < ntiles) ok = copy_q(tc + 1);
       // the two halves of the row: weights a_h = 2^(m_h - m) (0 for a half without keys)
       row_stat[hf][row_in_tile] = make_float2(m, l);
       if (softmax_bar_any(!ok)) break;  // all softmax warps leave together
