@@ -1858,13 +1858,19 @@ void Compiler::lower_small(int ci) {
   if (first >= 0) {
     S.layers = 2;
     layer(last, S.l2);
-    S.h_buf = new_buffer((size_t)M * S.l1.N * 4);
-    S.counter_buf = new_buffer(8);
-    Step ms;
-    ms.kind = StepKind::MEMSET;
-    ms.label = "zero small-GEMM arrival counter";
-    ms.memset_buf = S.counter_buf;
-    add_step(at, ms);
+    // clusters of 8 CTAs when the rows and weights stage whole in shared
+    // memory by 16-byte copies; otherwise one launch whose last CTA runs layer 2
+    S.cluster = small_mlp_cluster_fits(M, S.l1.N, K1, S.l2.N) && S.a.offset % 4 == 0 && S.lda % 4 == 0 &&
+                S.l1.w_off % 4 == 0 && S.l1.ldw % 4 == 0 && S.l2.w_off % 4 == 0 && S.l2.ldw % 4 == 0;
+    if (!S.cluster) {
+      S.h_buf = new_buffer((size_t)M * S.l1.N * 4);
+      S.counter_buf = new_buffer(8);
+      Step ms;
+      ms.kind = StepKind::MEMSET;
+      ms.label = "zero small-GEMM arrival counter";
+      ms.memset_buf = S.counter_buf;
+      add_step(at, ms);
+    }
     label = "small mlp [" + std::to_string(M) + "x" + std::to_string(S.l1.N) + "x" + std::to_string(K1) + " -> " +
             std::to_string(S.l2.N) + "]";
   }
@@ -1872,6 +1878,7 @@ void Compiler::lower_small(int ci) {
     S.softmax = N(sm).op == Op::SOFTMAX ? 1 : 2;
     label += S.softmax == 1 ? " +softmax" : " +log_softmax";
   }
+  if (S.cluster) label += " (clusters)";
   const int64_t nout = S.layers == 2 ? S.l2.N : S.l1.N;
   S.out = dense(N(result).shape, DType::F32);
   S.ldo = nout;
@@ -2951,6 +2958,7 @@ void Compiler::emit_operands_at_producers() {
         if (G.has_bias) add(G.bias.buf, i);
         if (G.has_residual) add(G.residual.buf, i);
         add(G.scale_buf, i); add(G.shift_buf, i); add(G.x_hi, i); add(G.x_lo, i);
+        if (G.pool) add(G.pool_y.buf, i);
         break;
       }
       case StepKind::POOL: add(st.pool.x.buf, i); add(st.pool.y.buf, i); break;
@@ -3082,6 +3090,46 @@ void Compiler::emit_operands_at_producers() {
       }
     }
   }
+  // A ReLU convolution read only by a 3x3 / stride 2 max pool (padding 0 or 1)
+  // (PyFlame's Conv2d -> BatchNorm -> ReLU -> MaxPool2d stem): the pool runs
+  // in the convolution's epilogue and the convolution's output never reaches
+  // memory.  The epilogue takes the windowed TMA feed with 64-pixel tiles and
+  // 64 output channels (launch_gemm's conv_tma_mode 2, not the halo feed).
+  for (int i = 0; i < (int)S.size(); ++i) {
+    if (drop[i] || S[i].kind != StepKind::POOL) continue;
+    PoolArgs& Pl = S[i].pool;
+    if (Pl.mode != 0 || Pl.kh != 3 || Pl.kw != 3 || Pl.sh != 2 || Pl.sw != 2 || Pl.ph != Pl.pw || Pl.ph < 0 ||
+        Pl.ph > 1)
+      continue;
+    const View& x = Pl.x;
+    if (x.is_splat || x.buf < 0) continue;
+    const int j = producer(x.buf);
+    if (j < 0 || j > i || drop[j] || S[j].kind != StepKind::GEMM) continue;
+    GemmArgs& G = S[j].gemm;
+    if (!G.conv || G.pool || G.act != 1 || G.has_residual || G.N != 64 || G.batch != 1 || G.op_hi >= 0 || !G.write_c)
+      continue;
+
+    if (x.offset != G.c.offset || x.shape != G.c.shape || x.strides != G.c.strides || others_read(x.buf, j, i)) continue;
+    const int64_t esz = G.precision == PFC_PRECISION_BF16 ? 2 : 4, bk = 128 / esz;
+    const int64_t kwp = G.KWp > 0 ? G.KWp : G.KW;
+    const bool halo = G.sh == 1 && G.sw == 1 && G.Cp % bk == 0 && kwp == G.KW;
+    if (halo || G.Hp == 0 || kwp * G.Cp != bk || G.dw != 1 || (G.sw * G.Cp * esz) % 16 != 0 || G.OW <= 32) continue;
+    const View& y = Pl.y;
+    if (y.shape.size() != 4 || y.strides[1] != 1 || y.offset % 4 != 0 || y.strides[0] % 4 != 0 ||
+        y.strides[2] % 4 != 0 || y.strides[3] % 4 != 0 || y.shape[1] != 64 ||
+        y.shape[2] != (G.OH + 2 * Pl.ph - 3) / 2 + 1 || y.shape[3] != (G.OW + 2 * Pl.pw - 3) / 2 + 1 ||
+        y.shape[2] < 1 || y.shape[3] < 1)
+      continue;
+    G.pool = true;
+    G.pool_pad = (int)Pl.ph;
+    G.pool_y = y;
+    G.write_pool_y = Pl.write_y;
+    G.op_hi = Pl.op_hi;
+    G.op_lo = Pl.op_lo;
+    G.write_c = false;
+    drop[i] = true;
+    S[j].label += Pl.op_hi >= 0 ? " +max_pool2d +operand" : " +max_pool2d";
+  }
   std::vector<Step> kept;
   for (int i = 0; i < (int)S.size(); ++i)
     if (!drop[i]) kept.push_back(std::move(S[i]));
@@ -3129,6 +3177,7 @@ void Compiler::finish() {
         const GemmArgs& G = s.gemm;
         use(G.a_hi, i); use(G.a_lo, i); use(G.b_hi, i); use(G.b_lo, i);
         if (G.write_c) use(G.c.buf, i);
+        if (G.pool && G.write_pool_y) use(G.pool_y.buf, i);
         use(G.op_hi, i); use(G.op_lo, i);
         if (G.conv) { use(G.x_hi, i); use(G.x_lo, i); }
         if (G.has_bias) use(G.bias.buf, i);

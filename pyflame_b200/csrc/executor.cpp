@@ -503,6 +503,14 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
         L.H = a.H; L.W = a.W; L.Cp = a.Cp; L.KH = a.KH; L.KW = a.KW; L.sh = a.sh; L.sw = a.sw;
         L.ph = a.ph; L.pw = a.pw; L.dh = a.dh; L.dw = a.dw; L.OH = a.OH; L.OW = a.OW;
         L.batch_images = a.Nimg; L.Hp = a.Hp; L.Wp = a.Wp; L.KWp = a.KWp;
+        if (a.pool) {
+          L.pool = true;
+          L.pool_pad = a.pool_pad;
+          L.c = nullptr;
+          L.pool_y = a.write_pool_y ? (float*)viewp(a.pool_y) : nullptr;
+          L.pool_sn = a.pool_y.strides[0]; L.pool_sh = a.pool_y.strides[2]; L.pool_sw = a.pool_y.strides[3];
+          L.PH = a.pool_y.shape[2]; L.PW = a.pool_y.shape[3];
+        }
       }
       launch_gemm(L, s);
       break;
@@ -578,6 +586,8 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
         L.h = (float*)bufp(a.h_buf, 0);
         L.ldh = a.l1.N;
         L.counter = (unsigned long long*)bufp(a.counter_buf, 0);
+        L.cluster = a.cluster;
+        L.err = err_dev_;
       }
       L.out = (float*)viewp(a.out);
       L.ldo = a.ldo;

@@ -10,27 +10,29 @@
 // One persistent CTA per SM walks tiles of (slice, 128 query rows):
 //   warp 0     TMA: Q of the tile once, then key blocks of 64 (K and V)
 //              through two-stage rings.
-//   warp 1     TMEM (512 columns) and the MMAs, all tf32 x3.  S = Q K_j^T
-//              takes Q from TMEM as the A operand and K from shared memory,
-//              into one of two 128-column S/P buffers.  O_h += P_j,h V_j,h
-//              for the two 32-key halves h of the block takes P from the same
-//              buffer as the A operand and V as an MN-major B operand (its
-//              rows are keys, as stored), into one of two O accumulators.
-//              The MMAs of a CTA run in issue order, so S_j+2 may be issued
-//              into the buffer that P_j*V_j, issued before it, reads.
-//   warps 2-9  two warps per TMEM lane quarter.  At the start of a tile they
-//              copy Q (hi / lo) from shared memory into TMEM.  Warp half h
-//              owns keys 32h..32h+31 of every block for its 32 query rows:
-//              it reads S, keeps a running max m_h and sum l_h, and writes
-//              P = exp2(alpha*log2(e)*s - m_h) as hi/lo tf32 over the S it
-//              read (hi) and beside it (lo).  m_h moves only when a block's
-//              max exceeds it by more than 2^8 (P stays below 256); then O_h
-//              and l_h are rescaled once the previous block's P*V has
-//              retired.  At the end of a tile the halves combine,
-//              O = (O_0 a_0 + O_1 a_1) / (l_0 a_0 + l_1 a_1) with
-//              a_h = 2^(m_h - max(m_0, m_1)).
-// Operands from TMEM leave shared memory to the K and V tiles: per key block
-// the tensor core reads 64 KB there instead of 192 KB.
+//   warp 1     TMEM (512 columns) and the MMAs, all tf32 x3 as two
+//              instructions per K step: the hi x hi and hi x lo products as
+//              ONE N = 128 instruction against the concatenated [hi | lo]
+//              B operand, then lo x hi (N = 64) into its first half.  (An
+//              N = 64 instruction measured ~79 cycles here, about what the
+//              N = 128 one costs: 32 wide instructions per key block do the
+//              work of 48 narrow ones.)  S = Q K_j^T from shared memory goes
+//              into one of two 128-column S/P buffers as [S_hh | S_hl].
+//              O_h += P_j,h V_j,h for the two 32-key halves h of the block
+//              takes P from the same buffer as the A operand and V as an
+//              MN-major B operand (its rows are keys, as stored), into one of
+//              two 128-column accumulators [O_hh | O_hl].  The MMAs of a CTA
+//              run in issue order, so S_j+2 may be issued into the buffer
+//              that P_j*V_j, issued before it, reads.
+//   warps 2-9  two warps per TMEM lane quarter; warp half h owns keys
+//              32h..32h+31 of every block for its 32 query rows: it reads S
+//              (the sum of its two halves), keeps a running max m_h and sum
+//              l_h, and writes P = exp2(alpha*log2(e)*s - m_h) as hi/lo tf32
+//              over the S it read.  m_h moves only when a block's max exceeds
+//              it by more than 2^8 (P stays below 256); then O_h and l_h are
+//              rescaled once the previous block's P*V has retired.  At the end
+//              of a tile the halves combine, O = (O_0 a_0 + O_1 a_1) /
+//              (l_0 a_0 + l_1 a_1) with a_h = 2^(m_h - max(m_0, m_1)).
 // Keys past L are masked; query rows past M and head columns past d are
 // dropped.  Every wait is bounded by the global timer and reports
 // PFC_ERR_TIMEOUT through *err.
@@ -62,17 +64,19 @@ constexpr int kQChunk = kAQ * 128;  // 128 rows x 32 tf32
 constexpr int kKChunk = kAK * 128;  // 64 keys x 32 tf32
 constexpr int kVChunk = kAK * 128;  // 64 keys x 32 head-dim columns
 constexpr int kQBytes = 2 * 2 * kQChunk;    // [hi/lo][k-chunk]
-constexpr int kKStage = 2 * 2 * kKChunk;    // [hi/lo][k-chunk]
+constexpr int kKStage = 2 * 2 * kKChunk;    // [k-chunk][hi/lo]: hi and lo of a chunk adjacent (one N = 128 operand)
 constexpr int kVStage = 2 * 2 * kVChunk;    // [hi/lo][head-dim chunk]
 constexpr int kStages = 2;
 constexpr int kASmem = kQBytes + kStages * (kKStage + kVStage) + 1024 /*barriers*/ + 1024 /*align*/;
-// TMEM columns: S/P buffers at 0 and 128 (S, then P hi, in the first 64
-// columns; P lo in the next 64); O accumulators of the two key halves at 256
-// and 320; Q hi at 384, Q lo at 448.
-constexpr uint32_t kTS = 0, kTO = 256, kTQ = 384, kATmemCols = 512;
+// TMEM columns: S/P buffers at 0 and 128 ([S_hh | S_hl], then P hi over the
+// first 64 columns and P lo over the next 64); O accumulators of the two key
+// halves at 256 and 384, each [O_hh | O_hl].
+constexpr uint32_t kTS = 0, kTO = 256, kATmemCols = 512;
 constexpr float kRescaleLog2 = 8.f;  // P < 2^8 between rescales
 constexpr uint32_t kIdesc = idesc(kAQ, 64, 2u);  // M 128, N 64, tf32
 constexpr uint32_t kIdescMnB = kIdesc | (1u << 16);  // ... with B MN-major
+constexpr uint32_t kIdescCat = idesc(kAQ, 128, 2u);  // M 128, N 128 over [hi | lo]
+constexpr uint32_t kIdescCatMnB = kIdescCat | (1u << 16);
 
 // Shared-memory descriptor of an MN-major tf32 operand, the one layout
 // tcgen05 takes for it: the 128-byte swizzle with 32-byte atoms.  Rows of 32
@@ -157,6 +161,19 @@ __device__ __forceinline__ float max32(const float (&v)[32]) {
   return a[0];
 }
 
+// 32 fp32 columns at taddr plus the 32 at taddr + step
+__device__ __forceinline__ void tmem_ld32_sum(uint32_t taddr, uint32_t step, float (&v)[32]) {
+  uint32_t r[32], r2[32];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    tmem_ld16_nowait(taddr + 16 * i, *reinterpret_cast<uint32_t(*)[16]>(&r[16 * i]));
+    tmem_ld16_nowait(taddr + step + 16 * i, *reinterpret_cast<uint32_t(*)[16]>(&r2[16 * i]));
+  }
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) + __uint_as_float(r2[i]);
+}
+
 // Barrier among the softmax warps only.  Every softmax warp passes the same
 // barriers in the same order, also after a failed wait: a warp never leaves
 // the tile loop except right after softmax_bar_any has told all of them.
@@ -187,7 +204,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
   uint8_t* sv = sk + kStages * kKStage;
   uint64_t* bars = (uint64_t*)(sv + kStages * kVStage);
   uint64_t* q_full = bars + 0;
-  uint64_t* q_tmem = bars + 1;   // Q copied into TMEM (and its shared memory free)
+  uint64_t* q_free = bars + 1;   // the tile's last S MMAs have read Q
   uint64_t* k_full = bars + 2;   // [2]
   uint64_t* k_free = bars + 4;   // [2]
   uint64_t* v_full = bars + 6;   // [2]
@@ -208,7 +225,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(q_full), 1);
-    mbar_init(smem_u32(q_tmem), kSoftWarps);
+    mbar_init(smem_u32(q_free), 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&k_full[i]), 1);
       mbar_init(smem_u32(&k_free[i]), 1);
@@ -241,7 +258,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
     const uint32_t kbytes = (uint32_t)(2 * p.nkc * kKChunk);
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
       const int b = t / p.ntq, q0 = (t - b * p.ntq) * kAQ;
-      if (tc > 0 && !mbar_wait(smem_u32(q_tmem), (uint32_t)(tc - 1) & 1u, p.err)) { ok = false; break; }
+      if (tc > 0 && !mbar_wait(smem_u32(q_free), (uint32_t)(tc - 1) & 1u, p.err)) { ok = false; break; }
       mbar_expect_tx(smem_u32(q_full), (uint32_t)(2 * p.nkc * kQChunk));
       for (int c = 0; c < p.nkc; ++c) {
         tma_load_3d(smem_u32(sq + c * kQChunk), &tq_hi, smem_u32(q_full), c * 32, q0, b);
@@ -254,8 +271,8 @@ __global__ void __launch_bounds__(kAThreads, 1)
           uint8_t* kst = sk + s * kKStage;
           mbar_expect_tx(smem_u32(&k_full[s]), kbytes);
           for (int c = 0; c < p.nkc; ++c) {
-            tma_load_3d(smem_u32(kst + c * kKChunk), &tk_hi, smem_u32(&k_full[s]), c * 32, j * kAK, b);
-            tma_load_3d(smem_u32(kst + (2 + c) * kKChunk), &tk_lo, smem_u32(&k_full[s]), c * 32, j * kAK, b);
+            tma_load_3d(smem_u32(kst + 2 * c * kKChunk), &tk_hi, smem_u32(&k_full[s]), c * 32, j * kAK, b);
+            tma_load_3d(smem_u32(kst + (2 * c + 1) * kKChunk), &tk_lo, smem_u32(&k_full[s]), c * 32, j * kAK, b);
           }
           ++gk;
           {
@@ -280,7 +297,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
     // ---------------- MMA issuer ----------------
     int gk = 0, gv = 0, gs = 0, gp = 0, tc = 0;
     bool ok = true;
-    const uint32_t qh_t = tmem + kTQ, ql_t = tmem + kTQ + 64;
+    const uint32_t q_base = smem_u32(sq);
     // S[gs & 1] = Q K^T of the next K block.  Its buffer last held P of
     // block gs-2, whose P*V MMAs were issued before these.
     auto issue_s = [&]() -> bool {
@@ -290,14 +307,14 @@ __global__ void __launch_bounds__(kAThreads, 1)
       const uint32_t d = tmem + kTS + (uint32_t)(sb * 128);
       const uint32_t k_base = smem_u32(sk + ks * kKStage);
       for (int c = 0; c < p.nkc; ++c) {
-        const uint64_t kh = sdesc(k_base + c * kKChunk), kl = sdesc(k_base + (2 + c) * kKChunk);
+        const uint64_t qh = sdesc(q_base + c * kQChunk), ql = sdesc(q_base + (2 + c) * kQChunk);
+        const uint64_t khl = sdesc(k_base + 2 * c * kKChunk);  // [K_hi | K_lo]; its first 64 rows are K_hi
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          const uint32_t off = kk * 32, col = (uint32_t)(c * 32 + kk * 8);
+          const uint32_t off = kk * 32;
           const uint32_t acc = (c > 0 || kk > 0) ? 1u : 0u;
-          umma_tmem_a<kIdesc>(d, ql_t + col, desc_add(kh, off), acc);
-          umma_tmem_a<kIdesc>(d, qh_t + col, desc_add(kl, off), 1u);
-          umma_tmem_a<kIdesc>(d, qh_t + col, desc_add(kh, off), 1u);
+          umma<PFC_PRECISION_TF32X3>(d, desc_add(qh, off), desc_add(khl, off), kIdescCat, acc);
+          umma<PFC_PRECISION_TF32X3>(d, desc_add(ql, off), desc_add(khl, off), kIdesc, 1u);
         }
       }
       umma_commit(smem_u32(&k_free[ks]));
@@ -315,20 +332,20 @@ __global__ void __launch_bounds__(kAThreads, 1)
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const uint32_t ph = tmem + kTS + (uint32_t)(pb * 128), pl = ph + 64;
       const uint32_t v_base = smem_u32(sv + vs * kVStage);
-      // V block [64 keys][64 head dims] as two 32-column chunks: K-step kk
-      // takes keys 8kk..8kk+7 (one 1024-byte row group further down); keys
-      // 32h.. go to accumulator O_h
-      const uint64_t vh = sdesc_mn(v_base, kVChunk), vl = sdesc_mn(v_base + 2 * kVChunk, kVChunk);
+      // V block [64 keys][64 head dims] as 32-column chunks [hi 0][hi 1]
+      // [lo 0][lo 1], LBO apart: one descriptor spans N = 128 ([V_hi | V_lo])
+      // or, at N = 64, V_hi.  K-step kk takes keys 8kk..8kk+7 (one 1024-byte
+      // row group further down); keys 32h.. go to accumulator O_h
+      const uint64_t vhl = sdesc_mn(v_base, kVChunk);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const uint32_t d = tmem + kTO + (uint32_t)(h * 64);
+        const uint32_t d = tmem + kTO + (uint32_t)(h * 128);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           const uint32_t col = (uint32_t)(h * 32 + kk * 8), off = (uint32_t)(h * 4 + kk) * 1024u;
           const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
-          umma_tmem_a<kIdescMnB>(d, pl + col, desc_add(vh, off), acc);
-          umma_tmem_a<kIdescMnB>(d, ph + col, desc_add(vl, off), 1u);
-          umma_tmem_a<kIdescMnB>(d, ph + col, desc_add(vh, off), 1u);
+          umma_tmem_a<kIdescCatMnB>(d, ph + col, desc_add(vhl, off), acc);
+          umma_tmem_a<kIdescMnB>(d, pl + col, desc_add(vhl, off), 1u);
         }
       }
       umma_commit(smem_u32(&v_free[vs]));
@@ -338,13 +355,14 @@ __global__ void __launch_bounds__(kAThreads, 1)
       return true;
     };
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tc) {
-      if (!mbar_wait(smem_u32(q_tmem), (uint32_t)tc & 1u, p.err)) { ok = false; break; }
+      if (!mbar_wait(smem_u32(q_full), (uint32_t)tc & 1u, p.err)) { ok = false; break; }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       // S of the next block goes in before P V of this one, so the softmax
       // warps work on one block while the tensor core does the other
       ok = issue_s();
       for (int j = 0; j < p.nblk && ok; ++j) {
         if (j + 1 < p.nblk) ok = issue_s();
+        if (ok && j + 1 == p.nblk) umma_commit(smem_u32(q_free));  // the last S of the tile is issued
         if (ok) ok = issue_pv(j);
       }
       if (ok) umma_commit(smem_u32(o_full));
@@ -359,48 +377,20 @@ __global__ void __launch_bounds__(kAThreads, 1)
     const float scale = (p.alpha_ptr ? *p.alpha_ptr : p.alpha) * 1.4426950408889634f;  // alpha * log2(e)
     int gs = 0, gp = 0, tc = 0;
     bool ok = true;
-    // Q of the CTA's tile number `tq` from shared memory (as TMA wrote it:
-    // 128-byte rows, 16-byte units swizzled by row & 7) into TMEM: this
-    // warp's 32 rows, hi (warp half 0) or lo (half 1), 32 head dims per
-    // chunk.  Its arrival frees the shared copy and starts the tile's MMAs.
-    auto copy_q = [&](int tq) -> bool {
-      if (!mbar_wait_warp(smem_u32(q_full), (uint32_t)tq & 1u, p.err)) return false;
-      const uint8_t* src = sq + hf * 2 * kQChunk + row_in_tile * 128;
-      for (int c = 0; c < p.nkc; ++c) {
-        uint32_t r[32];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const uint4 x = *reinterpret_cast<const uint4*>(src + c * kQChunk + ((u ^ (row_in_tile & 7)) << 4));
-          r[4 * u] = x.x;
-          r[4 * u + 1] = x.y;
-          r[4 * u + 2] = x.z;
-          r[4 * u + 3] = x.w;
-        }
-        const uint32_t dst = lane_base + kTQ + (uint32_t)(hf * 64 + c * 32);
-        tmem_st16(dst, *reinterpret_cast<const uint32_t(*)[16]>(&r[0]));
-        tmem_st16(dst + 16, *reinterpret_cast<const uint32_t(*)[16]>(&r[16]));
-      }
-      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(q_tmem));
-      return true;
-    };
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tc) {
       const int b = t / p.ntq, q0 = (t - b * p.ntq) * kAQ;
       float m = -INFINITY, l = 0.f;
       float v[32];
+      // this warp's 32 keys of S: the sum of the hi x hi and hi x lo halves
+      // (the lo x hi product is in the first)
       auto read_s = [&]() -> bool {
         const int sb = gs & 1;
         if (!mbar_wait_warp(smem_u32(&s_full[sb]), (uint32_t)(gs >> 1) & 1u, p.err)) return false;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        tmem_ld32(lane_base + kTS + (uint32_t)(sb * 128 + hf * 32), v);
+        tmem_ld32_sum(lane_base + kTS + (uint32_t)(sb * 128 + hf * 32), 64u, v);
         ++gs;
         return true;
       };
-      if (tc == 0 && !(ok = copy_q(0))) {
-        // fall through to the tile's barrier with ok false
-      }
       // one pass: this half's keys, running max m (log2 units, moved lazily)
       // and sum l of P = exp2(scale * s - m)
       for (int j = 0; j < p.nblk && ok; ++j) {
@@ -425,10 +415,10 @@ __global__ void __launch_bounds__(kAThreads, 1)
           if (!(ok = mbar_wait_warp(smem_u32(&p_free[prev & 1]), (uint32_t)(prev >> 1) & 1u, p.err))) break;
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const float a = (move && !first) ? exp2f(m - mn) : 1.f;
-          const uint32_t oaddr = lane_base + kTO + (uint32_t)(hf * 64);
+          const uint32_t oaddr = lane_base + kTO + (uint32_t)(hf * 128);
           float o[32];
 #pragma unroll
-          for (int c = 0; c < 64; c += 32) {
+          for (int c = 0; c < 128; c += 32) {
             tmem_ld32(oaddr + c, o);
             uint32_t w[32];
 #pragma unroll
@@ -468,9 +458,6 @@ __global__ void __launch_bounds__(kAThreads, 1)
         if (lane == 0) mbar_arrive(smem_u32(&p_full[pb]));
         ++gp;
       }
-      // every S MMA of this tile has completed (its last S was read): Q of
-      // the next tile may replace it while the last P*V runs
-      if (ok && t + (int)gridDim.x < ntiles) ok = copy_q(tc + 1);
       // the two halves of the row: weights a_h = 2^(m_h - m) (0 for a half without keys)
       row_stat[hf][row_in_tile] = make_float2(m, l);
       if (softmax_bar_any(!ok)) break;  // all softmax warps leave together
@@ -492,8 +479,8 @@ __global__ void __launch_bounds__(kAThreads, 1)
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       {
         float o1[32];
-        tmem_ld32(lane_base + kTO + (uint32_t)(hf * 32), v);        // O_0, this warp's 32 columns
-        tmem_ld32(lane_base + kTO + 64u + (uint32_t)(hf * 32), o1);  // O_1, the same columns
+        tmem_ld32_sum(lane_base + kTO + (uint32_t)(hf * 32), 64u, v);           // O_0, this warp's 32 columns
+        tmem_ld32_sum(lane_base + kTO + 128u + (uint32_t)(hf * 32), 64u, o1);  // O_1, the same columns
 #pragma unroll
         for (int n = 0; n < 32; ++n) v[n] = v[n] * a0 + o1[n] * a1;
       }

@@ -92,6 +92,13 @@ struct GemmParams {
   //     block.
   int conv_tma, TW, TH, tiles_w, tiles_h;
   int nimg, halo_rows;
+  // 3x3 / stride 2 max pool (padding pool_pad, 0 or 1) fused into a ReLU
+  // convolution (gemm_kernel POOL): pooled [img][PH][PW][N] at py + img*py_sn
+  // + ph*py_sh + pw*py_sw + n (fp32, or null), and the operand at the same
+  // offsets of o_hi / o_lo (or null)
+  float* py;
+  long long py_sn, py_sh, py_sw;
+  int PH, PW, pool_pad;
 };
 
 
@@ -329,6 +336,48 @@ __device__ __forceinline__ void conv_tile(const GemmParams& p, int tm, int& img,
   ow0 = (r % p.tiles_w) * p.TW;
 }
 
+// Tiles of a pool-fused convolution: strips of tiles_h tiles, one strip per
+// (image, column tile colt), u = (img*tiles_w + colt)*tiles_h + pos.  Tile
+// (a, colt) is conv rows 2a, 2a+1 and columns 62colt-pad .. 62colt-pad+63
+// (64 output pixels, TH = 2, TW = 64): pooled row a, columns 31colt ..
+// 31colt+30, with one more conv row carried from the tile walked before it
+// in the strip.  Padding 1: row 2a-1, walking top-down (a = pos); padding 0:
+// row 2a+2, walking bottom-up (a = tiles_h-1-pos).  The first tile of a strip
+// carries a padding row.  pos is returned for that test.
+__device__ __forceinline__ void pool_tile(const GemmParams& p, int u, int& img, int& oh0, int& ow0, int& a,
+                                          int& colt, int& pos) {
+  const int strip = u / p.tiles_h;
+  pos = u - strip * p.tiles_h;
+  img = strip / p.tiles_w;
+  colt = strip - img * p.tiles_w;
+  a = p.pool_pad ? pos : p.tiles_h - 1 - pos;
+  oh0 = 2 * a;
+  ow0 = 62 * colt - p.pool_pad;
+}
+
+// The CTA's run of consecutive tiles [own0, u1), so that each tile's carry
+// comes from the tile before it; a run that starts inside a strip first
+// recomputes the tile above (u0 = own0 - 1), for its carry only.
+__device__ __forceinline__ void pool_run(const GemmParams& p, int ntiles, int& u0, int& u1, int& own0) {
+  own0 = (int)((long long)blockIdx.x * ntiles / gridDim.x);
+  u1 = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
+  u0 = (own0 < u1 && own0 % p.tiles_h != 0) ? own0 - 1 : own0;
+}
+
+// Barrier among the eight epilogue warps (named barrier 1) that also tells
+// them whether any of them passed `v` true.
+__device__ __forceinline__ bool epi_bar_any(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(kEpiWarps * 32)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory"); }
+
 // Epilogue warp e (0..7) on TMEM lane quarter q: for every tile this CTA
 // owns, sum the chunk accumulators in registers (handing each accumulator
 // back to the MMA warp at once), then apply alpha/bias/folded-BN/activation/
@@ -422,10 +471,157 @@ __device__ __forceinline__ void run_epilogue(const GemmParams& p, uint32_t tmem,
   }
 }
 
+// Epilogue of a convolution with BN = N = 64 whose ReLU output feeds a 3x3 /
+// stride 2 max pool (padding 0 or 1) and nothing else (PyFlame's Conv2d ->
+// BatchNorm -> ReLU -> MaxPool2d stem): the conv output never reaches
+// memory.  Thread (lane quarter q, lane) holds conv pixel (row r = q >> 1,
+// column x = 32(q & 1) + lane) of the tile, channels 32(e >> 2) .. +31.
+// Values are >= +0 after the ReLU and never NaN (ReLU maps NaN to 0), so the
+// pool's max is exact in any order and pixels outside the image can enter it
+// as 0: every window holds a real pixel.  Of the tile's two rows, row rc
+// (1 for padding 1, 0 for padding 0) is the one the next tile of the strip
+// needs; the other, ro, makes pooled row a with it and the carried row.  Per
+// tile:
+//   1. v = relu(acc*scale + shift) (0 outside the image); even columns take
+//      the max of columns x, x+1, x+2 by shuffles (pooled column x/2).
+//   2. Row rc writes its window maxima to the next-carry buffer; the pixels
+//      of the one window that spans two warps (columns 30..32) go to shared
+//      memory; barrier.
+//   3. Row ro combines the carry, its own and row rc's maxima into pooled row
+//      a and stores it as fp32 and / or the next convolution's operand.
+// The eight epilogue warps meet at two named barriers per tile, so every
+// warp takes every tile; a failed wait is agreed on at the first barrier.
+template <int PREC, int BN>
+__device__ __forceinline__ void run_pool_epilogue(const GemmParams& p, uint32_t tmem, uint64_t* acc_full,
+                                                  uint64_t* acc_empty, float* sm, int e, int q, int lane, int u0,
+                                                  int u1, int own0) {
+  using C = Cfg<PREC, BN, false>;
+  static_assert(BN == 64, "the pooled epilogue takes 64-channel tiles");
+  static_assert((2 * 64 * 32 + 4 * 64) * 4 <= C::EPI_BYTES, "pool buffers exceed the epilogue staging area");
+  constexpr int HALF = BN / 2;
+  constexpr int KW = 31;  // pooled columns per tile
+  const int col0 = (e >> 2) * HALF;
+  const int r = q >> 1, x = (q & 1) * 32 + lane, kq = x >> 1;
+  const int rc = p.pool_pad ? 1 : 0, ro = 1 - rc;
+  // window maxima of the carried conv row, [2][64 channels][32 pooled
+  // columns]: lanes at consecutive pooled columns touch consecutive words
+  // (no bank conflicts beside the tensor core's operand reads)
+  float* rowbuf = sm;
+  float* bnd = sm + 2 * 64 * 32;  // [4][64]: row ro column 32, row rc columns 30, 31, 32
+  // the lanes that hold the pixels of the spanning window (columns 30..32)
+  const bool span = q == 2 * ro && lane == 30;  // finishes pooled column 15
+  const int bslot = q == 2 * ro + 1 && lane == 0 ? 0
+                    : q == 2 * rc && lane == 30  ? 1
+                    : q == 2 * rc && lane == 31  ? 2
+                    : q == 2 * rc + 1 && lane == 0 ? 3
+                                                   : -1;
+  const float alpha = p.alpha_ptr ? *p.alpha_ptr : p.alpha;
+  const float bsc = p.bias_scalar ? *p.bias_scalar : 0.f;
+  const bool has_shift = p.scale || p.bias || p.bias_scalar;
+  int u = 0;
+  bool ok = true;
+  for (int t = u0; t < u1; ++t) {
+    float acc[HALF];
+#pragma unroll
+    for (int j = 0; j < HALF; ++j) acc[j] = 0.f;
+    for (int ch = 0; ch < p.nchunks && ok; ++ch, ++u) {
+      const int b = u & 1;
+      const uint32_t use = (uint32_t)(u >> 1);
+      if (!__all_sync(0xffffffffu, mbar_wait_backoff(smem_u32(&acc_full[b]), use & 1u, p.err))) { ok = false; break; }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      uint32_t rr[32];
+      const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * C::ACC_COLS + col0);
+      tmem_ld16_nowait(ta, *reinterpret_cast<uint32_t(*)[16]>(&rr[0]));
+      tmem_ld16_nowait(ta + 16, *reinterpret_cast<uint32_t(*)[16]>(&rr[16]));
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc[j] += __uint_as_float(rr[j]);
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&acc_empty[b]));
+    }
+    // all warps leave together on a failed wait; otherwise the barrier after
+    // which the previous tile's reads of the shared buffers are done
+    if (epi_bar_any(!ok)) break;
+    int img, oh0, ow0, a, colt, pos;
+    pool_tile(p, t, img, oh0, ow0, a, colt, pos);
+    const int oh = oh0 + r, ow = ow0 + x;
+    const bool real = oh < p.OH && ow >= 0 && ow < p.OW;
+    float v[HALF], hm[HALF];
+#pragma unroll
+    for (int j = 0; j < HALF; ++j) {
+      const int n = col0 + j;
+      float sc = alpha, sh = bsc;
+      if (p.scale) { sc = p.scale[n]; sh = p.shift[n]; }
+      else if (p.bias) sh = p.bias[n];
+      float w = acc[j] * sc;
+      if (has_shift) w = w + sh;
+      w = act_apply<1>(w);
+      v[j] = real ? w : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < HALF; ++j) {
+      const float a1 = __shfl_down_sync(0xffffffffu, v[j], 1);
+      const float a2 = __shfl_down_sync(0xffffffffu, v[j], 2);  // lanes 30, 31: their own value
+      hm[j] = fmaxf(v[j], fmaxf(a1, a2));
+    }
+    float* next = rowbuf + (t & 1) * (64 * 32) + col0 * 32;  // this warp's channels
+    const float* carry = rowbuf + ((t - 1) & 1) * (64 * 32) + col0 * 32;
+    if (r == rc && (lane & 1) == 0 && kq < KW && kq != 15) {
+#pragma unroll
+      for (int j = 0; j < HALF; ++j) next[j * 32 + kq] = hm[j];
+    }
+    if (bslot >= 0) {
+#pragma unroll
+      for (int j = 0; j < HALF; j += 4)
+        *reinterpret_cast<float4*>(bnd + bslot * 64 + col0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    }
+    epi_bar();
+    if (span) {
+      // row rc's window of column 15 (its next carry) and row ro's, finished here
+#pragma unroll
+      for (int j = 0; j < HALF; ++j) {
+        const int n = col0 + j;
+        const float h1 = fmaxf(bnd[64 + n], fmaxf(bnd[128 + n], bnd[192 + n]));
+        next[j * 32 + 15] = h1;
+        hm[j] = fmaxf(fmaxf(hm[j], bnd[n]), h1);
+      }
+    }
+    // the tile recomputed before a run only feeds the carry
+    if (r == ro && (lane & 1) == 0 && kq < KW && t >= own0) {
+      const int pw = KW * colt + kq;
+      if (pw < p.PW && a < p.PH) {
+        float o[HALF];
+#pragma unroll
+        for (int j = 0; j < HALF; ++j) {
+          const float h1 = span ? 0.f : next[j * 32 + kq];
+          const float c = pos == 0 ? 0.f : carry[j * 32 + kq];  // a strip's first tile carries padding
+          o[j] = fmaxf(c, fmaxf(hm[j], h1));
+        }
+        const long long off = (long long)img * p.py_sn + (long long)a * p.py_sh + (long long)pw * p.py_sw + col0;
+        if (p.py) {
+#pragma unroll
+          for (int j = 0; j < HALF; j += 4)
+            *reinterpret_cast<float4*>(p.py + off + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
+        }
+        if (p.o_hi) {
+#pragma unroll
+          for (int j = 0; j < HALF; j += 4) {
+            const float w4[4] = {o[j], o[j + 1], o[j + 2], o[j + 3]};
+            store_operand4<PREC>(p.o_hi, p.o_lo, off + j, w4);
+          }
+        }
+      }
+    }
+  }
+}
+
 // Persistent kernel: each CTA walks tiles blockIdx.x, +gridDim.x, ...
 // CONV: the A operand is gathered by four producer warps from a channels-last
-// input (implicit-GEMM Conv2d) instead of loaded by TMA.
-template <int PREC, int BN, bool CONV, bool CAT>
+// input (implicit-GEMM Conv2d) instead of loaded by TMA.  POOL: a windowed
+// TMA convolution (conv_tma 2) with the max pool fused into its epilogue;
+// each CTA walks a run of consecutive tiles (pool_run).
+template <int PREC, int BN, bool CONV, bool CAT, bool POOL = false>
 __global__ void __launch_bounds__(kThreads<CONV>, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
                 const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
@@ -475,6 +671,12 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
 
   const int nkb = p.nkb;
   const int ntiles = p.num_m * p.num_n * p.batch;
+  // this CTA's tiles: t0, t0 + ts, ... below t1
+  int t0 = blockIdx.x, t1 = ntiles, ts = gridDim.x, own0 = 0;
+  if constexpr (POOL) {
+    pool_run(p, ntiles, t0, t1, own0);
+    ts = 1;
+  }
   if (CONV && warp < PW) {
     // ---------------- implicit-GEMM producer: thread r gathers A row r ----------------
     const int r = threadIdx.x;
@@ -551,7 +753,7 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
     // ---------------- TMA producer ----------------
     int g = 0;  // k-block counter across all tiles of this CTA
     bool ok = true;
-    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+    for (int t = t0; t < t1 && ok; t += ts) {
       int bz, tm, tn;
       tile_coords(p, t, bz, tm, tn);
       const int ca = p.a_batched ? bz : 0, cb = p.b_batched ? bz : 0;
@@ -579,7 +781,12 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
         } else if (p.conv_tma == 2) {
           // filter row kb: for every output pixel a 128-byte window of the padded input
           int img, oh0, ow0;
-          conv_tile(p, tm, img, oh0, ow0);
+          if constexpr (POOL) {
+            int a, colt, pos;
+            pool_tile(p, t, img, oh0, ow0, a, colt, pos);
+          } else {
+            conv_tile(p, tm, img, oh0, ow0);
+          }
           tma_load_5d(a_hi_dst, &ta_hi, fb, 0, ow0, kb, oh0, img);
           if constexpr (C::NOPS == 2) tma_load_5d(a_lo_dst, &ta_lo, fb, 0, ow0, kb, oh0, img);
         } else {
@@ -601,7 +808,7 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
     // long contractions (K = 16384) within fp32-reference accuracy.
     int g = 0, u = 0;  // k-blocks consumed; accumulator uses
     bool ok = true;
-    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+    for (int t = t0; t < t1 && ok; t += ts) {
       for (int ch = 0; ch < p.nchunks && ok; ++ch, ++u) {
         const int b = u & 1;
         const uint32_t use = (uint32_t)(u >> 1);
@@ -644,6 +851,9 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
   } else if (warp > PW) {
     // ---------------- epilogue ----------------
     const int e = warp - PW - 1;  // 0..7
+    if constexpr (POOL) {
+      run_pool_epilogue<PREC, BN>(p, tmem, acc_full, acc_empty, epi, e, warp & 3, lane, t0, t1, own0);
+    } else
     run_epilogue<PREC, BN, CAT, false>(p, tmem, acc_full, acc_empty, epi + e * C::EPI_WARP_FLOATS, e, warp & 3, lane,
                                   [&](int tm, long long& m_base, int& nvalid) {
                                     const int q = warp & 3;
@@ -991,6 +1201,9 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const 
     if constexpr (Cfg<PREC, BN, true>::CAT)
       PFB_CUDA(cudaFuncSetAttribute(gemm_kernel<PREC, BN, CONV, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     C::SMEM));
+    if constexpr (!CONV && BN == 64)
+      PFB_CUDA(cudaFuncSetAttribute(gemm_kernel<PREC, BN, false, false, true>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     if constexpr (!CONV) {
       PFB_CUDA(cudaFuncSetAttribute(conv_halo_kernel<PREC, BN, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     HaloCfg<PREC, BN>::SMEM));
@@ -1063,6 +1276,21 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const 
     p.batch = 1;
   }
   if (L.K == 0) p.nkb = 0;
+  p.py = L.pool_y;
+  p.py_sn = L.pool_sn;
+  p.py_sh = L.pool_sh;
+  p.py_sw = L.pool_sw;
+  p.PH = (int)L.PH;
+  p.PW = (int)L.PW;
+  p.pool_pad = L.pool_pad;
+  if (L.pool) {
+    // pooled rows by conv row pairs, 31 pooled columns per 64-pixel tile
+    PFB_CHECK_ARG(conv_tma == 2 && p.TW == 64 && BN == 64 && L.N == 64, "gemm: the fused max pool needs the windowed "
+                  "TMA convolution with 64 output channels");
+    p.tiles_h = (int)ceil_div(L.OH, 2);
+    p.tiles_w = (int)ceil_div(L.PW, 31);
+    p.num_m = (int)(L.batch_images * p.tiles_h * p.tiles_w);
+  }
   // The concatenated-B instantiation (Cfg::CAT) where a tile has enough
   // k-blocks that the MMAs, not the epilogue, set the pace: it doubles the
   // epilogue's TMEM reads, which a 7-k-block tile (the 7x7 stem convolution)
@@ -1092,6 +1320,15 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const 
       return;
     }
   }
+  if constexpr (!CONV && BN == 64) {
+    if (L.pool) {
+      gemm_kernel<PREC, BN, false, false, true><<<grid, kThreads<false>, C::SMEM, stream>>>(ta_hi, ta_lo, tb_hi, tb_lo,
+                                                                                          p);
+      PFB_CUDA(cudaGetLastError());
+      return;
+    }
+  }
+  PFB_CHECK_ARG(!L.pool, "gemm: the fused max pool needs the windowed TMA convolution");
   if constexpr (Cfg<PREC, BN, true>::CAT) {
     if (cat) {
       gemm_kernel<PREC, BN, CONV, true><<<grid, kThreads<CONV>, C::SMEM, stream>>>(ta_hi, ta_lo, tb_hi, tb_lo, p);
@@ -1156,13 +1393,24 @@ void launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
   PFB_CHECK_ARG(L.M > 0 && L.N > 0 && L.batch > 0, "gemm: empty problem");
   PFB_CHECK_ARG(L.M < (1ll << 31) && L.N < (1ll << 31), "gemm: dimension too large");
   PFB_CHECK_ARG(L.err != nullptr, "gemm: error flag pointer required");
-  PFB_CHECK_ARG(L.c || L.out_hi, "gemm: no output");
+  PFB_CHECK_ARG(L.c || L.out_hi || L.pool_y, "gemm: no output");
+  if (L.pool) {
+    PFB_CHECK_ARG(L.conv && L.N == 64 && L.act == 1 && !L.residual && L.batch == 1 && L.Hp > 0 && L.PH > 0 &&
+                      L.PW > 0 && (L.pool_pad == 0 || L.pool_pad == 1) &&
+                      L.PH == (L.OH + 2 * L.pool_pad - 3) / 2 + 1 && L.PW == (L.OW + 2 * L.pool_pad - 3) / 2 + 1 &&
+                      L.OW > 32,
+                  "gemm: a fused max pool needs a ReLU convolution with 64 output channels over a padded input");
+    PFB_CHECK_ARG(L.pool_sw % 4 == 0 && L.pool_sh % 4 == 0 && L.pool_sn % 4 == 0 &&
+                      (((uintptr_t)L.pool_y | (uintptr_t)L.out_hi | (uintptr_t)L.out_lo) & 15) == 0 &&
+                      (L.pool_y || L.out_hi) && (!L.out_hi || L.precision == PFC_PRECISION_BF16 || L.out_lo),
+                  "gemm: the pooled output needs 16-byte aligned channels-last rows");
+  }
   if (L.out_hi && L.o_heads > 0) {
     PFB_CHECK_ARG(L.batch == 1 && L.o_sm % 16 == 0 && L.o_heads * L.o_sm == L.N && L.o_rows % 32 == 0 &&
                       L.M % L.o_rows == 0 && !L.conv,
                   "gemm: head-split operand output needs 16-column heads, 32-row groups and batch 1");
   }
-  if (L.out_hi) {
+  if (L.out_hi && !L.pool) {
     PFB_CHECK_ARG(L.N % 4 == 0 && L.o_sm % 4 == 0 && (L.o_heads > 0 || L.o_sm >= L.N) && ((uintptr_t)L.out_hi & 15) == 0 &&
                       (L.precision == PFC_PRECISION_BF16 || (L.out_lo && ((uintptr_t)L.out_lo & 15) == 0)),
                   "gemm: operand output needs 16-byte aligned rows of a multiple of 4 columns");

@@ -51,6 +51,14 @@ struct GemmLaunch {
   int64_t Hp = 0, Wp = 0;
   int64_t KWp = 0;  // taps per filter row in the weight layout (>= KW; 0 = KW)
   bool allow_tma_conv = true;  // TMA-fed A when the geometry allows it
+  // pool: a 3x3 / stride 2 max pool (padding pool_pad, 0 or 1) of the ReLU
+  // output (N = 64, act 1, the windowed TMA feed) replaces c: pooled
+  // [N][PH][PW][64] at pool_y + n*pool_sn + ph*pool_sh + pw*pool_sw + channel
+  // (or null), and the operand at the same offsets of out_hi / out_lo (or null)
+  bool pool = false;
+  int pool_pad = 0;
+  float* pool_y = nullptr;
+  int64_t pool_sn = 0, pool_sh = 0, pool_sw = 0, PH = 0, PW = 0;
 };
 void launch_gemm(const GemmLaunch& L, cudaStream_t stream);
 
@@ -185,8 +193,17 @@ struct SmallMlpLaunch {
   int64_t ldo = 0;
   int softmax = 0;
   unsigned long long* counter = nullptr;
+  // Two layers on clusters of 8 CTAs (small_mlp_cluster_fits): h, ldh and
+  // counter are unused; err receives a timed-out wait.
+  bool cluster = false;
+  int* err = nullptr;
 };
 void launch_small_mlp(const SmallMlpLaunch& L, cudaStream_t stream);
+// Whether a two-layer chain of these sizes runs on clusters of 8 CTAs, each
+// cluster a block of rows and each CTA an eighth of the hidden units: x rows
+// and the CTA's weight rows staged whole in shared memory (K % 4 == 0 and
+// 16-byte aligned rows, checked again at launch), at most 256 outputs per row.
+bool small_mlp_cluster_fits(int64_t M, int64_t N1, int64_t K1, int64_t N2);
 
 struct BnFoldLaunch {
   const float* gamma = nullptr; int64_t gs = 0;  // strides in elements (0 = splat)

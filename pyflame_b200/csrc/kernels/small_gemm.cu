@@ -16,6 +16,7 @@
 // launch with no grid-wide barrier.  Products accumulate in fp32 FMAs, in a
 // different order than PyFlame's sequential sums (matmul.cpp:12-31): within
 // a few ulp times sqrt(K) of them.
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -25,6 +26,7 @@
 #include "../common.hpp"
 #include "act.cuh"
 #include "kernels.hpp"
+#include "tcgen05.cuh"
 
 namespace pfb {
 
@@ -332,7 +334,171 @@ __global__ void __launch_bounds__(kSWarps * 32) small_mlp_kernel(SParams p) {
 
 bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
+// ---------------------------------------------------------------------------
+// Two layers on clusters of kCluster CTAs.  The last-CTA scheme above leaves
+// layer 2 and the softmax to one SM, whose loads of the layer-1 rows and
+// serial work measured 20 of a 26 us launch at 64 x 784 -> 256 -> 10.  Here
+// cluster g owns rows [gR, gR+R) and CTA c of it hidden units [cS, cS+S):
+//   1. one 16-byte bulk copy per row brings the cluster's x rows and the CTA's
+//      weight rows into shared memory (one memory round trip);
+//   2. the warps' 4 x 4 blocks compute h = act1(alpha1 x W1^T + bias1) for
+//      those rows and units from shared memory;
+//   3. each CTA multiplies its slice of h by the matching columns of W2: a
+//      partial [R][N2] sum, kept in its shared memory;
+//   4. after a cluster barrier, CTA c sums the kCluster partials of rows
+//      c, c+kCluster, ... (distributed shared memory, in rank order), applies
+//      alpha2 / bias2 / act2 and the softmax, and writes the rows;
+//   5. a last cluster barrier keeps every CTA's partials alive until read.
+// No grid-wide dependency and no arrival counter; the summation order is
+// fixed.
+constexpr int kCluster = 8;
+constexpr size_t kClusterSmemMax = 200 * 1024;
+constexpr int kClusterMaxN2 = 256;
+
+struct CParams {
+  const float* a;
+  long long lda;
+  int M;
+  SLayer l1, l2;
+  float* out;
+  long long ldo;
+  int softmax;
+  int R, S;  // rows per cluster, hidden units per CTA (a multiple of 4)
+  int* err;
+};
+
+void cluster_shape(int64_t M, int64_t N1, int* R, int* S) {
+  const int64_t G = std::min<int64_t>(16, (M + 3) / 4);  // at most 128 CTAs
+  *R = (int)ceil_div(M, std::max<int64_t>(G, 1));
+  *S = (int)(4 * ceil_div(N1, 4 * kCluster));
+}
+size_t cluster_smem(int R, int S, int64_t K, int64_t N2) {
+  return ((size_t)(R + S) * (size_t)K + (size_t)R * S + (size_t)R * (size_t)N2) * sizeof(float) + 16;
+}
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(mbar)
+               : "memory");
+}
+
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kSWarps * 32) small_mlp_cluster_kernel(CParams p) {
+  namespace cg = cooperative_groups;
+  extern __shared__ __align__(16) unsigned char smc[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smc);
+  const int K = p.l1.K, R = p.R, S = p.S, N2 = p.l2.N;
+  float* xs = reinterpret_cast<float*>(smc + 16);  // [R][K]
+  float* ws = xs + (size_t)R * K;                   // [S][K]
+  float* hs = ws + (size_t)S * K;                   // [R][S]
+  float* zp = hs + (size_t)R * S;                   // [R][N2] partial layer-2 sums
+  cg::cluster_group cl = cg::this_cluster();
+  const int c = (int)cl.block_rank();
+  const int m0 = (blockIdx.x / kCluster) * R;
+  const int rows = max(0, min(R, p.M - m0));
+  const int j0 = c * S, cols = max(0, min(S, p.l1.N - j0));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(bar), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t bytes = (uint32_t)K * 4u;
+    mbar_expect_tx(smem_u32(bar), bytes * (uint32_t)(rows + cols));
+    for (int i = 0; i < rows; ++i)
+      bulk_g2s(smem_u32(xs + (size_t)i * K), p.a + (long long)(m0 + i) * p.lda, bytes, smem_u32(bar));
+    for (int i = 0; i < cols; ++i)
+      bulk_g2s(smem_u32(ws + (size_t)i * K), p.l1.w + (long long)(j0 + i) * p.l1.ldw, bytes, smem_u32(bar));
+  }
+  // a copy that never lands is reported and waited for once more, bounded
+  if (!mbar_wait(smem_u32(bar), 0u, p.err)) mbar_wait_own(smem_u32(bar), 0u, p.err);
+  if (rows > 0 && cols > 0) {
+    SLayer l1 = p.l1;
+    l1.w = ws;
+    l1.ldw = K;
+    l1.N = cols;
+    if (l1.bias) l1.bias += (long long)j0 * l1.bstride;
+    layer_tiles<true, 2, 2>(xs, K, rows, l1, hs, S, warp, kSWarps, lane);
+  }
+  __syncthreads();
+  // this CTA's share of layer 2: zp[m][n] = sum over its units j of h[m][j] * W2[n][j0 + j]
+  for (int i = threadIdx.x; i < rows * N2; i += blockDim.x) {
+    const int m = i / N2, n = i - m * N2;
+    const float* hr = hs + (size_t)m * S;
+    const float* wr = p.l2.w + (long long)n * p.l2.ldw + j0;
+    float acc = 0.f;
+    for (int j = 0; j < cols; j += 4) {
+      if (j + 4 <= cols) {
+        const float4 w4 = __ldg(reinterpret_cast<const float4*>(wr + j));
+        const float4 h4 = *reinterpret_cast<const float4*>(hr + j);
+        acc = fmaf(h4.x, w4.x, acc);
+        acc = fmaf(h4.y, w4.y, acc);
+        acc = fmaf(h4.z, w4.z, acc);
+        acc = fmaf(h4.w, w4.w, acc);
+      } else {
+        for (int jj = j; jj < cols; ++jj) acc = fmaf(hr[jj], __ldg(wr + jj), acc);
+      }
+    }
+    zp[i] = acc;
+  }
+  cl.sync();
+  const float alpha2 = p.l2.alpha_ptr ? *p.l2.alpha_ptr : p.l2.alpha;
+  for (int m = c + kCluster * warp; m < rows; m += kCluster * kSWarps) {
+    float z[kClusterMaxN2 / 32];
+#pragma unroll
+    for (int k = 0; k < kClusterMaxN2 / 32; ++k) {
+      const int n = lane + 32 * k;
+      z[k] = -__int_as_float(0x7f800000);
+      if (n < N2) {
+        float sum = 0.f;
+#pragma unroll
+        for (int r = 0; r < kCluster; ++r) sum += cl.map_shared_rank(zp, r)[(size_t)m * N2 + n];
+        float v = sum * alpha2;
+        if (p.l2.bias) v += p.l2.bias[(long long)n * p.l2.bstride];
+        z[k] = act_apply_rt(p.l2.act, v);
+      }
+    }
+    float* row = p.out + (long long)(m0 + m) * p.ldo;
+    if (!p.softmax) {
+#pragma unroll
+      for (int k = 0; k < kClusterMaxN2 / 32; ++k)
+        if (lane + 32 * k < N2) row[lane + 32 * k] = z[k];
+      continue;
+    }
+    float mx = -__int_as_float(0x7f800000);
+#pragma unroll
+    for (int k = 0; k < kClusterMaxN2 / 32; ++k)
+      if (lane + 32 * k < N2) mx = fmaxf(mx, z[k]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < kClusterMaxN2 / 32; ++k)
+      if (lane + 32 * k < N2) sum += expf(z[k] - mx);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    if (p.softmax == 1) {
+#pragma unroll
+      for (int k = 0; k < kClusterMaxN2 / 32; ++k)
+        if (lane + 32 * k < N2) row[lane + 32 * k] = expf(z[k] - mx) / sum;
+    } else {
+      const float ls = logf(sum);
+#pragma unroll
+      for (int k = 0; k < kClusterMaxN2 / 32; ++k)
+        if (lane + 32 * k < N2) row[lane + 32 * k] = z[k] - mx - ls;
+    }
+  }
+  cl.sync();  // the partials stay in shared memory until every CTA has read them
+}
+
 }  // namespace
+
+bool small_mlp_cluster_fits(int64_t M, int64_t N1, int64_t K1, int64_t N2) {
+  if (M < 1 || M > kSmallMaxRows || N1 < 1 || K1 < 4 || K1 % 4 != 0 || N2 < 1 || N2 > kClusterMaxN2) return false;
+  int R, S;
+  cluster_shape(M, N1, &R, &S);
+  return cluster_smem(R, S, K1, N2) <= kClusterSmemMax;
+}
 
 void launch_small_mlp(const SmallMlpLaunch& L, cudaStream_t stream) {
   PFB_CHECK_ARG(L.M > 0 && L.M <= kSmallMaxRows, "small GEMM: 1..256 rows");
@@ -363,7 +529,8 @@ void launch_small_mlp(const SmallMlpLaunch& L, cudaStream_t stream) {
   };
   layer(p.l1, L.w1, L.ldw1, L.bias1, L.bstride1, L.alpha1, L.alpha1_ptr, L.N1, L.K1, L.act1, L.a, L.lda);
   if (L.layers == 2) {
-    PFB_CHECK_ARG(L.w2 && L.h && L.counter && L.N2 > 0 && L.ldw2 >= L.N1 && L.ldh >= L.N1 && L.N2 < (1 << 20),
+    PFB_CHECK_ARG(L.w2 && (L.cluster || (L.h && L.counter && L.ldh >= L.N1)) && L.N2 > 0 && L.ldw2 >= L.N1 &&
+                      L.N2 < (1 << 20),
                   "small GEMM: bad layer-2 operands");
     layer(p.l2, L.w2, L.ldw2, L.bias2, L.bstride2, L.alpha2, L.alpha2_ptr, L.N2, L.N1, L.act2, L.h, L.ldh);
     p.h = L.h;
@@ -373,6 +540,33 @@ void launch_small_mlp(const SmallMlpLaunch& L, cudaStream_t stream) {
   } else {
     PFB_CHECK_ARG(L.softmax == 0, "small GEMM: a fused softmax needs two layers");
     PFB_CHECK_ARG(L.ldo >= L.N1, "small GEMM: output pitch below the row length");
+  }
+  if (L.cluster) {
+    PFB_CHECK_ARG(L.layers == 2 && small_mlp_cluster_fits(L.M, L.N1, L.K1, L.N2) && L.err && p.l1.vec &&
+                      L.ldw2 % 4 == 0 && aligned16(L.w2) && L.softmax >= 0 && L.softmax <= 2,
+                  "small MLP on clusters: unaligned rows or sizes past the shared-memory staging");
+    CParams c;
+    c.a = L.a;
+    c.lda = L.lda;
+    c.M = (int)L.M;
+    c.l1 = p.l1;
+    c.l2 = p.l2;
+    c.out = L.out;
+    c.ldo = L.ldo;
+    c.softmax = L.softmax;
+    c.err = L.err;
+    cluster_shape(L.M, L.N1, &c.R, &c.S);
+    const size_t smem = cluster_smem(c.R, c.S, L.K1, L.N2);
+    const int dev = current_device();
+    static std::once_flag attr_once[64];
+    std::call_once(attr_once[dev], [] {
+      PFB_CUDA(cudaFuncSetAttribute(small_mlp_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)kClusterSmemMax));
+    });
+    const unsigned clusters = (unsigned)ceil_div(L.M, (int64_t)c.R);
+    small_mlp_cluster_kernel<<<clusters * kCluster, kSWarps * 32, smem, stream>>>(c);
+    PFB_CUDA(cudaGetLastError());
+    return;
   }
   size_t smem = 0;
   if (L.layers == 2) {

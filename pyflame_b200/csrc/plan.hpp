@@ -132,6 +132,14 @@ struct GemmArgs {
   int x_hi = -1, x_lo = -1;
   int64_t H = 0, W = 0, Cp = 0, KH = 1, KW = 1, sh = 1, sw = 1, ph = 0, pw = 0, dh = 1, dw = 1, OH = 0, OW = 0;
   int64_t Nimg = 1, Hp = 0, Wp = 0, KWp = 0;
+  // A 3x3 / stride 2 max pool (padding pool_pad, 0 or 1) of the (ReLU)
+  // output, in the epilogue: pooled pool_y (channels-last; written when
+  // write_pool_y) and its operand copy (op_hi / op_lo at pool_y's offsets)
+  // replace c
+  bool pool = false;
+  int pool_pad = 0;
+  View pool_y;
+  bool write_pool_y = true;
 };
 
 struct PoolArgs {
@@ -192,6 +200,7 @@ struct SmallArgs {
   View out;
   int64_t ldo = 0;
   int softmax = 0;
+  bool cluster = false;  // two layers on clusters of 8 CTAs (no h or counter buffer)
 };
 
 struct Step {

@@ -283,22 +283,27 @@ def test_linear_relu_softmax_mlp(cuda_executor, oracle_mod):
     (g,), (r,) = run(cuda_executor, w.outputs, oracle_mod)
     close(g, r, rtol=1e-4, atol=1e-6, what="mlp softmax")
     plan = cuda_executor.describe_plan(w.outputs[0].graph(), [w.outputs[0].node().id()])
-    # Linear, ReLU, Linear and softmax in one launch (the arrival-counter reset is a memset)
-    assert "small mlp [64x256x784 -> 10] +softmax" in plan and "row kernel" not in plan, plan
+    # Linear, ReLU, Linear and softmax in one launch on clusters of 8 CTAs
+    assert "small mlp [64x256x784 -> 10] +softmax (clusters)" in plan and "row kernel" not in plan, plan
+    assert "arrival counter" not in plan, plan
 
 
 @pytest.mark.parametrize("m,k,n1,n2,act,soft", [(64, 784, 256, 10, "relu", "softmax"), (1, 7, 5, 3, "tanh", "log"),
                                                 (256, 130, 96, 70, "gelu", "softmax"), (33, 64, 48, 17, "sigmoid", ""),
                                                 (200, 64, 1000, 0, "", ""), (5, 12, 9, 0, "silu", ""),
                                                 (17, 301, 40, 9, "relu", "softmax"),
-                                                (256, 300, 200, 20, "gelu", "log")])
+                                                (256, 300, 200, 20, "gelu", "log"),
+                                                (48, 128, 300, 130, "relu", "softmax")])
 def test_small_batch_linear_layers(cuda_executor, oracle_mod, rng, m, k, n1, n2, act, soft):
     """Small batches of Linear layers run on the CUDA cores: one layer alone,
     or Linear -> activation -> Linear (-> softmax / log-softmax) as one
     launch; short rows (lane per column) and long rows (lanes split K), float4
     and scalar loads (K not a multiple of 4), layer 2 from shared memory or,
     when h and the weight do not fit there, from L2; softmax rows past 32;
-    single rows."""
+    single rows.  Two layers with K a multiple of 4 run on clusters of 8 CTAs
+    (a partial last row block, hidden units not a multiple of 32, rows of
+    130 outputs); the others on the single-launch kernel with its last-CTA
+    layer 2."""
     x = pf.tensor(rng.standard_normal((m, k)).astype(np.float32))
     with nn.deferred_init():
         l1 = nn.Linear(k, n1)
@@ -315,6 +320,7 @@ def test_small_batch_linear_layers(cuda_executor, oracle_mod, rng, m, k, n1, n2,
             y = (pf.softmax if soft == "softmax" else pf.log_softmax)(y, -1)
     plan = cuda_executor.describe_plan(y.graph(), [y.node().id()])
     assert ("small mlp" if n2 else "small gemm") in plan and "row kernel" not in plan, plan
+    assert ("(clusters)" in plan) == (n2 > 0 and k % 4 == 0), plan
     (g,), (r,) = run(cuda_executor, [y], oracle_mod)
     close_rows(g, r, RTOL_GEMM_TF32X3, what="small batch layers")
     # scaled product without a bias
@@ -423,6 +429,56 @@ def test_conv_bn_relu_pool_stack(cuda_executor, oracle_mod, rng):
         close(g2, r2, rtol=RTOL_GEMM_TF32X3, atol=RTOL_GEMM_TF32X3 * term_scale)
     close_rows(gpu[3].reshape(-1, gpu[3].shape[-1] * gpu[3].shape[-2]),
                ref[3].reshape(-1, ref[3].shape[-1] * ref[3].shape[-2]), RTOL_GEMM_TF32X3)
+
+
+@pytest.mark.parametrize("precision", ["tf32x3", "bf16"])
+@pytest.mark.parametrize("n,h,w,pad", [(2, 64, 70, 0), (2, 64, 70, 1), (1, 224, 224, 0), (1, 224, 224, 1),
+                                       (3, 150, 290, 0), (2, 151, 131, 1)])
+def test_conv_bn_relu_maxpool_fused(oracle_mod, rng, native, precision, n, h, w, pad):
+    """Conv2d(3 -> 64, 7x7 / 2) -> BatchNorm -> ReLU -> MaxPool2d(3, 2, pad)
+    with the pool in the convolution's epilogue: strips of 1-3 column tiles,
+    odd and even conv heights, runs of tiles that start inside a strip (the
+    carried row recomputed), and the pooled map read both as an output and as
+    the next convolution's operand.  Checked against the oracle and against
+    the same graph evaluated without the fusion (the conv output also an
+    output), which may differ only by the epilogue's rounding."""
+    ex = pf.CudaExecutor(pf.CudaExecutor.Config(precision=precision))
+    x = pf.tensor(rng.random((n, 3, h, w)).astype(np.float32))
+    conv = nn.Conv2d(3, 64, 7, 2, 3)
+    conv.set_parameter("weight", (rng.standard_normal((64, 3, 7, 7)) * np.sqrt(2 / 147)).astype(np.float32))
+    bn = nn.BatchNorm2d(64)
+    bn.eval()
+    params = {}
+    for name, lo, hi in [("weight", 0.5, 1.5), ("bias", -0.3, 0.3), ("running_mean", -0.3, 0.3),
+                         ("running_var", 0.5, 2.0)]:
+        params[name] = rng.uniform(lo, hi, 64).astype(np.float32)
+        bn.set_parameter(name, params[name])
+    c = conv(x)
+    r = pf.relu(bn(c))
+    pooled = nn.MaxPool2d(3, 2, pad)(r)
+    conv2 = nn.Conv2d(64, 64, 3, 1, 1)
+    conv2.set_parameter("weight", (rng.standard_normal((64, 64, 3, 3)) * np.sqrt(2 / 576)).astype(np.float32))
+    nxt = conv2(pooled)
+    g = pooled.graph()
+    plan = ex.describe_plan(g, [pooled.node().id(), nxt.node().id()])
+    assert "+max_pool2d" in plan and "] max_pool2d" not in plan, plan
+    gpu, ref = run(ex, [pooled, nxt], oracle_mod)
+    # unfused: the ReLU output is an output too, so the pool runs on its own
+    plan2 = ex.describe_plan(g, [pooled.node().id(), r.node().id()])
+    assert "+max_pool2d" not in plan2, plan2
+    res2 = ex.execute(g, [pooled.node().id(), r.node().id()])
+    assert res2.success, res2.error_message
+    unfused, conv_ref = res2.outputs[pooled.node().id()], oracle_mod.run(g, [c.node().id()])[c.node().id()]
+    tol = RTOL_GEMM_TF32X3 if precision == "tf32x3" else RTOL_GEMM_BF16
+    bn_scale = np.abs(params["weight"] / np.sqrt(params["running_var"].astype(np.float64) + 1e-5))
+    conv_rms = np.sqrt(np.mean(conv_ref.astype(np.float64) ** 2, axis=(2, 3)))
+    term = (conv_rms * bn_scale[None, :]).reshape(-1, 1)
+    flat = lambda a: a.reshape(-1, a.shape[-1] * a.shape[-2])
+    close(flat(gpu[0]), flat(ref[0]), rtol=tol, atol=tol * term, what="fused pool vs oracle")
+    np.testing.assert_allclose(flat(gpu[0]), flat(unfused), rtol=1e-6, atol=1e-6 * term.max(),
+                               err_msg="fused pool vs unfused")
+    close_rows(flat(gpu[1]), flat(ref[1]), tol if precision == "tf32x3" else 4 * tol, what="conv after the pool")
+    ex.close()
 
 
 def test_batchnorm_alone_and_pools(cuda_executor, oracle_mod, rng):
