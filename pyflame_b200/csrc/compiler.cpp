@@ -1686,7 +1686,7 @@ void Compiler::absorb_epilogues() {
 // kernel: the scores and probabilities never reach HBM.  This is the core of
 // PyFlame's MultiheadAttention::forward (attention.cpp).
 void Compiler::detect_attention() {
-  if (in_.precision != PFC_PRECISION_TF32X3) return;
+  if (in_.precision != PFC_PRECISION_TF32X3 && in_.precision != PFC_PRECISION_BF16) return;
   for (int c2 = 0; c2 < (int)chains_.size(); ++c2) {
     const GemmChain& ch2 = chains_[c2];
     if (cls_[ch2.mm] != Cls::GEMM || !ch2.absorbed.empty() || chain_of_.at(ch2.mm) != c2) continue;
@@ -1902,7 +1902,8 @@ void Compiler::lower_attention(int c2) {
   const int64_t M = q.shape[r - 2], d = q.shape[r - 1], L = kt.shape[r - 1], dv = v.shape[r - 1];
   if (kt.shape[r - 2] != d || v.shape[r - 2] != L) fail(PFC_ERR_GRAPH, "matmul: inner dimensions don't match");
   const int prec = in_.precision;
-  const int64_t kq = round_up(d, 32), kv = round_up(dv, 32);
+  const int64_t kal = prec == PFC_PRECISION_BF16 ? 64 : 32;  // 128-byte rows
+  const int64_t kq = round_up(d, kal), kv = round_up(dv, kal);
   // K as [batch..., L, d]: swap the last two dims of K^T (V is used as stored)
   View k = kt;
   std::swap(k.shape[r - 2], k.shape[r - 1]);

@@ -440,6 +440,7 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
     case StepKind::ATTENTION: {
       const AttnArgs& a = st.attn;
       AttnLaunch L;
+      L.precision = P.precision;
       L.batch = a.batch; L.M = a.M; L.L = a.L; L.d = a.d; L.kq = a.kq; L.kv = a.kv;
       L.q_hi = bufp(a.q_hi, 0);
       L.q_lo = (const float*)bufp(a.q_lo, 0);
@@ -458,8 +459,9 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
       L.c_sn = a.c.strides[r - 1];
       if (a.op_hi >= 0) {
         // operand buffers share the element offsets of c
-        L.o_hi = (float*)bufp(a.op_hi, a.c.offset * 4);
-        L.o_lo = (float*)bufp(a.op_lo, a.c.offset * 4);
+        const int64_t esz = P.precision == PFC_PRECISION_BF16 ? 2 : 4;
+        L.o_hi = (float*)bufp(a.op_hi, a.c.offset * esz);
+        L.o_lo = (float*)bufp(a.op_lo, a.c.offset * esz);
       }
       L.err = err_dev_;
       launch_attention(L, s);

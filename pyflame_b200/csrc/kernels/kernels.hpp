@@ -69,6 +69,7 @@ void launch_gemm(const GemmLaunch& L, cudaStream_t stream);
 // and PV GEMM that rocm_executor.cpp:278-335 and rocm_kernels.hip run as
 // separate passes for PyFlame's MultiheadAttention graphs.
 struct AttnLaunch {
+  int precision = 0;  // tf32x3 (hi/lo operands) or bf16 (q_hi, k_hi, v_hi, o_hi only; kq = kv = 64)
   int64_t batch = 0, M = 0, L = 0, d = 0, kq = 0, kv = 0;
   const void* q_hi = nullptr;
   const float* q_lo = nullptr;
@@ -81,7 +82,8 @@ struct AttnLaunch {
   // O of slice s = b*heads + h at c + b*c_sb + h*c_sh + m*c_sm + n*c_sn
   float* c = nullptr;  // may be null when only the operand is written
   int64_t heads = 1, c_sb = 0, c_sh = 0, c_sm = 0, c_sn = 1;
-  // O also as tf32 hi/lo at the same element offsets (or null)
+  // O also as the next GEMM's operand at the same element offsets (or null):
+  // tf32 hi/lo, or bf16 in o_hi
   float* o_hi = nullptr;
   float* o_lo = nullptr;
   int* err = nullptr;

@@ -532,6 +532,48 @@ def test_fused_attention(cuda_executor, oracle_mod, rng, b, h, m, l, d, scale):
     close_rows(g.reshape(-1, d), r.reshape(-1, d), RTOL_GEMM_TF32X3, what="attention")
 
 
+@pytest.mark.parametrize("b,h,m,l,d,scale", [(2, 3, 300, 200, 64, 0.125), (1, 2, 128, 512, 32, 1.0),
+                                             (3, 1, 50, 70, 40, 4.0)])
+def test_fused_attention_bf16(native, rng, b, h, m, l, d, scale):
+    """The bf16 mode's fused attention (bf16 Q, K, V and P, fp32 softmax and
+    accumulation), the same shapes as the tf32 test.  The reference is the
+    attention of the bf16-rounded Q, K and V in float64: rounding the inputs
+    alone moves a peaked softmax (scaled logits of spread 5-25 here) by a few
+    per cent, which is the mode's contract, not the kernel's error; against
+    it the kernel's own arithmetic (bf16 P, fp32 sums) is held to 1e-2."""
+    def bf16(x):
+        u = x.astype(np.float32).view(np.uint32).astype(np.uint64)
+        u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+        return u.astype(np.uint32).view(np.float32)
+    ex = pf.CudaExecutor(pf.CudaExecutor.Config(precision="bf16"))
+    qa, ka, va = (rng.standard_normal((b, h, n, d)).astype(np.float32) for n in (m, l, l))
+    q, k, v = pf.tensor(qa), pf.tensor(ka), pf.tensor(va)
+    out = pf.matmul(pf.softmax(pf.matmul(q, k.transpose(-2, -1)) * scale, -1), v)
+    assert "attention " in ex.describe_plan(out.graph(), [out.node().id()])
+    res = ex.execute(out.graph(), [out.node().id()])
+    assert res.success, res.error_message
+    g = res.outputs[out.node().id()]
+    qb, kb, vb = (bf16(a).astype(np.float64) for a in (qa, ka, va))
+    s64 = np.float64(np.float32(scale)) * (qb @ kb.swapaxes(-1, -2))
+    p64 = np.exp(s64 - s64.max(-1, keepdims=True))
+    r = (p64 / p64.sum(-1, keepdims=True)) @ vb
+    close_rows(g.reshape(-1, d), r.reshape(-1, d), 1e-2, what="bf16 attention")
+    ex.close()
+
+
+def test_encoder_block_bf16(oracle_mod, native):
+    """A whole encoder block in the bf16 mode: head-split bf16 projections,
+    the fused attention writing the out-projection's bf16 operand."""
+    from pyflame_b200 import workloads
+    ex = pf.CudaExecutor(pf.CudaExecutor.Config(precision="bf16"))
+    w = workloads.encoder(batch=2, seq=64, d=128, heads=2, ff=256)
+    plan = ex.describe_plan(w.outputs[0].graph(), w.output_ids())
+    assert "attention " in plan and "+operand" in plan, plan
+    (g,), (r,) = run(ex, w.outputs, oracle_mod)
+    close_rows(g, r, 2 * RTOL_GEMM_BF16, what="bf16 encoder")
+    ex.close()
+
+
 def test_encoder_block_small(cuda_executor, oracle_mod):
     from pyflame_b200 import workloads
     w = workloads.encoder(batch=2, seq=16, d=64, heads=4, ff=256)
