@@ -466,7 +466,7 @@ def measure_e2e(name, args, d: Dist, w, ex, shard, strong, weights):
     world = d.world
     key = BATCH_KEY[name]
     n_e2e = max(3, min(args.steps if args.steps is not None else 20, 20))
-    pinned_in = {iname: torch.from_numpy(np.ascontiguousarray(t.node().constant_data())).pin_memory()
+    pinned_in = {iname: torch.from_numpy(np.array(t.node().constant_data(), copy=True)).pin_memory()
                  for iname, t in w.inputs.items()}
     shared = []
     out_np = []
