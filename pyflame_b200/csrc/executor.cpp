@@ -119,6 +119,7 @@ cudaError_t CudaExecutor::release_constants() {
   for (auto& [k, pe] : plans_) {
     for (auto& gr : pe.graphs) note(cudaGraphExecDestroy(gr.second));
     if (pe.arena) note(pool_->deallocate(pe.arena, stream_));
+    if (pe.tail) note(pool_->deallocate(pe.tail, stream_));
     for (int k2 = 0; k2 < 2; ++k2)
       for (void* p : pe.slots[k2]) note(pool_->deallocate(p, stream_));
   }
@@ -295,6 +296,12 @@ CudaExecutor::PlanEntry& CudaExecutor::prepare(Graph& g, const std::vector<uint6
       }
     }
     if (pe.plan->arena_bytes) pe.arena = pool_->allocate(pe.plan->arena_bytes, stream_);
+    bool has_gemm = false;
+    for (const Step& st : pe.plan->steps) has_gemm = has_gemm || (st.kind == StepKind::GEMM && !st.gemm.conv);
+    if (has_gemm) {
+      pe.tail = pool_->allocate(tail_ws_bytes() + kTailCounters * sizeof(unsigned), stream_);
+      PFB_CUDA(cudaMemsetAsync((char*)pe.tail + tail_ws_bytes(), 0, kTailCounters * sizeof(unsigned), stream_));
+    }
     it = plans_.emplace(key, std::move(pe)).first;
   } else {
     // refresh the splat values seen by this call (the structure is unchanged)
@@ -492,6 +499,12 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
         L.r_sb = a.r_sb; L.r_sm = a.r_sm; L.r_sn = a.r_sn;
       }
       L.err = err_dev_;
+      if (pe.tail) {
+        L.tail_ws = (float*)pe.tail;
+        L.tail_ws_bytes = (int64_t)tail_ws_bytes();
+        L.tail_cnt = (unsigned*)((char*)pe.tail + tail_ws_bytes());
+        L.tail_cnt_len = kTailCounters;
+      }
       if (!a.write_c) L.c = nullptr;
       L.out_hi = bufp(a.op_hi, 0);
       L.out_lo = (float*)bufp(a.op_lo, 0);
@@ -696,6 +709,10 @@ void CudaExecutor::check_device_error(cudaStream_t s) {
   PFB_CUDA(cudaStreamSynchronize(s));
   if (h != 0) {
     PFB_CUDA(cudaMemsetAsync(err_dev_, 0, 4, s));
+    // a GEMM that stopped part-way may have left split-tail counters raised
+    for (auto& kv : plans_)
+      if (kv.second.tail)
+        PFB_CUDA(cudaMemsetAsync((char*)kv.second.tail + tail_ws_bytes(), 0, kTailCounters * sizeof(unsigned), s));
     PFB_CUDA(cudaStreamSynchronize(s));
     fail(h, "a device-side bounded wait expired (tensor-core pipeline did not make progress)");
   }

@@ -61,6 +61,10 @@ class CudaExecutor {
   struct PlanEntry {
     std::unique_ptr<Plan> plan;
     void* arena = nullptr;
+    // split-last-wave workspace of the plan's GEMMs (one 128 x 128 fp32 slot
+    // per SM, then kTailCounters zeroed counters); null without plain GEMMs.
+    // Like the arena, one execution of the plan at a time uses it.
+    void* tail = nullptr;
     std::vector<cudaKernel_t> kernels;  // per step (JIT steps)
     // captured CUDA graphs of the plan, one per set of buffer pointers (a
     // streamed call alternates between two sets); at most kGraphsPerPlan
@@ -104,6 +108,8 @@ class CudaExecutor {
   std::unique_ptr<CudaMemoryPool> pool_;
   int* err_dev_ = nullptr;
   int num_sms_ = 148;
+  static constexpr int kTailCounters = 1024;
+  size_t tail_ws_bytes() const { return (size_t)num_sms_ * 128 * 128 * sizeof(float); }
   std::mutex mu_;
   std::unordered_map<uint64_t, PlanEntry> plans_;
   std::map<std::pair<uint64_t, size_t>, Resident> resident_;

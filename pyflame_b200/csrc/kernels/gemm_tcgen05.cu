@@ -99,7 +99,40 @@ struct GemmParams {
   float* py;
   long long py_sn, py_sh, py_sw;
   int PH, PW, pool_pad;
+  // Split tail: the last partial wave's tail_r tiles (tail_first on) are each
+  // split along K into tail_s parts, part i taken by CTA i; the parts'
+  // accumulators meet in tail_ws (one 128 x BN slot per CTA), and the part
+  // that arrives last (tail_cnt, one counter per tile, left at 0) sums them in
+  // part order and runs the epilogue.  tail_s == 0: round-robin whole tiles.
+  int tail_s, tail_r, tail_first;
+  float* tail_ws;
+  unsigned* tail_cnt;
 };
+
+// Work item j of this CTA: a whole tile, or one part of a split tail tile
+// (part >= 0); k-blocks [k0, k1).  False past the CTA's last item.
+__device__ __forceinline__ bool work_at(const GemmParams& p, int ntiles, int t0, int ts, int j, int& tile, int& k0,
+                                        int& k1, int& part) {
+  part = -1;
+  k0 = 0;
+  k1 = p.nkb;
+  if (p.tail_s == 0) {
+    tile = t0 + j * ts;
+    return tile < ntiles;
+  }
+  const int nfull = (p.tail_first - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  if (j < nfull) {
+    tile = (int)blockIdx.x + j * (int)gridDim.x;
+    return true;
+  }
+  const int item = (int)blockIdx.x;
+  if (j > nfull || item >= p.tail_r * p.tail_s) return false;
+  tile = p.tail_first + item / p.tail_s;
+  part = item % p.tail_s;
+  k0 = part * p.nkb / p.tail_s;
+  k1 = (part + 1) * p.nkb / p.tail_s;
+  return true;
+}
 
 
 // Store one 32-row x 16-column block of a tile.  `ep` holds it row-major
@@ -394,14 +427,21 @@ __device__ __forceinline__ void run_epilogue(const GemmParams& p, uint32_t tmem,
   const float alpha = p.alpha_ptr ? *p.alpha_ptr : p.alpha;
   const float bsc = p.bias_scalar ? *p.bias_scalar : 0.f;
   const bool has_shift = p.scale || p.bias || p.bias_scalar;
+  __shared__ int s_last;  // a split tail tile: this CTA's part arrived last
   int u = 0;
   bool ok = true;
-  for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+  // With a split tail a warp whose wait failed keeps walking its items (no
+  // more waits) so that every warp meets the split tile's barriers, where
+  // all eight leave together; otherwise it leaves at once.
+  for (int wj = 0; ok || (!MAPPED && p.tail_s); ++wj) {
+    int t, k0, k1, part;
+    if (!work_at(p, ntiles, blockIdx.x, gridDim.x, wj, t, k0, k1, part)) break;
+    const int nch = k1 > k0 ? (k1 - k0 + p.kchunk - 1) / p.kchunk : 1;
     // this thread's row of the tile, columns col0..col0+HALF: the sum of the chunk accumulators
     float acc[HALF];
 #pragma unroll
     for (int j = 0; j < HALF; ++j) acc[j] = 0.f;
-    for (int ch = 0; ch < p.nchunks; ++ch, ++u) {
+    for (int ch = 0; ch < nch && ok; ++ch, ++u) {
       const int b = u & 1;
       const uint32_t use = (uint32_t)(u >> 1);
       // one outcome per warp: the TMEM loads below are warp-collective
@@ -435,7 +475,43 @@ __device__ __forceinline__ void run_epilogue(const GemmParams& p, uint32_t tmem,
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&acc_empty[b]));
     }
-    if (!ok) break;
+    if (!MAPPED && part >= 0) {
+      // a part of a split tail tile: its accumulator rows go to this CTA's
+      // slot; the part that arrives last sums all parts in part order
+      // (deterministic whichever CTA it is) and stores the tile
+      float* slot = p.tail_ws + (size_t)blockIdx.x * (kBM * BN) + (size_t)(q * 32 + lane) * BN + col0;
+#pragma unroll
+      for (int j = 0; j < HALF; j += 4)
+        *reinterpret_cast<float4*>(slot + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+      __threadfence();
+      if (epi_bar_any(!ok)) break;
+      if (e == 0 && lane == 0) {
+        const unsigned prev = atomicAdd(&p.tail_cnt[t - p.tail_first], 1u);
+        s_last = prev == (unsigned)(p.tail_s - 1);
+        if (s_last) p.tail_cnt[t - p.tail_first] = 0u;  // ready for the next launch
+      }
+      epi_bar();
+      if (!s_last) continue;
+      __threadfence();  // the other parts' slots, written before their arrivals
+      const int item0 = (t - p.tail_first) * p.tail_s;
+#pragma unroll
+      for (int j = 0; j < HALF; ++j) acc[j] = 0.f;
+      for (int s2 = 0; s2 < p.tail_s; ++s2) {
+        const float* src = p.tail_ws + (size_t)(item0 + s2) * (kBM * BN) + (size_t)(q * 32 + lane) * BN + col0;
+#pragma unroll
+        for (int j = 0; j < HALF; j += 4) {
+          const float4 v4 = __ldcg(reinterpret_cast<const float4*>(src + j));
+          acc[j] += v4.x;
+          acc[j + 1] += v4.y;
+          acc[j + 2] += v4.z;
+          acc[j + 3] += v4.w;
+        }
+      }
+    }
+    if (!ok) {
+      if (MAPPED || p.tail_s == 0) break;
+      continue;
+    }
     int bz, tm, tn;
     tile_coords(p, t, bz, tm, tn);
     const int n0 = tn * BN + col0;
@@ -753,12 +829,14 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
     // ---------------- TMA producer ----------------
     int g = 0;  // k-block counter across all tiles of this CTA
     bool ok = true;
-    for (int t = t0; t < t1 && ok; t += ts) {
+    for (int wj = 0; ok; ++wj) {
+      int t, k0, k1, part;
+      if (!work_at(p, t1, t0, ts, wj, t, k0, k1, part)) break;
       int bz, tm, tn;
       tile_coords(p, t, bz, tm, tn);
       const int ca = p.a_batched ? bz : 0, cb = p.b_batched ? bz : 0;
       const int m0 = tm * kBM, n0 = tn * BN;
-      for (int kb = 0; kb < nkb; ++kb, ++g) {
+      for (int kb = k0; kb < k1; ++kb, ++g) {
         const int s = g % C::STAGES;
         const uint32_t ph = (uint32_t)(g / C::STAGES) & 1u;
         if (g >= C::STAGES && !mbar_wait(smem_u32(&empty[s]), ph ^ 1u, p.err)) { ok = false; break; }
@@ -808,14 +886,17 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
     // long contractions (K = 16384) within fp32-reference accuracy.
     int g = 0, u = 0;  // k-blocks consumed; accumulator uses
     bool ok = true;
-    for (int t = t0; t < t1 && ok; t += ts) {
-      for (int ch = 0; ch < p.nchunks && ok; ++ch, ++u) {
+    for (int wj = 0; ok; ++wj) {
+      int t, k0, k1, part;
+      if (!work_at(p, t1, t0, ts, wj, t, k0, k1, part)) break;
+      const int nch = k1 > k0 ? (k1 - k0 + p.kchunk - 1) / p.kchunk : 1;
+      for (int ch = 0; ch < nch && ok; ++ch, ++u) {
         const int b = u & 1;
         const uint32_t use = (uint32_t)(u >> 1);
         if (u >= 2 && !mbar_wait(smem_u32(&acc_empty[b]), (use & 1u) ^ 1u, p.err)) { ok = false; break; }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t acc_t = tmem + (uint32_t)(b * C::ACC_COLS);
-        const int kb0 = ch * p.kchunk, kb1 = min(nkb, kb0 + p.kchunk);
+        const int kb0 = k0 + ch * p.kchunk, kb1 = min(k1, kb0 + p.kchunk);
         for (int kb = kb0; kb < kb1; ++kb, ++g) {
           const int s = g % C::STAGES;
           const uint32_t ph = (uint32_t)(g / C::STAGES) & 1u;
@@ -1304,6 +1385,25 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const 
   PFB_CHECK_ARG(ntiles < (1ll << 31), "gemm: too many tiles");
   // persistent: one CTA per SM (the shared-memory ring admits one), never more CTAs than tiles
   const unsigned grid = (unsigned)std::min<int64_t>(ntiles, device_sm_count(dev));
+  // Split tail: a last wave of r < grid tiles keeps r SMs busy for a whole
+  // tile while the rest idle; instead each of those tiles is split along K
+  // into s = grid / r parts, one per CTA.  Only where every part keeps at
+  // least 16 k-blocks (K >= 512 per part): shorter parts measured slower
+  // than the whole tile (768-deep GEMMs lost 15-20 us each, 3072-deep ones
+  // gained 24 us).  Plain GEMMs only (the convolution feeds walk their own
+  // schedules).
+  p.tail_s = p.tail_r = p.tail_first = 0;
+  p.tail_ws = L.tail_ws;
+  p.tail_cnt = L.tail_cnt;
+  if (!CONV && !conv_tma && !L.pool && L.tail_ws && L.tail_cnt && ntiles > grid) {
+    const int64_t r = ntiles % grid;
+    const int64_t sp = r > 0 ? std::min<int64_t>(grid / r, p.nkb / 16) : 0;
+    if (sp >= 2 && r <= L.tail_cnt_len && (int64_t)grid * kBM * BN * 4 <= L.tail_ws_bytes) {
+      p.tail_s = (int)sp;
+      p.tail_r = (int)r;
+      p.tail_first = (int)(ntiles - r);
+    }
+  }
   if constexpr (!CONV) {
     if (conv_tma == 3) {
       if constexpr (Cfg<PREC, BN, true>::CAT) {

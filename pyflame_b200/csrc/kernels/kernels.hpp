@@ -59,6 +59,14 @@ struct GemmLaunch {
   int pool_pad = 0;
   float* pool_y = nullptr;
   int64_t pool_sn = 0, pool_sh = 0, pool_sw = 0, PH = 0, PW = 0;
+  // Workspace for a split last wave (plain GEMMs): tail_ws_bytes of fp32
+  // slots (one 128 x BN tile per CTA) and tail_cnt_len counters that start
+  // at 0 and are left at 0.  Null: whole tiles only.  Launches sharing them
+  // must not run at the same time.
+  float* tail_ws = nullptr;
+  int64_t tail_ws_bytes = 0;
+  unsigned* tail_cnt = nullptr;
+  int64_t tail_cnt_len = 0;
 };
 void launch_gemm(const GemmLaunch& L, cudaStream_t stream);
 

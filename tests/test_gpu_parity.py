@@ -341,6 +341,22 @@ def test_gemm_epilogues(cuda_executor, oracle_mod, rng):
         close_rows(g, r, RTOL_GEMM_TF32X3)
 
 
+@pytest.mark.parametrize("m,n,k", [(1664, 1536, 2048), (1000, 1408, 1024)])
+def test_gemm_split_last_wave(cuda_executor, oracle_mod, rng, m, n, k):
+    """A partial last wave of long-K tiles is split along K over the idle
+    CTAs (13 x 12 = 156 tiles on 148 SMs: 8 tiles in 4 parts; 8 x 11 = 88
+    tiles fill one wave and stay whole), with a bias and GELU epilogue.  Two
+    calls in a row: the parts' arrival counters must be back at zero."""
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    lin = nn.Linear(k, n)
+    lin.set_parameter("weight", (rng.standard_normal((n, k)) / np.sqrt(k)).astype(np.float32))
+    lin.set_parameter("bias", rng.standard_normal(n).astype(np.float32))
+    out = pf.gelu(lin(pf.tensor(x)))
+    for _ in range(2):
+        (g,), (r,) = run(cuda_executor, [out], oracle_mod)
+        close_rows(g, r, RTOL_GEMM_TF32X3, what="split last wave")
+
+
 def test_gemm_bf16_mode(oracle_mod, rng, native):
     ex = pf.CudaExecutor(pf.CudaExecutor.Config(precision="bf16"))
     a = rng.standard_normal((200, 300)).astype(np.float32)
