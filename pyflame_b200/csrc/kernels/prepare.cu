@@ -265,14 +265,15 @@ __global__ void pool_kernel(PoolLaunch L) {
 // when every index fits in 32 bits.
 template <int PREC, typename IDX>
 __global__ void conv_input_kernel(ConvInputLaunch L) {
-  // output extent: the padded image when hp > 0 (zeros outside the input)
+  // output extent: the padded image when hp > 0 (zeros outside the input).
+  // One thread per output pixel, walking its Cp/4 channel groups: lanes take
+  // neighbouring pixels, so an NCHW source is read along its channel planes
+  // (coalesced) and each pixel's index arithmetic is paid once.
   const IDX C = (IDX)L.c, G = (IDX)(L.cp / 4), H = (IDX)L.h, W = (IDX)L.w;
   const IDX OHp = L.hp > 0 ? (IDX)L.hp : H, OWp = L.hp > 0 ? (IDX)L.wp : W;
   const IDX PH = L.hp > 0 ? (IDX)L.ph : 0, PW = L.hp > 0 ? (IDX)L.pw : 0;
-  const IDX total = (IDX)L.n * OHp * OWp * G;
-  for (IDX i = (IDX)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (IDX)gridDim.x * blockDim.x) {
-    const IDX g = i % G;
-    const IDX pix = i / G;
+  const IDX total = (IDX)L.n * OHp * OWp;
+  for (IDX pix = (IDX)blockIdx.x * blockDim.x + threadIdx.x; pix < total; pix += (IDX)gridDim.x * blockDim.x) {
     const IDX wq = pix % OWp;
     const IDX hn = pix / OWp;
     const IDX hq = hn % OHp;
@@ -280,26 +281,40 @@ __global__ void conv_input_kernel(ConvInputLaunch L) {
     const IDX h = hq - PH, w = wq - PW;
     const bool inside = h >= 0 && h < H && w >= 0 && w < W;
     const float* src = L.x + (long long)n * L.sn + (long long)h * L.sh + (long long)w * L.sw;
-    float x[4];
+    auto group = [&](IDX g, float (&x)[4]) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const IDX c = 4 * g + j;
-      x[j] = (inside && c < C) ? src[(long long)c * L.sc] : 0.f;
-    }
+      for (int j = 0; j < 4; ++j) {
+        const IDX c = 4 * g + j;
+        x[j] = (inside && c < C) ? src[(long long)c * L.sc] : 0.f;
+      }
+    };
     if constexpr (PREC == PFC_PRECISION_BF16) {
-      __nv_bfloat162 a = __floats2bfloat162_rn(x[0], x[1]), b = __floats2bfloat162_rn(x[2], x[3]);
-      uint2 pk;
-      pk.x = *(uint32_t*)&a;
-      pk.y = *(uint32_t*)&b;
-      *(uint2*)((__nv_bfloat16*)L.hi + 4 * i) = pk;
+      // pairs of groups as one 16-byte store (Cp is a multiple of 8 here)
+      for (IDX g = 0; g < G; g += 2) {
+        float x[4], y[4];
+        group(g, x);
+        group(g + 1, y);
+        const __nv_bfloat162 a = __floats2bfloat162_rn(x[0], x[1]), b = __floats2bfloat162_rn(x[2], x[3]);
+        const __nv_bfloat162 c = __floats2bfloat162_rn(y[0], y[1]), d = __floats2bfloat162_rn(y[2], y[3]);
+        uint4 pk;
+        pk.x = *(const uint32_t*)&a;
+        pk.y = *(const uint32_t*)&b;
+        pk.z = *(const uint32_t*)&c;
+        pk.w = *(const uint32_t*)&d;
+        *(uint4*)((__nv_bfloat16*)L.hi + 4 * (pix * G + g)) = pk;
+      }
     } else {
-      float4 hv, lv;
-      split_tf32(x[0], hv.x, lv.x);
-      split_tf32(x[1], hv.y, lv.y);
-      split_tf32(x[2], hv.z, lv.z);
-      split_tf32(x[3], hv.w, lv.w);
-      *(float4*)((float*)L.hi + 4 * i) = hv;
-      *(float4*)(L.lo + 4 * i) = lv;
+      for (IDX g = 0; g < G; ++g) {
+        float x[4];
+        group(g, x);
+        float4 hv, lv;
+        split_tf32(x[0], hv.x, lv.x);
+        split_tf32(x[1], hv.y, lv.y);
+        split_tf32(x[2], hv.z, lv.z);
+        split_tf32(x[3], hv.w, lv.w);
+        *(float4*)((float*)L.hi + 4 * (pix * G + g)) = hv;
+        *(float4*)(L.lo + 4 * (pix * G + g)) = lv;
+      }
     }
   }
 }
@@ -625,10 +640,11 @@ void launch_conv_input(const ConvInputLaunch& L, cudaStream_t stream) {
   PFB_CHECK_ARG(L.cp >= L.c && L.c > 0 && L.cp % 4 == 0, "conv input: padded channels must cover the channels");
   PFB_CHECK_ARG(((uintptr_t)L.hi & 15) == 0 && ((uintptr_t)L.lo & 15) == 0, "conv input: outputs must be 16-byte aligned");
   PFB_CHECK_ARG(L.hp == 0 || (L.hp >= L.h + L.ph && L.wp >= L.w + L.pw), "conv input: padded extent too small");
-  const long long total = L.n * (L.hp > 0 ? L.hp * L.wp : L.h * L.w) * (L.cp / 4);
+  PFB_CHECK_ARG(L.precision != PFC_PRECISION_BF16 || L.cp % 8 == 0, "conv input: bf16 channels come in groups of 8");
+  const long long total = L.n * (L.hp > 0 ? L.hp * L.wp : L.h * L.w);  // output pixels, one thread each
   if (total == 0) return;
   const unsigned g = grid_for(total, 256);
-  const bool small = total < (1ll << 30);  // i + grid stride stays below 2^31
+  const bool small = total * L.cp < (1ll << 30);  // element offsets and pixel + grid stride stay below 2^31
   if (L.precision == PFC_PRECISION_BF16) {
     if (small) conv_input_kernel<PFC_PRECISION_BF16, int><<<g, 256, 0, stream>>>(L);
     else conv_input_kernel<PFC_PRECISION_BF16, long long><<<g, 256, 0, stream>>>(L);
