@@ -2960,6 +2960,7 @@ void Compiler::emit_operands_at_producers() {
         if (G.has_residual) add(G.residual.buf, i);
         add(G.scale_buf, i); add(G.shift_buf, i); add(G.x_hi, i); add(G.x_lo, i);
         if (G.pool) add(G.pool_y.buf, i);
+        add(G.gap_buf, i);
         break;
       }
       case StepKind::POOL: add(st.pool.x.buf, i); add(st.pool.y.buf, i); break;
@@ -3130,6 +3131,62 @@ void Compiler::emit_operands_at_producers() {
     G.write_c = false;
     drop[i] = true;
     S[j].label += Pl.op_hi >= 0 ? " +max_pool2d +operand" : " +max_pool2d";
+    // A stride-2 stem whose filter rows are 8 taps of 16-byte pixels reads
+    // its padded input as row runs (even columns, then odd ones: a 1 KB run
+    // per input row and tile instead of overlapping windows) when nothing
+    // else reads the padded copy.
+    if (G.Cp * esz == 16 && kwp == 8 && G.sh == 2 && G.sw == 2 && G.dh == 1 && G.KH <= 7 && G.Wp % 2 == 0 &&
+        G.Wp / 2 >= G.OW + 3) {
+      for (int k = 0; k < j; ++k) {
+        if (drop[k] || S[k].kind != StepKind::CONV_INPUT || S[k].convin.out_hi != G.x_hi) continue;
+        ConvInputArgs& I = S[k].convin;
+        if (I.hp != G.Hp || I.wp != G.Wp || others_read(G.x_hi, k, j) || (G.x_lo >= 0 && others_read(G.x_lo, k, j)))
+          break;
+        I.deint = true;
+        G.deint = true;
+        S[k].label += " (de-interleaved rows)";
+        S[j].label += " (row runs)";
+        break;
+      }
+    }
+  }
+  // A convolution (no activation or ReLU) read only by AdaptiveAvgPool2d(1)
+  // whose A operand is fed by TMA boxes or windows (output tiles inside one
+  // image): the epilogue writes per-tile column sums instead of the output
+  // (774400 x 64 fp32 for the conv stack's last convolution), and the pool
+  // step adds each image's sums.
+  for (int i = 0; i < (int)S.size(); ++i) {
+    if (drop[i] || S[i].kind != StepKind::POOL) continue;
+    PoolArgs& Pl = S[i].pool;
+    if (Pl.mode != 2 || Pl.y.shape.size() != 4 || Pl.y.shape[2] != 1 || Pl.y.shape[3] != 1) continue;
+    const View& x = Pl.x;
+    if (x.is_splat || x.buf < 0) continue;
+    const int j = producer(x.buf);
+    if (j < 0 || j > i || drop[j] || S[j].kind != StepKind::GEMM) continue;
+    GemmArgs& G = S[j].gemm;
+    if (!G.conv || G.pool || G.gap_buf >= 0 || G.has_residual || G.batch != 1 || G.op_hi >= 0 || !G.write_c ||
+        G.OW < 32 || (G.act != 0 && G.act != 1))
+      continue;
+    if (x.offset != G.c.offset || x.shape != G.c.shape || x.strides != G.c.strides || others_read(x.buf, j, i)) continue;
+    // the feeds of launch_gemm's conv_tma_mode 1 and 2 (not the halo feed)
+    const int64_t esz = G.precision == PFC_PRECISION_BF16 ? 2 : 4, bk = 128 / esz;
+    const int64_t kwp = G.KWp > 0 ? G.KWp : G.KW;
+    const bool halo = G.Hp > 0 && G.sh == 1 && G.sw == 1 && G.Cp % bk == 0 && kwp == G.KW;
+    const bool boxes = G.Hp == 0 && G.Cp % bk == 0 && G.sh == 1 && G.sw == 1 && kwp == G.KW;
+    const bool windows = G.Hp > 0 && kwp * G.Cp == bk && G.dw == 1 && (G.sw * G.Cp * esz) % 16 == 0;
+    if (halo || !(boxes || windows)) continue;
+    const int64_t slots = conv_gap_slots(G.OH, G.OW);
+    G.gap_buf = new_buffer((size_t)(G.Nimg * slots * G.N) * 4);
+    G.write_c = false;
+    View pv;
+    pv.buf = G.gap_buf;
+    pv.shape = {G.Nimg, G.N, slots, 1};
+    pv.strides = {slots * G.N, 1, G.N, G.N};
+    Pl.x = pv;
+    Pl.mode = 3;
+    Pl.count = G.OH * G.OW;
+    S[j].label += " +average sums";
+    S[i].label = "adaptive_avg_pool2d (from the convolution's sums)";
   }
   std::vector<Step> kept;
   for (int i = 0; i < (int)S.size(); ++i)
@@ -3179,7 +3236,7 @@ void Compiler::finish() {
         use(G.a_hi, i); use(G.a_lo, i); use(G.b_hi, i); use(G.b_lo, i);
         if (G.write_c) use(G.c.buf, i);
         if (G.pool && G.write_pool_y) use(G.pool_y.buf, i);
-        use(G.op_hi, i); use(G.op_lo, i);
+        use(G.op_hi, i); use(G.op_lo, i); use(G.gap_buf, i);
         if (G.conv) { use(G.x_hi, i); use(G.x_lo, i); }
         if (G.has_bias) use(G.bias.buf, i);
         if (G.has_residual) use(G.residual.buf, i);

@@ -426,6 +426,7 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
       L.sn = a.x.strides[0]; L.sc = a.x.strides[1]; L.sh = a.x.strides[2]; L.sw = a.x.strides[3];
       L.cp = a.cp; L.precision = a.precision;
       L.hp = a.hp; L.wp = a.wp; L.ph = a.ph; L.pw = a.pw;
+      L.deint = a.deint;
       L.hi = bufp(a.out_hi, 0);
       L.lo = (float*)bufp(a.out_lo, 0);
       launch_conv_input(L, s);
@@ -518,6 +519,7 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
         L.H = a.H; L.W = a.W; L.Cp = a.Cp; L.KH = a.KH; L.KW = a.KW; L.sh = a.sh; L.sw = a.sw;
         L.ph = a.ph; L.pw = a.pw; L.dh = a.dh; L.dw = a.dw; L.OH = a.OH; L.OW = a.OW;
         L.batch_images = a.Nimg; L.Hp = a.Hp; L.Wp = a.Wp; L.KWp = a.KWp;
+        L.deint = a.deint;
         if (a.pool) {
           L.pool = true;
           L.pool_pad = a.pool_pad;
@@ -525,6 +527,10 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
           L.pool_y = a.write_pool_y ? (float*)viewp(a.pool_y) : nullptr;
           L.pool_sn = a.pool_y.strides[0]; L.pool_sh = a.pool_y.strides[2]; L.pool_sw = a.pool_y.strides[3];
           L.PH = a.pool_y.shape[2]; L.PW = a.pool_y.shape[3];
+        }
+        if (a.gap_buf >= 0) {
+          L.gap = (float*)bufp(a.gap_buf, 0);
+          L.c = nullptr;
         }
       }
       launch_gemm(L, s);
@@ -545,6 +551,7 @@ void CudaExecutor::launch_step(PlanEntry& pe, size_t i, const std::vector<void*>
       L.out_hi = bufp(a.op_hi, 0);
       L.out_lo = (float*)bufp(a.op_lo, 0);
       L.precision = P.precision;
+      L.count = a.count;
       launch_pool(L, s);
       break;
     }

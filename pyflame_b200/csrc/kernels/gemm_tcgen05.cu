@@ -99,6 +99,7 @@ struct GemmParams {
   float* py;
   long long py_sn, py_sh, py_sw;
   int PH, PW, pool_pad;
+  int pool_kw;  // pooled columns per tile: 31 (64-column windowed tiles) or 30 (row runs)
   // Split tail: the last partial wave's tail_r tiles (tail_first on) are each
   // split along K into tail_s parts, part i taken by CTA i; the parts'
   // accumulators meet in tail_ws (one 128 x BN slot per CTA), and the part
@@ -107,6 +108,10 @@ struct GemmParams {
   int tail_s, tail_r, tail_first;
   float* tail_ws;
   unsigned* tail_cnt;
+  // Global average pool of a TMA-fed convolution's output (tiles inside one
+  // image) replacing c: the column sums of lane quarter q of row tile tm go
+  // to gap[(tm*4 + q)*N + n], to be added up per image by a pool step.
+  float* gap;
 };
 
 // Work item j of this CTA: a whole tile, or one part of a split tail tile
@@ -370,10 +375,11 @@ __device__ __forceinline__ void conv_tile(const GemmParams& p, int tm, int& img,
 }
 
 // Tiles of a pool-fused convolution: strips of tiles_h tiles, one strip per
-// (image, column tile colt), u = (img*tiles_w + colt)*tiles_h + pos.  Tile
-// (a, colt) is conv rows 2a, 2a+1 and columns 62colt-pad .. 62colt-pad+63
-// (64 output pixels, TH = 2, TW = 64): pooled row a, columns 31colt ..
-// 31colt+30, with one more conv row carried from the tile walked before it
+// (image, column tile colt), u = (img*tiles_w + colt)*tiles_h + pos.  With
+// kw = pool_kw pooled columns per tile, tile (a, colt) is conv rows 2a, 2a+1
+// and columns 2kw*colt-pad .. +63 (64 output pixels, TH = 2, TW = 64, of
+// which the first 2kw+1 are used): pooled row a, columns kw*colt ..
+// kw*colt+kw-1, with one more conv row carried from the tile walked before it
 // in the strip.  Padding 1: row 2a-1, walking top-down (a = pos); padding 0:
 // row 2a+2, walking bottom-up (a = tiles_h-1-pos).  The first tile of a strip
 // carries a padding row.  pos is returned for that test.
@@ -385,7 +391,7 @@ __device__ __forceinline__ void pool_tile(const GemmParams& p, int u, int& img, 
   colt = strip - img * p.tiles_w;
   a = p.pool_pad ? pos : p.tiles_h - 1 - pos;
   oh0 = 2 * a;
-  ow0 = 62 * colt - p.pool_pad;
+  ow0 = 2 * p.pool_kw * colt - p.pool_pad;
 }
 
 // The CTA's run of consecutive tiles [own0, u1), so that each tile's carry
@@ -411,12 +417,54 @@ __device__ __forceinline__ bool epi_bar_any(bool v) {
 }
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory"); }
 
+// Column sums of v = act(acc*sc[n] + sh[n]) over this warp's first nvalid
+// rows (lane = row) for columns n0 .. n0+HALF, written to slot[n]: each
+// 32-column block is reduced across the lanes by halving exchanges (31
+// shuffles, a fixed order), after which lane l holds column l's sum.
+template <int ACT, int HALF>
+__device__ __forceinline__ void gap_block(const GemmParams& p, const float (&acc)[HALF], int n0, int nvalid,
+                                          float alpha, float bsc, bool has_shift, int lane, float* slot) {
+#pragma unroll
+  for (int cc = 0; cc < HALF; cc += 32) {
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = n0 + cc + j;
+      float sc = alpha, sh = bsc;
+      if (n < p.N) {
+        if (p.scale) {
+          sc = p.scale[n];
+          sh = p.shift[n];
+        } else if (p.bias) {
+          sh = p.bias[n];
+        }
+      }
+      float x = acc[cc + j] * sc;
+      if (has_shift) x = x + sh;
+      x = act_apply<ACT>(x);
+      v[j] = lane < nvalid ? x : 0.f;  // a select: rows outside the image add nothing, NaN included
+    }
+#pragma unroll
+    for (int w = 16; w >= 1; w >>= 1) {
+      const bool up = (lane & w) != 0;
+#pragma unroll
+      for (int j = 0; j < w; ++j) {
+        const float send = up ? v[j] : v[j + w];
+        const float keep = up ? v[j + w] : v[j];
+        v[j] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+      }
+    }
+    if (n0 + cc + lane < p.N) slot[n0 + cc + lane] = v[0];
+  }
+}
+
 // Epilogue warp e (0..7) on TMEM lane quarter q: for every tile this CTA
 // owns, sum the chunk accumulators in registers (handing each accumulator
 // back to the MMA warp at once), then apply alpha/bias/folded-BN/activation/
 // residual and store 32 x 16 blocks through this warp's staging area ep.
-// rows(tm, m_base, nvalid) names the warp's 32 output rows.
-template <int PREC, int BN, bool CAT, bool MAPPED, class Rows>
+// rows(tm, m_base, nvalid) names the warp's 32 output rows.  GAP: column
+// sums into GemmParams::gap instead of stores (activation 0 or 1 only).
+template <int PREC, int BN, bool CAT, bool MAPPED, bool GAP, class Rows>
 __device__ __forceinline__ void run_epilogue(const GemmParams& p, uint32_t tmem, uint64_t* acc_full,
                                              uint64_t* acc_empty, float* ep, int e, int q, int lane, Rows rows) {
   using C = Cfg<PREC, BN, CAT>;
@@ -519,30 +567,37 @@ __device__ __forceinline__ void run_epilogue(const GemmParams& p, uint32_t tmem,
     long long m_base;
     int nvalid;
     rows(tm, m_base, nvalid);
-    float* cbase = p.c ? p.c + (long long)bz * p.c_sb : nullptr;
-    const float* rbase = p.res ? p.res + (long long)bz * p.r_sb : nullptr;
-    const long long obatch = (long long)bz * p.M * p.o_sm;
-    void* ohi = p.o_hi ? (void*)((char*)p.o_hi + obatch * C::ESZ) : nullptr;
-    float* olo = p.o_lo ? p.o_lo + obatch : nullptr;
-    // float4 stores need contiguous, 16-byte aligned rows of the output (and residual)
-    const bool vec_c = !cbase || (p.c_sn == 1 && (p.c_sm & 3) == 0 && (((uintptr_t)cbase) & 15) == 0);
-    const bool vec_r = rbase && p.r_sn == 1 && (p.r_sm & 3) == 0 && (((uintptr_t)rbase) & 15) == 0;
+    if constexpr (GAP) {
+      float* slot = p.gap + ((long long)tm * 4 + q) * p.N;
+      if (p.act == 1) gap_block<1, HALF>(p, acc, n0, nvalid, alpha, bsc, has_shift, lane, slot);
+      else gap_block<0, HALF>(p, acc, n0, nvalid, alpha, bsc, has_shift, lane, slot);
+      continue;
+    } else {
+      float* cbase = p.c ? p.c + (long long)bz * p.c_sb : nullptr;
+      const float* rbase = p.res ? p.res + (long long)bz * p.r_sb : nullptr;
+      const long long obatch = (long long)bz * p.M * p.o_sm;
+      void* ohi = p.o_hi ? (void*)((char*)p.o_hi + obatch * C::ESZ) : nullptr;
+      float* olo = p.o_lo ? p.o_lo + obatch : nullptr;
+      // float4 stores need contiguous, 16-byte aligned rows of the output (and residual)
+      const bool vec_c = !cbase || (p.c_sn == 1 && (p.c_sm & 3) == 0 && (((uintptr_t)cbase) & 15) == 0);
+      const bool vec_r = rbase && p.r_sn == 1 && (p.r_sm & 3) == 0 && (((uintptr_t)rbase) & 15) == 0;
 #pragma unroll
-    for (int cc = 0; cc < HALF; cc += 16) {
-      // transpose through shared memory: this lane's row in, 8 rows x 16 columns out per pass
+      for (int cc = 0; cc < HALF; cc += 16) {
+        // transpose through shared memory: this lane's row in, 8 rows x 16 columns out per pass
 #pragma unroll
-      for (int j = 0; j < 16; j += 4)
-        *reinterpret_cast<float4*>(ep + lane * 20 + j) = make_float4(acc[cc + j], acc[cc + j + 1], acc[cc + j + 2], acc[cc + j + 3]);
-      __syncwarp();
-      switch (p.act) {
-        case 1: store_block<1, PREC, MAPPED>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-        case 2: store_block<2, PREC, MAPPED>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-        case 3: store_block<3, PREC, MAPPED>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-        case 4: store_block<4, PREC, MAPPED>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-        case 5: store_block<5, PREC, MAPPED>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
-        default: store_block<0, PREC, MAPPED>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+        for (int j = 0; j < 16; j += 4)
+          *reinterpret_cast<float4*>(ep + lane * 20 + j) = make_float4(acc[cc + j], acc[cc + j + 1], acc[cc + j + 2], acc[cc + j + 3]);
+        __syncwarp();
+        switch (p.act) {
+          case 1: store_block<1, PREC, MAPPED>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          case 2: store_block<2, PREC, MAPPED>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          case 3: store_block<3, PREC, MAPPED>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          case 4: store_block<4, PREC, MAPPED>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          case 5: store_block<5, PREC, MAPPED>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+          default: store_block<0, PREC, MAPPED>(p, ep, m_base, nvalid, n0 + cc, cbase, rbase, ohi, olo, vec_c, vec_r, alpha, bsc, has_shift, lane); break;
+        }
+        __syncwarp();
       }
-      __syncwarp();
     }
   }
 }
@@ -564,18 +619,25 @@ __device__ __forceinline__ void run_epilogue(const GemmParams& p, uint32_t tmem,
 //      of the one window that spans two warps (columns 30..32) go to shared
 //      memory; barrier.
 //   3. Row ro combines the carry, its own and row rc's maxima into pooled row
-//      a and stores it as fp32 and / or the next convolution's operand.
+//      a and stores it as fp32 and / or the next convolution's operand; the
+//      spanning window (pooled column 15) is finished by one warp with a
+//      channel per lane.
 // The eight epilogue warps meet at two named barriers per tile, so every
 // warp takes every tile; a failed wait is agreed on at the first barrier.
-template <int PREC, int BN>
+// Scale and shift are staged per channel in shared memory once.  (Clock
+// counters in a copy built outside the product put the epilogue, not the
+// MMAs, on the critical path of the 7-k-block stem: 3.3K cycles per tile
+// computing v with the scale and shift read from global memory, 2.9K in a
+// single lane finishing column 15, against 4.8K cycles of MMA issue.)
+template <int PREC, int BN, bool CAT>
 __device__ __forceinline__ void run_pool_epilogue(const GemmParams& p, uint32_t tmem, uint64_t* acc_full,
                                                   uint64_t* acc_empty, float* sm, int e, int q, int lane, int u0,
                                                   int u1, int own0) {
-  using C = Cfg<PREC, BN, false>;
+  using C = Cfg<PREC, BN, CAT>;
   static_assert(BN == 64, "the pooled epilogue takes 64-channel tiles");
-  static_assert((2 * 64 * 32 + 4 * 64) * 4 <= C::EPI_BYTES, "pool buffers exceed the epilogue staging area");
+  static_assert((2 * 64 * 32 + 4 * 64 + 2 * 64) * 4 <= C::EPI_BYTES, "pool buffers exceed the epilogue staging area");
   constexpr int HALF = BN / 2;
-  constexpr int KW = 31;  // pooled columns per tile
+  const int KW = p.pool_kw;  // pooled columns per tile (30 or 31; column 15 spans the warps)
   const int col0 = (e >> 2) * HALF;
   const int r = q >> 1, x = (q & 1) * 32 + lane, kq = x >> 1;
   const int rc = p.pool_pad ? 1 : 0, ro = 1 - rc;
@@ -584,8 +646,9 @@ __device__ __forceinline__ void run_pool_epilogue(const GemmParams& p, uint32_t 
   // (no bank conflicts beside the tensor core's operand reads)
   float* rowbuf = sm;
   float* bnd = sm + 2 * 64 * 32;  // [4][64]: row ro column 32, row rc columns 30, 31, 32
-  // the lanes that hold the pixels of the spanning window (columns 30..32)
-  const bool span = q == 2 * ro && lane == 30;  // finishes pooled column 15
+  float2* scsh = reinterpret_cast<float2*>(sm + 2 * 64 * 32 + 4 * 64);  // [64] (scale, shift) per channel
+  // warp q = 2ro finishes pooled column 15 (conv columns 30..32 span two warps)
+  const bool span = q == 2 * ro;
   const int bslot = q == 2 * ro + 1 && lane == 0 ? 0
                     : q == 2 * rc && lane == 30  ? 1
                     : q == 2 * rc && lane == 31  ? 2
@@ -594,6 +657,21 @@ __device__ __forceinline__ void run_pool_epilogue(const GemmParams& p, uint32_t 
   const float alpha = p.alpha_ptr ? *p.alpha_ptr : p.alpha;
   const float bsc = p.bias_scalar ? *p.bias_scalar : 0.f;
   const bool has_shift = p.scale || p.bias || p.bias_scalar;
+  {
+    // per-channel scale and shift once, in shared memory (visible after the
+    // first tile's barrier): every tile reads them with broadcast loads
+    const int i = e * 32 + lane;
+    if (i < 64) {
+      float sc = alpha, sh = bsc;
+      if (p.scale) {
+        sc = p.scale[i];
+        sh = p.shift[i];
+      } else if (p.bias) {
+        sh = p.bias[i];
+      }
+      scsh[i] = make_float2(sc, sh);
+    }
+  }
   int u = 0;
   bool ok = true;
   for (int t = u0; t < u1; ++t) {
@@ -609,9 +687,19 @@ __device__ __forceinline__ void run_pool_epilogue(const GemmParams& p, uint32_t 
       const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * C::ACC_COLS + col0);
       tmem_ld16_nowait(ta, *reinterpret_cast<uint32_t(*)[16]>(&rr[0]));
       tmem_ld16_nowait(ta + 16, *reinterpret_cast<uint32_t(*)[16]>(&rr[16]));
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      if constexpr (C::CAT) {
+        // the A_hi x B_lo half of a concatenated accumulator
+        uint32_t r2[32];
+        tmem_ld16_nowait(ta + BN, *reinterpret_cast<uint32_t(*)[16]>(&r2[0]));
+        tmem_ld16_nowait(ta + BN + 16, *reinterpret_cast<uint32_t(*)[16]>(&r2[16]));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-      for (int j = 0; j < 32; ++j) acc[j] += __uint_as_float(rr[j]);
+        for (int j = 0; j < 32; ++j) acc[j] += __uint_as_float(rr[j]) + __uint_as_float(r2[j]);
+      } else {
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[j] += __uint_as_float(rr[j]);
+      }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&acc_empty[b]));
@@ -622,16 +710,14 @@ __device__ __forceinline__ void run_pool_epilogue(const GemmParams& p, uint32_t 
     int img, oh0, ow0, a, colt, pos;
     pool_tile(p, t, img, oh0, ow0, a, colt, pos);
     const int oh = oh0 + r, ow = ow0 + x;
-    const bool real = oh < p.OH && ow >= 0 && ow < p.OW;
+    // (tile columns past 2KW feed no window: row runs leave them unloaded)
+    const bool real = oh < p.OH && ow >= 0 && ow < p.OW && x <= 2 * KW;
     float v[HALF], hm[HALF];
 #pragma unroll
     for (int j = 0; j < HALF; ++j) {
-      const int n = col0 + j;
-      float sc = alpha, sh = bsc;
-      if (p.scale) { sc = p.scale[n]; sh = p.shift[n]; }
-      else if (p.bias) sh = p.bias[n];
-      float w = acc[j] * sc;
-      if (has_shift) w = w + sh;
+      const float2 ss = scsh[col0 + j];
+      float w = acc[j] * ss.x;
+      if (has_shift) w = w + ss.y;
       w = act_apply<1>(w);
       v[j] = real ? w : 0.f;
     }
@@ -654,23 +740,35 @@ __device__ __forceinline__ void run_pool_epilogue(const GemmParams& p, uint32_t 
     }
     epi_bar();
     if (span) {
-      // row rc's window of column 15 (its next carry) and row ro's, finished here
+      // pooled column 15 with one channel per lane (n = col0 + lane): row
+      // rc's window (its next carry) from the boundary pixels, row ro's from
+      // lane 30's maxima of columns 30, 31 and the other warp's column 32
+      const int n = col0 + lane;
+      const float h1 = fmaxf(bnd[64 + n], fmaxf(bnd[128 + n], bnd[192 + n]));
+      next[lane * 32 + 15] = h1;
+      float m30 = 0.f;
 #pragma unroll
       for (int j = 0; j < HALF; ++j) {
-        const int n = col0 + j;
-        const float h1 = fmaxf(bnd[64 + n], fmaxf(bnd[128 + n], bnd[192 + n]));
-        next[j * 32 + 15] = h1;
-        hm[j] = fmaxf(fmaxf(hm[j], bnd[n]), h1);
+        const float y = __shfl_sync(0xffffffffu, hm[j], 30);
+        if (lane == j) m30 = y;
+      }
+      const int pw = KW * colt + 15;
+      if (t >= own0 && 15 < KW && pw < p.PW && a < p.PH) {
+        const float c = pos == 0 ? 0.f : carry[lane * 32 + 15];
+        const float o = fmaxf(c, fmaxf(fmaxf(m30, bnd[n]), h1));
+        const long long off = (long long)img * p.py_sn + (long long)a * p.py_sh + (long long)pw * p.py_sw + n;
+        if (p.py) p.py[off] = o;
+        if (p.o_hi) store_operand1<PREC>(p.o_hi, p.o_lo, off, o);
       }
     }
     // the tile recomputed before a run only feeds the carry
-    if (r == ro && (lane & 1) == 0 && kq < KW && t >= own0) {
+    if (r == ro && (lane & 1) == 0 && kq < KW && !(span && kq == 15) && t >= own0) {
       const int pw = KW * colt + kq;
       if (pw < p.PW && a < p.PH) {
         float o[HALF];
 #pragma unroll
         for (int j = 0; j < HALF; ++j) {
-          const float h1 = span ? 0.f : next[j * 32 + kq];
+          const float h1 = next[j * 32 + kq];
           const float c = pos == 0 ? 0.f : carry[j * 32 + kq];  // a strip's first tile carries padding
           o[j] = fmaxf(c, fmaxf(hm[j], h1));
         }
@@ -692,17 +790,24 @@ __device__ __forceinline__ void run_pool_epilogue(const GemmParams& p, uint32_t 
   }
 }
 
+// Epilogue forms of gemm_kernel (separate instantiations, so that each
+// carries only its own code): stores; a 3x3 / stride 2 max pool; the column
+// sums of a global average pool.
+constexpr int kEpiStore = 0, kEpiMaxPool = 1, kEpiAvg = 2;
+
 // Persistent kernel: each CTA walks tiles blockIdx.x, +gridDim.x, ...
 // CONV: the A operand is gathered by four producer warps from a channels-last
-// input (implicit-GEMM Conv2d) instead of loaded by TMA.  POOL: a windowed
-// TMA convolution (conv_tma 2) with the max pool fused into its epilogue;
-// each CTA walks a run of consecutive tiles (pool_run).
-template <int PREC, int BN, bool CONV, bool CAT, bool POOL = false>
+// input (implicit-GEMM Conv2d) instead of loaded by TMA.  EPI kEpiMaxPool: a
+// windowed TMA convolution (conv_tma 2) with the max pool fused into its
+// epilogue; each CTA walks a run of consecutive tiles (pool_run).  kEpiAvg:
+// a TMA-fed convolution whose epilogue writes column sums (GemmParams::gap).
+template <int PREC, int BN, bool CONV, bool CAT, int EPI = kEpiStore>
 __global__ void __launch_bounds__(kThreads<CONV>, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
                 const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
                 const GemmParams p) {
   using C = Cfg<PREC, BN, CAT>;
+  constexpr bool POOL = EPI == kEpiMaxPool;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   float* epi = (float*)(smem + C::STAGES * C::STAGE);
@@ -933,9 +1038,10 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
     // ---------------- epilogue ----------------
     const int e = warp - PW - 1;  // 0..7
     if constexpr (POOL) {
-      run_pool_epilogue<PREC, BN>(p, tmem, acc_full, acc_empty, epi, e, warp & 3, lane, t0, t1, own0);
+      run_pool_epilogue<PREC, BN, CAT>(p, tmem, acc_full, acc_empty, epi, e, warp & 3, lane, t0, t1, own0);
     } else
-    run_epilogue<PREC, BN, CAT, false>(p, tmem, acc_full, acc_empty, epi + e * C::EPI_WARP_FLOATS, e, warp & 3, lane,
+    run_epilogue<PREC, BN, CAT, false, EPI == kEpiAvg>(p, tmem, acc_full, acc_empty, epi + e * C::EPI_WARP_FLOATS, e,
+                                                   warp & 3, lane,
                                   [&](int tm, long long& m_base, int& nvalid) {
                                     const int q = warp & 3;
                                     if (p.conv_tma) {
@@ -952,6 +1058,195 @@ __global__ void __launch_bounds__(kThreads<CONV>, 1)
                                   });
   }
   // teardown: wait until every MMA of this CTA retired, then release TMEM
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == PW) {
+    if (lane == 0) mbar_wait_own(smem_u32(done), 0u, p.err);
+    __syncwarp();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)C::TMEM_COLS));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// The pooled stem over row runs.
+//
+// A stride-2 convolution whose filter row is one k-block of 8 taps of
+// 16-byte pixels (tf32: 4 channels, bf16: 8), over a zero-padded input whose
+// rows hold their even columns first, then their odd columns ([N][Hp][2]
+// [Wp/2][16 bytes], ConvInputLaunch::deint).  At stride 2, taps 2i and 2i+1
+// of output column ow read even and odd column ow + i: so the 64 output
+// columns of a tile read, from each padded input row, a run of 64 even and a
+// run of 64 odd pixels (1 KB each), and the A operand of k-step i is that
+// pair of runs entered i pixels later.  That is a K-major operand without
+// swizzle: 8 pixels x 16 bytes per core matrix (rows 16 bytes apart, 8-row
+// groups 128 bytes apart), the odd run LBO bytes after the even one.
+// The tile's conv rows oh and oh+1 read padded rows 2oh + kh and 2oh + kh + 2.
+// Its KH + 2 input rows are stored in the order 0, 2, 4, .., 1, 3, .., 1 KB
+// apart, so row 2oh+kh+2 directly follows row 2oh+kh and MMA rows 64..127
+// (conv row oh+1) continue rows 0..63 (conv row oh) with the same group
+// stride.  Output columns 61..63 of each conv row read into the following
+// run and feed no pooled window: a tile covers 61 columns, 30 pooled ones.
+// Per tile the input crosses L2 once (36 KB for tf32x3, against 7 x 32 KB of
+// overlapping TMA windows), and the filter stays in shared memory.
+// Warps: 0 loads the filter once, then each tile's runs (1-D bulk copies)
+// into NA buffers; 1 issues the MMAs; 2..9 run the pooled epilogue.
+template <int PREC, bool CAT>
+struct RowsCfg {
+  using G = Cfg<PREC, 64, CAT>;
+  static constexpr int RUN = 64 * 16;                // one run: 64 pixels of 16 bytes
+  static constexpr int MAXKH = 7;
+  static constexpr int SLOTS = MAXKH + 2;            // input rows per tile
+  static constexpr int A_OP = 2 * SLOTS * RUN;       // per operand: even runs, then odd runs
+  static constexpr int A_BUF = G::NOPS * A_OP;
+  static constexpr int B_KB = G::NOPS * G::B_TILE;   // one filter row, [B_hi | B_lo]
+  static constexpr int B_BYTES = MAXKH * B_KB;
+  static constexpr int NA_FIT = (G::SMEM_LIMIT - 1024 - B_BYTES - G::EPI_BYTES - 2048) / A_BUF;
+  static constexpr int NA = NA_FIT > 4 ? 4 : NA_FIT;
+  static constexpr int SMEM = B_BYTES + NA * A_BUF + G::EPI_BYTES + 1024 /*barriers*/ + 1024 /*align*/;
+  static_assert(NA >= 2, "shared memory too small for two run buffers");
+  static_assert(G::KSTEPS == 4, "a k-block is 8 taps of 16-byte pixels");
+};
+
+template <int PREC, bool CAT>
+__global__ void __launch_bounds__(kThreads<false>, 1)
+    conv_rows_pool_kernel(const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
+                          const GemmParams p) {
+  using C = Cfg<PREC, 64, CAT>;
+  using R = RowsCfg<PREC, CAT>;
+  constexpr int NA = R::NA;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* bres = smem;                              // [KH][B_hi | B_lo]
+  uint8_t* abuf = smem + R::B_BYTES;                 // [NA][NOPS][even runs | odd runs]
+  float* epi = (float*)(abuf + NA * R::A_BUF);
+  uint64_t* bfull = (uint64_t*)((uint8_t*)epi + C::EPI_BYTES);  // filter landed
+  uint64_t* afull = bfull + 1;                                  // [NA] runs landed
+  uint64_t* aempty = afull + NA;                                // [NA] runs consumed
+  uint64_t* acc_full = aempty + NA;                             // [2] MMA -> epilogue
+  uint64_t* acc_empty = acc_full + 2;                           // [2] epilogue -> MMA
+  uint64_t* done = acc_empty + 2;                               // all MMAs retired
+  uint32_t* tmem_slot = (uint32_t*)(done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ int s_stop;
+  if (threadIdx.x == 0) s_stop = *(volatile int*)p.err;
+  __syncthreads();
+  if (s_stop != 0) return;
+
+  constexpr int PW = 1;  // MMA warp
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(bfull), 1);
+    for (int s = 0; s < NA; ++s) {
+      mbar_init(smem_u32(&afull[s]), 1);
+      mbar_init(smem_u32(&aempty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&acc_full[b]), 1);
+      mbar_init(smem_u32(&acc_empty[b]), kEpiWarps);
+    }
+    mbar_init(smem_u32(done), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == PW) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"((uint32_t)C::TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  int u0, u1, own0;
+  pool_run(p, p.num_m, u0, u1, own0);
+  const int KH = p.KH, nev = (KH + 3) / 2;  // input rows 0..KH+1; nev of them even
+  if (warp == 0 && lane == 0) {
+    // ---------------- producer: the filter once, then each tile's runs ----------------
+    const uint32_t bb = smem_u32(bfull);
+    mbar_expect_tx(bb, (uint32_t)(KH * R::B_KB));
+    for (int kh = 0; kh < KH; ++kh) {
+      tma_load_3d(smem_u32(bres + kh * R::B_KB), &tb_hi, bb, kh * C::BK, 0, 0);
+      if constexpr (C::NOPS == 2) tma_load_3d(smem_u32(bres + kh * R::B_KB + C::B_TILE), &tb_lo, bb, kh * C::BK, 0, 0);
+    }
+    const int half = p.Wp / 2;  // pixels per run of a padded row
+    const uint8_t* xh = (const uint8_t*)p.x_hi;
+    const uint8_t* xl = (const uint8_t*)p.x_lo;
+    int g = 0;
+    for (int t = u0; t < u1; ++t, ++g) {
+      const int s = g % NA;
+      const uint32_t ph = (uint32_t)(g / NA) & 1u;
+      if (g >= NA && !mbar_wait(smem_u32(&aempty[s]), ph ^ 1u, p.err)) break;
+      int img, oh0, ow0, a, colt, pos;
+      pool_tile(p, t, img, oh0, ow0, a, colt, pos);
+      // pixels [ow0, ow0 + 64) of each run, clipped to the row; input rows
+      // past the padded image feed only conv rows past OH
+      const int e0 = max(ow0, 0), e1 = min(ow0 + 64, half);
+      const int r0 = 2 * oh0, nr = min(KH + 2, p.Hp - r0);
+      const uint32_t bytes = e1 > e0 ? (uint32_t)(e1 - e0) * 16u : 0u;
+      uint8_t* dst = abuf + s * R::A_BUF;
+      const uint32_t fb = smem_u32(&afull[s]);
+      mbar_expect_tx(fb, bytes * (uint32_t)(2 * nr * C::NOPS));
+      if (bytes == 0) continue;
+      for (int r = 0; r < nr; ++r) {
+        const int slot = (r & 1) ? nev + (r >> 1) : (r >> 1);
+        const long long rowpix = ((long long)img * p.Hp + r0 + r) * p.Wp;
+        for (int par = 0; par < 2; ++par) {
+          const long long src = (rowpix + (long long)par * half + e0) * 16;
+          const uint32_t off = (uint32_t)((par * R::SLOTS + slot) * R::RUN + (e0 - ow0) * 16);
+          bulk_g2s(smem_u32(dst + off), xh + src, bytes, fb);
+          if constexpr (C::NOPS == 2) bulk_g2s(smem_u32(dst + R::A_OP + off), xl + src, bytes, fb);
+        }
+      }
+    }
+    // every issued copy must have landed before the CTA can exit
+    mbar_wait_own(bb, 0u, p.err);
+    for (int k = g > NA ? g - NA : 0; k < g; ++k)
+      mbar_wait_own(smem_u32(&afull[k % NA]), (uint32_t)(k / NA) & 1u, p.err);
+  } else if (warp == PW && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    bool ok = mbar_wait(smem_u32(bfull), 0u, p.err);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t a_base = smem_u32(abuf), b_base = smem_u32(bres);
+    int g = 0;
+    for (int t = u0; t < u1 && ok; ++t, ++g) {
+      const int b = g & 1;
+      const uint32_t use = (uint32_t)(g >> 1);
+      if (g >= 2 && !mbar_wait(smem_u32(&acc_empty[b]), (use & 1u) ^ 1u, p.err)) break;
+      const int s = g % NA;
+      if (!mbar_wait(smem_u32(&afull[s]), (uint32_t)(g / NA) & 1u, p.err)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t acc_t = tmem + (uint32_t)(b * C::ACC_COLS);
+      const uint32_t ab = a_base + (uint32_t)(s * R::A_BUF);
+      for (int kh = 0; kh < KH; ++kh) {
+        const int slot = (kh & 1) ? nev + (kh >> 1) : (kh >> 1);
+        const uint64_t da_hi = sdesc_kint(ab + (uint32_t)(slot * R::RUN), R::SLOTS * R::RUN, 128);
+        const uint64_t da_lo = desc_add(da_hi, R::A_OP);
+        const uint64_t db_hi = sdesc(b_base + (uint32_t)(kh * R::B_KB));
+        const uint64_t db_lo = desc_add(db_hi, C::B_TILE);
+#pragma unroll
+        for (int ks = 0; ks < C::KSTEPS; ++ks) {
+          const uint32_t aoff = ks * 16, koff = ks * 32;  // one pixel further along both runs; 32 bytes of K
+          const uint32_t acc = (kh > 0 || ks > 0) ? 1u : 0u;
+          if constexpr (C::CAT) {
+            umma<PREC>(acc_t, desc_add(da_hi, aoff), desc_add(db_hi, koff), C::IDESC_CAT, acc);
+            umma<PREC>(acc_t, desc_add(da_lo, aoff), desc_add(db_hi, koff), C::IDESC, 1u);
+          } else if constexpr (C::NOPS == 2) {
+            umma<PREC>(acc_t, desc_add(da_lo, aoff), desc_add(db_hi, koff), C::IDESC, acc);
+            umma<PREC>(acc_t, desc_add(da_hi, aoff), desc_add(db_lo, koff), C::IDESC, 1u);
+            umma<PREC>(acc_t, desc_add(da_hi, aoff), desc_add(db_hi, koff), C::IDESC, 1u);
+          } else {
+            umma<PREC>(acc_t, desc_add(da_hi, aoff), desc_add(db_hi, koff), C::IDESC, acc);
+          }
+        }
+      }
+      umma_commit(smem_u32(&aempty[s]));
+      umma_commit(smem_u32(&acc_full[b]));
+    }
+    umma_commit(smem_u32(done));
+  } else if (warp > PW) {
+    run_pool_epilogue<PREC, 64, CAT>(p, tmem, acc_full, acc_empty, epi, warp - PW - 1, warp & 3, lane, u0, u1, own0);
+  }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == PW) {
@@ -1161,7 +1456,8 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
   } else if (warp > PW && warp <= PW + kEpiWarps) {
     // ---------------- epilogue ----------------
     const int e = warp - PW - 1;
-    run_epilogue<PREC, BN, CAT, true>(p, tmem, acc_full, acc_empty, epi + e * C::EPI_WARP_FLOATS, e, warp & 3, lane,
+    run_epilogue<PREC, BN, CAT, true, false>(p, tmem, acc_full, acc_empty, epi + e * C::EPI_WARP_FLOATS, e, warp & 3,
+                                             lane,
                                  [&](int tm, long long& m_base, int& nvalid) {
                                    m_base = (long long)tm * kBM + (warp & 3) * 32;  // virtual rows
                                    nvalid = -1;
@@ -1282,9 +1578,23 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const 
     if constexpr (Cfg<PREC, BN, true>::CAT)
       PFB_CUDA(cudaFuncSetAttribute(gemm_kernel<PREC, BN, CONV, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     C::SMEM));
-    if constexpr (!CONV && BN == 64)
-      PFB_CUDA(cudaFuncSetAttribute(gemm_kernel<PREC, BN, false, false, true>,
+    if constexpr (!CONV && BN == 64) {
+      PFB_CUDA(cudaFuncSetAttribute(conv_rows_pool_kernel<PREC, Cfg<PREC, BN, true>::CAT>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    RowsCfg<PREC, Cfg<PREC, BN, true>::CAT>::SMEM));
+      PFB_CUDA(cudaFuncSetAttribute(gemm_kernel<PREC, BN, false, false, kEpiMaxPool>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+      if constexpr (Cfg<PREC, BN, true>::CAT)
+        PFB_CUDA(cudaFuncSetAttribute(gemm_kernel<PREC, BN, false, true, kEpiMaxPool>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    }
+    if constexpr (!CONV) {
+      PFB_CUDA(cudaFuncSetAttribute(gemm_kernel<PREC, BN, false, false, kEpiAvg>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+      if constexpr (Cfg<PREC, BN, true>::CAT)
+        PFB_CUDA(cudaFuncSetAttribute(gemm_kernel<PREC, BN, false, true, kEpiAvg>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    }
     if constexpr (!CONV) {
       PFB_CUDA(cudaFuncSetAttribute(conv_halo_kernel<PREC, BN, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     HaloCfg<PREC, BN>::SMEM));
@@ -1364,19 +1674,39 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const 
   p.PH = (int)L.PH;
   p.PW = (int)L.PW;
   p.pool_pad = L.pool_pad;
+  p.gap = L.gap;
+  if (L.gap) {
+    // slots of an image: 4 per row tile, tiles_h x tiles_w row tiles
+    PFB_CHECK_ARG((conv_tma == 1 || conv_tma == 2) && !L.pool && p.tiles_h * p.tiles_w * 4 == conv_gap_slots(L.OH, L.OW),
+                  "gemm: a fused global average pool needs a TMA-fed convolution tiled inside each image");
+  }
+  p.pool_kw = 31;
   if (L.pool) {
-    // pooled rows by conv row pairs, 31 pooled columns per 64-pixel tile
-    PFB_CHECK_ARG(conv_tma == 2 && p.TW == 64 && BN == 64 && L.N == 64, "gemm: the fused max pool needs the windowed "
-                  "TMA convolution with 64 output channels");
+    // pooled rows by conv row pairs; 31 pooled columns per 64-pixel tile of
+    // windows, 30 per tile of row runs
+    if (L.deint) {
+      const int64_t esz = PREC == PFC_PRECISION_BF16 ? 2 : 4;
+      PFB_CHECK_ARG(BN == 64 && L.N == 64 && L.Cp * esz == 16 && p.KWp * L.Cp == C::BK && L.K == L.KH * C::BK &&
+                        L.sh == 2 && L.sw == 2 && L.dh == 1 && L.dw == 1 && L.KH >= 1 && L.KH <= 7 && L.Wp % 2 == 0 &&
+                        L.Wp / 2 >= L.OW + 3 && L.batch_images * L.Hp * L.Wp < (1ll << 40),
+                    "gemm: the row-run stem needs a stride-2 convolution of 8-tap, 16-byte-pixel filter rows over a "
+                    "de-interleaved padded input");
+      p.pool_kw = 30;
+    } else {
+      PFB_CHECK_ARG(conv_tma == 2 && p.TW == 64 && BN == 64 && L.N == 64, "gemm: the fused max pool needs the windowed "
+                    "TMA convolution with 64 output channels");
+    }
     p.tiles_h = (int)ceil_div(L.OH, 2);
-    p.tiles_w = (int)ceil_div(L.PW, 31);
+    p.tiles_w = (int)ceil_div(L.PW, p.pool_kw);
     p.num_m = (int)(L.batch_images * p.tiles_h * p.tiles_w);
   }
   // The concatenated-B instantiation (Cfg::CAT) where a tile has enough
   // k-blocks that the MMAs, not the epilogue, set the pace: it doubles the
-  // epilogue's TMEM reads, which a 7-k-block tile (the 7x7 stem convolution)
-  // does not hide (measured 0.96 -> 1.20 ms), while 18-k-block tiles gain
-  // (3x3 convolutions, 0.54 -> 0.45 ms).
+  // epilogue's TMEM reads, which a 7-k-block tile with the full store
+  // epilogue (the 7x7 stem convolution) does not hide (measured 0.96 -> 1.20
+  // ms), while 18-k-block tiles gain (3x3 convolutions, 0.54 -> 0.45 ms).
+  // The pooled stem, whose epilogue stores a quarter of its tile, takes it
+  // regardless (0.97 -> 0.94 ms).
   const bool cat = Cfg<PREC, BN, true>::CAT && p.nkb >= 12;
   // accumulation chunks of 512 elements of K (16 tf32 / 8 bf16 k-blocks)
   p.kchunk = 512 / C::BK;
@@ -1421,14 +1751,49 @@ void launch_t(const GemmLaunch& L, cudaStream_t stream, int conv_tma = 0, const 
     }
   }
   if constexpr (!CONV && BN == 64) {
+    if (L.pool && L.deint) {
+      if constexpr (Cfg<PREC, BN, true>::CAT) {
+        conv_rows_pool_kernel<PREC, true><<<grid, kThreads<false>, RowsCfg<PREC, true>::SMEM, stream>>>(tb_hi, tb_lo, p);
+      } else {
+        conv_rows_pool_kernel<PREC, false><<<grid, kThreads<false>, RowsCfg<PREC, false>::SMEM, stream>>>(tb_hi, tb_lo,
+                                                                                                         p);
+      }
+      PFB_CUDA(cudaGetLastError());
+      return;
+    }
     if (L.pool) {
-      gemm_kernel<PREC, BN, false, false, true><<<grid, kThreads<false>, C::SMEM, stream>>>(ta_hi, ta_lo, tb_hi, tb_lo,
-                                                                                          p);
+      // the pooled stem takes the concatenated-B MMAs (its epilogue stores a
+      // quarter of the tile, which leaves room for the doubled TMEM reads)
+      if constexpr (Cfg<PREC, BN, true>::CAT) {
+        gemm_kernel<PREC, BN, false, true, kEpiMaxPool><<<grid, kThreads<false>, C::SMEM, stream>>>(ta_hi, ta_lo, tb_hi,
+                                                                                                   tb_lo, p);
+        PFB_CUDA(cudaGetLastError());
+        return;
+      }
+      gemm_kernel<PREC, BN, false, false, kEpiMaxPool><<<grid, kThreads<false>, C::SMEM, stream>>>(ta_hi, ta_lo, tb_hi,
+                                                                                                  tb_lo, p);
       PFB_CUDA(cudaGetLastError());
       return;
     }
   }
   PFB_CHECK_ARG(!L.pool, "gemm: the fused max pool needs the windowed TMA convolution");
+  if constexpr (!CONV) {
+    if (L.gap) {
+      if constexpr (Cfg<PREC, BN, true>::CAT) {
+        if (cat) {
+          gemm_kernel<PREC, BN, false, true, kEpiAvg><<<grid, kThreads<false>, C::SMEM, stream>>>(ta_hi, ta_lo, tb_hi,
+                                                                                                 tb_lo, p);
+          PFB_CUDA(cudaGetLastError());
+          return;
+        }
+      }
+      gemm_kernel<PREC, BN, false, false, kEpiAvg><<<grid, kThreads<false>, C::SMEM, stream>>>(ta_hi, ta_lo, tb_hi,
+                                                                                              tb_lo, p);
+      PFB_CUDA(cudaGetLastError());
+      return;
+    }
+  }
+  PFB_CHECK_ARG(!L.gap, "gemm: the fused global average pool needs a TMA-fed convolution");
   if constexpr (Cfg<PREC, BN, true>::CAT) {
     if (cat) {
       gemm_kernel<PREC, BN, CONV, true><<<grid, kThreads<CONV>, C::SMEM, stream>>>(ta_hi, ta_lo, tb_hi, tb_lo, p);
@@ -1478,7 +1843,7 @@ int conv_tma_mode(const GemmLaunch& L, int prec, CUtensorMap* maps, int* TW) {
     }
   }
   if (L.OW < 32) return 0;
-  *TW = L.OW > 32 ? 64 : 32;
+  *TW = conv_tile_w(L.OW);
   int mode = 0;
   if (L.Hp == 0 && L.Cp % bk == 0 && L.sh == 1 && L.sw == 1 && kwp == L.KW) mode = 1;
   else if (L.Hp > 0 && kwp * L.Cp == bk && L.dw == 1 && (L.sw * L.Cp * esz) % 16 == 0) mode = 2;
@@ -1493,7 +1858,13 @@ void launch_gemm(const GemmLaunch& L, cudaStream_t stream) {
   PFB_CHECK_ARG(L.M > 0 && L.N > 0 && L.batch > 0, "gemm: empty problem");
   PFB_CHECK_ARG(L.M < (1ll << 31) && L.N < (1ll << 31), "gemm: dimension too large");
   PFB_CHECK_ARG(L.err != nullptr, "gemm: error flag pointer required");
-  PFB_CHECK_ARG(L.c || L.out_hi || L.pool_y, "gemm: no output");
+  PFB_CHECK_ARG(L.c || L.out_hi || L.pool_y || L.gap, "gemm: no output");
+  if (L.gap) {
+    PFB_CHECK_ARG(L.conv && !L.pool && !L.residual && L.batch == 1 && !L.c && !L.out_hi && L.OW >= 32 &&
+                      (L.act == 0 || L.act == 1),
+                  "gemm: a fused global average pool replaces the output of a convolution with rows of 32+ pixels "
+                  "(no activation or ReLU)");
+  }
   if (L.pool) {
     PFB_CHECK_ARG(L.conv && L.N == 64 && L.act == 1 && !L.residual && L.batch == 1 && L.Hp > 0 && L.PH > 0 &&
                       L.PW > 0 && (L.pool_pad == 0 || L.pool_pad == 1) &&

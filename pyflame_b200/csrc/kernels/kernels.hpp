@@ -58,6 +58,10 @@ struct GemmLaunch {
   bool pool = false;
   int pool_pad = 0;
   float* pool_y = nullptr;
+  // deint: x is a de-interleaved padded copy (ConvInputLaunch::deint); a
+  // pooled stride-2 stem with 8-tap filter rows of 16-byte pixels then reads
+  // it as row runs (conv_rows_pool_kernel)
+  bool deint = false;
   int64_t pool_sn = 0, pool_sh = 0, pool_sw = 0, PH = 0, PW = 0;
   // Workspace for a split last wave (plain GEMMs): tail_ws_bytes of fp32
   // slots (one 128 x BN tile per CTA) and tail_cnt_len counters that start
@@ -67,8 +71,22 @@ struct GemmLaunch {
   int64_t tail_ws_bytes = 0;
   unsigned* tail_cnt = nullptr;
   int64_t tail_cnt_len = 0;
+  // gap: AdaptiveAvgPool2d(1) of the output of a TMA-fed convolution (rows of
+  // 32+ output pixels) replaces c: per image conv_gap_slots(OH, OW) rows of
+  // N column sums, [N][slots][N] (a PoolLaunch of mode 3 adds them up)
+  float* gap = nullptr;
 };
 void launch_gemm(const GemmLaunch& L, cudaStream_t stream);
+
+// Output tile width (pixels) of a TMA-fed convolution whose output rows are
+// ow >= 32 pixels wide; tiles are conv_tile_w x 128 / conv_tile_w pixels.
+inline int conv_tile_w(int64_t ow) { return ow > 32 ? 64 : 32; }
+// Partial-sum rows per image of a convolution with a fused global average
+// pool: four (one per TMEM lane quarter) per output tile.
+inline int64_t conv_gap_slots(int64_t oh, int64_t ow) {
+  const int64_t tw = conv_tile_w(ow), th = 128 / tw;
+  return 4 * ((oh + th - 1) / th) * ((ow + tw - 1) / tw);
+}
 
 // Fused attention O = softmax(alpha * Q K^T) V over batch slices (3xTF32
 // operands as prepared for the GEMM): Q [batch][M][kq], K [batch][L][kq] and
@@ -111,6 +129,9 @@ struct ConvInputLaunch {
   int64_t cp = 0;
   // zero-padded output [N][hp][wp][cp] with the image at (ph, pw); hp = 0: unpadded
   int64_t hp = 0, wp = 0, ph = 0, pw = 0;
+  // deint (padded, wp even): each padded row stores its even columns first,
+  // then its odd columns (column w at (w & 1) * wp/2 + w/2)
+  bool deint = false;
   int precision = 0;
   void* hi = nullptr;
   float* lo = nullptr;
@@ -169,6 +190,10 @@ struct PoolLaunch {
   void* out_hi = nullptr;
   float* out_lo = nullptr;
   int precision = 0;
+  // mode 3: the global average pool finished from a convolution's partial
+  // sums (GemmLaunch::gap): x [n][h slots][c] (strides sn, sh, sc), out =
+  // the sum of an image's slots in slot order / count
+  int64_t count = 0;
 };
 void launch_pool(const PoolLaunch& L, cudaStream_t stream);
 

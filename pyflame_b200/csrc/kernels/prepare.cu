@@ -273,9 +273,12 @@ __global__ void conv_input_kernel(ConvInputLaunch L) {
   const IDX OHp = L.hp > 0 ? (IDX)L.hp : H, OWp = L.hp > 0 ? (IDX)L.wp : W;
   const IDX PH = L.hp > 0 ? (IDX)L.ph : 0, PW = L.hp > 0 ? (IDX)L.pw : 0;
   const IDX total = (IDX)L.n * OHp * OWp;
+  const IDX half = OWp / 2;
   for (IDX pix = (IDX)blockIdx.x * blockDim.x + threadIdx.x; pix < total; pix += (IDX)gridDim.x * blockDim.x) {
     const IDX wq = pix % OWp;
     const IDX hn = pix / OWp;
+    // destination pixel: de-interleaved rows keep even columns, then odd ones
+    const IDX dpix = L.deint ? hn * OWp + (wq & 1) * half + (wq >> 1) : pix;
     const IDX hq = hn % OHp;
     const IDX n = hn / OHp;
     const IDX h = hq - PH, w = wq - PW;
@@ -301,7 +304,7 @@ __global__ void conv_input_kernel(ConvInputLaunch L) {
         pk.y = *(const uint32_t*)&b;
         pk.z = *(const uint32_t*)&c;
         pk.w = *(const uint32_t*)&d;
-        *(uint4*)((__nv_bfloat16*)L.hi + 4 * (pix * G + g)) = pk;
+        *(uint4*)((__nv_bfloat16*)L.hi + 4 * (dpix * G + g)) = pk;
       }
     } else {
       for (IDX g = 0; g < G; ++g) {
@@ -312,8 +315,8 @@ __global__ void conv_input_kernel(ConvInputLaunch L) {
         split_tf32(x[1], hv.y, lv.y);
         split_tf32(x[2], hv.z, lv.z);
         split_tf32(x[3], hv.w, lv.w);
-        *(float4*)((float*)L.hi + 4 * (pix * G + g)) = hv;
-        *(float4*)(L.lo + 4 * (pix * G + g)) = lv;
+        *(float4*)((float*)L.hi + 4 * (dpix * G + g)) = hv;
+        *(float4*)(L.lo + 4 * (dpix * G + g)) = lv;
       }
     }
   }
@@ -516,6 +519,53 @@ __global__ void __launch_bounds__(256) global_avg_cl4_kernel(PoolLaunch L) {
   }
 }
 
+// Global average pool finished from a convolution's per-tile column sums
+// (PoolLaunch mode 3): one CTA per image.  For each block of 64 channels,
+// four thread groups add a quarter of the image's slots each (four loads in
+// flight, coalesced across channels), and the four parts are added in part
+// order: a fixed summation order.
+__global__ void __launch_bounds__(256) gap_finish_kernel(PoolLaunch L) {
+  __shared__ float part[4][64];
+  const int t = threadIdx.x, cl = t & 63, g = t >> 6;
+  const long long n = blockIdx.x;
+  const long long r0 = L.h * g / 4, r1 = L.h * (g + 1) / 4;
+  for (long long c0 = 0; c0 < L.c; c0 += 64) {
+    const long long c = c0 + cl;
+    float s = 0.f;
+    if (c < L.c) {
+      const float* xb = L.x + n * L.sn + c * L.sc;
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      long long r = r0;
+      for (; r + 3 < r1; r += 4) {
+        a0 += xb[r * L.sh];
+        a1 += xb[(r + 1) * L.sh];
+        a2 += xb[(r + 2) * L.sh];
+        a3 += xb[(r + 3) * L.sh];
+      }
+      for (; r < r1; ++r) a0 += xb[r * L.sh];
+      s = (a0 + a1) + (a2 + a3);
+    }
+    part[g][cl] = s;
+    __syncthreads();
+    if (g == 0 && c < L.c) {
+      const float out = (((part[0][cl] + part[1][cl]) + part[2][cl]) + part[3][cl]) / (float)L.count;
+      const long long yo = n * L.osn + c * L.osc;
+      if (L.y) L.y[yo] = out;
+      if (L.out_hi) {
+        if (L.precision == PFC_PRECISION_BF16) {
+          ((__nv_bfloat16*)L.out_hi)[yo] = __float2bfloat16_rn(out);
+        } else {
+          float hv, lv;
+          split_tf32(out, hv, lv);
+          ((float*)L.out_hi)[yo] = hv;
+          L.out_lo[yo] = lv;
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
 __global__ void bn_fold_kernel(BnFoldLaunch L) {
   for (long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x; c < L.channels; c += (long long)gridDim.x * blockDim.x) {
     const float g = L.gamma ? L.gamma[c * L.gs] : L.gamma_c;
@@ -604,6 +654,13 @@ void launch_pool(const PoolLaunch& L, cudaStream_t stream) {
   PFB_CHECK_ARG(!L.out_hi || (L.osc == 1 && L.osw == L.c && L.osh == L.ow * L.c && L.osn == L.oh * L.ow * L.c &&
                               (L.precision == PFC_PRECISION_BF16 || L.out_lo)),
                 "pool: operand output needs a dense channels-last layout");
+  if (L.mode == 3) {
+    PFB_CHECK_ARG(L.oh == 1 && L.ow == 1 && L.w == 1 && L.count > 0 && L.n < (1ll << 31),
+                  "pool: a finished global average needs 1x1 outputs and a pixel count");
+    gap_finish_kernel<<<(unsigned)L.n, 256, 0, stream>>>(L);
+    PFB_CUDA(cudaGetLastError());
+    return;
+  }
   if (L.mode == 2 && L.oh == 1 && L.ow == 1 && L.sc == 1 && L.sw == L.c && L.sh == L.w * L.c && L.c % 4 == 0 &&
       L.c <= 1024 && L.sn % 4 == 0 && ((uintptr_t)L.x & 15) == 0 && L.h * L.w < (1ll << 30) && L.n < (1ll << 31)) {
     global_avg_cl4_kernel<<<(unsigned)L.n, 256, 0, stream>>>(L);
@@ -641,6 +698,7 @@ void launch_conv_input(const ConvInputLaunch& L, cudaStream_t stream) {
   PFB_CHECK_ARG(((uintptr_t)L.hi & 15) == 0 && ((uintptr_t)L.lo & 15) == 0, "conv input: outputs must be 16-byte aligned");
   PFB_CHECK_ARG(L.hp == 0 || (L.hp >= L.h + L.ph && L.wp >= L.w + L.pw), "conv input: padded extent too small");
   PFB_CHECK_ARG(L.precision != PFC_PRECISION_BF16 || L.cp % 8 == 0, "conv input: bf16 channels come in groups of 8");
+  PFB_CHECK_ARG(!L.deint || (L.hp > 0 && L.wp % 2 == 0), "conv input: de-interleaved rows need an even padded width");
   const long long total = L.n * (L.hp > 0 ? L.hp * L.wp : L.h * L.w);  // output pixels, one thread each
   if (total == 0) return;
   const unsigned g = grid_for(total, 256);

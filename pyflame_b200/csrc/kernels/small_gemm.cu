@@ -376,11 +376,6 @@ size_t cluster_smem(int R, int S, int64_t K, int64_t N2) {
   return ((size_t)(R + S) * (size_t)K + (size_t)R * S + (size_t)R * (size_t)N2) * sizeof(float) + 16;
 }
 
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-               "l"(src), "r"(bytes), "r"(mbar)
-               : "memory");
-}
 
 __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kSWarps * 32) small_mlp_cluster_kernel(CParams p) {
   namespace cg = cooperative_groups;

@@ -151,6 +151,27 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
 // descriptor directly: its low 14 bits hold the address in 16-byte units.
 __device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t bytes) { return d + (bytes >> 4); }
 
+// Descriptor of a K-major operand without swizzle: core matrices of 8 rows x
+// 16 bytes, each stored as 128 contiguous bytes (rows 16 bytes apart); lbo =
+// bytes from the first to the second 16-byte half of a 32-byte K step, sbo =
+// bytes between consecutive 8-row groups.
+__device__ __forceinline__ uint64_t sdesc_kint(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // version; layout type 0: no swizzle
+  return d;
+}
+
+// 1-D bulk copy global -> shared (16-byte aligned addresses, a multiple of
+// 16 bytes), completing on the mbarrier's transaction count.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(mbar)
+               : "memory");
+}
+
 // Instruction descriptor for kind::tf32 / kind::f16: D fp32, K-major A and B.
 __host__ __device__ constexpr uint32_t idesc(int M, int N, uint32_t ab_fmt) {
   return (1u << 4) | (ab_fmt << 7) | (ab_fmt << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);

@@ -96,6 +96,7 @@ struct ConvInputArgs {
   int64_t cp = 0;
   int64_t hp = 0, wp = 0, ph = 0, pw = 0;
   int precision = 0;
+  bool deint = false;  // padded rows stored even columns first, then odd (ConvInputLaunch::deint)
 };
 
 struct Im2colArgs {
@@ -140,6 +141,13 @@ struct GemmArgs {
   int pool_pad = 0;
   View pool_y;
   bool write_pool_y = true;
+  // AdaptiveAvgPool2d(1) of the output in the epilogue: per-tile column sums
+  // into gap_buf (conv_gap_slots rows per image), finished by a POOL step of
+  // mode 3; replaces c
+  int gap_buf = -1;
+  // the input copy x_hi / x_lo is de-interleaved (ConvInputArgs::deint): the
+  // pooled stem reads it as row runs
+  bool deint = false;
 };
 
 struct PoolArgs {
@@ -150,6 +158,9 @@ struct PoolArgs {
   // channels-last operand copy for a following implicit-GEMM Conv2d
   int op_hi = -1, op_lo = -1;
   bool write_y = true;
+  // mode 3 (global average from a convolution's partial sums, x = [n][slots][c]):
+  // pixels per image
+  int64_t count = 0;
 };
 
 struct BnFoldArgs {

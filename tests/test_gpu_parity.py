@@ -478,6 +478,7 @@ def test_conv_bn_relu_maxpool_fused(oracle_mod, rng, native, precision, n, h, w,
     g = pooled.graph()
     plan = ex.describe_plan(g, [pooled.node().id(), nxt.node().id()])
     assert "+max_pool2d" in plan and "] max_pool2d" not in plan, plan
+    assert "(row runs)" in plan and "(de-interleaved rows)" in plan, plan
     gpu, ref = run(ex, [pooled, nxt], oracle_mod)
     # unfused: the ReLU output is an output too, so the pool runs on its own
     plan2 = ex.describe_plan(g, [pooled.node().id(), r.node().id()])
@@ -494,6 +495,85 @@ def test_conv_bn_relu_maxpool_fused(oracle_mod, rng, native, precision, n, h, w,
     np.testing.assert_allclose(flat(gpu[0]), flat(unfused), rtol=1e-6, atol=1e-6 * term.max(),
                                err_msg="fused pool vs unfused")
     close_rows(flat(gpu[1]), flat(ref[1]), tol if precision == "tf32x3" else 4 * tol, what="conv after the pool")
+    ex.close()
+
+
+@pytest.mark.parametrize("precision", ["tf32x3", "bf16"])
+@pytest.mark.parametrize("pad", [0, 1])
+def test_conv_relu_maxpool_fused_windows(oracle_mod, rng, native, precision, pad):
+    """A stride-1 5x5 convolution of 3 channels with ReLU and MaxPool2d(3, 2):
+    the pool runs in the epilogue of the overlapping-window feed (64-column
+    tiles, 31 pooled columns each), not the row-run feed of the stride-2
+    stem."""
+    ex = pf.CudaExecutor(pf.CudaExecutor.Config(precision=precision))
+    x = pf.tensor(rng.random((2, 3, 41, 75)).astype(np.float32))
+    conv = nn.Conv2d(3, 64, 5, 1, 2)
+    conv.set_parameter("weight", (rng.standard_normal((64, 3, 5, 5)) * np.sqrt(2 / 75)).astype(np.float32))
+    conv.set_parameter("bias", rng.uniform(-0.2, 0.2, 64).astype(np.float32))
+    c = conv(x)
+    pooled = nn.MaxPool2d(3, 2, pad)(pf.relu(c))
+    g = pooled.graph()
+    plan = ex.describe_plan(g, [pooled.node().id()])
+    assert "+max_pool2d" in plan and "(row runs)" not in plan, plan
+    (gpu,), (ref,) = run(ex, [pooled], oracle_mod)
+    conv_ref = oracle_mod.run(g, [c.node().id()])[c.node().id()].astype(np.float64)
+    term = np.sqrt(np.mean(conv_ref ** 2, axis=(2, 3))).reshape(-1, 1) + 0.2
+    tol = RTOL_GEMM_TF32X3 if precision == "tf32x3" else RTOL_GEMM_BF16
+    flat = lambda a: a.reshape(-1, a.shape[-1] * a.shape[-2])
+    close(flat(gpu), flat(ref), rtol=tol, atol=tol * term, what="windowed fused pool vs oracle")
+    ex.close()
+
+
+@pytest.mark.parametrize("precision", ["tf32x3", "bf16"])
+@pytest.mark.parametrize("cin,cout,k,st,pd,n,h,w,act", [
+    (64, 64, 3, 1, 1, 3, 55, 55, "relu"),    # the conv stack's last convolution: 64 x 2 boxes, 9 columns dropped
+    (64, 128, 3, 1, 1, 2, 33, 40, "none"),   # 128-column tiles, an odd height, 24 columns dropped per tile
+    (128, 64, 1, 1, 0, 2, 20, 32, "bnrelu"),  # 32 x 4 boxes
+    (3, 64, 7, 2, 3, 2, 96, 100, "bnrelu"),  # windows over the padded input (the stem's feed)
+])
+def test_conv_global_avg_pool_fused(oracle_mod, rng, native, precision, cin, cout, k, st, pd, n, h, w, act):
+    """Conv2d (+ bias or BatchNorm) (+ ReLU) -> AdaptiveAvgPool2d(1) with the
+    pool's sums in the convolution's epilogue (one row of column sums per
+    tile and TMEM lane quarter, added per image in slot order by the pool
+    step): tiles with columns or rows outside the image, 64- and 128-column
+    tiles, boxes and windows.  Checked against the oracle and against the
+    unfused graph (the conv output also an output)."""
+    ex = pf.CudaExecutor(pf.CudaExecutor.Config(precision=precision))
+    x = pf.tensor(rng.standard_normal((n, cin, h, w)).astype(np.float32))
+    conv = nn.Conv2d(cin, cout, k, st, pd)
+    conv.set_parameter("weight", (rng.standard_normal((cout, cin, k, k)) * np.sqrt(2 / (cin * k * k))).astype(np.float32))
+    conv.set_parameter("bias", rng.uniform(-0.2, 0.2, cout).astype(np.float32))
+    c = conv(x)
+    scale = np.ones(cout)
+    if act == "bnrelu":
+        bn = nn.BatchNorm2d(cout)
+        bn.eval()
+        params = {}
+        for name, lo, hi in [("weight", 0.5, 1.5), ("bias", -0.3, 0.3), ("running_mean", -0.3, 0.3),
+                             ("running_var", 0.5, 2.0)]:
+            params[name] = rng.uniform(lo, hi, cout).astype(np.float32)
+            bn.set_parameter(name, params[name])
+        r = pf.relu(bn(c))
+        scale = np.abs(params["weight"] / np.sqrt(params["running_var"].astype(np.float64) + 1e-5))
+    else:
+        r = pf.relu(c) if act == "relu" else c
+    gap = nn.AdaptiveAvgPool2d(1)(r)
+    g = gap.graph()
+    plan = ex.describe_plan(g, [gap.node().id()])
+    assert "+average sums" in plan and "from the convolution's sums" in plan, plan
+    (fused,), (ref,) = run(ex, [gap], oracle_mod)
+    plan2 = ex.describe_plan(g, [gap.node().id(), r.node().id()])
+    assert "+average sums" not in plan2, plan2
+    res2 = ex.execute(g, [gap.node().id(), r.node().id()])
+    assert res2.success, res2.error_message
+    unfused = res2.outputs[gap.node().id()]
+    conv_ref = oracle_mod.run(g, [c.node().id()])[c.node().id()].astype(np.float64)
+    term = np.sqrt(np.mean(conv_ref ** 2, axis=(2, 3))) * scale[None, :] + 0.2
+    tol = RTOL_GEMM_TF32X3 if precision == "tf32x3" else RTOL_GEMM_BF16
+    assert fused.shape == (n, cout, 1, 1)
+    close(fused.reshape(n, cout), ref.reshape(n, cout), rtol=tol, atol=tol * term, what="fused average vs oracle")
+    close(unfused.reshape(n, cout), ref.reshape(n, cout), rtol=tol, atol=tol * term, what="unfused average vs oracle")
+    close(fused.reshape(n, cout), unfused.reshape(n, cout), rtol=1e-5, atol=1e-5 * term, what="fused average vs unfused")
     ex.close()
 
 
