@@ -761,29 +761,37 @@ __device__ __forceinline__ void run_pool_epilogue(const GemmParams& p, uint32_t 
         if (p.o_hi) store_operand1<PREC>(p.o_hi, p.o_lo, off, o);
       }
     }
-    // the tile recomputed before a run only feeds the carry
-    if (r == ro && (lane & 1) == 0 && kq < KW && !(span && kq == 15) && t >= own0) {
+    // Row ro: pooled column kq of lane pair (2kq, 2kq+1), the even lane
+    // taking channels 8i..8i+3 and the odd lane 8i+4..8i+7 (i = 0..3), so
+    // that each store instruction writes whole 32-byte sectors; the odd lane
+    // takes its window maxima from the even one.  (t, own0 and r are uniform
+    // over the warp.)  The tile recomputed before a run only feeds the carry.
+    if (r == ro && t >= own0) {
+      const int odd = lane & 1;
+      float hs[HALF / 2];
+#pragma unroll
+      for (int i = 0; i < HALF / 8; ++i) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float y = __shfl_sync(0xffffffffu, hm[8 * i + 4 + u], lane & ~1);
+          hs[4 * i + u] = odd ? y : hm[8 * i + u];
+        }
+      }
       const int pw = KW * colt + kq;
-      if (pw < p.PW && a < p.PH) {
-        float o[HALF];
-#pragma unroll
-        for (int j = 0; j < HALF; ++j) {
-          const float h1 = next[j * 32 + kq];
-          const float c = pos == 0 ? 0.f : carry[j * 32 + kq];  // a strip's first tile carries padding
-          o[j] = fmaxf(c, fmaxf(hm[j], h1));
-        }
+      if (kq < KW && !(span && kq == 15) && pw < p.PW && a < p.PH) {
         const long long off = (long long)img * p.py_sn + (long long)a * p.py_sh + (long long)pw * p.py_sw + col0;
-        if (p.py) {
 #pragma unroll
-          for (int j = 0; j < HALF; j += 4)
-            *reinterpret_cast<float4*>(p.py + off + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
-        }
-        if (p.o_hi) {
+        for (int i = 0; i < HALF / 8; ++i) {
+          const int j0 = 8 * i + 4 * odd;
+          float o[4];
 #pragma unroll
-          for (int j = 0; j < HALF; j += 4) {
-            const float w4[4] = {o[j], o[j + 1], o[j + 2], o[j + 3]};
-            store_operand4<PREC>(p.o_hi, p.o_lo, off + j, w4);
+          for (int u = 0; u < 4; ++u) {
+            const float h1 = next[(j0 + u) * 32 + kq];
+            const float c = pos == 0 ? 0.f : carry[(j0 + u) * 32 + kq];  // a strip's first tile carries padding
+            o[u] = fmaxf(c, fmaxf(hs[4 * i + u], h1));
           }
+          if (p.py) *reinterpret_cast<float4*>(p.py + off + j0) = make_float4(o[0], o[1], o[2], o[3]);
+          if (p.o_hi) store_operand4<PREC>(p.o_hi, p.o_lo, off + j0, o);
         }
       }
     }
