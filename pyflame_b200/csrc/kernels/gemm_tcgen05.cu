@@ -620,8 +620,8 @@ __device__ __forceinline__ void run_epilogue(const GemmParams& p, uint32_t tmem,
 //      memory; barrier.
 //   3. Row ro combines the carry, its own and row rc's maxima into pooled row
 //      a and stores it as fp32 and / or the next convolution's operand; the
-//      spanning window (pooled column 15) is finished by one warp with a
-//      channel per lane.
+//      spanning window (pooled column 15) is finished by a warp of row rc,
+//      whose other work is lighter, with a channel per lane.
 // The eight epilogue warps meet at two named barriers per tile, so every
 // warp takes every tile; a failed wait is agreed on at the first barrier.
 // Scale and shift are staged per channel in shared memory once.  (Clock
@@ -635,7 +635,7 @@ __device__ __forceinline__ void run_pool_epilogue(const GemmParams& p, uint32_t 
                                                   int u1, int own0) {
   using C = Cfg<PREC, BN, CAT>;
   static_assert(BN == 64, "the pooled epilogue takes 64-channel tiles");
-  static_assert((2 * 64 * 32 + 4 * 64 + 2 * 64) * 4 <= C::EPI_BYTES, "pool buffers exceed the epilogue staging area");
+  static_assert((2 * 64 * 32 + 4 * 64 + 3 * 64) * 4 <= C::EPI_BYTES, "pool buffers exceed the epilogue staging area");
   constexpr int HALF = BN / 2;
   const int KW = p.pool_kw;  // pooled columns per tile (30 or 31; column 15 spans the warps)
   const int col0 = (e >> 2) * HALF;
@@ -647,8 +647,11 @@ __device__ __forceinline__ void run_pool_epilogue(const GemmParams& p, uint32_t 
   float* rowbuf = sm;
   float* bnd = sm + 2 * 64 * 32;  // [4][64]: row ro column 32, row rc columns 30, 31, 32
   float2* scsh = reinterpret_cast<float2*>(sm + 2 * 64 * 32 + 4 * 64);  // [64] (scale, shift) per channel
+  float* h30 = sm + 2 * 64 * 32 + 4 * 64 + 2 * 64;  // [64]: row ro's maxima of columns 30, 31
   // warp q = 2ro finishes pooled column 15 (conv columns 30..32 span two warps)
-  const bool span = q == 2 * ro;
+  // warp q = 2rc (of the lighter row) finishes pooled column 15 (conv
+  // columns 30..32 span two warps), from lane 30 of warp q = 2ro
+  const bool span = q == 2 * rc, ro30 = q == 2 * ro && lane == 30;
   const int bslot = q == 2 * ro + 1 && lane == 0 ? 0
                     : q == 2 * rc && lane == 30  ? 1
                     : q == 2 * rc && lane == 31  ? 2
@@ -738,24 +741,23 @@ __device__ __forceinline__ void run_pool_epilogue(const GemmParams& p, uint32_t 
       for (int j = 0; j < HALF; j += 4)
         *reinterpret_cast<float4*>(bnd + bslot * 64 + col0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
     }
+    if (ro30) {
+#pragma unroll
+      for (int j = 0; j < HALF; j += 4)
+        *reinterpret_cast<float4*>(h30 + col0 + j) = make_float4(hm[j], hm[j + 1], hm[j + 2], hm[j + 3]);
+    }
     epi_bar();
     if (span) {
       // pooled column 15 with one channel per lane (n = col0 + lane): row
       // rc's window (its next carry) from the boundary pixels, row ro's from
-      // lane 30's maxima of columns 30, 31 and the other warp's column 32
+      // its lane 30's maxima of columns 30, 31 and column 32
       const int n = col0 + lane;
       const float h1 = fmaxf(bnd[64 + n], fmaxf(bnd[128 + n], bnd[192 + n]));
       next[lane * 32 + 15] = h1;
-      float m30 = 0.f;
-#pragma unroll
-      for (int j = 0; j < HALF; ++j) {
-        const float y = __shfl_sync(0xffffffffu, hm[j], 30);
-        if (lane == j) m30 = y;
-      }
       const int pw = KW * colt + 15;
       if (t >= own0 && 15 < KW && pw < p.PW && a < p.PH) {
         const float c = pos == 0 ? 0.f : carry[lane * 32 + 15];
-        const float o = fmaxf(c, fmaxf(fmaxf(m30, bnd[n]), h1));
+        const float o = fmaxf(c, fmaxf(fmaxf(h30[n], bnd[n]), h1));
         const long long off = (long long)img * p.py_sn + (long long)a * p.py_sh + (long long)pw * p.py_sw + n;
         if (p.py) p.py[off] = o;
         if (p.o_hi) store_operand1<PREC>(p.o_hi, p.o_lo, off, o);
@@ -778,7 +780,7 @@ __device__ __forceinline__ void run_pool_epilogue(const GemmParams& p, uint32_t 
         }
       }
       const int pw = KW * colt + kq;
-      if (kq < KW && !(span && kq == 15) && pw < p.PW && a < p.PH) {
+      if (kq < KW && !(q == 2 * ro && kq == 15) && pw < p.PW && a < p.PH) {
         const long long off = (long long)img * p.py_sn + (long long)a * p.py_sh + (long long)pw * p.py_sw + col0;
 #pragma unroll
         for (int i = 0; i < HALF / 8; ++i) {
