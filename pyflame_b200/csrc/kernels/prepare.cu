@@ -520,35 +520,36 @@ __global__ void __launch_bounds__(256) global_avg_cl4_kernel(PoolLaunch L) {
 }
 
 // Global average pool finished from a convolution's per-tile column sums
-// (PoolLaunch mode 3): one CTA per image.  For each block of 64 channels,
-// four thread groups add a quarter of the image's slots each (four loads in
-// flight, coalesced across channels), and the four parts are added in part
-// order: a fixed summation order.
-__global__ void __launch_bounds__(256) gap_finish_kernel(PoolLaunch L) {
-  __shared__ float part[4][64];
+// (PoolLaunch mode 3): one 512-thread CTA per image.  For each block of 64
+// channels, eight thread groups add an eighth of the image's slots each
+// (eight loads in flight per thread, coalesced across channels), and the
+// eight parts are added in part order: a fixed summation order.
+__global__ void __launch_bounds__(512) gap_finish_kernel(PoolLaunch L) {
+  __shared__ float part[8][64];
   const int t = threadIdx.x, cl = t & 63, g = t >> 6;
   const long long n = blockIdx.x;
-  const long long r0 = L.h * g / 4, r1 = L.h * (g + 1) / 4;
+  const long long r0 = L.h * g / 8, r1 = L.h * (g + 1) / 8;
   for (long long c0 = 0; c0 < L.c; c0 += 64) {
     const long long c = c0 + cl;
     float s = 0.f;
     if (c < L.c) {
       const float* xb = L.x + n * L.sn + c * L.sc;
-      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       long long r = r0;
-      for (; r + 3 < r1; r += 4) {
-        a0 += xb[r * L.sh];
-        a1 += xb[(r + 1) * L.sh];
-        a2 += xb[(r + 2) * L.sh];
-        a3 += xb[(r + 3) * L.sh];
+      for (; r + 7 < r1; r += 8) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) a[k] += xb[(r + k) * L.sh];
       }
-      for (; r < r1; ++r) a0 += xb[r * L.sh];
-      s = (a0 + a1) + (a2 + a3);
+      for (; r < r1; ++r) a[0] += xb[r * L.sh];
+      s = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
     }
     part[g][cl] = s;
     __syncthreads();
     if (g == 0 && c < L.c) {
-      const float out = (((part[0][cl] + part[1][cl]) + part[2][cl]) + part[3][cl]) / (float)L.count;
+      float tot = part[0][cl];
+#pragma unroll
+      for (int k = 1; k < 8; ++k) tot += part[k][cl];
+      const float out = tot / (float)L.count;
       const long long yo = n * L.osn + c * L.osc;
       if (L.y) L.y[yo] = out;
       if (L.out_hi) {
@@ -657,7 +658,7 @@ void launch_pool(const PoolLaunch& L, cudaStream_t stream) {
   if (L.mode == 3) {
     PFB_CHECK_ARG(L.oh == 1 && L.ow == 1 && L.w == 1 && L.count > 0 && L.n < (1ll << 31),
                   "pool: a finished global average needs 1x1 outputs and a pixel count");
-    gap_finish_kernel<<<(unsigned)L.n, 256, 0, stream>>>(L);
+    gap_finish_kernel<<<(unsigned)L.n, 512, 0, stream>>>(L);
     PFB_CUDA(cudaGetLastError());
     return;
   }
